@@ -1,0 +1,169 @@
+/* qwen_cuda.h — C ABI of the B200 decode engine for Qwen3-MoE GGUF models.
+ *
+ * Library: qwen-30brust_b200/libqwen_cuda.so (sm_100a kernels, CUDA runtime linked statically).
+ *
+ * This is the drop-in boundary for the reference crate K410Sh4/QWEN-30BRust
+ * (qwen-rust 0.1.0).  Its plugin API is the per-matvec trait
+ *     trait Backend { fn matvec(&mut self, model: &Gguf, name: &str,
+ *                               expert: Option<usize>, x: &[f32]) -> Result<Vec<f32>>;
+ *                     fn stats(&self) -> &Stats; }            (src/backend.rs:14-23)
+ * called 29*layers+1 times per token by Model::forward_inner (src/model.rs:217-302).
+ * Here the boundary moves up to the whole token: qc_forward replaces
+ * Model::forward + every Backend::matvec of that token, so activations never
+ * leave the device between matvecs.  The per-matvec entry points
+ * (qc_matrix_*, qc_packed_matvec) remain for the reference's matvec tests
+ * and microbenchmarks.
+ *
+ * Conventions (mirroring the Rust side):
+ *   - every call returns an int status, QC_OK (0) on success;
+ *   - the message of the last failure is qc_engine_error(engine) or, for calls
+ *     without an engine, qc_last_error() (thread-local);
+ *   - a failed qc_forward / qc_forward_tokens / qc_decode_greedy resets the KV
+ *     cache and position, as Model::forward does (src/model.rs:210-216);
+ *   - one engine is used by one thread at a time (the reference takes &mut self);
+ *   - the caller keeps ownership of every host buffer; the engine copies the
+ *     weights to the device at creation and never reads `base` afterwards.
+ */
+#ifndef QWEN_CUDA_H
+#define QWEN_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  QC_OK = 0,
+  QC_ERR_INVALID = 1,   /* bad argument, shape, type or metadata */
+  QC_ERR_CUDA = 2,      /* a CUDA runtime call failed */
+  QC_ERR_CONTEXT = 3,   /* "context limit reached" (model.rs:219-223) */
+  QC_ERR_TOKEN = 4,     /* "token outside vocabulary" (model.rs:224) */
+  QC_ERR_NONFINITE = 5, /* "nonfinite model output" (model.rs:296-299) or non-finite router logits (ops.rs:50-52) */
+  QC_ERR_NOMEM = 6      /* device allocation failed */
+};
+
+typedef struct qc_engine qc_engine;
+typedef struct qc_matrix qc_matrix;
+
+/* Model hyper-parameters; same fields and meaning as model.rs:5-19 Config. */
+typedef struct qc_config {
+  uint32_t hidden, layers, heads, kvheads, head_dim, experts, top, intermediate, vocab, max_context;
+  float eps, theta;
+} qc_config;
+
+/* One GGUF tensor; same fields as gguf.rs:14-21 Tensor.  dims are in GGUF order
+ * (dims[0] = columns).  `offset` is the absolute byte offset of the tensor data
+ * in the caller's buffer (gguf.rs:175-178 after adding the data start). */
+typedef struct qc_tensor_desc {
+  const char* name;
+  uint32_t kind;
+  uint32_t n_dims;
+  uint64_t dims[3];
+  uint64_t offset;
+  uint64_t len;
+} qc_tensor_desc;
+
+/* Counters; the first four fields are backend.rs:7-13 Stats. */
+typedef struct qc_stats {
+  uint64_t matvecs;        /* matvecs the reference would have issued: (5+3*top)*layers+1 per token */
+  uint64_t uploaded_bytes; /* host->device weight bytes (at creation only) */
+  uint64_t cache_hits;     /* always 0: every weight stays resident, there is no cache */
+  double matvec_ms;        /* device time of the forward steps run so far (CUDA events) */
+  uint64_t tokens;         /* forward steps run */
+  uint64_t weight_bytes;   /* device bytes holding weights */
+  uint64_t kv_bytes;       /* device bytes of the fp32 KV cache */
+} qc_stats;
+
+/* ---- engine life cycle ------------------------------------------------- */
+
+/* Build an engine from an already parsed GGUF: the tensor table and the mapped
+ * file (replaces Model::new, model.rs:173-201, plus the reference's weight
+ * upload in Vulkan::packed_matvec, backend.rs:174-261).  Validates the config
+ * and tensor shapes like Config::from_gguf/validate_tensors (model.rs:58-149)
+ * and context in 1..=max_context (model.rs:176-180). */
+int qc_engine_create(const qc_tensor_desc* tensors, size_t n_tensors, const uint8_t* base, size_t base_len,
+                     const qc_config* cfg, uint32_t context, int device, qc_engine** out);
+
+/* Parse a GGUF image held in memory (gguf.rs:102-195, model.rs:21-90) and build the engine. */
+int qc_engine_create_gguf(const uint8_t* image, size_t len, uint32_t context, int device, qc_engine** out);
+
+/* Map a GGUF file read-only and build the engine (Gguf::open + Model::new). */
+int qc_engine_open(const char* path, uint32_t context, int device, qc_engine** out);
+
+void qc_engine_destroy(qc_engine* e);
+const char* qc_engine_error(const qc_engine* e);
+const char* qc_last_error(void);
+int qc_engine_config(const qc_engine* e, qc_config* out);
+
+/* Run subsequent work on the caller's CUDA stream (a cudaStream_t; NULL = the engine's own stream). */
+int qc_engine_set_stream(qc_engine* e, void* stream);
+
+/* ---- decode ------------------------------------------------------------ */
+
+/* One causal single-token forward at the current position: Model::forward
+ * (model.rs:210-216).  Writes `vocab` logits to `logits` (host memory; may be
+ * NULL to keep them on the device).  On error the cache and position are reset. */
+int qc_forward(qc_engine* e, uint32_t token, float* logits);
+
+/* Sequential forwards of n tokens (the `logits` command's loop, main.rs:144-146);
+ * the logits of the last token go to `logits` (may be NULL). */
+int qc_forward_tokens(qc_engine* e, const uint32_t* tokens, size_t n, float* logits);
+
+/* Greedy decode of n tokens entirely on the device.  Step i feeds the argmax
+ * (ties to the lower id, sampling.rs:31-35) of the previous logits and records
+ * it in tokens_out[i] (host, may be NULL); requires a previous forward.  The
+ * last step's logits go to `logits` (may be NULL).  Fails before running when
+ * position + n exceeds the context (main.rs:219-227). */
+int qc_decode_greedy(qc_engine* e, uint32_t n, uint32_t* tokens_out, float* logits);
+
+/* As qc_decode_greedy, but only enqueues the n steps on the engine's stream and
+ * returns; qc_sync waits and reports a non-finite output or a bad token. */
+int qc_decode_enqueue(qc_engine* e, uint32_t n);
+int qc_sync(qc_engine* e);
+
+/* model.rs:202-208: clear the KV cache and set the position to 0. */
+int qc_reset(qc_engine* e);
+int qc_position(const qc_engine* e, uint32_t* pos);
+int qc_get_stats(const qc_engine* e, qc_stats* out);
+/* Device time of each kernel kind over one decode step, from CUDA events
+ * recorded between the kernels of a captured step graph (each span also holds
+ * the launch gap before its kernel).  Runs one real step: it feeds the argmax
+ * of the previous step (token 0 at position 0) and advances the position. */
+typedef struct qc_phase_times {
+  double embed_ms, attn_in_ms, attention_ms, oproj_ms, router_ms, gateup_ms, down_ms, output_ms;
+  uint32_t launches; /* kernels in one step: 2 + 6*layers */
+} qc_phase_times;
+int qc_profile_step(qc_engine* e, qc_phase_times* out);
+
+/* Device pointer of the logits of the latest step (vocab floats). */
+int qc_logits_device(const qc_engine* e, const float** out);
+
+/* ---- per-matrix boundary (backend.rs:14-23 Backend::matvec, 174-261 packed_matvec) ---- */
+
+/* Bytes of one GGUF row (quant.rs:12-21). */
+int qc_row_bytes(uint32_t kind, uint64_t cols, uint64_t* out);
+
+/* Upload `experts` stacked (rows x cols) matrices of GGML type `kind` from host
+ * blocks (len = experts*rows*row_bytes) into the device layout. */
+int qc_matrix_create(uint32_t kind, uint64_t rows, uint64_t cols, uint64_t experts, const uint8_t* blocks,
+                     uint64_t len, int device, qc_matrix** out);
+/* y = W_expert x with device pointers on `stream` (cudaStream_t, NULL = default stream). */
+int qc_matrix_matvec(const qc_matrix* m, uint32_t expert, const float* x, float* y, void* stream);
+/* Dequantize expert `expert` to out[rows*cols] (device), bit-exact with quant.rs:36-80. */
+int qc_matrix_dequant(const qc_matrix* m, uint32_t expert, float* out, void* stream);
+/* Device bytes held, and packed GGUF bytes represented. */
+int qc_matrix_bytes(const qc_matrix* m, uint64_t* device_bytes, uint64_t* packed_bytes);
+void qc_matrix_destroy(qc_matrix* m);
+
+/* Host-to-host matvec of one packed matrix: Vulkan::packed_matvec (backend.rs:174-261)
+ * without the cache key: uploads, computes, copies y back. */
+int qc_packed_matvec(uint32_t kind, uint64_t rows, uint64_t cols, const uint8_t* blocks, uint64_t len,
+                     const float* x, float* y);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QWEN_CUDA_H */

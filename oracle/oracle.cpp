@@ -1,0 +1,792 @@
+// CPU ORACLE — test infrastructure only.
+//
+// This file restates, in C++, the CPU path of the reference Rust crate
+// (qwen-rust 0.1.0) so that the CUDA engine can be checked against it on the
+// same inputs.  Only tests/, __graft_entry__.smoke() and bench.py's CPU
+// baseline arm load it; the engine never links or calls it.
+//
+// Parity is pinned by tests/test_oracle.py against the reference's own golden
+// vectors: the two-block dequant fixtures of tests/core.rs:50-151 (bit-exact),
+// the rope / route / GQA known answers of tests/core.rs:3-27, and the 4x16
+// expected logits of tests/data/expected-logits.json produced by
+// tools/reference_fixture.py (abs 2e-5, tests/model.rs:48-69).
+//
+// Every function cites the reference file:line it follows.  Floating-point
+// operations are written in the same order as the Rust source (sequential
+// left folds, product of scale and weight first, division by sqrt(d), ...),
+// and the file is compiled with -ffp-contract=off so no multiply-add is fused
+// where Rust would round twice.
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+#include <thread>
+
+namespace {
+
+thread_local std::string g_err;
+
+// Row-parallel loop over [0, n) on `threads` std::threads (0 = all hardware
+// threads).  Each index is computed by exactly one thread with the same
+// sequential arithmetic, so results do not depend on the thread count.
+template <class F>
+void parallel_for(size_t n, int threads, F&& f) {
+  size_t nt = threads > 0 ? (size_t)threads : std::max(1u, std::thread::hardware_concurrency());
+  nt = std::min(nt, n ? n : 1);
+  if (nt <= 1) {
+    for (size_t i = 0; i < n; i++) f(i);
+    return;
+  }
+  std::vector<std::thread> pool;
+  for (size_t t = 0; t < nt; t++)
+    pool.emplace_back([&, t] {
+      size_t lo = n * t / nt, hi = n * (t + 1) / nt;
+      for (size_t i = lo; i < hi; i++) f(i);
+    });
+  for (auto& th : pool) th.join();
+}
+
+struct Fail {
+  std::string msg;
+};
+[[noreturn]] void fail(const std::string& m) { throw Fail{m}; }
+#define ENSURE(c, m)       \
+  do {                     \
+    if (!(c)) fail(m);     \
+  } while (0)
+
+// ---------------------------------------------------------------- quant.rs
+// quant.rs:5-11
+bool layout(uint32_t kind, size_t* block, size_t* bytes) {
+  switch (kind) {
+    case 0: *block = 1; *bytes = 4; return true;
+    case 1: *block = 1; *bytes = 2; return true;
+    case 2: *block = 32; *bytes = 18; return true;
+    case 8: *block = 32; *bytes = 34; return true;
+    case 12: *block = 256; *bytes = 144; return true;
+    case 13: *block = 256; *bytes = 176; return true;
+    case 14: *block = 256; *bytes = 210; return true;
+    default: return false;
+  }
+}
+// quant.rs:12-21
+size_t row_bytes(uint32_t kind, size_t cols) {
+  size_t block, bytes;
+  if (!layout(kind, &block, &bytes))
+    fail("GGML tensor type " + std::to_string(kind) +
+         " is not supported (supported: F32/F16/Q4_0/Q8_0/Q4_K/Q5_K/Q6_K)");
+  ENSURE(cols > 0 && cols % block == 0,
+         "row width " + std::to_string(cols) + " is not divisible by block size " +
+             std::to_string(block));
+  size_t n = cols / block;
+  ENSURE(n == 0 || bytes <= SIZE_MAX / n, "row size overflow");
+  return n * bytes;
+}
+// IEEE binary16 -> binary32, exact (the `half` crate's f16::to_f32, quant.rs:22-24).
+float f16_to_f32(uint16_t h) {
+  uint32_t sign = (uint32_t)(h >> 15) << 31;
+  uint32_t exp = (h >> 10) & 0x1f;
+  uint32_t man = h & 0x3ff;
+  uint32_t bits;
+  if (exp == 0) {
+    if (man == 0) {
+      bits = sign;
+    } else {  // subnormal: normalise
+      int e = -1;
+      do {
+        man <<= 1;
+        e++;
+      } while (!(man & 0x400));
+      man &= 0x3ff;
+      bits = sign | ((uint32_t)(127 - 15 - e) << 23) | (man << 13);
+    }
+  } else if (exp == 31) {
+    bits = sign | 0x7f800000u | (man << 13);
+  } else {
+    bits = sign | ((exp + 127 - 15) << 23) | (man << 13);
+  }
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
+}
+inline float h(const uint8_t* b, size_t p) { return f16_to_f32((uint16_t)(b[p] | (b[p + 1] << 8))); }
+// quant.rs:25-34
+inline void scale(const uint8_t* b, size_t j, uint8_t* s, uint8_t* m) {
+  if (j < 4) {
+    *s = b[j] & 63;
+    *m = b[j + 4] & 63;
+  } else {
+    *s = (uint8_t)((b[j + 4] & 15) | ((b[j - 4] >> 6) << 4));
+    *m = (uint8_t)((b[j + 4] >> 4) | ((b[j] >> 6) << 4));
+  }
+}
+// quant.rs:36-80 — one element of a validated row.
+float value(const uint8_t* b, uint32_t kind, size_t col) {
+  switch (kind) {
+    case 0: {
+      float f;
+      memcpy(&f, b + col * 4, 4);
+      return f;
+    }
+    case 1:
+      return h(b, col * 2);
+    case 2: {
+      size_t p = col / 32 * 18, i = col % 32;
+      uint8_t q = (uint8_t)((b[p + 2 + i % 16] >> (i < 16 ? 0 : 4)) & 15);
+      return h(b, p) * (float)((int)q - 8);
+    }
+    case 8: {
+      size_t p = col / 32 * 34;
+      return h(b, p) * (float)(int8_t)b[p + 2 + col % 32];
+    }
+    case 12:
+    case 13: {
+      size_t size = kind == 12 ? 144 : 176;
+      size_t p = col / 256 * size, i = col % 256, group = i / 32;
+      uint8_t s, m;
+      scale(b + p + 4, group, &s, &m);
+      size_t qs = p + (kind == 12 ? 16 : 48);
+      uint8_t q = (uint8_t)((b[qs + (i / 64) * 32 + i % 32] >> ((group % 2) * 4)) & 15);
+      if (kind == 13 && (b[p + 16 + i % 32] & (1u << group)) != 0) q += 16;
+      // h(b,p) * s as f32 * q as f32 - h(b,p+2) * m as f32  (left to right, no fusion)
+      float a = h(b, p) * (float)s;
+      a = a * (float)q;
+      float c = h(b, p + 2) * (float)m;
+      return a - c;
+    }
+    case 14: {
+      size_t p = col / 256 * 210, i = col % 256, chunk = i / 128, j = i % 128;
+      size_t quarter = j / 32, lane = j % 32;
+      uint8_t low = b[p + chunk * 64 + (quarter % 2) * 32 + lane];
+      uint8_t lo = (uint8_t)((low >> ((quarter / 2) * 4)) & 15);
+      uint8_t hi = (uint8_t)((b[p + 128 + chunk * 32 + lane] >> (quarter * 2)) & 3);
+      int q = (int)(lo | (hi << 4)) - 32;
+      float a = h(b, p + 208) * (float)(int8_t)b[p + 192 + chunk * 8 + quarter * 2 + lane / 16];
+      return a * (float)q;
+    }
+  }
+  fail("tensor types validated by reader");
+}
+
+// Rust's `Iterator::sum::<f32>()` is a sequential left fold that starts from -0.0.
+constexpr float kSumInit = -0.0f;
+
+// backend.rs:112-136 — y[r] = sequential f32 fold of x[i] * value(row, i).
+void matvec(const uint8_t* data, uint32_t kind, size_t rows, size_t cols, const float* x, float* y,
+            int threads) {
+  size_t rb = row_bytes(kind, cols);
+  parallel_for(rows, threads, [&](size_t r) {
+    const uint8_t* b = data + r * rb;
+    float acc = kSumInit;
+    for (size_t i = 0; i < cols; i++) acc = acc + x[i] * value(b, kind, i);
+    y[r] = acc;
+  });
+}
+
+// ---------------------------------------------------------------- ops.rs
+// ops.rs:3-15
+void rms(float* x, const float* w, size_t n, float eps) {
+  ENSURE(n > 0 && eps > 0.f, "RMSNorm shape/epsilon invalid");
+  float ss = kSumInit;
+  for (size_t i = 0; i < n; i++) ss = ss + x[i] * x[i];
+  float s = 1.0f / sqrtf(ss / (float)n + eps);
+  for (size_t i = 0; i < n; i++) x[i] *= s * w[i];
+}
+// ops.rs:17-28 (NeoX split-half rotation)
+void rope(float* x, size_t n, size_t head, size_t pos, float theta) {
+  for (size_t o = 0; o + head <= n; o += head) {
+    float* hh = x + o;
+    for (size_t i = 0; i < head / 2; i++) {
+      float e = -2.0f * (float)i / (float)head;
+      float angle = (float)pos * powf(theta, e);
+      float s = sinf(angle), c = cosf(angle);
+      float a = hh[i], b = hh[i + head / 2];
+      hh[i] = a * c - b * s;
+      hh[i + head / 2] = a * s + b * c;
+    }
+  }
+}
+// ops.rs:29-44
+void softmax(float* x, size_t n) {
+  ENSURE(n > 0, "invalid softmax logits");
+  for (size_t i = 0; i < n; i++) ENSURE(std::isfinite(x[i]), "invalid softmax logits");
+  float mx = -INFINITY;
+  for (size_t i = 0; i < n; i++) mx = std::fmax(mx, x[i]);
+  float sum = 0.f;
+  for (size_t i = 0; i < n; i++) {
+    x[i] = expf(x[i] - mx);
+    sum += x[i];
+  }
+  for (size_t i = 0; i < n; i++) x[i] /= sum;
+}
+// f32::total_cmp key (IEEE totalOrder): larger key == larger value.
+inline int32_t total_key(float f) {
+  int32_t i;
+  memcpy(&i, &f, 4);
+  i ^= (int32_t)(((uint32_t)(i >> 31)) >> 1);
+  return i;
+}
+// ops.rs:45-56 — descending by total_cmp, ties to the lower index, softmax of the kept logits.
+void route(const float* logits, size_t n, size_t top, uint32_t* ids, float* weights) {
+  ENSURE(top > 0 && top <= n, "invalid MoE router");
+  for (size_t i = 0; i < n; i++) ENSURE(std::isfinite(logits[i]), "invalid MoE router");
+  std::vector<uint32_t> idx(n);
+  for (size_t i = 0; i < n; i++) idx[i] = (uint32_t)i;
+  std::sort(idx.begin(), idx.end(), [&](uint32_t a, uint32_t b) {
+    int32_t ka = total_key(logits[a]), kb = total_key(logits[b]);
+    if (ka != kb) return ka > kb;
+    return a < b;
+  });
+  for (size_t i = 0; i < top; i++) {
+    ids[i] = idx[i];
+    weights[i] = logits[idx[i]];
+  }
+  softmax(weights, top);
+}
+// ops.rs:57-98 — GQA causal attention over the whole cache, layout [t][kvhead][d].
+void attention(const float* q, const float* k, const float* v, size_t heads, size_t kvheads, size_t d,
+               size_t time, float* out) {
+  ENSURE(kvheads > 0 && heads > 0 && d > 0 && heads % kvheads == 0, "attention shape mismatch");
+  ENSURE(time > 0, "empty KV cache");
+  for (size_t i = 0; i < heads * d; i++) out[i] = 0.f;
+  std::vector<float> scores(time);
+  float sd = sqrtf((float)d);
+  for (size_t hh = 0; hh < heads; hh++) {
+    size_t kh = hh / (heads / kvheads);
+    const float* qs = q + hh * d;
+    for (size_t t = 0; t < time; t++) {
+      const float* kr = k + (t * kvheads + kh) * d;
+      float acc = kSumInit;
+      for (size_t j = 0; j < d; j++) acc = acc + qs[j] * kr[j];
+      scores[t] = acc / sd;
+    }
+    softmax(scores.data(), time);
+    for (size_t t = 0; t < time; t++) {
+      float sc = scores[t];
+      const float* vr = v + (t * kvheads + kh) * d;
+      for (size_t j = 0; j < d; j++) out[hh * d + j] += sc * vr[j];
+    }
+  }
+}
+
+// ---------------------------------------------------------------- gguf.rs
+struct Value {
+  enum Kind { U, I, F, B, S, A } kind = U;
+  uint64_t u = 0;
+  int64_t i = 0;
+  double f = 0;
+  std::string s;
+  std::vector<Value> arr;
+  // serde_json::Value::as_u64
+  bool as_u64(uint64_t* o) const {
+    if (kind == U) { *o = u; return true; }
+    if (kind == I && i >= 0) { *o = (uint64_t)i; return true; }
+    return false;
+  }
+  // serde_json::Value::as_f64
+  bool as_f64(double* o) const {
+    if (kind == U) { *o = (double)u; return true; }
+    if (kind == I) { *o = (double)i; return true; }
+    if (kind == F) { *o = f; return true; }
+    return false;
+  }
+};
+struct Tensor {
+  std::string name;
+  std::vector<size_t> dims;
+  uint32_t kind;
+  size_t offset, len;
+};
+struct Reader {
+  const uint8_t* p;
+  size_t n, pos = 0;
+  size_t budget = 128u * 1024 * 1024;
+  void take(void* out, size_t k) {
+    ENSURE(k <= n - pos, "failed to fill whole buffer");
+    memcpy(out, p + pos, k);
+    pos += k;
+  }
+  uint8_t u8() { uint8_t v; take(&v, 1); return v; }
+  uint32_t u32() { uint32_t v; take(&v, 4); return v; }
+  uint64_t u64() { uint64_t v; take(&v, 8); return v; }
+  size_t count(size_t max) {  // gguf.rs:44-48
+    uint64_t c = u64();
+    ENSURE(c <= max, "GGUF count " + std::to_string(c) + " exceeds limit " + std::to_string(max));
+    return (size_t)c;
+  }
+  std::string str() {  // gguf.rs:49-56
+    size_t c = count(16 * 1024 * 1024);
+    ENSURE(c <= budget, "GGUF metadata budget exceeded");
+    budget -= c;
+    std::string s(c, '\0');
+    take(s.data(), c);
+    return s;
+  }
+  Value val(uint32_t t, size_t depth) {  // gguf.rs:57-99
+    ENSURE(depth <= 4 && budget >= 8, "excessive metadata depth/size");
+    budget -= 8;
+    Value v;
+    switch (t) {
+      case 0: v.kind = Value::U; v.u = u8(); break;
+      case 1: v.kind = Value::I; v.i = (int8_t)u8(); break;
+      case 2: { uint16_t x; take(&x, 2); v.kind = Value::U; v.u = x; break; }
+      case 3: { int16_t x; take(&x, 2); v.kind = Value::I; v.i = x; break; }
+      case 4: v.kind = Value::U; v.u = u32(); break;
+      case 5: { int32_t x; take(&x, 4); v.kind = Value::I; v.i = x; break; }
+      case 6: {
+        float x; take(&x, 4);
+        ENSURE(std::isfinite(x), "nonfinite metadata");
+        v.kind = Value::F; v.f = x; break;
+      }
+      case 7: {
+        uint8_t x = u8();
+        ENSURE(x <= 1, "invalid boolean");
+        v.kind = Value::B; v.u = x; break;
+      }
+      case 8: v.kind = Value::S; v.s = str(); break;
+      case 9: {
+        uint32_t ty = u32();
+        size_t c = count(1000000);
+        v.kind = Value::A;
+        for (size_t k = 0; k < c; k++) v.arr.push_back(val(ty, depth + 1));
+        break;
+      }
+      case 10: v.kind = Value::U; v.u = u64(); break;
+      case 11: { int64_t x; take(&x, 8); v.kind = Value::I; v.i = x; break; }
+      case 12: {
+        double x; take(&x, 8);
+        ENSURE(std::isfinite(x), "nonfinite metadata");
+        v.kind = Value::F; v.f = x; break;
+      }
+      default: fail("unknown GGUF metadata type " + std::to_string(t));
+    }
+    return v;
+  }
+};
+struct Gguf {
+  std::map<std::string, Value> meta;
+  std::map<std::string, Tensor> tensors;
+  const uint8_t* base = nullptr;
+  size_t len = 0;
+  void* map = nullptr;  // owned mmap, if any
+  std::vector<uint8_t> owned;
+  ~Gguf() {
+    if (map) munmap(map, len);
+  }
+  // gguf.rs:102-195
+  void parse() {
+    Reader r{base, len};
+    uint8_t magic[4];
+    r.take(magic, 4);
+    ENSURE(memcmp(magic, "GGUF", 4) == 0, "not a GGUF file");
+    uint32_t ver = r.u32();
+    ENSURE(ver == 2 || ver == 3, "GGUF version " + std::to_string(ver) + " unsupported");
+    size_t nt = r.count(100000), nk = r.count(100000);
+    for (size_t k = 0; k < nk; k++) {
+      std::string key = r.str();
+      uint32_t t = r.u32();
+      Value v = r.val(t, 0);
+      ENSURE(meta.emplace(key, std::move(v)).second, "duplicate metadata key");
+    }
+    auto sc = meta.find("split.count");
+    uint64_t split = 1;
+    if (sc != meta.end() && !sc->second.as_u64(&split)) split = 1;
+    ENSURE(split == 1, "split GGUF not supported; merge shards first");
+    for (size_t k = 0; k < nt; k++) {
+      Tensor t;
+      t.name = r.str();
+      uint32_t nd = r.u32();
+      ENSURE(nd >= 1 && nd <= 3, "unsupported tensor rank " + std::to_string(nd) + ": " + t.name);
+      for (uint32_t d = 0; d < nd; d++) {
+        uint64_t dd = r.u64();
+        ENSURE(dd > 0, "zero tensor dimension");
+        t.dims.push_back((size_t)dd);
+      }
+      t.kind = r.u32();
+      t.offset = (size_t)r.u64();
+      size_t l = row_bytes(t.kind, t.dims[0]);
+      for (size_t d = 1; d < t.dims.size(); d++) {
+        ENSURE(t.dims[d] == 0 || l <= SIZE_MAX / t.dims[d], "tensor length overflow");
+        l *= t.dims[d];
+      }
+      t.len = l;
+      std::string name = t.name;
+      ENSURE(tensors.emplace(name, std::move(t)).second, "duplicate tensor name");
+    }
+    uint64_t alignment = 32;
+    auto al = meta.find("general.alignment");
+    if (al != meta.end() && !al->second.as_u64(&alignment)) alignment = 32;
+    ENSURE(alignment && (alignment & (alignment - 1)) == 0 && alignment <= 4096, "invalid GGUF alignment");
+    size_t start = (r.pos + alignment - 1) & ~(size_t)(alignment - 1);
+    std::vector<std::pair<size_t, size_t>> ranges;
+    for (auto& kv : tensors) {
+      Tensor& t = kv.second;
+      ENSURE(t.offset % alignment == 0, "unaligned tensor " + t.name);
+      ENSURE(t.offset <= SIZE_MAX - start, "tensor offset overflow");
+      t.offset += start;
+      ENSURE(t.len <= SIZE_MAX - t.offset, "tensor end overflow");
+      size_t end = t.offset + t.len;
+      ENSURE(end <= len, "truncated tensor " + t.name);
+      ranges.push_back({t.offset, end});
+    }
+    std::sort(ranges.begin(), ranges.end());
+    for (size_t k = 1; k < ranges.size(); k++) ENSURE(ranges[k - 1].second <= ranges[k].first, "overlapping tensors");
+  }
+  const Tensor& tensor(const std::string& n) const {  // gguf.rs:196-200
+    auto it = tensors.find(n);
+    ENSURE(it != tensors.end(), "missing tensor " + n);
+    return it->second;
+  }
+  const uint8_t* data(const Tensor& t) const { return base + t.offset; }
+  std::vector<float> row(const std::string& n, size_t row) const {  // gguf.rs:204-213
+    const Tensor& t = tensor(n);
+    size_t size = row_bytes(t.kind, t.dims[0]);
+    ENSURE(row < t.len / size, "row out of bounds: " + n);
+    std::vector<float> out(t.dims[0]);
+    const uint8_t* b = data(t) + row * size;
+    for (size_t i = 0; i < t.dims[0]; i++) out[i] = value(b, t.kind, i);
+    return out;
+  }
+  size_t uint(const std::string& key) const {  // gguf.rs:214-222
+    auto it = meta.find(key);
+    uint64_t v;
+    ENSURE(it != meta.end() && it->second.as_u64(&v), "missing integer " + key);
+    return (size_t)v;
+  }
+  float flt(const std::string& key, float def) const {  // gguf.rs:223-229
+    auto it = meta.find(key);
+    double v;
+    if (it == meta.end() || !it->second.as_f64(&v)) return def;
+    return (float)v;
+  }
+};
+
+// ---------------------------------------------------------------- model.rs
+struct Config {  // model.rs:5-19
+  size_t hidden, layers, heads, kvheads, head_dim, experts, top, intermediate, vocab, max_context;
+  float eps, theta;
+};
+Config config_from(const Gguf& m) {  // model.rs:21-90
+  auto arch = m.meta.find("general.architecture");
+  ENSURE(arch != m.meta.end() && arch->second.kind == Value::S && arch->second.s == "qwen3moe",
+         "only qwen3moe architecture is implemented");
+  auto get = [&](const std::string& k) { return m.uint("qwen3moe." + k); };
+  auto has = [&](const std::string& k) {
+    auto it = m.meta.find("qwen3moe." + k);
+    uint64_t v;
+    return it != m.meta.end() && it->second.as_u64(&v);
+  };
+  Config c{};
+  c.hidden = get("embedding_length");
+  c.heads = get("attention.head_count");
+  c.top = get("expert_used_count");
+  c.head_dim = has("attention.key_length") ? get("attention.key_length") : c.hidden / std::max<size_t>(c.heads, 1);
+  size_t vl = has("attention.value_length") ? get("attention.value_length") : c.head_dim;
+  ENSURE(vl == c.head_dim, "different key/value head sizes unsupported");
+  c.layers = get("block_count");
+  c.kvheads = get("attention.head_count_kv");
+  c.experts = get("expert_count");
+  c.intermediate = has("expert_feed_forward_length") ? get("expert_feed_forward_length")
+                                                     : get("feed_forward_length") / std::max<size_t>(c.top, 1);
+  const Tensor& te = m.tensor("token_embd.weight");
+  ENSURE(te.dims.size() > 1, "invalid embedding rank");
+  c.vocab = te.dims[1];
+  c.max_context = get("context_length");
+  c.eps = m.flt("qwen3moe.attention.layer_norm_rms_epsilon", 1e-6f);
+  c.theta = m.flt("qwen3moe.rope.freq_base", 1000000.f);
+  ENSURE(c.hidden > 0 && c.layers > 0 && c.layers <= 256 && c.kvheads > 0 && c.heads > 0 &&
+             c.heads % c.kvheads == 0 && c.head_dim > 0 && c.head_dim % 2 == 0 && c.top > 0 &&
+             c.top <= c.experts && c.experts <= 1024 && c.intermediate > 0 && std::isfinite(c.eps) &&
+             c.eps > 0.f && std::isfinite(c.theta) && c.theta > 0.f,
+         "invalid Qwen3 MoE config");
+  size_t rd = has("rope.dimension_count") ? get("rope.dimension_count") : c.head_dim;
+  ENSURE(rd == c.head_dim, "partial rotary dimensions unsupported");
+  auto rs = m.meta.find("qwen3moe.rope.scaling.type");
+  ENSURE(rs == m.meta.end() || rs->second.kind != Value::S || rs->second.s == "none",
+         "RoPE scaling is not implemented; use the original native-context model");
+  return c;
+}
+void validate_tensors(const Config& c, const Gguf& m) {  // model.rs:91-149
+  auto check = [&](const std::string& n, std::vector<size_t> shape) {
+    const Tensor& t = m.tensor(n);
+    ENSURE(t.dims == shape, n + ": unexpected shape");
+  };
+  check("token_embd.weight", {c.hidden, c.vocab});
+  check("output_norm.weight", {c.hidden});
+  if (m.tensors.count("output.weight")) check("output.weight", {c.hidden, c.vocab});
+  for (size_t i = 0; i < c.layers; i++) {
+    std::string b = "blk." + std::to_string(i) + ".";
+    check(b + "attn_norm.weight", {c.hidden});
+    check(b + "ffn_norm.weight", {c.hidden});
+    check(b + "attn_q_norm.weight", {c.head_dim});
+    check(b + "attn_k_norm.weight", {c.head_dim});
+    check(b + "attn_q.weight", {c.hidden, c.heads * c.head_dim});
+    check(b + "attn_k.weight", {c.hidden, c.kvheads * c.head_dim});
+    check(b + "attn_v.weight", {c.hidden, c.kvheads * c.head_dim});
+    check(b + "attn_output.weight", {c.heads * c.head_dim, c.hidden});
+    check(b + "ffn_gate_inp.weight", {c.hidden, c.experts});
+    check(b + "ffn_gate_exps.weight", {c.hidden, c.intermediate, c.experts});
+    check(b + "ffn_up_exps.weight", {c.hidden, c.intermediate, c.experts});
+    check(b + "ffn_down_exps.weight", {c.intermediate, c.hidden, c.experts});
+    for (auto& kv : m.tensors) {
+      const std::string& n = kv.first;
+      bool bias = n.size() >= 5 && n.compare(n.size() - 5, 5, ".bias") == 0;
+      ENSURE(!(n.rfind(b, 0) == 0 && bias), "unexpected bias tensors");
+    }
+  }
+}
+
+struct Model {
+  std::unique_ptr<Gguf> g;
+  Config c;
+  std::vector<std::vector<float>> kk, vv;  // per-layer fp32 KV, layout [t][kvhead][d]
+  std::vector<std::vector<std::vector<float>>> norms;
+  std::vector<float> output_norm;
+  size_t position = 0, context = 0;
+  int threads = 0;
+  uint64_t matvecs = 0;
+
+  // backend.rs:141-159 + Cpu::matvec
+  std::vector<float> mv(const std::string& name, long expert, const std::vector<float>& x) {
+    const Tensor& t = g->tensor(name);
+    ENSURE(t.dims.size() == (expert >= 0 ? 3u : 2u), "matrix rank mismatch: " + name);
+    size_t cols = t.dims[0], rows = t.dims[1];
+    size_t len = row_bytes(t.kind, cols) * rows;
+    size_t e = expert >= 0 ? (size_t)expert : 0;
+    ENSURE(expert < 0 || e < t.dims[2], "expert out of bounds");
+    ENSURE(cols == x.size(), "matvec shape mismatch " + name);
+    std::vector<float> y(rows);
+    matvec(g->data(t) + e * len, t.kind, rows, cols, x.data(), y.data(), threads);
+    matvecs++;
+    return y;
+  }
+  void reset() {  // model.rs:202-208
+    for (auto& k : kk) k.clear();
+    for (auto& v : vv) v.clear();
+    position = 0;
+  }
+  std::vector<float> forward_inner(uint32_t token) {  // model.rs:217-302
+    ENSURE(position < context, "context limit " + std::to_string(context) + " reached");
+    ENSURE(token < c.vocab, "token outside vocabulary");
+    std::vector<float> x = g->row("token_embd.weight", token);
+    size_t D = c.head_dim;
+    for (size_t i = 0; i < c.layers; i++) {
+      std::string base = "blk." + std::to_string(i);
+      std::vector<float> xn = x;
+      rms(xn.data(), norms[i][0].data(), xn.size(), c.eps);
+      std::vector<float> q = mv(base + ".attn_q.weight", -1, xn);
+      std::vector<float> k = mv(base + ".attn_k.weight", -1, xn);
+      std::vector<float> v = mv(base + ".attn_v.weight", -1, xn);
+      for (size_t o = 0; o + D <= q.size(); o += D) rms(q.data() + o, norms[i][1].data(), D, c.eps);
+      for (size_t o = 0; o + D <= k.size(); o += D) rms(k.data() + o, norms[i][2].data(), D, c.eps);
+      rope(q.data(), q.size(), D, position, c.theta);
+      rope(k.data(), k.size(), D, position, c.theta);
+      kk[i].insert(kk[i].end(), k.begin(), k.end());
+      vv[i].insert(vv[i].end(), v.begin(), v.end());
+      size_t time = kk[i].size() / (c.kvheads * D);
+      std::vector<float> a(c.heads * D);
+      ENSURE(q.size() == c.heads * D, "attention shape mismatch");
+      attention(q.data(), kk[i].data(), vv[i].data(), c.heads, c.kvheads, D, time, a.data());
+      std::vector<float> o = mv(base + ".attn_output.weight", -1, a);
+      for (size_t j = 0; j < x.size(); j++) x[j] += o[j];
+      xn = x;
+      rms(xn.data(), norms[i][3].data(), xn.size(), c.eps);
+      std::vector<float> logits = mv(base + ".ffn_gate_inp.weight", -1, xn);
+      std::vector<uint32_t> ids(c.top);
+      std::vector<float> w(c.top);
+      route(logits.data(), logits.size(), c.top, ids.data(), w.data());
+      std::vector<float> moe(c.hidden, 0.f);
+      for (size_t s = 0; s < c.top; s++) {
+        std::vector<float> gate = mv(base + ".ffn_gate_exps.weight", ids[s], xn);
+        std::vector<float> up = mv(base + ".ffn_up_exps.weight", ids[s], xn);
+        for (size_t j = 0; j < gate.size(); j++) {
+          float gg = gate[j];
+          gate[j] = (gg / (1.f + expf(-gg))) * up[j];
+        }
+        std::vector<float> down = mv(base + ".ffn_down_exps.weight", ids[s], gate);
+        for (size_t j = 0; j < moe.size(); j++) moe[j] += w[s] * down[j];
+      }
+      for (size_t j = 0; j < x.size(); j++) x[j] += moe[j];
+    }
+    rms(x.data(), output_norm.data(), x.size(), c.eps);
+    const char* out = g->tensors.count("output.weight") ? "output.weight" : "token_embd.weight";
+    std::vector<float> logits = mv(out, -1, x);
+    for (float f : logits) ENSURE(std::isfinite(f), "nonfinite model output");
+    position++;
+    return logits;
+  }
+};
+
+Model* model_new(std::unique_ptr<Gguf> g, size_t context) {  // model.rs:173-201
+  std::unique_ptr<Model> m(new Model);
+  m->c = config_from(*g);
+  validate_tensors(m->c, *g);
+  ENSURE(context > 0 && context <= m->c.max_context,
+         "context must be in 1..=" + std::to_string(m->c.max_context));
+  for (size_t i = 0; i < m->c.layers; i++) {
+    std::vector<std::vector<float>> n;
+    for (const char* nm : {"attn_norm", "attn_q_norm", "attn_k_norm", "ffn_norm"})
+      n.push_back(g->row("blk." + std::to_string(i) + "." + nm + ".weight", 0));
+    m->norms.push_back(std::move(n));
+  }
+  m->output_norm = g->row("output_norm.weight", 0);
+  m->kk.resize(m->c.layers);
+  m->vv.resize(m->c.layers);
+  m->context = context;
+  m->g = std::move(g);
+  return m.release();
+}
+
+template <class F>
+int guarded(F&& f) {
+  try {
+    f();
+    return 0;
+  } catch (const Fail& e) {
+    g_err = e.msg;
+    return 1;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return 1;
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* or_last_error(void) { return g_err.c_str(); }
+
+int or_layout(uint32_t kind, size_t* block, size_t* bytes) {
+  return guarded([&] { ENSURE(layout(kind, block, bytes), "GGML tensor type " + std::to_string(kind) + " is not supported"); });
+}
+int or_row_bytes(uint32_t kind, size_t cols, size_t* out) {
+  return guarded([&] { *out = row_bytes(kind, cols); });
+}
+// quant.rs:81-84
+int or_decode(const uint8_t* b, size_t len, uint32_t kind, size_t cols, float* out) {
+  return guarded([&] {
+    ENSURE(len >= row_bytes(kind, cols), "truncated quantized row");
+    for (size_t i = 0; i < cols; i++) out[i] = value(b, kind, i);
+  });
+}
+// Decodes `rows` consecutive rows (whole tensor or one expert slice).
+int or_decode_rows(const uint8_t* b, uint32_t kind, size_t rows, size_t cols, float* out) {
+  return guarded([&] {
+    size_t rb = row_bytes(kind, cols);
+    parallel_for(rows, 0, [&](size_t r) {
+      for (size_t i = 0; i < cols; i++) out[r * cols + i] = value(b + r * rb, kind, i);
+    });
+  });
+}
+int or_matvec(const uint8_t* data, size_t len, uint32_t kind, size_t rows, size_t cols, const float* x, float* y,
+              int threads) {
+  return guarded([&] {
+    ENSURE(rows > 0 && len >= row_bytes(kind, cols) * rows, "matvec shape mismatch");
+    matvec(data, kind, rows, cols, x, y, threads);
+  });
+}
+int or_rms(float* x, const float* w, size_t n, float eps) { return guarded([&] { rms(x, w, n, eps); }); }
+void or_rope(float* x, size_t n, size_t head, size_t pos, float theta) { rope(x, n, head, pos, theta); }
+int or_softmax(float* x, size_t n) { return guarded([&] { softmax(x, n); }); }
+int or_route(const float* logits, size_t n, size_t top, uint32_t* ids, float* weights) {
+  return guarded([&] { route(logits, n, top, ids, weights); });
+}
+int or_attention(const float* q, const float* k, const float* v, size_t heads, size_t kvheads, size_t d,
+                 size_t time, float* out) {
+  return guarded([&] { attention(q, k, v, heads, kvheads, d, time, out); });
+}
+// sampling.rs:26-35 — greedy: the first id after sorting by total_cmp descending, ties to the lower index.
+int or_sample_greedy(const float* logits, size_t n, uint32_t* out) {
+  return guarded([&] {
+    ENSURE(n > 0, "invalid logits");
+    for (size_t i = 0; i < n; i++) ENSURE(std::isfinite(logits[i]), "invalid logits");
+    size_t best = 0;
+    for (size_t i = 1; i < n; i++)
+      if (total_key(logits[i]) > total_key(logits[best])) best = i;
+    *out = (uint32_t)best;
+  });
+}
+
+void* or_model_open(const char* path, size_t context, int threads) {
+  Model* out = nullptr;
+  int rc = guarded([&] {
+    std::unique_ptr<Gguf> g(new Gguf);
+    int fd = open(path, O_RDONLY);
+    ENSURE(fd >= 0, std::string("open ") + path);
+    struct stat st;
+    fstat(fd, &st);
+    g->len = (size_t)st.st_size;
+    if (g->len) {
+      g->map = mmap(nullptr, g->len, PROT_READ, MAP_PRIVATE, fd, 0);
+      if (g->map == MAP_FAILED) g->map = nullptr;
+    }
+    close(fd);
+    ENSURE(g->len == 0 || g->map, "mmap failed");
+    g->base = (const uint8_t*)g->map;
+    g->parse();
+    out = model_new(std::move(g), context);
+    out->threads = threads;
+  });
+  return rc == 0 ? out : nullptr;
+}
+// Borrows `buf` (the caller keeps it alive), like the reference's mmap.
+void* or_model_from_memory(const uint8_t* buf, size_t len, size_t context, int threads) {
+  Model* out = nullptr;
+  int rc = guarded([&] {
+    std::unique_ptr<Gguf> g(new Gguf);
+    g->base = buf;
+    g->len = len;
+    g->parse();
+    out = model_new(std::move(g), context);
+    out->threads = threads;
+  });
+  return rc == 0 ? out : nullptr;
+}
+// model.rs:210-216 — on error the cache and position are reset.
+int or_model_forward(void* h, uint32_t token, float* logits) {
+  Model* m = (Model*)h;
+  std::vector<float> out;
+  int rc = guarded([&] { out = m->forward_inner(token); });
+  if (rc) {
+    m->reset();
+    return rc;
+  }
+  memcpy(logits, out.data(), out.size() * sizeof(float));
+  return 0;
+}
+void or_model_reset(void* h) { ((Model*)h)->reset(); }
+size_t or_model_position(void* h) { return ((Model*)h)->position; }
+uint64_t or_model_matvecs(void* h) { return ((Model*)h)->matvecs; }
+// hidden, layers, heads, kvheads, head_dim, experts, top, intermediate, vocab, max_context
+void or_model_config(void* h, size_t* out10, float* eps_theta) {
+  const Config& c = ((Model*)h)->c;
+  size_t v[10] = {c.hidden, c.layers, c.heads, c.kvheads, c.head_dim, c.experts, c.top, c.intermediate, c.vocab, c.max_context};
+  memcpy(out10, v, sizeof v);
+  eps_theta[0] = c.eps;
+  eps_theta[1] = c.theta;
+}
+void or_model_free(void* h) { delete (Model*)h; }
+// Header parse only (gguf.rs:102-195); returns 0 when the file is accepted.
+int or_gguf_check(const uint8_t* buf, size_t len) {
+  return guarded([&] {
+    Gguf g;
+    g.base = buf;
+    g.len = len;
+    g.parse();
+    g.base = nullptr;
+  });
+}
+float or_f16_to_f32(uint16_t v) { return f16_to_f32(v); }
+
+}  // extern "C"

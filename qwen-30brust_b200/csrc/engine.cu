@@ -1,0 +1,913 @@
+// Host side of the decode engine and the C ABI of include/qwen_cuda.h.
+//
+// An engine owns, on one GPU:
+//   * every weight tensor in the device layout of common.cuh (one allocation);
+//   * the fp32 KV cache, [layer][kv head][position][head_dim] (K and V);
+//   * scratch activations, the RoPE table and the step state;
+//   * a CUDA graph holding the kernels of one token step (decode.cu), replayed
+//     once per token.
+// It replaces reference src/model.rs Model (config, KV cache, forward) and the
+// Backend of src/backend.rs for a whole token at a time.
+#include <cuda_runtime.h>
+#include <fcntl.h>
+#include <math.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "../../include/qwen_cuda.h"
+#include "gguf.h"
+#include "kernels.h"
+#include "layout.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+struct ApiError : std::runtime_error {
+  int code;
+  ApiError(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+#define QC_CK(call)                                                                                        \
+  do {                                                                                                     \
+    cudaError_t e_ = (call);                                                                               \
+    if (e_ != cudaSuccess)                                                                                 \
+      throw ApiError(e_ == cudaErrorMemoryAllocation ? QC_ERR_NOMEM : QC_ERR_CUDA,                         \
+                     std::string(#call) + ": " + cudaGetErrorString(e_));                                  \
+  } while (0)
+
+void ensure(bool c, const std::string& m, int code = QC_ERR_INVALID) {
+  if (!c) throw ApiError(code, m);
+}
+
+constexpr uint64_t kChunk = 256ull << 20;  // staging size for weight upload
+constexpr int kMaxSmem = 200 * 1024;
+
+// One-time per-device kernel attributes.
+void prepare_device(int device) {
+  static std::mutex mu;
+  static bool done[64] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (device < 0 || device >= 64 || done[device]) return;
+  QC_CK(qc::matvec_prepare(kMaxSmem));
+  QC_CK(qc::decode_prepare(kMaxSmem));
+  done[device] = true;
+}
+
+struct TensorIn {
+  std::string name;
+  uint32_t kind = 0;
+  std::vector<uint64_t> dims;
+  const uint8_t* data = nullptr;
+  uint64_t len = 0;
+};
+
+uint64_t align256(uint64_t v) { return (v + 255) & ~255ull; }
+
+// Device placement of one tensor: main plane, d plane, and (for vectors) an f32 copy.
+struct Placed {
+  const TensorIn* t = nullptr;
+  uint64_t rows = 1, experts = 1, cols = 0;
+  qc::DevLayout lay;
+  uint64_t off_main = 0, off_d = 0, off_f32 = 0;
+  bool vector = false;
+};
+
+// Uploads raw GGUF rows to the device layout through double-buffered staging.
+class Uploader {
+ public:
+  // Staging holds at least one row and at most max(kChunk, one row); `total` caps it for small uploads.
+  Uploader(cudaStream_t s, uint64_t max_row, uint64_t total = kChunk) : s_(s) {
+    uint64_t n = total < kChunk ? total : kChunk;
+    n = max_row > n ? max_row : n;
+    QC_CK(cudaMalloc(&buf_[0], n));
+    QC_CK(cudaMalloc(&buf_[1], n));
+    cap_ = n;
+  }
+  ~Uploader() {
+    cudaStreamSynchronize(s_);
+    cudaFree(buf_[0]);
+    cudaFree(buf_[1]);
+  }
+  // rows x raw_row bytes from host `src`, repacked for kind/cols into dst / dplane.
+  uint64_t put(const uint8_t* src, uint64_t rows, uint64_t raw_row, uint32_t kind, uint64_t cols, uint8_t* dst,
+               uint64_t row_stride, __half* dplane, uint64_t d_stride) {
+    const uint64_t per = cap_ / raw_row;
+    uint64_t done = 0;
+    while (done < rows) {
+      const uint64_t n = rows - done < per ? rows - done : per;
+      uint8_t* b = buf_[k_++ & 1];
+      QC_CK(cudaMemcpyAsync(b, src + done * raw_row, n * raw_row, cudaMemcpyHostToDevice, s_));
+      qc::launch_repack(b, n, raw_row, kind, cols, dst + done * row_stride, row_stride,
+                        dplane ? dplane + done * d_stride : nullptr, d_stride, s_);
+      QC_CK(cudaGetLastError());
+      done += n;
+    }
+    return rows * raw_row;
+  }
+
+ private:
+  cudaStream_t s_;
+  uint8_t* buf_[2] = {nullptr, nullptr};
+  uint64_t cap_ = 0;
+  unsigned k_ = 0;
+};
+
+qc::MatDesc make_desc(const Placed& p, uint8_t* base) {
+  qc::MatDesc m{};
+  m.w = base + p.off_main;
+  m.d = p.lay.d_stride ? reinterpret_cast<const __half*>(base + p.off_d) : nullptr;
+  m.kind = p.t->kind;
+  m.rows = (uint32_t)p.rows;
+  m.cols = (uint32_t)p.cols;
+  m.units = p.lay.units;
+  m.lpr = p.lay.lpr;
+  m.upl = p.lay.upl;
+  m.row_stride = p.lay.row_stride;
+  m.d_stride = p.lay.d_stride;
+  m.expert_stride = p.rows * p.lay.row_stride;
+  m.d_expert_stride = p.rows * p.lay.d_stride;
+  return m;
+}
+
+// Same matrix, processed with `lpr` lanes per row (a power of two dividing units).
+qc::MatDesc with_lpr(qc::MatDesc m, uint32_t lpr) {
+  m.lpr = lpr;
+  m.upl = m.units / lpr;
+  return m;
+}
+
+}  // namespace
+
+struct qc_engine {
+  int device = 0, sms = 148;
+  qc_config cfg{};
+  uint32_t context = 0;
+  uint8_t* d_weights = nullptr;
+  uint64_t weight_bytes = 0;
+  float* d_kv = nullptr;
+  uint64_t kv_bytes = 0;
+  uint8_t* d_scratch = nullptr;
+  qc::DevState* d_state = nullptr;
+  qc::DevState h_template{};
+  std::vector<qc::LayerDev> layers;
+  qc::MatDesc embd{}, out{};
+  const float* out_norm = nullptr;
+  qc::Scratch sc{};
+  qc::DecodeDims dims{};
+  uint32_t* d_gen = nullptr;
+  cudaStream_t own = nullptr, stream = nullptr;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  uint32_t* h_pinned = nullptr;  // [0] token, [2..3] flags, then gen_count/cap
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  uint32_t pos = 0;
+  qc_stats stats{};
+  std::string err;
+
+  ~qc_engine() {
+    cudaSetDevice(device);
+    if (stream) cudaStreamSynchronize(stream);
+    if (exec) cudaGraphExecDestroy(exec);
+    if (prof_exec) cudaGraphExecDestroy(prof_exec);
+    if (prof_graph) cudaGraphDestroy(prof_graph);
+    for (cudaEvent_t ev : prof_ev) cudaEventDestroy(ev);
+    if (graph) cudaGraphDestroy(graph);
+    if (ev0) cudaEventDestroy(ev0);
+    if (ev1) cudaEventDestroy(ev1);
+    if (h_pinned) cudaFreeHost(h_pinned);
+    cudaFree(d_weights);
+    cudaFree(d_kv);
+    cudaFree(d_scratch);
+    if (own) cudaStreamDestroy(own);
+  }
+
+  // ---- model.rs:58-149: config and tensor validation -------------------------------------
+  static void validate_config(const qc_config& c) {
+    ensure(c.hidden > 0 && c.layers > 0 && c.layers <= 256 && c.kvheads > 0 && c.heads > 0 &&
+               c.heads % c.kvheads == 0 && c.head_dim > 0 && c.head_dim % 2 == 0 && c.top > 0 &&
+               c.top <= c.experts && c.experts <= 1024 && c.intermediate > 0 && std::isfinite(c.eps) && c.eps > 0.f &&
+               std::isfinite(c.theta) && c.theta > 0.f,
+           "invalid Qwen3 MoE config");
+    // limits of this engine's kernels (shared-memory tiles), beyond the reference's own checks
+    ensure(c.head_dim <= 256, "head_dim > 256 is not supported by the CUDA engine");
+    ensure(c.heads / c.kvheads <= 64 && c.kvheads <= 64, "more than 64 query heads per KV head or KV heads");
+    ensure(c.top <= 64, "more than 64 experts per token is not supported by the CUDA engine");
+  }
+
+  void check_shape(const std::map<std::string, TensorIn>& t, const std::string& n, std::vector<uint64_t> shape) {
+    auto it = t.find(n);
+    ensure(it != t.end(), "missing tensor " + n);
+    ensure(it->second.dims == shape, n + ": unexpected shape");
+  }
+
+  void validate_tensors(const std::map<std::string, TensorIn>& t) {
+    const qc_config& c = cfg;
+    check_shape(t, "token_embd.weight", {c.hidden, c.vocab});
+    check_shape(t, "output_norm.weight", {c.hidden});
+    if (t.count("output.weight")) check_shape(t, "output.weight", {c.hidden, c.vocab});
+    for (uint32_t i = 0; i < c.layers; i++) {
+      const std::string b = "blk." + std::to_string(i) + ".";
+      check_shape(t, b + "attn_norm.weight", {c.hidden});
+      check_shape(t, b + "ffn_norm.weight", {c.hidden});
+      check_shape(t, b + "attn_q_norm.weight", {c.head_dim});
+      check_shape(t, b + "attn_k_norm.weight", {c.head_dim});
+      check_shape(t, b + "attn_q.weight", {c.hidden, (uint64_t)c.heads * c.head_dim});
+      check_shape(t, b + "attn_k.weight", {c.hidden, (uint64_t)c.kvheads * c.head_dim});
+      check_shape(t, b + "attn_v.weight", {c.hidden, (uint64_t)c.kvheads * c.head_dim});
+      check_shape(t, b + "attn_output.weight", {(uint64_t)c.heads * c.head_dim, c.hidden});
+      check_shape(t, b + "ffn_gate_inp.weight", {c.hidden, c.experts});
+      check_shape(t, b + "ffn_gate_exps.weight", {c.hidden, c.intermediate, c.experts});
+      check_shape(t, b + "ffn_up_exps.weight", {c.hidden, c.intermediate, c.experts});
+      check_shape(t, b + "ffn_down_exps.weight", {c.intermediate, c.hidden, c.experts});
+      for (auto& kv : t) {
+        const std::string& n = kv.first;
+        const bool bias = n.size() >= 5 && n.compare(n.size() - 5, 5, ".bias") == 0;
+        ensure(!(n.rfind(b, 0) == 0 && bias), "unexpected bias tensors");
+      }
+    }
+  }
+
+  // ---- build ------------------------------------------------------------------------------
+  void build(const std::map<std::string, TensorIn>& t, const qc_config& c, uint32_t ctx, int dev) {
+    cfg = c;
+    validate_config(cfg);
+    validate_tensors(t);
+    ensure(ctx > 0 && ctx <= cfg.max_context, "context must be in 1..=" + std::to_string(cfg.max_context));
+    context = ctx;
+    device = dev;
+    QC_CK(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    QC_CK(cudaGetDeviceProperties(&prop, device));
+    sms = prop.multiProcessorCount;
+    prepare_device(device);
+    QC_CK(cudaStreamCreateWithFlags(&own, cudaStreamNonBlocking));
+    stream = own;
+
+    // placement of every tensor the forward reads
+    std::vector<std::string> names = {"token_embd.weight", "output_norm.weight"};
+    const bool tied = !t.count("output.weight");
+    if (!tied) names.push_back("output.weight");
+    static const char* per_layer[] = {"attn_norm", "attn_q", "attn_k", "attn_v", "attn_q_norm", "attn_k_norm",
+                                      "attn_output", "ffn_norm", "ffn_gate_inp", "ffn_gate_exps", "ffn_up_exps",
+                                      "ffn_down_exps"};
+    for (uint32_t i = 0; i < cfg.layers; i++)
+      for (const char* n : per_layer) names.push_back("blk." + std::to_string(i) + "." + n + ".weight");
+    std::map<std::string, Placed> placed;
+    uint64_t off = 0, max_row = 0;
+    for (const std::string& n : names) {
+      const TensorIn& ti = t.at(n);
+      Placed p;
+      p.t = &ti;
+      p.cols = ti.dims[0];
+      p.rows = ti.dims.size() > 1 ? ti.dims[1] : 1;
+      p.experts = ti.dims.size() > 2 ? ti.dims[2] : 1;
+      p.vector = ti.dims.size() == 1;
+      uint64_t raw_row;
+      if (const char* e = qc::ggml_row_bytes(ti.kind, p.cols, &raw_row)) throw ApiError(QC_ERR_INVALID, n + ": " + e);
+      ensure(ti.len == raw_row * p.rows * p.experts, n + ": tensor length does not match its shape");
+      ensure(p.rows <= 0xffffffffull && p.cols <= 0xffffffffull, n + ": tensor too large");
+      max_row = raw_row > max_row ? raw_row : max_row;
+      p.lay = qc::dev_layout(ti.kind, p.cols);
+      p.off_main = off;
+      off = align256(off + p.lay.main_bytes(p.rows) * p.experts);
+      if (p.lay.d_stride) {
+        p.off_d = off;
+        off = align256(off + p.lay.d_bytes(p.rows) * p.experts);
+      }
+      if (p.vector) {
+        p.off_f32 = off;
+        off = align256(off + p.cols * sizeof(float));
+      }
+      placed[n] = p;
+    }
+    weight_bytes = off;
+    QC_CK(cudaMalloc(&d_weights, weight_bytes));
+    {
+      Uploader up(stream, max_row);
+      for (const std::string& n : names) {
+        const Placed& p = placed[n];
+        uint64_t raw_row;
+        qc::ggml_row_bytes(p.t->kind, p.cols, &raw_row);
+        stats.uploaded_bytes +=
+            up.put(p.t->data, p.rows * p.experts, raw_row, p.t->kind, p.cols, d_weights + p.off_main,
+                   p.lay.row_stride, p.lay.d_stride ? reinterpret_cast<__half*>(d_weights + p.off_d) : nullptr,
+                   p.lay.d_stride);
+        if (p.vector) {
+          qc::launch_dequant(make_desc(p, d_weights), 0, reinterpret_cast<float*>(d_weights + p.off_f32), stream);
+          QC_CK(cudaGetLastError());
+        }
+      }
+      QC_CK(cudaStreamSynchronize(stream));
+    }
+    auto vec = [&](const std::string& n) { return reinterpret_cast<const float*>(d_weights + placed[n].off_f32); };
+    embd = make_desc(placed["token_embd.weight"], d_weights);
+    out = tied ? embd : make_desc(placed["output.weight"], d_weights);
+    out_norm = vec("output_norm.weight");
+
+    // KV cache: [layer][kvhead][ctx][D], K then V
+    const uint64_t D = cfg.head_dim, per_layer_kv = (uint64_t)cfg.kvheads * context * D;
+    kv_bytes = per_layer_kv * cfg.layers * 2 * sizeof(float);
+    QC_CK(cudaMalloc(&d_kv, kv_bytes));
+    layers.resize(cfg.layers);
+    for (uint32_t i = 0; i < cfg.layers; i++) {
+      const std::string b = "blk." + std::to_string(i) + ".";
+      qc::LayerDev& L = layers[i];
+      L.q = make_desc(placed[b + "attn_q.weight"], d_weights);
+      L.k = make_desc(placed[b + "attn_k.weight"], d_weights);
+      L.v = make_desc(placed[b + "attn_v.weight"], d_weights);
+      uint32_t lpr = L.q.lpr < L.k.lpr ? L.q.lpr : L.k.lpr;
+      lpr = lpr < L.v.lpr ? lpr : L.v.lpr;
+      L.q = with_lpr(L.q, lpr);
+      L.k = with_lpr(L.k, lpr);
+      L.v = with_lpr(L.v, lpr);
+      L.o = make_desc(placed[b + "attn_output.weight"], d_weights);
+      L.router = make_desc(placed[b + "ffn_gate_inp.weight"], d_weights);
+      L.gate = make_desc(placed[b + "ffn_gate_exps.weight"], d_weights);
+      L.up = make_desc(placed[b + "ffn_up_exps.weight"], d_weights);
+      const uint32_t lg = L.gate.lpr < L.up.lpr ? L.gate.lpr : L.up.lpr;
+      L.gate = with_lpr(L.gate, lg);
+      L.up = with_lpr(L.up, lg);
+      L.down = make_desc(placed[b + "ffn_down_exps.weight"], d_weights);
+      L.attn_norm = vec(b + "attn_norm.weight");
+      L.q_norm = vec(b + "attn_q_norm.weight");
+      L.k_norm = vec(b + "attn_k_norm.weight");
+      L.ffn_norm = vec(b + "ffn_norm.weight");
+      L.kc = d_kv + (uint64_t)i * 2 * per_layer_kv;
+      L.vc = L.kc + per_layer_kv;
+    }
+
+    // scratch
+    dims.hidden = cfg.hidden;
+    dims.heads = cfg.heads;
+    dims.kvheads = cfg.kvheads;
+    dims.head_dim = cfg.head_dim;
+    dims.experts = cfg.experts;
+    dims.top = cfg.top;
+    dims.inter = cfg.intermediate;
+    dims.vocab = cfg.vocab;
+    dims.ctx = context;
+    dims.eps = cfg.eps;
+    uint32_t nsplit = 32;
+    while ((context + nsplit - 1) / nsplit > 512) nsplit *= 2;
+    dims.nsplit = nsplit;
+    const uint64_t G = cfg.heads / cfg.kvheads, QD = (uint64_t)cfg.heads * D, KD = (uint64_t)cfg.kvheads * D;
+    uint64_t so = 0;
+    auto take = [&](uint64_t bytes) {
+      const uint64_t o = so;
+      so = align256(so + bytes);
+      return o;
+    };
+    const uint64_t o_x = take(cfg.hidden * 4), o_xn = take(cfg.hidden * 4), o_qkv = take((QD + 2 * KD) * 4);
+    const uint64_t o_attn = take(QD * 4), o_part = take((uint64_t)cfg.kvheads * nsplit * G * (D + 2) * 4);
+    const uint64_t o_rl = take(cfg.experts * 4), o_sel = take(cfg.top * 4), o_selw = take(cfg.top * 4);
+    const uint64_t o_h = take((uint64_t)cfg.top * cfg.intermediate * 4), o_log = take((uint64_t)cfg.vocab * 4);
+    const uint64_t o_rope = take((uint64_t)context * (D / 2) * 8), o_gen = take((uint64_t)context * 4);
+    const uint64_t o_st = take(sizeof(qc::DevState));
+    QC_CK(cudaMalloc(&d_scratch, so));
+    QC_CK(cudaMemsetAsync(d_scratch, 0, so, stream));
+    sc.x = reinterpret_cast<float*>(d_scratch + o_x);
+    sc.xn = reinterpret_cast<float*>(d_scratch + o_xn);
+    sc.qkv = reinterpret_cast<float*>(d_scratch + o_qkv);
+    sc.attn = reinterpret_cast<float*>(d_scratch + o_attn);
+    sc.part = reinterpret_cast<float*>(d_scratch + o_part);
+    sc.rlogit = reinterpret_cast<float*>(d_scratch + o_rl);
+    sc.sel = reinterpret_cast<uint32_t*>(d_scratch + o_sel);
+    sc.selw = reinterpret_cast<float*>(d_scratch + o_selw);
+    sc.h = reinterpret_cast<float*>(d_scratch + o_h);
+    sc.logits = reinterpret_cast<float*>(d_scratch + o_log);
+    sc.rope = reinterpret_cast<const float2*>(d_scratch + o_rope);
+    d_gen = reinterpret_cast<uint32_t*>(d_scratch + o_gen);
+    d_state = reinterpret_cast<qc::DevState*>(d_scratch + o_st);
+
+    // RoPE angles exactly as ops.rs:17-28 computes them on the host: pos * theta^(-2i/D) in f32.
+    std::vector<float2> rope((uint64_t)context * (D / 2));
+    for (uint64_t p = 0; p < context; p++)
+      for (uint64_t i = 0; i < D / 2; i++) {
+        const float e = -2.0f * (float)i / (float)D;
+        const float angle = (float)p * powf(cfg.theta, e);
+        rope[p * (D / 2) + i] = make_float2(cosf(angle), sinf(angle));
+      }
+    QC_CK(cudaMemcpyAsync(d_scratch + o_rope, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice,
+                          stream));
+    h_template = qc::DevState{};
+    h_template.gen_tokens = d_gen;
+    h_template.gen_cap = context;
+    QC_CK(cudaMemcpyAsync(d_state, &h_template, sizeof h_template, cudaMemcpyHostToDevice, stream));
+    QC_CK(cudaMallocHost(&h_pinned, 64));
+    QC_CK(cudaEventCreate(&ev0));
+    QC_CK(cudaEventCreate(&ev1));
+    QC_CK(cudaStreamSynchronize(stream));
+    capture();
+  }
+
+  qc::StepArgs step_args() const {
+    qc::StepArgs a{};
+    a.dims = dims;
+    a.sc = sc;
+    a.st = d_state;
+    a.layers = layers.data();
+    a.n_layers = cfg.layers;
+    a.embd = embd;
+    a.out = out;
+    a.out_norm = out_norm;
+    a.sms = sms;
+    return a;
+  }
+
+  void capture() {
+    cudaStream_t cs;
+    QC_CK(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+    QC_CK(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+    qc::launch_step(step_args(), cs);
+    cudaError_t le = cudaGetLastError();
+    cudaError_t ce = cudaStreamEndCapture(cs, &graph);
+    cudaStreamDestroy(cs);
+    QC_CK(le);
+    QC_CK(ce);
+    QC_CK(cudaGraphInstantiate(&exec, graph, 0));
+  }
+
+  // ---- model.rs:202-216 ------------------------------------------------------------------
+  void reset() {
+    cudaSetDevice(device);
+    // any earlier asynchronous failure is reported by the caller; the reset itself must not throw past here
+    cudaMemcpyAsync(d_state, &h_template, sizeof h_template, cudaMemcpyHostToDevice, stream);
+    cudaStreamSynchronize(stream);
+    pos = 0;
+  }
+
+  // ---- per-kernel timing: a second graph with external event records between kernels ----
+  cudaGraphExec_t prof_exec = nullptr;
+  cudaGraph_t prof_graph = nullptr;
+  std::vector<cudaEvent_t> prof_ev;
+  std::vector<int> prof_kind;
+
+  struct ProfCtx {
+    qc_engine* e;
+    cudaError_t err;
+  };
+  static void prof_hook(void* p, int kind, cudaStream_t s) {
+    ProfCtx* c = static_cast<ProfCtx*>(p);
+    qc_engine* e = c->e;
+    cudaEvent_t ev;
+    cudaError_t r = cudaEventCreate(&ev);
+    if (r == cudaSuccess) r = cudaEventRecordWithFlags(ev, s, cudaEventRecordExternal);
+    if (r != cudaSuccess && c->err == cudaSuccess) c->err = r;
+    e->prof_ev.push_back(ev);
+    e->prof_kind.push_back(kind);
+  }
+
+  void profile(qc_phase_times* out) {
+    ensure(pos < context, "context limit " + std::to_string(context) + " reached", QC_ERR_CONTEXT);
+    QC_CK(cudaSetDevice(device));
+    if (!prof_exec) {
+      cudaStream_t cs;
+      QC_CK(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+      ProfCtx ctx{this, cudaSuccess};
+      QC_CK(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+      qc::launch_step(step_args(), cs, &qc_engine::prof_hook, &ctx);
+      cudaError_t le = cudaGetLastError();
+      cudaError_t ce = cudaStreamEndCapture(cs, &prof_graph);
+      cudaStreamDestroy(cs);
+      QC_CK(ctx.err);
+      QC_CK(le);
+      QC_CK(ce);
+      QC_CK(cudaGraphInstantiate(&prof_exec, prof_graph, 0));
+    }
+    QC_CK(cudaGraphLaunch(prof_exec, stream));
+    check_flags();
+    double* slot[qc::K_COUNT] = {&out->embed_ms, &out->attn_in_ms, &out->attention_ms, &out->oproj_ms,
+                                 &out->router_ms, &out->gateup_ms, &out->down_ms, &out->output_ms};
+    *out = qc_phase_times{};
+    for (size_t i = 0; i + 1 < prof_ev.size(); i++) {
+      float ms = 0.f;
+      QC_CK(cudaEventElapsedTime(&ms, prof_ev[i], prof_ev[i + 1]));
+      *slot[prof_kind[i]] += ms;
+    }
+    out->launches = qc::step_launches(cfg.layers);
+    pos += 1;
+    stats.tokens += 1;
+  }
+
+  void launch_steps(uint32_t n) {
+    for (uint32_t i = 0; i < n; i++) QC_CK(cudaGraphLaunch(exec, stream));
+  }
+
+  // Reads the sticky flags after `stream` is drained; a set flag is an error.
+  void check_flags() {
+    QC_CK(cudaMemcpyAsync(h_pinned + 2, &d_state->nonfinite, 8, cudaMemcpyDeviceToHost, stream));
+    QC_CK(cudaStreamSynchronize(stream));
+    if (h_pinned[3]) throw ApiError(QC_ERR_TOKEN, "token outside vocabulary");
+    if (h_pinned[2]) throw ApiError(QC_ERR_NONFINITE, "nonfinite model output");
+  }
+
+  void forward(uint32_t token, float* logits) {
+    ensure(pos < context, "context limit " + std::to_string(context) + " reached", QC_ERR_CONTEXT);
+    ensure(token < cfg.vocab, "token outside vocabulary", QC_ERR_TOKEN);
+    QC_CK(cudaSetDevice(device));
+    h_pinned[0] = token;
+    QC_CK(cudaMemcpyAsync(&d_state->token, h_pinned, 4, cudaMemcpyHostToDevice, stream));
+    QC_CK(cudaEventRecord(ev0, stream));
+    launch_steps(1);
+    QC_CK(cudaEventRecord(ev1, stream));
+    if (logits) QC_CK(cudaMemcpyAsync(logits, sc.logits, (size_t)cfg.vocab * 4, cudaMemcpyDeviceToHost, stream));
+    check_flags();
+    float ms = 0.f;
+    QC_CK(cudaEventElapsedTime(&ms, ev0, ev1));
+    stats.matvec_ms += ms;
+    stats.tokens += 1;
+    stats.matvecs += (5ull + 3ull * cfg.top) * cfg.layers + 1;
+    pos += 1;
+  }
+
+  void decode(uint32_t n, uint32_t* tokens_out, float* logits, bool wait) {
+    ensure(pos > 0, "greedy decode needs the logits of a previous forward");
+    ensure((uint64_t)pos + n <= context, "prompt + max-tokens exceed --ctx", QC_ERR_CONTEXT);
+    QC_CK(cudaSetDevice(device));
+    h_pinned[4] = 0;  // gen_count
+    QC_CK(cudaMemcpyAsync(&d_state->gen_count, h_pinned + 4, 4, cudaMemcpyHostToDevice, stream));
+    if (wait) QC_CK(cudaEventRecord(ev0, stream));
+    launch_steps(n);
+    pos += n;
+    stats.tokens += n;
+    stats.matvecs += ((5ull + 3ull * cfg.top) * cfg.layers + 1) * n;
+    if (!wait) return;
+    QC_CK(cudaEventRecord(ev1, stream));
+    if (tokens_out && n) QC_CK(cudaMemcpyAsync(tokens_out, d_gen, (size_t)n * 4, cudaMemcpyDeviceToHost, stream));
+    if (logits) QC_CK(cudaMemcpyAsync(logits, sc.logits, (size_t)cfg.vocab * 4, cudaMemcpyDeviceToHost, stream));
+    check_flags();
+    float ms = 0.f;
+    QC_CK(cudaEventElapsedTime(&ms, ev0, ev1));
+    stats.matvec_ms += ms;
+  }
+};
+
+struct qc_matrix {
+  int device = 0;
+  qc::MatDesc desc{};
+  uint8_t* d = nullptr;
+  uint64_t bytes = 0, packed = 0, experts = 1;
+  ~qc_matrix() {
+    cudaSetDevice(device);
+    cudaFree(d);
+  }
+};
+
+namespace {
+
+// model.rs:21-90 Config::from_gguf
+qc_config config_from(const qc::GgufFile& g) {
+  const std::string* arch = g.str("general.architecture");
+  ensure(arch && *arch == "qwen3moe", "only qwen3moe architecture is implemented");
+  auto get = [&](const char* k) { return g.need_uint(std::string("qwen3moe.") + k); };
+  auto opt = [&](const char* k, uint64_t* v) { return g.uint(std::string("qwen3moe.") + k, v); };
+  qc_config c{};
+  uint64_t v;
+  const uint64_t hidden = get("embedding_length"), heads = get("attention.head_count"), top = get("expert_used_count");
+  const uint64_t head_dim = opt("attention.key_length", &v) ? v : hidden / (heads ? heads : 1);
+  ensure((opt("attention.value_length", &v) ? v : head_dim) == head_dim, "different key/value head sizes unsupported");
+  const uint64_t layers = get("block_count"), kvh = get("attention.head_count_kv"), experts = get("expert_count");
+  const uint64_t inter =
+      opt("expert_feed_forward_length", &v) ? v : get("feed_forward_length") / (top ? top : 1);
+  const qc::GgufTensor& te = g.tensor("token_embd.weight");
+  ensure(te.dims.size() > 1, "invalid embedding rank");
+  const uint64_t maxctx = get("context_length");
+  auto u32 = [](uint64_t x) {
+    ensure(x <= 0xffffffffull, "invalid Qwen3 MoE config");
+    return (uint32_t)x;
+  };
+  c.hidden = u32(hidden);
+  c.heads = u32(heads);
+  c.top = u32(top);
+  c.head_dim = u32(head_dim);
+  c.layers = u32(layers);
+  c.kvheads = u32(kvh);
+  c.experts = u32(experts);
+  c.intermediate = u32(inter);
+  c.vocab = u32(te.dims[1]);
+  c.max_context = u32(maxctx);
+  c.eps = g.real("qwen3moe.attention.layer_norm_rms_epsilon", 1e-6f);
+  c.theta = g.real("qwen3moe.rope.freq_base", 1000000.f);
+  qc_engine::validate_config(c);
+  ensure((opt("rope.dimension_count", &v) ? v : head_dim) == head_dim, "partial rotary dimensions unsupported");
+  const std::string* scaling = g.str("qwen3moe.rope.scaling.type");
+  ensure(!scaling || *scaling == "none", "RoPE scaling is not implemented; use the original native-context model");
+  return c;
+}
+
+template <class F>
+int api(qc_engine* e, F&& f) {
+  try {
+    f();
+    return QC_OK;
+  } catch (const ApiError& x) {
+    g_last_error = x.what();
+    if (e) e->err = x.what();
+    return x.code;
+  } catch (const qc::GgufError& x) {
+    g_last_error = x.what();
+    if (e) e->err = x.what();
+    return QC_ERR_INVALID;
+  } catch (const std::bad_alloc&) {
+    g_last_error = "host allocation failed";
+    if (e) e->err = g_last_error;
+    return QC_ERR_NOMEM;
+  } catch (const std::exception& x) {
+    g_last_error = x.what();
+    if (e) e->err = x.what();
+    return QC_ERR_INVALID;
+  }
+}
+
+// A forward-type call: on failure the cache and position are reset (model.rs:210-216).
+template <class F>
+int api_forward(qc_engine* e, F&& f) {
+  if (!e) return g_last_error = "null engine", QC_ERR_INVALID;
+  const int rc = api(e, f);
+  if (rc != QC_OK) e->reset();
+  return rc;
+}
+
+int create_from(const qc::GgufFile& g, const uint8_t* base, uint32_t context, int device, qc_engine** out) {
+  std::unique_ptr<qc_engine> e(new qc_engine);
+  const qc_config c = config_from(g);
+  std::map<std::string, TensorIn> t;
+  for (auto& kv : g.tensors) {
+    TensorIn ti;
+    ti.name = kv.first;
+    ti.kind = kv.second.kind;
+    ti.dims = kv.second.dims;
+    ti.data = base + kv.second.offset;
+    ti.len = kv.second.len;
+    t[kv.first] = ti;
+  }
+  e->build(t, c, context, device);
+  *out = e.release();
+  return QC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* qc_last_error(void) { return g_last_error.c_str(); }
+const char* qc_engine_error(const qc_engine* e) { return e ? e->err.c_str() : g_last_error.c_str(); }
+
+int qc_row_bytes(uint32_t kind, uint64_t cols, uint64_t* out) {
+  return api(nullptr, [&] {
+    if (const char* e = qc::ggml_row_bytes(kind, cols, out)) throw ApiError(QC_ERR_INVALID, e);
+  });
+}
+
+int qc_engine_create(const qc_tensor_desc* tensors, size_t n_tensors, const uint8_t* base, size_t base_len,
+                     const qc_config* cfg, uint32_t context, int device, qc_engine** out) {
+  return api(nullptr, [&] {
+    ensure(tensors && cfg && out && (base || !base_len), "null argument");
+    *out = nullptr;
+    std::map<std::string, TensorIn> t;
+    for (size_t k = 0; k < n_tensors; k++) {
+      const qc_tensor_desc& d = tensors[k];
+      ensure(d.name && d.n_dims >= 1 && d.n_dims <= 3, "invalid tensor descriptor");
+      ensure(d.offset <= base_len && d.len <= base_len - d.offset, std::string("truncated tensor ") + d.name);
+      TensorIn ti;
+      ti.name = d.name;
+      ti.kind = d.kind;
+      ti.dims.assign(d.dims, d.dims + d.n_dims);
+      ti.data = base + d.offset;
+      ti.len = d.len;
+      ensure(t.emplace(ti.name, ti).second, "duplicate tensor name");
+    }
+    auto emb = t.find("token_embd.weight");
+    ensure(emb != t.end() && emb->second.dims.size() > 1 && emb->second.dims[1] == cfg->vocab,
+           "config vocab does not match token_embd.weight");
+    std::unique_ptr<qc_engine> e(new qc_engine);
+    e->build(t, *cfg, context, device);
+    *out = e.release();
+  });
+}
+
+int qc_engine_create_gguf(const uint8_t* image, size_t len, uint32_t context, int device, qc_engine** out) {
+  return api(nullptr, [&] {
+    ensure(out && (image || !len), "null argument");
+    *out = nullptr;
+    qc::GgufFile g;
+    g.parse(image, len);
+    create_from(g, image, context, device, out);
+  });
+}
+
+int qc_engine_open(const char* path, uint32_t context, int device, qc_engine** out) {
+  return api(nullptr, [&] {
+    ensure(path && out, "null argument");
+    *out = nullptr;
+    const int fd = open(path, O_RDONLY);
+    ensure(fd >= 0, std::string("open ") + path);
+    struct stat st;
+    fstat(fd, &st);
+    const size_t len = (size_t)st.st_size;
+    void* map = len ? mmap(nullptr, len, PROT_READ, MAP_PRIVATE, fd, 0) : nullptr;
+    close(fd);
+    ensure(!len || map != MAP_FAILED, std::string("mmap ") + path);
+    struct Unmap {
+      void* p;
+      size_t n;
+      ~Unmap() {
+        if (p && p != MAP_FAILED) munmap(p, n);
+      }
+    } unmap{map, len};
+    qc::GgufFile g;
+    g.parse(static_cast<const uint8_t*>(map), len);
+    create_from(g, static_cast<const uint8_t*>(map), context, device, out);
+  });
+}
+
+void qc_engine_destroy(qc_engine* e) { delete e; }
+
+int qc_engine_config(const qc_engine* e, qc_config* out) {
+  return api(const_cast<qc_engine*>(e), [&] {
+    ensure(e && out, "null argument");
+    *out = e->cfg;
+  });
+}
+
+int qc_engine_set_stream(qc_engine* e, void* stream) {
+  return api(e, [&] {
+    ensure(e, "null engine");
+    QC_CK(cudaSetDevice(e->device));
+    QC_CK(cudaStreamSynchronize(e->stream));
+    e->stream = stream ? static_cast<cudaStream_t>(stream) : e->own;
+  });
+}
+
+int qc_forward(qc_engine* e, uint32_t token, float* logits) {
+  return api_forward(e, [&] { e->forward(token, logits); });
+}
+
+int qc_forward_tokens(qc_engine* e, const uint32_t* tokens, size_t n, float* logits) {
+  return api_forward(e, [&] {
+    ensure(tokens || !n, "null tokens");
+    for (size_t i = 0; i < n; i++) e->forward(tokens[i], i + 1 == n ? logits : nullptr);
+  });
+}
+
+int qc_decode_greedy(qc_engine* e, uint32_t n, uint32_t* tokens_out, float* logits) {
+  if (e && (e->pos == 0 || (uint64_t)e->pos + n > e->context))  // argument errors: no reset (main.rs:219-227)
+    return api(e, [&] { e->decode(n, tokens_out, logits, true); });
+  return api_forward(e, [&] { e->decode(n, tokens_out, logits, true); });
+}
+
+int qc_decode_enqueue(qc_engine* e, uint32_t n) {
+  if (e && (e->pos == 0 || (uint64_t)e->pos + n > e->context)) return api(e, [&] { e->decode(n, nullptr, nullptr, false); });
+  return api_forward(e, [&] { e->decode(n, nullptr, nullptr, false); });
+}
+
+int qc_sync(qc_engine* e) {
+  return api_forward(e, [&] { e->check_flags(); });
+}
+
+int qc_reset(qc_engine* e) {
+  return api(e, [&] {
+    ensure(e, "null engine");
+    e->reset();
+  });
+}
+
+int qc_position(const qc_engine* e, uint32_t* pos) {
+  return api(const_cast<qc_engine*>(e), [&] {
+    ensure(e && pos, "null argument");
+    *pos = e->pos;
+  });
+}
+
+int qc_get_stats(const qc_engine* e, qc_stats* out) {
+  return api(const_cast<qc_engine*>(e), [&] {
+    ensure(e && out, "null argument");
+    *out = e->stats;
+    out->weight_bytes = e->weight_bytes;
+    out->kv_bytes = e->kv_bytes;
+  });
+}
+
+int qc_profile_step(qc_engine* e, qc_phase_times* out) {
+  return api_forward(e, [&] {
+    ensure(out != nullptr, "null argument");
+    e->profile(out);
+  });
+}
+
+int qc_logits_device(const qc_engine* e, const float** out) {
+  return api(const_cast<qc_engine*>(e), [&] {
+    ensure(e && out, "null argument");
+    *out = e->sc.logits;
+  });
+}
+
+int qc_matrix_create(uint32_t kind, uint64_t rows, uint64_t cols, uint64_t experts, const uint8_t* blocks,
+                     uint64_t len, int device, qc_matrix** out) {
+  return api(nullptr, [&] {
+    ensure(out && blocks, "null argument");
+    *out = nullptr;
+    uint64_t raw_row;
+    if (const char* e = qc::ggml_row_bytes(kind, cols, &raw_row)) throw ApiError(QC_ERR_INVALID, e);
+    ensure(rows > 0 && experts > 0 && rows <= 0xffffffffull && cols <= 0xffffffffull, "matvec shape mismatch");
+    ensure(len == raw_row * rows * experts, "GPU matvec shape mismatch");
+    QC_CK(cudaSetDevice(device));
+    prepare_device(device);
+    std::unique_ptr<qc_matrix> m(new qc_matrix);
+    m->device = device;
+    const qc::DevLayout lay = qc::dev_layout(kind, cols);
+    const uint64_t main = align256(lay.main_bytes(rows) * experts), dp = align256(lay.d_bytes(rows) * experts);
+    m->bytes = main + dp;
+    m->packed = len;
+    m->experts = experts;
+    QC_CK(cudaMalloc(&m->d, m->bytes));
+    {
+      Uploader up(nullptr, raw_row, len);
+      up.put(blocks, rows * experts, raw_row, kind, cols, m->d, lay.row_stride,
+             lay.d_stride ? reinterpret_cast<__half*>(m->d + main) : nullptr, lay.d_stride);
+    }
+    QC_CK(cudaDeviceSynchronize());
+    qc::MatDesc& d = m->desc;
+    d.w = m->d;
+    d.d = lay.d_stride ? reinterpret_cast<const __half*>(m->d + main) : nullptr;
+    d.kind = kind;
+    d.rows = (uint32_t)rows;
+    d.cols = (uint32_t)cols;
+    d.units = lay.units;
+    d.lpr = lay.lpr;
+    d.upl = lay.upl;
+    d.row_stride = lay.row_stride;
+    d.d_stride = lay.d_stride;
+    d.expert_stride = rows * lay.row_stride;
+    d.d_expert_stride = rows * lay.d_stride;
+    *out = m.release();
+  });
+}
+
+int qc_matrix_matvec(const qc_matrix* m, uint32_t expert, const float* x, float* y, void* stream) {
+  return api(nullptr, [&] {
+    ensure(m && x && y, "null argument");
+    ensure(expert < m->experts, "expert out of bounds");
+    QC_CK(cudaSetDevice(m->device));
+    ensure(qc::matvec_smem(m->desc) <= (size_t)kMaxSmem, "row too wide for the shared-memory activation tile");
+    qc::launch_matvec(m->desc, expert, x, y, 148, static_cast<cudaStream_t>(stream));
+    QC_CK(cudaGetLastError());
+  });
+}
+
+int qc_matrix_dequant(const qc_matrix* m, uint32_t expert, float* outp, void* stream) {
+  return api(nullptr, [&] {
+    ensure(m && outp, "null argument");
+    ensure(expert < m->experts, "expert out of bounds");
+    QC_CK(cudaSetDevice(m->device));
+    qc::launch_dequant(m->desc, expert, outp, static_cast<cudaStream_t>(stream));
+    QC_CK(cudaGetLastError());
+  });
+}
+
+int qc_matrix_bytes(const qc_matrix* m, uint64_t* device_bytes, uint64_t* packed_bytes) {
+  return api(nullptr, [&] {
+    ensure(m, "null argument");
+    if (device_bytes) *device_bytes = m->bytes;
+    if (packed_bytes) *packed_bytes = m->packed;
+  });
+}
+
+void qc_matrix_destroy(qc_matrix* m) { delete m; }
+
+int qc_packed_matvec(uint32_t kind, uint64_t rows, uint64_t cols, const uint8_t* blocks, uint64_t len,
+                     const float* x, float* y) {
+  return api(nullptr, [&] {
+    ensure(x && y, "null argument");
+    qc_matrix* m = nullptr;
+    int rc = qc_matrix_create(kind, rows, cols, 1, blocks, len, 0, &m);
+    if (rc) throw ApiError(rc, g_last_error);
+    std::unique_ptr<qc_matrix> own(m);
+    float *dx = nullptr, *dy = nullptr;
+    QC_CK(cudaMalloc(&dx, cols * 4));
+    struct Free {
+      float** a;
+      float** b;
+      ~Free() {
+        cudaFree(*a);
+        cudaFree(*b);
+      }
+    } fr{&dx, &dy};
+    QC_CK(cudaMalloc(&dy, rows * 4));
+    QC_CK(cudaMemcpy(dx, x, cols * 4, cudaMemcpyHostToDevice));
+    rc = qc_matrix_matvec(m, 0, dx, dy, nullptr);
+    if (rc) throw ApiError(rc, g_last_error);
+    QC_CK(cudaMemcpy(y, dy, rows * 4, cudaMemcpyDeviceToHost));
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,67 @@
+// Host-side description of GGML formats and of the engine's device layout.
+#pragma once
+#include <stdint.h>
+
+#include <string>
+
+namespace qc {
+
+// Reference quant.rs:5-11: (elements per block, bytes per block); false for unknown kinds.
+inline bool ggml_block(uint32_t kind, uint64_t* elems, uint64_t* bytes) {
+  switch (kind) {
+    case 0: *elems = 1; *bytes = 4; return true;
+    case 1: *elems = 1; *bytes = 2; return true;
+    case 2: *elems = 32; *bytes = 18; return true;
+    case 8: *elems = 32; *bytes = 34; return true;
+    case 12: *elems = 256; *bytes = 144; return true;
+    case 13: *elems = 256; *bytes = 176; return true;
+    case 14: *elems = 256; *bytes = 210; return true;
+  }
+  return false;
+}
+
+// Reference quant.rs:12-21.  Returns 0 on success, or an error message.
+inline const char* ggml_row_bytes(uint32_t kind, uint64_t cols, uint64_t* out) {
+  uint64_t e, b;
+  if (!ggml_block(kind, &e, &b)) return "GGML tensor type is not supported (supported: F32/F16/Q4_0/Q8_0/Q4_K/Q5_K/Q6_K)";
+  if (cols == 0 || cols % e) return "row width is not divisible by block size";
+  *out = cols / e * b;
+  return nullptr;
+}
+
+// Device layout of a (rows x cols) matrix of `kind` (see MatDesc in common.cuh).
+struct DevLayout {
+  uint64_t row_stride = 0;  // bytes per row, main plane (multiple of 16)
+  uint64_t d_stride = 0;    // halves per row, d plane (0: no d plane)
+  uint32_t units = 0, lpr = 1, upl = 1;
+  uint64_t main_bytes(uint64_t rows) const { return rows * row_stride; }
+  uint64_t d_bytes(uint64_t rows) const { return rows * d_stride * 2; }
+};
+
+inline DevLayout dev_layout(uint32_t kind, uint64_t cols) {
+  DevLayout l;
+  switch (kind) {
+    case 12: l.row_stride = cols / 256 * 144; l.units = (uint32_t)(cols / 256 * 4); break;
+    case 13: l.row_stride = cols / 256 * 176; l.units = (uint32_t)(cols / 256 * 4); break;
+    case 14: l.row_stride = cols / 256 * 208; l.d_stride = cols / 256; l.units = (uint32_t)(cols / 256 * 4); break;
+    case 8: l.row_stride = cols / 32 * 32; l.d_stride = cols / 32; l.units = (uint32_t)(cols / 32); break;
+    case 2: l.row_stride = cols / 32 * 16; l.d_stride = cols / 32; l.units = (uint32_t)(cols / 32); break;
+    case 1: l.units = (uint32_t)((cols + 31) / 32); l.row_stride = (uint64_t)l.units * 64; break;
+    default: l.units = (uint32_t)((cols + 15) / 16); l.row_stride = (uint64_t)l.units * 64; break;
+  }
+  uint32_t lpr = 1;
+  while (lpr < 32 && l.units % (lpr * 2) == 0) lpr *= 2;
+  l.lpr = lpr;
+  l.upl = l.units / lpr;
+  return l;
+}
+
+inline uint32_t unit_elems_host(uint32_t kind) {
+  switch (kind) {
+    case 12: case 13: case 14: return 64;
+    case 8: case 2: case 1: return 32;
+    default: return 16;
+  }
+}
+
+}  // namespace qc

@@ -1,0 +1,297 @@
+"""ctypes bindings of the C ABI in include/qwen_cuda.h (libqwen_cuda.so).
+
+This mirrors the reference crate's interface on the host side:
+  Engine.forward(token)         ~ Model::forward (src/model.rs:210-216)
+  Engine.forward_tokens(ids)    ~ the `logits` command's loop (src/main.rs:144-146)
+  Engine.decode_greedy(n)       ~ the chat loop with temperature 0 (src/main.rs:261-282)
+  packed_matvec(...)            ~ Vulkan::packed_matvec (src/backend.rs:174-261)
+  Matrix                        ~ a resident weight matrix for Backend::matvec
+Errors raise QwenCudaError with the engine's message and status code.  There is
+no CPU fallback: if the library is missing, loading fails.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libqwen_cuda.so"
+
+OK, ERR_INVALID, ERR_CUDA, ERR_CONTEXT, ERR_TOKEN, ERR_NONFINITE, ERR_NOMEM = range(7)
+
+EXPORTS = (
+    "qc_engine_create", "qc_engine_create_gguf", "qc_engine_open", "qc_engine_destroy", "qc_engine_error",
+    "qc_last_error", "qc_engine_config", "qc_engine_set_stream", "qc_forward", "qc_forward_tokens",
+    "qc_decode_greedy", "qc_decode_enqueue", "qc_sync", "qc_reset", "qc_position", "qc_get_stats",
+    "qc_logits_device", "qc_row_bytes", "qc_matrix_create", "qc_matrix_matvec", "qc_matrix_dequant",
+    "qc_matrix_bytes", "qc_matrix_destroy", "qc_packed_matvec", "qc_profile_step",
+)
+
+
+class QwenCudaError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+        self.msg = msg
+
+
+class Config(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in ("hidden", "layers", "heads", "kvheads", "head_dim", "experts", "top",
+                                           "intermediate", "vocab", "max_context")] + [
+        ("eps", C.c_float), ("theta", C.c_float)]
+
+    def as_dict(self) -> dict:
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+class TensorDesc(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("kind", C.c_uint32), ("n_dims", C.c_uint32), ("dims", C.c_uint64 * 3),
+                ("offset", C.c_uint64), ("len", C.c_uint64)]
+
+
+PHASES = ("embed", "attn_in", "attention", "oproj", "router", "gateup", "down", "output")
+
+
+class PhaseTimes(C.Structure):
+    _fields_ = [(p + "_ms", C.c_double) for p in PHASES] + [("launches", C.c_uint32)]
+
+
+class Stats(C.Structure):
+    _fields_ = [("matvecs", C.c_uint64), ("uploaded_bytes", C.c_uint64), ("cache_hits", C.c_uint64),
+                ("matvec_ms", C.c_double), ("tokens", C.c_uint64), ("weight_bytes", C.c_uint64),
+                ("kv_bytes", C.c_uint64)]
+
+    def as_dict(self) -> dict:
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Load libqwen_cuda.so (built by qwen-30brust_b200/build.py); fails loudly if absent."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is not built; run `python __graft_entry__.py` / build()")
+        L = C.CDLL(str(LIB_PATH))
+        vp, u32, u64, sz, i = C.c_void_p, C.c_uint32, C.c_uint64, C.c_size_t, C.c_int
+        pp = C.POINTER(vp)
+        L.qc_engine_create.argtypes = [C.POINTER(TensorDesc), sz, vp, sz, C.POINTER(Config), u32, i, pp]
+        L.qc_engine_create_gguf.argtypes = [vp, sz, u32, i, pp]
+        L.qc_engine_open.argtypes = [C.c_char_p, u32, i, pp]
+        L.qc_engine_destroy.argtypes = [vp]
+        L.qc_engine_destroy.restype = None
+        L.qc_engine_error.argtypes = [vp]
+        L.qc_engine_error.restype = C.c_char_p
+        L.qc_last_error.restype = C.c_char_p
+        L.qc_engine_config.argtypes = [vp, C.POINTER(Config)]
+        L.qc_engine_set_stream.argtypes = [vp, vp]
+        L.qc_forward.argtypes = [vp, u32, vp]
+        L.qc_forward_tokens.argtypes = [vp, vp, sz, vp]
+        L.qc_decode_greedy.argtypes = [vp, u32, vp, vp]
+        L.qc_decode_enqueue.argtypes = [vp, u32]
+        L.qc_sync.argtypes = [vp]
+        L.qc_reset.argtypes = [vp]
+        L.qc_position.argtypes = [vp, C.POINTER(u32)]
+        L.qc_get_stats.argtypes = [vp, C.POINTER(Stats)]
+        L.qc_logits_device.argtypes = [vp, pp]
+        L.qc_row_bytes.argtypes = [u32, u64, C.POINTER(u64)]
+        L.qc_matrix_create.argtypes = [u32, u64, u64, u64, vp, u64, i, pp]
+        L.qc_matrix_matvec.argtypes = [vp, u32, vp, vp, vp]
+        L.qc_matrix_dequant.argtypes = [vp, u32, vp, vp]
+        L.qc_matrix_bytes.argtypes = [vp, C.POINTER(u64), C.POINTER(u64)]
+        L.qc_matrix_destroy.argtypes = [vp]
+        L.qc_matrix_destroy.restype = None
+        L.qc_packed_matvec.argtypes = [u32, u64, u64, vp, u64, vp, vp]
+        L.qc_profile_step.argtypes = [vp, C.POINTER(PhaseTimes)]
+        _lib = L
+    return _lib
+
+
+def _global_check(rc: int) -> None:
+    if rc != OK:
+        raise QwenCudaError(rc, lib().qc_last_error().decode())
+
+
+def row_bytes(kind: int, cols: int) -> int:
+    out = C.c_uint64()
+    _global_check(lib().qc_row_bytes(kind, cols, C.byref(out)))
+    return out.value
+
+
+def _u8(a) -> np.ndarray:
+    if isinstance(a, (bytes, bytearray)):
+        return np.frombuffer(bytes(a), dtype=np.uint8)
+    return np.ascontiguousarray(a, dtype=np.uint8)
+
+
+class Engine:
+    """A resident Qwen3-MoE model on one GPU (see include/qwen_cuda.h)."""
+
+    def __init__(self, source, context: int, device: int = 0):
+        L = lib()
+        h = C.c_void_p()
+        if isinstance(source, (str, os.PathLike)):
+            rc = L.qc_engine_open(str(source).encode(), context, device, C.byref(h))
+        else:
+            img = _u8(source)
+            rc = L.qc_engine_create_gguf(img.ctypes.data, img.size, context, device, C.byref(h))
+        _global_check(rc)
+        self._h = h
+        cfg = Config()
+        self._check(L.qc_engine_config(h, C.byref(cfg)))
+        self.config = cfg.as_dict()
+        self.vocab = cfg.vocab
+        self.context = context
+
+    @classmethod
+    def from_tensors(cls, tensors: list[dict], base: np.ndarray, config: dict, context: int, device: int = 0):
+        """qc_engine_create: a parsed tensor table over `base` (name, kind, dims, offset, len)."""
+        L = lib()
+        arr = (TensorDesc * len(tensors))()
+        names = []
+        for k, t in enumerate(tensors):
+            nm = t["name"].encode()
+            names.append(nm)
+            arr[k].name = nm
+            arr[k].kind = t["kind"]
+            arr[k].n_dims = len(t["dims"])
+            for j, d in enumerate(t["dims"]):
+                arr[k].dims[j] = d
+            arr[k].offset = t["offset"]
+            arr[k].len = t["len"]
+        cfg = Config(**{k: config[k] for k, _ in Config._fields_})
+        b = _u8(base)
+        h = C.c_void_p()
+        _global_check(L.qc_engine_create(arr, len(tensors), b.ctypes.data, b.size, C.byref(cfg), context, device,
+                                         C.byref(h)))
+        self = cls.__new__(cls)
+        self._h = h
+        self.config = cfg.as_dict()
+        self.vocab = cfg.vocab
+        self.context = context
+        return self
+
+    def _check(self, rc: int) -> None:
+        if rc != OK:
+            raise QwenCudaError(rc, lib().qc_engine_error(self._h).decode())
+
+    def forward(self, token: int, want_logits: bool = True) -> np.ndarray | None:
+        out = np.empty(self.vocab, dtype=np.float32) if want_logits else None
+        self._check(lib().qc_forward(self._h, token, out.ctypes.data if out is not None else None))
+        return out
+
+    def forward_into(self, token: int, out: np.ndarray) -> None:
+        """qc_forward writing into a caller-owned (e.g. pinned) float32 buffer."""
+        self._check(lib().qc_forward(self._h, token, out.ctypes.data))
+
+    def forward_tokens(self, tokens, want_logits: bool = True) -> np.ndarray | None:
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        out = np.empty(self.vocab, dtype=np.float32) if want_logits else None
+        self._check(lib().qc_forward_tokens(self._h, t.ctypes.data, t.size,
+                                            out.ctypes.data if out is not None else None))
+        return out
+
+    def decode_greedy(self, n: int, want_logits: bool = False):
+        toks = np.empty(max(n, 1), dtype=np.uint32)
+        out = np.empty(self.vocab, dtype=np.float32) if want_logits else None
+        self._check(lib().qc_decode_greedy(self._h, n, toks.ctypes.data, out.ctypes.data if out is not None else None))
+        return toks[:n], out
+
+    def decode_enqueue(self, n: int) -> None:
+        self._check(lib().qc_decode_enqueue(self._h, n))
+
+    def sync(self) -> None:
+        self._check(lib().qc_sync(self._h))
+
+    def reset(self) -> None:
+        self._check(lib().qc_reset(self._h))
+
+    def set_stream(self, stream_ptr: int | None) -> None:
+        self._check(lib().qc_engine_set_stream(self._h, stream_ptr))
+
+    @property
+    def position(self) -> int:
+        p = C.c_uint32()
+        self._check(lib().qc_position(self._h, C.byref(p)))
+        return p.value
+
+    def stats(self) -> dict:
+        s = Stats()
+        self._check(lib().qc_get_stats(self._h, C.byref(s)))
+        return s.as_dict()
+
+    def profile_step(self) -> dict:
+        """Per-kernel-kind device ms of one real decode step (advances the position)."""
+        t = PhaseTimes()
+        self._check(lib().qc_profile_step(self._h, C.byref(t)))
+        out = {p: getattr(t, p + "_ms") for p in PHASES}
+        out["launches"] = t.launches
+        return out
+
+    def logits_device_ptr(self) -> int:
+        p = C.c_void_p()
+        self._check(lib().qc_logits_device(self._h, C.byref(p)))
+        return p.value
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().qc_engine_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+
+class Matrix:
+    """`experts` stacked (rows x cols) GGML matrices resident in the device layout."""
+
+    def __init__(self, kind: int, rows: int, cols: int, blocks, experts: int = 1, device: int = 0):
+        b = _u8(blocks)
+        h = C.c_void_p()
+        _global_check(lib().qc_matrix_create(kind, rows, cols, experts, b.ctypes.data, b.size, device, C.byref(h)))
+        self._h = h
+        self.kind, self.rows, self.cols, self.experts = kind, rows, cols, experts
+
+    def matvec(self, x_ptr: int, y_ptr: int, stream: int | None = None, expert: int = 0) -> None:
+        _global_check(lib().qc_matrix_matvec(self._h, expert, x_ptr, y_ptr, stream))
+
+    def dequant(self, out_ptr: int, stream: int | None = None, expert: int = 0) -> None:
+        _global_check(lib().qc_matrix_dequant(self._h, expert, out_ptr, stream))
+
+    def nbytes(self) -> tuple[int, int]:
+        d, p = C.c_uint64(), C.c_uint64()
+        _global_check(lib().qc_matrix_bytes(self._h, C.byref(d), C.byref(p)))
+        return d.value, p.value
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().qc_matrix_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def packed_matvec(kind: int, rows: int, cols: int, blocks, x) -> np.ndarray:
+    b = _u8(blocks)
+    xx = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(rows, dtype=np.float32)
+    _global_check(lib().qc_packed_matvec(kind, rows, cols, b.ctypes.data, b.size, xx.ctypes.data, y.ctypes.data))
+    return y
