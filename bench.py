@@ -203,7 +203,8 @@ def run_ours(args) -> None:
     t = time.time()
     eng = E.Engine(path if path is not None else img, CTX, device=local)
     log(f"rank {rank}: engine up in {time.time() - t:.1f} s")
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()  # a real stream: NULL would mean the engine's own stream
+    torch.cuda.set_stream(stream)
     eng.set_stream(stream.cuda_stream)
     prompt = np.random.default_rng(1).integers(0, spec.vocab, PROMPT).astype(np.uint32)
     eng.forward_tokens(prompt, want_logits=False)

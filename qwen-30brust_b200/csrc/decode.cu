@@ -10,40 +10,85 @@
 //   k_down      down matvecs, weighted combine, residual              (model.rs:275-287)
 // then k_output: RMSNorm(output_norm), vocab matvec, finiteness check and
 // greedy argmax (model.rs:289-301, sampling.rs:31-35).
+//
+// Launch chaining: every kernel is launched with programmatic stream
+// serialization.  A kernel first issues L2 bulk prefetches of the weight rows
+// its block will read (these do not depend on earlier kernels), then waits for
+// the previous kernel (griddepcontrol.wait), then lets the next kernel launch
+// (griddepcontrol.launch_dependents) and does its work.  The weight stream of
+// kernel k+1 therefore overlaps the tail of kernel k.
+#include <utility>
+
 #include "kernels.h"
 
 namespace qc {
 
 constexpr int NT = 256;
 
-// xs[i] = x[i] * (s * w[i]) with s = 1/sqrt(mean(x^2) + eps) (reference ops.rs:3-15), zero padded.
-QC_DEV void stage_rms(float* xs, const float* __restrict__ x, const float* __restrict__ w, uint32_t n, uint32_t padded,
-                      float eps, float* red) {
+QC_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+QC_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Prefetch [p, p + bytes) into L2 (16-byte aligned start; whole 16-byte granules).
+QC_DEV void prefetch_l2(const void* p, uint64_t bytes) {
+  const uint64_t a = reinterpret_cast<uint64_t>(p) & ~15ull;
+  const uint64_t end = (reinterpret_cast<uint64_t>(p) + bytes + 15) & ~15ull;
+  for (uint64_t o = a + threadIdx.x * 65536ull; o < end; o += blockDim.x * 65536ull) {
+    const uint32_t n = (uint32_t)(end - o < 65536ull ? end - o : 65536ull);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(o), "r"(n) : "memory");
+  }
+}
+// Prefetch rows [r0, r1) of expert e of m (main plane and d plane).
+QC_DEV void prefetch_rows(const MatDesc& m, uint32_t e, uint32_t r0, uint32_t r1) {
+  if (r1 <= r0) return;
+  prefetch_l2(m.w + e * m.expert_stride + (uint64_t)r0 * m.row_stride, (uint64_t)(r1 - r0) * m.row_stride);
+  if (m.d) prefetch_l2(m.d + e * m.d_expert_stride + (uint64_t)r0 * m.d_stride, (uint64_t)(r1 - r0) * m.d_stride * 2);
+}
+
+// rms scale 1/sqrt(mean(x^2) + eps) of x[0..n) (reference ops.rs:3-15), block-wide.
+QC_DEV float rms_scale(const float* __restrict__ x, uint32_t n, float eps, float* red) {
   float ss = 0.f;
   for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
     const float v = x[i];
     ss = fmaf(v, v, ss);
   }
   ss = block_sum(ss, red);
-  const float s = 1.0f / sqrtf(ss / (float)n + eps);
-  for (uint32_t i = threadIdx.x; i < padded; i += blockDim.x) xs[i] = i < n ? __fmul_rn(x[i], __fmul_rn(s, w[i])) : 0.f;
-  __syncthreads();
+  return 1.0f / sqrtf(ss / (float)n + eps);
 }
 
-QC_DEV void stage_copy(float* xs, const float* __restrict__ x, uint32_t n, uint32_t padded) {
-  for (uint32_t i = threadIdx.x; i < padded; i += blockDim.x) xs[i] = i < n ? x[i] : 0.f;
-  __syncthreads();
+// Rows [r0, r1) of this block for `rows` rows split over the grid in row groups of G.
+struct RowChunk {
+  uint32_t r0, r1;
+};
+QC_DEV RowChunk my_rows(uint32_t rows, uint32_t G) {
+  const uint32_t groups = (rows + G - 1) / G;
+  const uint32_t per = (groups + gridDim.x - 1) / gridDim.x;
+  const uint32_t g0 = blockIdx.x * per, g1 = min(groups, g0 + per);
+  return {min(rows, g0 * G), min(rows, g1 * G)};
+}
+
+// The block's warps walk row groups of its chunk; lpr lanes per row.
+template <class F>
+QC_DEV void for_rows(const MatDesc& m, RowChunk c, F&& body) {
+  const uint32_t lpr = m.lpr, G = 32 / lpr, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (uint32_t base = c.r0 + warp * G; base < c.r1; base += nw * G) {
+    const uint32_t r = base + lane / lpr, lr = lane % lpr;
+    const bool ok = r < c.r1;
+    body(r, lr, ok);
+  }
 }
 
 // ---------------------------------------------------------------------------
 // Embedding row, dequantized exactly as gguf.rs:204-213 (model.rs:225).
-// Block 0 also records the token fed at this step in gen_tokens (the greedy
-// sequence when steps are chained on the device) and clears the argmax slot.
+// Block 0 records the token fed at this step in gen_tokens (the greedy sequence
+// when steps are chained on the device) and clears the argmax slot.
 __global__ void k_embed(MatDesc embd, DevState* st, float* __restrict__ x, uint32_t vocab) {
+  pdl_wait();
+  pdl_trigger();
   uint32_t tok = st->token;
   if (threadIdx.x == 0 && blockIdx.x == 0) {
     if (st->gen_tokens && st->gen_count < st->gen_cap) st->gen_tokens[st->gen_count] = tok;
     st->gen_count = st->gen_count + 1;
+    st->best = 0ull;
   }
   if (tok >= vocab) {
     if (threadIdx.x == 0 && blockIdx.x == 0) st->bad_token = 1;
@@ -53,31 +98,35 @@ __global__ void k_embed(MatDesc embd, DevState* st, float* __restrict__ x, uint3
   const __half* drow = embd.d ? embd.d + (uint64_t)tok * embd.d_stride : nullptr;
   for (uint32_t c = blockIdx.x * blockDim.x + threadIdx.x; c < embd.cols; c += gridDim.x * blockDim.x)
     x[c] = dequant_one(embd, row, drow, c);
-  if (blockIdx.x == 0 && threadIdx.x == 0) st->best = 0ull;
 }
 
 // ---------------------------------------------------------------------------
-// Q, K, V = W_{q,k,v} * rms(x); rows of the three matrices form one task space.
+// Q, K, V = W_{q,k,v} * rms(x).  The three matrices share lpr; the block's
+// row chunk runs over the concatenated rows [Q | K | V].
 __global__ void __launch_bounds__(NT) k_attn_in(MatDesc mq, MatDesc mk, MatDesc mv, const float* __restrict__ x,
-                                                const float* __restrict__ norm, uint32_t hidden, uint32_t padded,
-                                                float eps, float* __restrict__ out) {
-  extern __shared__ __align__(16) float xs[];
+                                                const float* __restrict__ norm, uint32_t hidden, float eps,
+                                                float* __restrict__ out) {
+  extern __shared__ __align__(16) uint8_t smem[];
   __shared__ float red[32];
-  stage_rms(xs, x, norm, hidden, padded, eps, red);
-  const uint32_t lpr = mq.lpr, G = 32 / lpr, lane = threadIdx.x & 31;
-  const uint32_t gq = (mq.rows + G - 1) / G, gk = (mk.rows + G - 1) / G, gv = (mv.rows + G - 1) / G;
-  const uint32_t total = gq + gk + gv, wpb = blockDim.x >> 5;
-  for (uint32_t t = blockIdx.x * wpb + (threadIdx.x >> 5); t < total; t += gridDim.x * wpb) {
-    const MatDesc* m;
-    uint32_t grp, off;
-    if (t < gq) { m = &mq; grp = t; off = 0; }
-    else if (t < gq + gk) { m = &mk; grp = t - gq; off = mq.rows; }
-    else { m = &mv; grp = t - gq - gk; off = mq.rows + mk.rows; }
-    const uint32_t r = grp * G + lane / lpr, lr = lane % lpr;
-    float p = r < m->rows ? row_partial(*m, 0, r, lr, xs) : 0.f;
-    p = group_sum(p, lpr);
-    if (lr == 0 && r < m->rows) out[off + r] = p;
-  }
+  const uint32_t nq = mq.rows, nk = mk.rows, total = nq + nk + mv.rows;
+  const uint32_t G = 32 / mq.lpr;
+  const RowChunk c = my_rows(total, G);
+  // prefetch this block's rows of each matrix
+  prefetch_rows(mq, 0, min(c.r0, nq), min(c.r1, nq));
+  prefetch_rows(mk, 0, min(max(c.r0, nq), nq + nk) - nq, min(max(c.r1, nq), nq + nk) - nq);
+  prefetch_rows(mv, 0, max(c.r0, nq + nk) - nq - nk, max(c.r1, nq + nk) - nq - nk);
+  pdl_wait();
+  pdl_trigger();
+  const float s = rms_scale(x, hidden, eps, red);
+  const bool fl = uses_float_x(mq.kind) || uses_float_x(mk.kind) || uses_float_x(mv.kind);
+  const XView xv = stage_x(smem, hidden, mq.units, fl, [&](uint32_t i) { return __fmul_rn(x[i], __fmul_rn(s, norm[i])); });
+  for_rows(mq, c, [&](uint32_t r, uint32_t lr, bool ok) {
+    const MatDesc& m = r < nq ? mq : (r < nq + nk ? mk : mv);
+    const uint32_t rr = r < nq ? r : (r < nq + nk ? r - nq : r - nq - nk);
+    float p = ok ? row_partial(m, 0, rr, lr, xv) : 0.f;
+    p = group_sum(p, mq.lpr);
+    if (lr == 0 && ok) out[r] = p;
+  });
 }
 
 // ---------------------------------------------------------------------------
@@ -100,24 +149,33 @@ QC_DEV void head_norm_rope(float* v, const float* __restrict__ w, uint32_t D, fl
   __syncwarp();
 }
 
-// Split GQA decode attention.  Block (h, s) owns KV head h and time range s of
-// [0, pos]; it handles the G query heads of that KV head.  The block whose
-// range holds `pos` appends the new K/V row.  The last block of head h merges
-// the nsplit partial softmax states.
+constexpr uint32_t kMinChunk = 64;  // positions per attention split, at least
+
+// Split GQA decode attention.  Block (h, s) owns KV head h and positions
+// [s*chunk, (s+1)*chunk) of [0, pos], chunk = max(64, ceil((pos+1)/nsplit)); it
+// handles the G query heads of that KV head.  The block whose range holds `pos`
+// appends the new K/V row.  The last active block of head h merges the partial
+// softmax states.
 __global__ void __launch_bounds__(NT) k_attention(DecodeDims dd, const float* __restrict__ qkv,
                                                   const float* __restrict__ qn_w, const float* __restrict__ kn_w,
                                                   float* __restrict__ kc, float* __restrict__ vc,
                                                   const float2* __restrict__ rope, float* __restrict__ part,
                                                   float* __restrict__ attn, DevState* st) {
+  pdl_wait();
+  pdl_trigger();
   const uint32_t h = blockIdx.x, s = blockIdx.y, D = dd.head_dim, G = dd.heads / dd.kvheads;
   const uint32_t pos = st->pos, time = pos + 1;
-  const uint32_t chunk = (time + dd.nsplit - 1) / dd.nsplit, cmax = (dd.ctx + dd.nsplit - 1) / dd.nsplit;
-  const uint32_t t0 = min(time, s * chunk), t1 = min(time, t0 + chunk);
+  uint32_t chunk = (time + dd.nsplit - 1) / dd.nsplit;
+  chunk = chunk < kMinChunk ? kMinChunk : chunk;
+  const uint32_t active = (time + chunk - 1) / chunk;
+  if (s >= active) return;
+  const uint32_t cmax = max(kMinChunk, (dd.ctx + dd.nsplit - 1) / dd.nsplit);
+  const uint32_t t0 = s * chunk, t1 = min(time, t0 + chunk);
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   extern __shared__ __align__(16) float sm[];
-  float* qs = sm;            // [G][D]
-  float* sc = qs + G * D;    // [G][cmax]
-  float* kn = sc + G * cmax; // [D] the new key row
+  float* qs = sm;             // [G][D]
+  float* sc = qs + G * D;     // [G][cmax]
+  float* kn = sc + G * cmax;  // [D] the new key row
   __shared__ float ml[2 * 64];
   __shared__ int last;
   const float2* cs = rope + (uint64_t)pos * (D / 2);
@@ -189,67 +247,73 @@ __global__ void __launch_bounds__(NT) k_attention(DecodeDims dd, const float* __
   }
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) last = atomicAdd(&st->attn_done[h], 1u) == dd.nsplit - 1;
+  if (threadIdx.x == 0) last = atomicAdd(&st->attn_done[h], 1u) == active - 1;
   __syncthreads();
   if (!last) return;
   __threadfence();
+  // merge: weights f_k = exp(m_k - M) per (split, head) computed once into shared memory
   const float* ph = part + (uint64_t)h * dd.nsplit * G * (D + 2);
+  float* fw = sc;  // [active][G]
+  for (uint32_t g = warp; g < G; g += nw) {
+    float M = -INFINITY;
+    for (uint32_t k = lane; k < active; k += 32) M = fmaxf(M, __ldcg(ph + (k * G + g) * (D + 2) + D));
+    M = warp_max(M);
+    float L = 0.f;
+    for (uint32_t k = lane; k < active; k += 32) {
+      const float f = expf(__ldcg(ph + (k * G + g) * (D + 2) + D) - M);
+      fw[k * G + g] = f;
+      L = fmaf(__ldcg(ph + (k * G + g) * (D + 2) + D + 1), f, L);
+    }
+    L = warp_sum(L);
+    if (lane == 0) ml[g] = 1.f / L;
+  }
+  __syncthreads();
   for (uint32_t idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
     const uint32_t g = idx / D, d = idx % D;
-    float M = -INFINITY;
-    for (uint32_t k = 0; k < dd.nsplit; k++) M = fmaxf(M, __ldcg(ph + (k * G + g) * (D + 2) + D));
-    float L = 0.f, o = 0.f;
-    for (uint32_t k = 0; k < dd.nsplit; k++) {
-      const float* q = ph + (k * G + g) * (D + 2);
-      const float l = __ldcg(q + D + 1);
-      if (l == 0.f) continue;  // empty split
-      const float f = expf(__ldcg(q + D) - M);
-      L = fmaf(l, f, L);
-      o = fmaf(__ldcg(q + d), f, o);
-    }
-    attn[(h * G + g) * D + d] = o / L;
+    float o = 0.f;
+    for (uint32_t k = 0; k < active; k++) o = fmaf(__ldcg(ph + (k * G + g) * (D + 2) + d), fw[k * G + g], o);
+    attn[(h * G + g) * D + d] = o * ml[g];
   }
   if (threadIdx.x == 0) st->attn_done[h] = 0;
 }
 
 // ---------------------------------------------------------------------------
 // x += W_o * attn (model.rs:245-248).
-__global__ void __launch_bounds__(NT) k_oproj(MatDesc mo, const float* __restrict__ a, uint32_t padded,
-                                              float* __restrict__ x) {
-  extern __shared__ __align__(16) float xs[];
-  stage_copy(xs, a, mo.cols, padded);
-  const uint32_t lpr = mo.lpr, G = 32 / lpr, lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
-  const uint32_t total = (mo.rows + G - 1) / G;
-  for (uint32_t t = blockIdx.x * wpb + (threadIdx.x >> 5); t < total; t += gridDim.x * wpb) {
-    const uint32_t r = t * G + lane / lpr, lr = lane % lpr;
-    float p = r < mo.rows ? row_partial(mo, 0, r, lr, xs) : 0.f;
-    p = group_sum(p, lpr);
-    if (lr == 0 && r < mo.rows) x[r] = __fadd_rn(x[r], p);
-  }
+__global__ void __launch_bounds__(NT) k_oproj(MatDesc mo, const float* __restrict__ a, float* __restrict__ x) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const RowChunk c = my_rows(mo.rows, 32 / mo.lpr);
+  prefetch_rows(mo, 0, c.r0, c.r1);
+  pdl_wait();
+  pdl_trigger();
+  const XView xv = stage_x(smem, mo.cols, mo.units, uses_float_x(mo.kind), [&](uint32_t i) { return a[i]; });
+  for_rows(mo, c, [&](uint32_t r, uint32_t lr, bool ok) {
+    float p = ok ? row_partial(mo, 0, r, lr, xv) : 0.f;
+    p = group_sum(p, mo.lpr);
+    if (lr == 0 && ok) x[r] = __fadd_rn(x[r], p);
+  });
 }
 
 // ---------------------------------------------------------------------------
 // Router logits, then (last block) top-k with ties to the lower index and a
 // softmax over the kept logits (ops.rs:45-56, 29-44).
 __global__ void __launch_bounds__(NT) k_router(MatDesc mr, const float* __restrict__ x, const float* __restrict__ norm,
-                                               uint32_t hidden, uint32_t padded, float eps, uint32_t top,
-                                               float* __restrict__ xn, float* __restrict__ rlogit,
+                                               uint32_t hidden, float eps, uint32_t top, float* __restrict__ rlogit,
                                                uint32_t* __restrict__ sel, float* __restrict__ selw, DevState* st) {
-  extern __shared__ __align__(16) float xs[];
+  extern __shared__ __align__(16) uint8_t smem[];
   __shared__ float red[32];
   __shared__ int last;
-  __shared__ uint8_t taken[1024];
-  stage_rms(xs, x, norm, hidden, padded, eps, red);
-  if (blockIdx.x == 0)
-    for (uint32_t i = threadIdx.x; i < hidden; i += blockDim.x) xn[i] = xs[i];
-  const uint32_t lpr = mr.lpr, G = 32 / lpr, lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
-  const uint32_t total = (mr.rows + G - 1) / G;
-  for (uint32_t t = blockIdx.x * wpb + (threadIdx.x >> 5); t < total; t += gridDim.x * wpb) {
-    const uint32_t r = t * G + lane / lpr, lr = lane % lpr;
-    float p = r < mr.rows ? row_partial(mr, 0, r, lr, xs) : 0.f;
-    p = group_sum(p, lpr);
-    if (lr == 0 && r < mr.rows) rlogit[r] = p;
-  }
+  const RowChunk c = my_rows(mr.rows, 32 / mr.lpr);
+  prefetch_rows(mr, 0, c.r0, c.r1);
+  pdl_wait();
+  pdl_trigger();
+  const float s = rms_scale(x, hidden, eps, red);
+  const XView xv = stage_x(smem, hidden, mr.units, uses_float_x(mr.kind),
+                           [&](uint32_t i) { return __fmul_rn(x[i], __fmul_rn(s, norm[i])); });
+  for_rows(mr, c, [&](uint32_t r, uint32_t lr, bool ok) {
+    float p = ok ? row_partial(mr, 0, r, lr, xv) : 0.f;
+    p = group_sum(p, mr.lpr);
+    if (lr == 0 && ok) rlogit[r] = p;
+  });
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) last = atomicAdd(&st->router_done, 1u) == gridDim.x - 1;
@@ -257,31 +321,31 @@ __global__ void __launch_bounds__(NT) k_router(MatDesc mr, const float* __restri
   if (!last) return;
   __threadfence();
   const uint32_t E = mr.rows;
-  for (uint32_t i = threadIdx.x; i < E; i += blockDim.x) taken[i] = 0;
+  unsigned long long* key = reinterpret_cast<unsigned long long*>(smem);  // [E] (reuses the staging space)
+  for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) {
+    const float v = __ldcg(rlogit + e);
+    if (!isfinite(v)) atomicOr(&st->nonfinite, 1u);
+    key[e] = ((unsigned long long)total_key_u(v) << 32) | (0xffffffffu - e);
+  }
   __syncthreads();
   if (threadIdx.x < 32) {
-    __shared__ float kept[64];
+    const uint32_t lane = threadIdx.x;
+    float kept[64];
+    uint32_t ids[64];
     for (uint32_t k = 0; k < top; k++) {
       unsigned long long best = 0ull;
-      for (uint32_t e = lane; e < E; e += 32) {
-        if (taken[e]) continue;
-        const float v = __ldcg(rlogit + e);
-        if (k == 0 && !isfinite(v)) atomicOr(&st->nonfinite, 1u);
-        const unsigned long long key = ((unsigned long long)total_key_u(v) << 32) | (0xffffffffu - e);
-        best = key > best ? key : best;
-      }
+      for (uint32_t e = lane; e < E; e += 32) best = key[e] > best ? key[e] : best;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
         best = other > best ? other : best;
       }
       const uint32_t e = 0xffffffffu - (uint32_t)(best & 0xffffffffu);
-      if (lane == 0) {
-        taken[e] = 1;
-        sel[k] = e;
-        kept[k] = __ldcg(rlogit + e);
-      }
       __syncwarp();
+      if (lane == 0) key[e] = 0ull;
+      __syncwarp();
+      ids[k] = e;
+      kept[k] = __ldcg(rlogit + e);
     }
     if (lane == 0) {  // ops.rs:29-44, sequential in selection order
       float mx = -INFINITY;
@@ -291,28 +355,49 @@ __global__ void __launch_bounds__(NT) k_router(MatDesc mr, const float* __restri
         kept[k] = expf(kept[k] - mx);
         sum = __fadd_rn(sum, kept[k]);
       }
-      for (uint32_t k = 0; k < top; k++) selw[k] = kept[k] / sum;
+      for (uint32_t k = 0; k < top; k++) {
+        sel[k] = ids[k];
+        selw[k] = kept[k] / sum;
+      }
       st->router_done = 0;
     }
   }
 }
 
 // ---------------------------------------------------------------------------
-// h[s][r] = silu(gate_e[r] . xn) * (up_e[r] . xn) for the selected experts (model.rs:259-274).
-__global__ void __launch_bounds__(NT) k_gateup(MatDesc mg, MatDesc mu, const float* __restrict__ xn, uint32_t hidden,
-                                               uint32_t padded, uint32_t top, const uint32_t* __restrict__ sel,
+// h[s][r] = silu(gate_e[r] . xn) * (up_e[r] . xn) for the selected experts
+// (model.rs:259-274); xn = rms(x, ffn_norm) is recomputed from x.  Block b owns
+// a contiguous chunk of the (slot, row group) task space.
+__global__ void __launch_bounds__(NT) k_gateup(MatDesc mg, MatDesc mu, const float* __restrict__ x,
+                                               const float* __restrict__ norm, uint32_t hidden, float eps,
+                                               uint32_t top, const uint32_t* __restrict__ sel,
                                                float* __restrict__ hout) {
-  extern __shared__ __align__(16) float xs[];
-  stage_copy(xs, xn, hidden, padded);
-  const uint32_t lpr = mg.lpr, G = 32 / lpr, lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
-  const uint32_t I = mg.rows, groups = (I + G - 1) / G, total = groups * top;
-  for (uint32_t t = blockIdx.x * wpb + (threadIdx.x >> 5); t < total; t += gridDim.x * wpb) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ float red[32];
+  const uint32_t I = mg.rows, G = 32 / mg.lpr;
+  const uint32_t groups = (I + G - 1) / G;
+  const uint32_t tasks = top * groups, per = (tasks + gridDim.x - 1) / gridDim.x;
+  const uint32_t t0 = blockIdx.x * per, t1 = min(tasks, t0 + per);
+  pdl_wait();
+  pdl_trigger();
+  for (uint32_t t = t0; t < t1;) {  // prefetch this block's expert rows (sel is ready after the wait)
+    const uint32_t s = t / groups, g0 = t % groups, g1 = min(groups, g0 + (t1 - t));
+    const uint32_t e = sel[s];
+    prefetch_rows(mg, e, g0 * G, min(I, g1 * G));
+    prefetch_rows(mu, e, g0 * G, min(I, g1 * G));
+    t += g1 - g0;
+  }
+  const float sc = rms_scale(x, hidden, eps, red);
+  const bool fl = uses_float_x(mg.kind) || uses_float_x(mu.kind);
+  const XView xv = stage_x(smem, hidden, mg.units, fl, [&](uint32_t i) { return __fmul_rn(x[i], __fmul_rn(sc, norm[i])); });
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5, lpr = mg.lpr;
+  for (uint32_t t = t0 + warp; t < t1; t += nw) {
     const uint32_t s = t / groups, grp = t % groups, e = sel[s];
     const uint32_t r = grp * G + lane / lpr, lr = lane % lpr;
     float g = 0.f, u = 0.f;
     if (r < I) {
-      g = row_partial(mg, e, r, lr, xs);
-      u = row_partial(mu, e, r, lr, xs);
+      g = row_partial(mg, e, r, lr, xv);
+      u = row_partial(mu, e, r, lr, xv);
     }
     g = group_sum(g, lpr);
     u = group_sum(u, lpr);
@@ -322,31 +407,43 @@ __global__ void __launch_bounds__(NT) k_gateup(MatDesc mg, MatDesc mu, const flo
 
 // ---------------------------------------------------------------------------
 // x[r] += sum_s w_s * (down_{e_s}[r] . h_s), summed in selection order (model.rs:275-287).
-// Block b owns rows [b*G, b*G+G); warp w computes slots w, w+8, ...
-__global__ void __launch_bounds__(NT) k_down(MatDesc md, const float* __restrict__ hin, uint32_t padded, uint32_t top,
+// Block b owns a contiguous chunk of row groups; warp w computes slots w, w+8, ...
+__global__ void __launch_bounds__(NT) k_down(MatDesc md, const float* __restrict__ hin, uint32_t top,
                                              const uint32_t* __restrict__ sel, const float* __restrict__ selw,
                                              float* __restrict__ x) {
-  extern __shared__ __align__(16) float hs[];  // [top][padded] then [top][G] partials
+  extern __shared__ __align__(16) uint8_t smem[];
   const uint32_t I = md.cols, lpr = md.lpr, G = 32 / lpr, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t nw = blockDim.x >> 5;
-  for (uint32_t i = threadIdx.x; i < top * padded; i += blockDim.x) {
-    const uint32_t s = i / padded, c = i % padded;
-    hs[i] = c < I ? hin[s * I + c] : 0.f;
+  const RowChunk c = my_rows(md.rows, G);
+  // sel was written by the router two launches back: complete before the previous kernel started its work
+  for (uint32_t s = 0; s < top; s++) prefetch_rows(md, __ldcg(sel + s), c.r0, c.r1);
+  pdl_wait();
+  pdl_trigger();
+  const bool fl = uses_float_x(md.kind);
+  const uint32_t xb = xview_bytes(md.units, fl);
+  XView xs0;
+  for (uint32_t s = 0; s < top; s++) {  // one XView per slot; all threads take part in each
+    const XView v = stage_x(smem + s * xb, I, md.units, fl, [&](uint32_t i) { return hin[s * I + i]; });
+    if (s == 0) xs0 = v;
   }
-  __syncthreads();
-  float* pp = hs + top * padded;
-  const uint32_t groups = (md.rows + G - 1) / G;
-  for (uint32_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
-    const uint32_t r = grp * G + lane / lpr, lr = lane % lpr;
+  float* pp = reinterpret_cast<float*>(smem + top * xb);  // [top][G] partials
+  for (uint32_t grp = c.r0; grp < c.r1; grp += G) {
+    const uint32_t r = grp + lane / lpr, lr = lane % lpr;
     for (uint32_t s = warp; s < top; s += nw) {
-      float p = r < md.rows ? row_partial(md, sel[s], r, lr, hs + s * padded) : 0.f;
+      const uint64_t off = (uint64_t)s * xb;  // the slot's XView is xs0 shifted by s*xb bytes
+      XView xv;
+      xv.dig = xs0.dig + off;
+      xv.sx = reinterpret_cast<const int*>(reinterpret_cast<const uint8_t*>(xs0.sx) + off);
+      xv.sb = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(xs0.sb) + off);
+      xv.xf = xs0.xf ? reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(xs0.xf) + off) : nullptr;
+      float p = r < c.r1 ? row_partial(md, sel[s], r, lr, xv) : 0.f;
       p = group_sum(p, lpr);
       if (lr == 0) pp[s * G + lane / lpr] = p;
     }
     __syncthreads();
     if (threadIdx.x < G) {
-      const uint32_t rr = grp * G + threadIdx.x;
-      if (rr < md.rows) {
+      const uint32_t rr = grp + threadIdx.x;
+      if (rr < c.r1) {
         float acc = 0.f;
         for (uint32_t s = 0; s < top; s++) acc = __fadd_rn(acc, __fmul_rn(selw[s], pp[s * G + threadIdx.x]));
         x[rr] = __fadd_rn(x[rr], acc);
@@ -360,27 +457,30 @@ __global__ void __launch_bounds__(NT) k_down(MatDesc md, const float* __restrict
 // logits = W_out * rms(x, output_norm); finiteness flag; greedy argmax (ties to
 // the lower index); the last block advances the step state.
 __global__ void __launch_bounds__(NT) k_output(MatDesc mo, const float* __restrict__ x, const float* __restrict__ norm,
-                                               uint32_t hidden, uint32_t padded, float eps,
-                                               float* __restrict__ logits, DevState* st) {
-  extern __shared__ __align__(16) float xs[];
+                                               uint32_t hidden, float eps, float* __restrict__ logits, DevState* st) {
+  extern __shared__ __align__(16) uint8_t smem[];
   __shared__ float red[32];
   __shared__ int last;
-  stage_rms(xs, x, norm, hidden, padded, eps, red);
-  const uint32_t lpr = mo.lpr, G = 32 / lpr, lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
-  const uint32_t total = (mo.rows + G - 1) / G;
+  const RowChunk c = my_rows(mo.rows, 32 / mo.lpr);
+  prefetch_rows(mo, 0, c.r0, c.r1);
+  pdl_wait();
+  pdl_trigger();
+  const float s = rms_scale(x, hidden, eps, red);
+  const XView xv = stage_x(smem, hidden, mo.units, uses_float_x(mo.kind),
+                           [&](uint32_t i) { return __fmul_rn(x[i], __fmul_rn(s, norm[i])); });
   unsigned long long best = 0ull;
   bool bad = false;
-  for (uint32_t t = blockIdx.x * wpb + (threadIdx.x >> 5); t < total; t += gridDim.x * wpb) {
-    const uint32_t r = t * G + lane / lpr, lr = lane % lpr;
-    float p = r < mo.rows ? row_partial(mo, 0, r, lr, xs) : 0.f;
-    p = group_sum(p, lpr);
-    if (lr == 0 && r < mo.rows) {
+  for_rows(mo, c, [&](uint32_t r, uint32_t lr, bool ok) {
+    float p = ok ? row_partial(mo, 0, r, lr, xv) : 0.f;
+    p = group_sum(p, mo.lpr);
+    if (lr == 0 && ok) {
       logits[r] = p;
       bad |= !isfinite(p);
       const unsigned long long key = ((unsigned long long)total_key_u(p) << 32) | (0xffffffffu - r);
       best = key > best ? key : best;
     }
-  }
+  });
+  const uint32_t lane = threadIdx.x & 31;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
@@ -402,11 +502,27 @@ __global__ void __launch_bounds__(NT) k_output(MatDesc mo, const float* __restri
 }
 
 // ---------------------------------------------------------------------------
-static uint32_t padded_of(const MatDesc& m) { return m.units * unit_elems(m.kind); }
+// Launch with programmatic stream serialization (PDL); inside a captured graph
+// this becomes a programmatic dependency edge.
+template <typename... KArgs, typename... Args>
+static void launch(void (*k)(KArgs...), dim3 grid, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
 
-static uint32_t grid_for(uint32_t tasks_warps, int sms) {
-  const uint32_t need = (tasks_warps + 7) / 8;
-  const uint32_t cap = (uint32_t)sms * 4;
+static uint32_t grid_rows(uint32_t rows, uint32_t lpr, int sms, uint32_t per_sm) {
+  const uint32_t groups = (rows + 32 / lpr - 1) / (32 / lpr);
+  const uint32_t need = (groups + 7) / 8;  // at least one row group per warp
+  const uint32_t cap = (uint32_t)sms * per_sm;
   return need < 1 ? 1 : (need < cap ? need : cap);
 }
 
@@ -417,64 +533,57 @@ void launch_step(const StepArgs& a, cudaStream_t s, StepHook hook, void* ctx) {
     if (hook) hook(ctx, kind, s);
   };
   H(K_EMBED);
-  k_embed<<<(d.hidden + NT - 1) / NT, NT, 0, s>>>(a.embd, a.st, c.x, d.vocab);
+  launch(k_embed, dim3((d.hidden + NT - 1) / NT), 0, s, a.embd, a.st, c.x, d.vocab);
   const uint32_t G = d.heads / d.kvheads;
-  const uint32_t cmax = (d.ctx + d.nsplit - 1) / d.nsplit;
+  const uint32_t cmax = max(kMinChunk, (d.ctx + d.nsplit - 1) / d.nsplit);
   const size_t attn_smem = (size_t)(G * d.head_dim + G * cmax + d.head_dim) * sizeof(float);
-  float* qkv = c.qkv;
   for (uint32_t l = 0; l < a.n_layers; l++) {
     const LayerDev& L = a.layers[l];
     {
-      uint32_t pad = padded_of(L.q);
-      pad = pad > padded_of(L.k) ? pad : padded_of(L.k);
-      pad = pad > padded_of(L.v) ? pad : padded_of(L.v);
-      const uint32_t Gq = 32 / L.q.lpr;
-      const uint32_t warps = (L.q.rows + Gq - 1) / Gq + (L.k.rows + Gq - 1) / Gq + (L.v.rows + Gq - 1) / Gq;
+      const bool fl = uses_float_x(L.q.kind) || uses_float_x(L.k.kind) || uses_float_x(L.v.kind);
+      const size_t smem = xview_bytes(L.q.units, fl);
       H(K_ATTN_IN);
-      k_attn_in<<<grid_for(warps, a.sms), NT, pad * sizeof(float), s>>>(L.q, L.k, L.v, c.x, L.attn_norm, d.hidden,
-                                                                         pad, d.eps, qkv);
+      launch(k_attn_in, dim3(grid_rows(L.q.rows + L.k.rows + L.v.rows, L.q.lpr, a.sms, 1)), smem, s, L.q, L.k, L.v,
+             c.x, L.attn_norm, d.hidden, d.eps, c.qkv);
     }
     H(K_ATTENTION);
-    k_attention<<<dim3(d.kvheads, d.nsplit), NT, attn_smem, s>>>(d, qkv, L.q_norm, L.k_norm, L.kc, L.vc, c.rope,
-                                                                 c.part, c.attn, a.st);
+    launch(k_attention, dim3(d.kvheads, d.nsplit), attn_smem, s, d, c.qkv, L.q_norm, L.k_norm, L.kc, L.vc, c.rope,
+           c.part, c.attn, a.st);
+    H(K_OPROJ);
+    launch(k_oproj, dim3(grid_rows(L.o.rows, L.o.lpr, a.sms, 1)), xview_bytes(L.o.units, uses_float_x(L.o.kind)), s,
+           L.o, c.attn, c.x);
     {
-      const uint32_t pad = padded_of(L.o), Go = 32 / L.o.lpr;
-      H(K_OPROJ);
-      k_oproj<<<grid_for((L.o.rows + Go - 1) / Go, a.sms), NT, pad * sizeof(float), s>>>(L.o, c.attn, pad, c.x);
-    }
-    {
-      const uint32_t pad = padded_of(L.router), Gr = 32 / L.router.lpr;
-      const uint32_t warps = (L.router.rows + Gr - 1) / Gr;
-      uint32_t grid = (warps + 7) / 8;
-      if (grid > 32) grid = 32;
+      uint32_t grid = grid_rows(L.router.rows, L.router.lpr, a.sms, 1);
+      grid = grid > 32 ? 32 : grid;
+      size_t smem = xview_bytes(L.router.units, uses_float_x(L.router.kind));
+      const size_t keys = (size_t)L.router.rows * 8;
+      smem = smem > keys ? smem : keys;
       H(K_ROUTER);
-      k_router<<<grid, NT, pad * sizeof(float), s>>>(L.router, c.x, L.ffn_norm, d.hidden, pad, d.eps, d.top, c.xn,
-                                                      c.rlogit, c.sel, c.selw, a.st);
+      launch(k_router, dim3(grid), smem, s, L.router, c.x, L.ffn_norm, d.hidden, d.eps, d.top, c.rlogit, c.sel, c.selw,
+             a.st);
     }
     {
-      uint32_t pad = padded_of(L.gate);
-      pad = pad > padded_of(L.up) ? pad : padded_of(L.up);
+      const bool fl = uses_float_x(L.gate.kind) || uses_float_x(L.up.kind);
       const uint32_t Gg = 32 / L.gate.lpr;
-      const uint32_t warps = (L.gate.rows + Gg - 1) / Gg * d.top;
+      const uint32_t tasks = (L.gate.rows + Gg - 1) / Gg * d.top;
+      uint32_t grid = (tasks + 7) / 8;
+      grid = grid > (uint32_t)a.sms * 2 ? (uint32_t)a.sms * 2 : grid;
       H(K_GATEUP);
-      k_gateup<<<grid_for(warps, a.sms), NT, pad * sizeof(float), s>>>(L.gate, L.up, c.xn, d.hidden, pad, d.top,
-                                                                        c.sel, c.h);
+      launch(k_gateup, dim3(grid), xview_bytes(L.gate.units, fl), s, L.gate, L.up, c.x, L.ffn_norm, d.hidden, d.eps,
+             d.top, c.sel, c.h);
     }
     {
-      const uint32_t pad = padded_of(L.down), Gd = 32 / L.down.lpr;
+      const uint32_t Gd = 32 / L.down.lpr;
+      const size_t smem = (size_t)d.top * xview_bytes(L.down.units, uses_float_x(L.down.kind)) + (size_t)d.top * Gd * 4;
       const uint32_t groups = (L.down.rows + Gd - 1) / Gd;
-      const size_t smem = ((size_t)d.top * pad + (size_t)d.top * Gd) * sizeof(float);
+      const uint32_t grid = groups < (uint32_t)a.sms * 2 ? groups : (uint32_t)a.sms * 2;
       H(K_DOWN);
-      k_down<<<groups, NT, smem, s>>>(L.down, c.h, pad, d.top, c.sel, c.selw, c.x);
+      launch(k_down, dim3(grid), smem, s, L.down, c.h, d.top, c.sel, c.selw, c.x);
     }
   }
-  {
-    const uint32_t pad = padded_of(a.out), Go = 32 / a.out.lpr;
-    const uint32_t warps = (a.out.rows + Go - 1) / Go;
-    H(K_OUTPUT);
-    k_output<<<grid_for(warps, a.sms), NT, pad * sizeof(float), s>>>(a.out, c.x, a.out_norm, d.hidden, pad, d.eps,
-                                                                      c.logits, a.st);
-  }
+  H(K_OUTPUT);
+  launch(k_output, dim3(grid_rows(a.out.rows, a.out.lpr, a.sms, 4)), xview_bytes(a.out.units, uses_float_x(a.out.kind)),
+         s, a.out, c.x, a.out_norm, d.hidden, d.eps, c.logits, a.st);
   H(K_COUNT);
 }
 

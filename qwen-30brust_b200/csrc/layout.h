@@ -38,16 +38,19 @@ struct DevLayout {
   uint64_t d_bytes(uint64_t rows) const { return rows * d_stride * 2; }
 };
 
+// Every row is processed in units of 64 elements: units = ceil(cols / 64).
 inline DevLayout dev_layout(uint32_t kind, uint64_t cols) {
   DevLayout l;
+  const uint64_t units = (cols + 63) / 64;
+  l.units = (uint32_t)units;
   switch (kind) {
-    case 12: l.row_stride = cols / 256 * 144; l.units = (uint32_t)(cols / 256 * 4); break;
-    case 13: l.row_stride = cols / 256 * 176; l.units = (uint32_t)(cols / 256 * 4); break;
-    case 14: l.row_stride = cols / 256 * 208; l.d_stride = cols / 256; l.units = (uint32_t)(cols / 256 * 4); break;
-    case 8: l.row_stride = cols / 32 * 32; l.d_stride = cols / 32; l.units = (uint32_t)(cols / 32); break;
-    case 2: l.row_stride = cols / 32 * 16; l.d_stride = cols / 32; l.units = (uint32_t)(cols / 32); break;
-    case 1: l.units = (uint32_t)((cols + 31) / 32); l.row_stride = (uint64_t)l.units * 64; break;
-    default: l.units = (uint32_t)((cols + 15) / 16); l.row_stride = (uint64_t)l.units * 64; break;
+    case 12: l.row_stride = cols / 256 * 144; break;
+    case 13: l.row_stride = cols / 256 * 176; break;
+    case 14: l.row_stride = cols / 256 * 208; l.d_stride = cols / 256; break;
+    case 8: l.row_stride = units * 64; l.d_stride = units * 2; break;  // two 32-blocks per unit
+    case 2: l.row_stride = units * 32; l.d_stride = units * 2; break;
+    case 1: l.row_stride = units * 128; break;
+    default: l.row_stride = units * 256; break;
   }
   uint32_t lpr = 1;
   while (lpr < 32 && l.units % (lpr * 2) == 0) lpr *= 2;
@@ -56,12 +59,5 @@ inline DevLayout dev_layout(uint32_t kind, uint64_t cols) {
   return l;
 }
 
-inline uint32_t unit_elems_host(uint32_t kind) {
-  switch (kind) {
-    case 12: case 13: case 14: return 64;
-    case 8: case 2: case 1: return 32;
-    default: return 16;
-  }
-}
 
 }  // namespace qc

@@ -17,17 +17,18 @@ namespace qc {
 __global__ void k_repack(const uint8_t* __restrict__ src, uint64_t n_rows, uint64_t raw_row, uint32_t kind,
                          uint64_t cols, uint8_t* __restrict__ dst, uint64_t row_stride, __half* __restrict__ dplane,
                          uint64_t d_stride) {
-  uint64_t per_row;
+  uint64_t per_row, valid;  // output blocks (or 16-byte chunks) per row, and how many come from the source
   switch (kind) {
-    case Q4_K: case Q5_K: case Q6_K: per_row = cols / 256; break;
-    case Q8_0: case Q4_0: per_row = cols / 32; break;
-    default: per_row = row_stride / 16; break;
+    case Q4_K: case Q5_K: case Q6_K: per_row = valid = cols / 256; break;
+    case Q8_0: case Q4_0: per_row = d_stride; valid = cols / 32; break;
+    default: per_row = row_stride / 16; valid = per_row; break;
   }
   const uint64_t total = n_rows * per_row;
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
     const uint64_t r = i / per_row, k = i % per_row;
     const uint8_t* s = src + r * raw_row;
     uint8_t* o = dst + r * row_stride;
+    const bool pad = k >= valid;
     switch (kind) {
       case Q4_K:
         for (int j = 0; j < 144; j++) o[k * 144 + j] = s[k * 144 + j];
@@ -40,18 +41,20 @@ __global__ void k_repack(const uint8_t* __restrict__ src, uint64_t n_rows, uint6
         dplane[r * d_stride + k] = __ushort_as_half((unsigned short)(s[k * 210 + 208] | (s[k * 210 + 209] << 8)));
         break;
       case Q8_0:
-        for (int j = 0; j < 32; j++) o[k * 32 + j] = s[k * 34 + 2 + j];
-        dplane[r * d_stride + k] = __ushort_as_half((unsigned short)(s[k * 34] | (s[k * 34 + 1] << 8)));
+        for (int j = 0; j < 32; j++) o[k * 32 + j] = pad ? 0 : s[k * 34 + 2 + j];
+        dplane[r * d_stride + k] =
+            __ushort_as_half(pad ? (unsigned short)0 : (unsigned short)(s[k * 34] | (s[k * 34 + 1] << 8)));
         break;
       case Q4_0:
-        for (int j = 0; j < 16; j++) o[k * 16 + j] = s[k * 18 + 2 + j];
-        dplane[r * d_stride + k] = __ushort_as_half((unsigned short)(s[k * 18] | (s[k * 18 + 1] << 8)));
+        for (int j = 0; j < 16; j++) o[k * 16 + j] = pad ? 0 : s[k * 18 + 2 + j];
+        dplane[r * d_stride + k] =
+            __ushort_as_half(pad ? (unsigned short)0 : (unsigned short)(s[k * 18] | (s[k * 18 + 1] << 8)));
         break;
       default: {  // F16 / F32: 16-byte chunk k of the padded row
-        const uint64_t esz = kind == F16 ? 2 : 4, valid = cols * esz;
+        const uint64_t esz = kind == F16 ? 2 : 4, nbytes = cols * esz;
         for (int j = 0; j < 16; j++) {
           const uint64_t b = k * 16 + j;
-          o[b] = b < valid ? s[b] : 0;
+          o[b] = b < nbytes ? s[b] : 0;
         }
       }
     }
@@ -69,24 +72,18 @@ __global__ void k_dequant(MatDesc m, uint32_t e, float* __restrict__ out) {
   }
 }
 
-// Stage x (cols floats) into shared memory, zero padded to `padded` floats.
-QC_DEV void stage_x(float* xs, const float* __restrict__ x, uint32_t cols, uint32_t padded) {
-  for (uint32_t i = threadIdx.x; i < padded; i += blockDim.x) xs[i] = i < cols ? x[i] : 0.f;
-}
-
 // y = W_e x.  Each warp takes 32/lpr rows at a time; lpr lanes share a row.
 template <uint32_t KIND>
 __global__ void __launch_bounds__(256) k_matvec(MatDesc m, uint32_t e, const float* __restrict__ x,
                                                 float* __restrict__ y) {
-  extern __shared__ __align__(16) float xs[];
-  stage_x(xs, x, m.cols, m.units * unit_elems(m.kind));
-  __syncthreads();
+  extern __shared__ __align__(16) uint8_t smem[];
+  const XView xv = stage_x(smem, m.cols, m.units, uses_float_x(KIND), [&](uint32_t i) { return x[i]; });
   const uint32_t lane = threadIdx.x & 31, lpr = m.lpr, G = 32 / lpr;
   const uint32_t wpb = blockDim.x >> 5;
   const uint32_t gw = blockIdx.x * wpb + (threadIdx.x >> 5), nw = gridDim.x * wpb;
   for (uint32_t base = gw * G; base < m.rows; base += nw * G) {
     const uint32_t r = base + lane / lpr, lr = lane % lpr;
-    float p = r < m.rows ? row_partial_k<KIND>(m, e, r, lr, xs) : 0.f;
+    float p = r < m.rows ? row_partial_k<KIND>(m, e, r, lr, xv) : 0.f;
     p = group_sum(p, lpr);
     if (lr == 0 && r < m.rows) y[r] = p;
   }
@@ -111,7 +108,7 @@ uint32_t matvec_grid(const MatDesc& m, int sms) {
 
 void launch_matvec(const MatDesc& m, uint32_t e, const float* x, float* y, int sms, cudaStream_t s) {
   const uint32_t grid = matvec_grid(m, sms);
-  const size_t smem = (size_t)m.units * unit_elems(m.kind) * sizeof(float);
+  const size_t smem = matvec_smem(m);
   switch (m.kind) {
     case Q4_K: k_matvec<Q4_K><<<grid, 256, smem, s>>>(m, e, x, y); break;
     case Q5_K: k_matvec<Q5_K><<<grid, 256, smem, s>>>(m, e, x, y); break;
@@ -123,7 +120,7 @@ void launch_matvec(const MatDesc& m, uint32_t e, const float* x, float* y, int s
   }
 }
 
-size_t matvec_smem(const MatDesc& m) { return (size_t)m.units * unit_elems(m.kind) * sizeof(float); }
+size_t matvec_smem(const MatDesc& m) { return xview_bytes(m.units, uses_float_x(m.kind)); }
 
 cudaError_t matvec_prepare(int max_smem) {
   cudaError_t err = cudaSuccess;
