@@ -12,31 +12,55 @@ namespace qc {
 // GGML type ids (reference quant.rs:5-11).
 enum Kind : uint32_t { F32 = 0, F16 = 1, Q4_0 = 2, Q8_0 = 8, Q4_K = 12, Q5_K = 13, Q6_K = 14 };
 
-// Device layout of one matrix (or of expert 0 of an expert stack; expert e
-// starts e*expert_stride bytes / e*d_expert_stride halves further).  A row is
-// processed in "units" of 64 consecutive elements.
+// Device layout of one matrix (or of an expert stack).  A row is processed in
+// "units" of 64 consecutive elements.  Rows are stored in groups of 8,
+//   group g = [rows 8g..8g+7: main_bytes each][rows 8g..8g+7: d_bytes each],
+// so any run of whole groups is one contiguous, 16-byte-aligned span.
 //
-// Q4_K, Q5_K   raw GGUF super-blocks (144 / 176 bytes, already 16-aligned)
-// Q6_K         per block: ql[128] qh[64] scales[16] (208 bytes); d in a plane
-// Q8_0         per block: qs[32]; d in a plane; rows padded to an even block count
-// Q4_0         per block: qs[16]; d in a plane; rows padded to an even block count
+// main plane per row:
+// Q4_K, Q5_K   raw GGUF super-blocks (144 / 176 bytes); no d values
+// Q6_K         per block: ql[128] qh[64] scales[16] (208 bytes); d values (f16) after the group
+// Q8_0         per block: qs[32]; d values after the group; rows padded to an even block count
+// Q4_0         per block: qs[16]; d values after the group; rows padded to an even block count
 // F16, F32     raw rows padded with zeros to a multiple of 64 elements
 struct MatDesc {
   const uint8_t* w;
-  const __half* d;
   uint32_t kind, rows, cols;
   uint32_t units;  // ceil(cols / 64)
   uint32_t lpr;    // lanes cooperating on one row (power of two, divides units, <= 32)
   uint32_t upl;    // units per lane = units / lpr
-  uint64_t row_stride;       // bytes between rows of the main plane
-  uint64_t d_stride;         // halves between rows of the d plane
-  uint64_t expert_stride;    // bytes between experts of the main plane
-  uint64_t d_expert_stride;  // halves between experts of the d plane
+  uint32_t main_bytes, d_bytes, group_bytes;
+  uint64_t expert_stride;  // bytes between experts (ceil(rows/8) groups)
 };
+
+// Row r of expert e, relative to a base holding groups from `g_base` on.
+__host__ __device__ inline const uint8_t* row_ptr(const MatDesc& m, const uint8_t* base, uint32_t r) {
+  return base + (uint64_t)(r >> 3) * m.group_bytes + (r & 7) * m.main_bytes;
+}
+__host__ __device__ inline const __half* drow_ptr(const MatDesc& m, const uint8_t* base, uint32_t r) {
+  return reinterpret_cast<const __half*>(base + (uint64_t)(r >> 3) * m.group_bytes + 8 * m.main_bytes +
+                                         (r & 7) * m.d_bytes);
+}
+__host__ __device__ inline const uint8_t* expert_base(const MatDesc& m, uint32_t e) {
+  return m.w + (uint64_t)e * m.expert_stride;
+}
 
 __host__ __device__ inline bool uses_float_x(uint32_t kind) { return kind == F16 || kind == F32; }
 
 QC_DEV uint4 ldg16(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+// 16-byte load from global (S = false) or shared memory (S = true).
+template <bool S>
+QC_DEV uint4 ld16(const void* p) {
+  if constexpr (S) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"((uint32_t)__cvta_generic_to_shared(p)));
+    return v;
+  } else {
+    return ldg16(p);
+  }
+}
 QC_DEV float h2f(__half h) { return __half2float(h); }
 QC_DEV float h2f_bits(uint32_t bits16) { return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xffff))); }
 QC_DEV uint32_t byte_of(uint32_t w, uint32_t i) { return (w >> (8 * i)) & 0xffu; }
@@ -143,12 +167,12 @@ QC_DEV float dequant_one(const MatDesc& m, const uint8_t* row, const __half* dro
 // x is quantized per block of 256 elements to 22-bit integers,
 //   xi = rint(x * 2^21 / max|x_block|),  |xi| <= 2^21,
 // and split into three signed byte digits, xi = d0 + 256 d1 + 65536 d2
-// (d0, d1 in [-128, 127], |d2| <= 32).  Weight codes (nibbles, 6-bit, int8)
-// then meet the activations in exact dp4a integer dot products; the only
-// rounding is that of xi (2^-22 of the block maximum) and of the final float
-// combination.  Per unit u (64 elements) the three digit planes are stored as
-// [d0 x64][d1 x64][d2 x64][pad 16] = 208 bytes: the pad makes the 16-byte
-// reads of 8 consecutive units fall in 8 different bank groups.
+// (d0, d1 in [-128, 127], |d2| <= 32).  Weight codes (nibbles, 5/6-bit values,
+// int8) then meet the activations in exact dp4a integer dot products; the
+// only rounding is that of xi (2^-22 of the block maximum) and of the final
+// float combination.  Per unit u (64 elements) the three digit planes are
+// stored as [d0 x64][d1 x64][d2 x64][pad 16] = 208 bytes: the pad puts the
+// 16-byte reads of 8 consecutive units in 8 different bank groups.
 // F16/F32 matrices read a float copy instead: 64 floats + 4 pad per unit.
 constexpr uint32_t kUnitDigitBytes = 208;
 constexpr uint32_t kUnitFloats = 68;
@@ -157,108 +181,149 @@ constexpr float kXRange = 2097152.f;  // 2^21
 struct XView {
   const uint8_t* dig;  // [units][208]
   const int* sx;       // [units][4]: sum of xi over each 16 elements
-  const float* sb;     // [ceil(units/4)]: x scale of each 256-block (x = xi * sb)
+  const float* sb;     // [units/4]: x scale of each 256-block (x = xi * sb)
   const float* xf;     // [units][68] padded float copy (F16/F32 only), may be null
 };
 
-// Shared-memory bytes of an XView for `units` units.
+// Units are staged in whole 256-element blocks.
+__host__ __device__ inline uint32_t units4(uint32_t units) { return (units + 3) & ~3u; }
+// Shared-memory bytes of one XView of `units` units.
 __host__ __device__ inline uint32_t xview_bytes(uint32_t units, bool with_float) {
-  uint32_t b = units * kUnitDigitBytes + units * 16 + ((units + 3) / 4) * 4;
+  const uint32_t u = units4(units);
+  uint32_t b = u * kUnitDigitBytes + u * 16 + (u / 4) * 4;
   b = (b + 15) & ~15u;
-  if (with_float) b += units * kUnitFloats * 4;
+  if (with_float) b += u * kUnitFloats * 4;
   return b;
 }
+__host__ __device__ inline XView xview_at(const uint8_t* mem, uint32_t units, bool with_float) {
+  const uint32_t u = units4(units);
+  XView v;
+  v.dig = mem;
+  v.sx = reinterpret_cast<const int*>(mem + u * kUnitDigitBytes);
+  v.sb = reinterpret_cast<const float*>(mem + u * kUnitDigitBytes + u * 16);
+  v.xf = with_float
+             ? reinterpret_cast<const float*>(mem + ((u * kUnitDigitBytes + u * 16 + (u / 4) * 4 + 15) & ~15u))
+             : nullptr;
+  return v;
+}
 
-// Stage n values v(i) (i < n; zero beyond, up to units*64) into `mem` as an
-// XView.  Called by all threads of the block; ends with __syncthreads().
-// One warp per 256-block: max, scale, digits and sums in one pass.
-template <class F>
-QC_DEV XView stage_x(uint8_t* mem, uint32_t n, uint32_t units, bool with_float, F v) {
-  uint8_t* dig = mem;
-  int* sx = reinterpret_cast<int*>(mem + units * kUnitDigitBytes);
-  float* sb = reinterpret_cast<float*>(sx + units * 4);
-  float* xf = with_float ? reinterpret_cast<float*>(mem + ((units * kUnitDigitBytes + units * 16 + ((units + 3) / 4) * 4 + 15) & ~15u))
-                         : nullptr;
-  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  const uint32_t nblk = (units + 3) / 4;
-  for (uint32_t b = warp; b < nblk; b += nw) {
-    // lane holds elements b*256 + lane*8 .. +7 (two groups of 4)
-    float x[8];
-    float mx = 0.f;
+// Quantize the 8 values a lane holds (elements e..e+7 of unit u, one 256-block
+// per warp) and store digits, 16-element sums, the block scale and the float copy.
+QC_DEV void store_lane8(uint8_t* mem, uint32_t units, bool with_float, uint32_t u, uint32_t e, const float (&x)[8]) {
+  const uint32_t lane = threadIdx.x & 31;
+  float mx = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; k++) {
-      const uint32_t i = b * 256 + lane * 8 + k;
-      x[k] = (i < n) ? v(i) : 0.f;
-      mx = fmaxf(mx, fabsf(x[k]));
+  for (int k = 0; k < 8; k++) mx = fmaxf(mx, fabsf(x[k]));
+  mx = warp_max(mx);
+  const float inv = mx > 0.f ? kXRange / mx : 0.f;
+  const XView xv = xview_at(mem, units, with_float);
+  if (lane == 0) const_cast<float*>(xv.sb)[u >> 2] = mx > 0.f ? mx / kXRange : 0.f;
+  int s = 0;
+  uint32_t w0[2], w1[2], w2[2];
+#pragma unroll
+  for (int g = 0; g < 2; g++) {
+    uint32_t p0 = 0, p1 = 0, p2 = 0;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      int xi = __float2int_rn(x[g * 4 + k] * inv);
+      xi = max(-2097152, min(2097152, xi));
+      s += xi;
+      const int d0 = (int)(int8_t)(xi & 0xff);
+      const int r1 = (xi - d0) >> 8;
+      const int d1 = (int)(int8_t)(r1 & 0xff);
+      const int d2 = (r1 - d1) >> 8;
+      p0 |= (uint32_t)(d0 & 0xff) << (8 * k);
+      p1 |= (uint32_t)(d1 & 0xff) << (8 * k);
+      p2 |= (uint32_t)(d2 & 0xff) << (8 * k);
     }
-    mx = warp_max(mx);
-    const float inv = mx > 0.f ? kXRange / mx : 0.f;
-    if (lane == 0) sb[b] = mx > 0.f ? mx / kXRange : 0.f;
-    const uint32_t u = b * 4 + lane / 8;  // unit of this lane's elements
-    const uint32_t e = (lane % 8) * 8;    // element offset inside the unit
-    int s = 0;
-    uint32_t w0[2], w1[2], w2[2];
+    w0[g] = p0;
+    w1[g] = p1;
+    w2[g] = p2;
+  }
+  s += __shfl_xor_sync(0xffffffffu, s, 1);  // lanes (2j, 2j+1) of a unit hold one 16-group
+  uint8_t* du = mem + u * kUnitDigitBytes + e;
+  *reinterpret_cast<uint2*>(du) = make_uint2(w0[0], w0[1]);
+  *reinterpret_cast<uint2*>(du + 64) = make_uint2(w1[0], w1[1]);
+  *reinterpret_cast<uint2*>(du + 128) = make_uint2(w2[0], w2[1]);
+  if ((lane & 1) == 0) const_cast<int*>(xv.sx)[u * 4 + (e >> 4)] = s;
+  if (with_float) {
+    float* f = const_cast<float*>(xv.xf) + u * kUnitFloats + e;
+    *reinterpret_cast<float4*>(f) = make_float4(x[0], x[1], x[2], x[3]);
+    *reinterpret_cast<float4*>(f + 4) = make_float4(x[4], x[5], x[6], x[7]);
+  }
+}
+
+// Stage `nv` vectors of n elements each (v(j, i) for vector j, element i < n;
+// zero beyond) as consecutive XViews of xview_bytes(units) bytes.  If RMS, the
+// vector (nv must be 1) is x[i] and becomes x[i] * (s * w[i]) with
+// s = 1/sqrt(mean(x^2) + eps) (reference ops.rs:3-15, the product s*w first).
+// Each thread owns 8 consecutive elements per pass, a warp one 256-block; all
+// loads of up to 4 passes are issued before any arithmetic.  All threads of
+// the block must call; ends with __syncthreads().
+template <bool RMS, class F>
+QC_DEV void stage_vectors(uint8_t* mem, uint32_t nv, uint32_t n, uint32_t units, bool with_float, F v,
+                          const float* __restrict__ w, float eps, float* red) {
+  const uint32_t per = units4(units) * 64;  // padded elements per vector
+  const uint32_t total = nv * per, xb = xview_bytes(units, with_float);
+  constexpr int P = 4;
+  for (uint32_t base = 0; base < total; base += P * blockDim.x * 8) {
+    float x[P][8], ww[P][8];
 #pragma unroll
-    for (int g = 0; g < 2; g++) {
-      uint32_t p0 = 0, p1 = 0, p2 = 0;
+    for (int p = 0; p < P; p++) {
+      const uint32_t i0 = base + (p * blockDim.x + threadIdx.x) * 8;
+      const uint32_t j = i0 / per, e = i0 % per;
 #pragma unroll
-      for (int k = 0; k < 4; k++) {
-        int xi = __float2int_rn(x[g * 4 + k] * inv);
-        xi = max(-2097152, min(2097152, xi));
-        s += xi;
-        const int d0 = (int)(int8_t)(xi & 0xff);
-        const int r1 = (xi - d0) >> 8;
-        const int d1 = (int)(int8_t)(r1 & 0xff);
-        const int d2 = (r1 - d1) >> 8;
-        p0 |= (uint32_t)(d0 & 0xff) << (8 * k);
-        p1 |= (uint32_t)(d1 & 0xff) << (8 * k);
-        p2 |= (uint32_t)(d2 & 0xff) << (8 * k);
+      for (int k = 0; k < 8; k++) {
+        const bool ok = i0 < total && e + k < n;
+        x[p][k] = ok ? v(j, e + k) : 0.f;
+        if constexpr (RMS) ww[p][k] = ok ? w[e + k] : 0.f;
       }
-      w0[g] = p0;
-      w1[g] = p1;
-      w2[g] = p2;
     }
-    // sums over 16 elements: lanes (2j, 2j+1) of a unit hold one 16-group
-    s += __shfl_xor_sync(0xffffffffu, s, 1);
-    if (u < units) {
-      uint8_t* du = dig + u * kUnitDigitBytes + e;
-      *reinterpret_cast<uint2*>(du) = make_uint2(w0[0], w0[1]);
-      *reinterpret_cast<uint2*>(du + 64) = make_uint2(w1[0], w1[1]);
-      *reinterpret_cast<uint2*>(du + 128) = make_uint2(w2[0], w2[1]);
-      if ((lane & 1) == 0) sx[u * 4 + (lane % 8) / 2] = s;
-      if (xf) {
-        float* f = xf + u * kUnitFloats + e;
-        *reinterpret_cast<float4*>(f) = make_float4(x[0], x[1], x[2], x[3]);
-        *reinterpret_cast<float4*>(f + 4) = make_float4(x[4], x[5], x[6], x[7]);
+    if constexpr (RMS) {
+      float ss = 0.f;
+#pragma unroll
+      for (int p = 0; p < P; p++)
+#pragma unroll
+        for (int k = 0; k < 8; k++) ss = fmaf(x[p][k], x[p][k], ss);
+      ss = block_sum(ss, red);
+      const float sc = 1.0f / sqrtf(ss / (float)n + eps);
+#pragma unroll
+      for (int p = 0; p < P; p++)
+#pragma unroll
+        for (int k = 0; k < 8; k++) x[p][k] = __fmul_rn(x[p][k], __fmul_rn(sc, ww[p][k]));
+    }
+#pragma unroll
+    for (int p = 0; p < P; p++) {
+      const uint32_t i0 = base + (p * blockDim.x + threadIdx.x) * 8;
+      if (base + (p * blockDim.x + (threadIdx.x & ~31u)) * 8 < total) {  // warp-uniform: whole 256-blocks
+        const uint32_t j = i0 / per, e = i0 % per;
+        store_lane8(mem + j * xb, units, with_float, e >> 6, e & 63, x[p]);
       }
     }
   }
   __syncthreads();
-  return XView{dig, sx, sb, xf};
 }
 
 QC_DEV int dp4a(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
+QC_DEV float combine(int a0, int a1, int a2) { return (float)a0 + 256.f * (float)a1 + 65536.f * (float)a2; }
 
-// Dot of 32 codes (8 words of 4 bytes; codes are bytes: nibbles, 5/6-bit values
-// or int8) with the 32 activation integers xi starting at element `e` of the
-// unit: three exact dp4a sums, one per digit, combined in float (each digit sum
-// is below 2^24 in magnitude, so only the final combination rounds).
-struct Digits32 {
-  uint4 p0[2], p1[2], p2[2];
+// The activation data of one unit held in registers: d[4p + q] = digit plane p,
+// elements 16q..16q+15; s = sums of xi over the four 16-element groups; sb = scale.
+struct UnitX {
+  uint4 d[12];
+  int4 s;
+  float sb;
 };
-QC_DEV Digits32 load_digits32(const uint8_t* du, uint32_t e) {
-  Digits32 d;
-  const uint4* a = reinterpret_cast<const uint4*>(du + e);
-  d.p0[0] = a[0];
-  d.p0[1] = a[1];
-  d.p1[0] = a[4];
-  d.p1[1] = a[5];
-  d.p2[0] = a[8];
-  d.p2[1] = a[9];
-  return d;
+QC_DEV UnitX load_unit_x(const XView& xv, uint32_t u) {
+  UnitX ux;
+  const uint4* a = reinterpret_cast<const uint4*>(xv.dig + u * kUnitDigitBytes);
+#pragma unroll
+  for (int i = 0; i < 12; i++) ux.d[i] = a[i];
+  ux.s = *reinterpret_cast<const int4*>(xv.sx + u * 4);
+  ux.sb = xv.sb[u >> 2];
+  return ux;
 }
-QC_DEV uint32_t w4(const uint4 (&v)[2], int j) {
-  const uint4& t = v[j >> 2];
+QC_DEV uint32_t wsel(const uint4& t, int j) {
   switch (j & 3) {
     case 0: return t.x;
     case 1: return t.y;
@@ -266,60 +331,64 @@ QC_DEV uint32_t w4(const uint4 (&v)[2], int j) {
     default: return t.w;
   }
 }
-QC_DEV float combine(int a0, int a1, int a2) { return (float)a0 + 256.f * (float)a1 + 65536.f * (float)a2; }
-// codes[j] holds the 4 codes of elements 4j..4j+3.
-QC_DEV float idot32(const uint32_t (&codes)[8], const Digits32& d) {
+// Digit word j (elements 4j..4j+3, j < 16) of plane p.
+QC_DEV uint32_t dword(const UnitX& ux, int p, int j) { return wsel(ux.d[4 * p + (j >> 2)], j); }
+
+// sum of 32 codes (codes[j]: elements h*32 + 4j .. +3) times xi, exact in three dp4a chains.
+QC_DEV float idot32(const uint32_t (&codes)[8], const UnitX& ux, int h) {
   int a0 = 0, a1 = 0, a2 = 0;
 #pragma unroll
   for (int j = 0; j < 8; j++) {
-    a0 = dp4a(codes[j], w4(d.p0, j), a0);
-    a1 = dp4a(codes[j], w4(d.p1, j), a1);
-    a2 = dp4a(codes[j], w4(d.p2, j), a2);
+    a0 = dp4a(codes[j], dword(ux, 0, 8 * h + j), a0);
+    a1 = dp4a(codes[j], dword(ux, 1, 8 * h + j), a1);
+    a2 = dp4a(codes[j], dword(ux, 2, 8 * h + j), a2);
   }
   return combine(a0, a1, a2);
 }
 // As idot32 but split into the two 16-element halves (Q6_K scale groups).
-QC_DEV void idot16x2(const uint32_t (&codes)[8], const Digits32& d, float* lo, float* hi) {
+QC_DEV void idot16x2(const uint32_t (&codes)[8], const UnitX& ux, int h, float* lo, float* hi) {
   int a0 = 0, a1 = 0, a2 = 0, b0 = 0, b1 = 0, b2 = 0;
 #pragma unroll
   for (int j = 0; j < 4; j++) {
-    a0 = dp4a(codes[j], w4(d.p0, j), a0);
-    a1 = dp4a(codes[j], w4(d.p1, j), a1);
-    a2 = dp4a(codes[j], w4(d.p2, j), a2);
-    b0 = dp4a(codes[j + 4], w4(d.p0, j + 4), b0);
-    b1 = dp4a(codes[j + 4], w4(d.p1, j + 4), b1);
-    b2 = dp4a(codes[j + 4], w4(d.p2, j + 4), b2);
+    a0 = dp4a(codes[j], dword(ux, 0, 8 * h + j), a0);
+    a1 = dp4a(codes[j], dword(ux, 1, 8 * h + j), a1);
+    a2 = dp4a(codes[j], dword(ux, 2, 8 * h + j), a2);
+    b0 = dp4a(codes[j + 4], dword(ux, 0, 8 * h + j + 4), b0);
+    b1 = dp4a(codes[j + 4], dword(ux, 1, 8 * h + j + 4), b1);
+    b2 = dp4a(codes[j + 4], dword(ux, 2, 8 * h + j + 4), b2);
   }
   *lo = combine(a0, a1, a2);
   *hi = combine(b0, b1, b2);
 }
 
-// 6-bit scale and min of sub-block j from the 12 packed bytes s0|s1|s2 (quant.rs:25-34).
-QC_DEV void kq_scale_w(uint32_t s0, uint32_t s1, uint32_t s2, uint32_t j, float* sc, float* m) {
-  uint32_t a, b;
-  if (j < 4) {
-    a = byte_of(s0, j) & 63;
-    b = byte_of(s1, j) & 63;
-  } else {
-    const uint32_t jj = j - 4;
-    a = (byte_of(s2, jj) & 15) | ((byte_of(s0, jj) >> 6) << 4);
-    b = (byte_of(s2, jj) >> 4) | ((byte_of(s1, jj) >> 6) << 4);
-  }
-  *sc = (float)a;
-  *m = (float)b;
+// 6-bit scale and min of sub-blocks j and j+1 (j even) from the 12 packed bytes
+// s0|s1|s2 (quant.rs:25-34), without branches: both belong to the same half.
+QC_DEV void kq_scale_pair(uint32_t s0, uint32_t s1, uint32_t s2, uint32_t j, float* sc0, float* m0, float* sc1,
+                          float* m1) {
+  const uint32_t jj = j & 3, hi = j >> 2;
+  // bytes jj and jj+1 of each word
+  const uint32_t a = __byte_perm(s0, 0, 0x4440 | jj) | (__byte_perm(s0, 0, 0x4440 | (jj + 1)) << 8);
+  const uint32_t b = __byte_perm(s1, 0, 0x4440 | jj) | (__byte_perm(s1, 0, 0x4440 | (jj + 1)) << 8);
+  const uint32_t c = __byte_perm(s2, 0, 0x4440 | jj) | (__byte_perm(s2, 0, 0x4440 | (jj + 1)) << 8);
+  // low half (j < 4): a & 63, b & 63; high half: (c & 15) | (a >> 6) << 4, (c >> 4) | (b >> 6) << 4
+  const uint32_t sl = a & 0x3f3fu, ml = b & 0x3f3fu;
+  const uint32_t sh = (c & 0x0f0fu) | (((a >> 6) & 0x0303u) << 4), mh = ((c >> 4) & 0x0f0fu) | (((b >> 6) & 0x0303u) << 4);
+  const uint32_t sv = hi ? sh : sl, mv = hi ? mh : ml;
+  *sc0 = (float)(sv & 0xff);
+  *sc1 = (float)(sv >> 8);
+  *m0 = (float)(mv & 0xff);
+  *m1 = (float)(mv >> 8);
 }
 
-// ---- unit dot products: contribution of unit u (64 elements) of one row, in x units (times sb) ----
+// ---- unit dot products: the contribution of unit u (64 elements) of one row ----
 
 // Q4_K unit u = (block u/4, pair p = u%4): sub-blocks 2p (low nibbles) and 2p+1 (high nibbles).
-QC_DEV float unit_q4k(const uint8_t* row, uint32_t u, const XView& xv) {
+template <bool S>
+QC_DEV float unit_q4k(const uint8_t* row, uint32_t u, const UnitX& ux) {
   const uint32_t b = u >> 2, p = u & 3;
   const uint8_t* blk = row + b * 144;
-  const uint4 hd = ldg16(blk);
-  const uint4 q0 = ldg16(blk + 16 + 32 * p), q1 = ldg16(blk + 32 + 32 * p);
-  const uint8_t* du = xv.dig + u * kUnitDigitBytes;
-  const Digits32 dlo = load_digits32(du, 0), dhi = load_digits32(du, 32);
-  const int4 s4 = *reinterpret_cast<const int4*>(xv.sx + u * 4);
+  const uint4 hd = ld16<S>(blk);
+  const uint4 q0 = ld16<S>(blk + 16 + 32 * p), q1 = ld16<S>(blk + 32 + 32 * p);
   const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
   uint32_t lo[8], hi[8];
 #pragma unroll
@@ -327,26 +396,23 @@ QC_DEV float unit_q4k(const uint8_t* row, uint32_t u, const XView& xv) {
     lo[j] = w[j] & 0x0f0f0f0fu;
     hi[j] = (w[j] >> 4) & 0x0f0f0f0fu;
   }
-  const float qlo = idot32(lo, dlo), qhi = idot32(hi, dhi);
+  const float qlo = idot32(lo, ux, 0), qhi = idot32(hi, ux, 1);
   float sc0, m0, sc1, m1;
-  kq_scale_w(hd.y, hd.z, hd.w, 2 * p, &sc0, &m0);
-  kq_scale_w(hd.y, hd.z, hd.w, 2 * p + 1, &sc1, &m1);
+  kq_scale_pair(hd.y, hd.z, hd.w, 2 * p, &sc0, &m0, &sc1, &m1);
   const float d = h2f_bits(hd.x), dmin = h2f_bits(hd.x >> 16);
   const float r = sc0 * qlo + sc1 * qhi;
-  const float mm = m0 * (float)(s4.x + s4.y) + m1 * (float)(s4.z + s4.w);
-  return (d * r - dmin * mm) * xv.sb[b];
+  const float mm = m0 * (float)(ux.s.x + ux.s.y) + m1 * (float)(ux.s.z + ux.s.w);
+  return (d * r - dmin * mm) * ux.sb;
 }
 
 // Q5_K: as Q4_K plus the fifth bit: qh[t] bit g belongs to element 32g + t.
-QC_DEV float unit_q5k(const uint8_t* row, uint32_t u, const XView& xv) {
+template <bool S>
+QC_DEV float unit_q5k(const uint8_t* row, uint32_t u, const UnitX& ux) {
   const uint32_t b = u >> 2, p = u & 3;
   const uint8_t* blk = row + b * 176;
-  const uint4 hd = ldg16(blk);
-  const uint4 h0 = ldg16(blk + 16), h1 = ldg16(blk + 32);
-  const uint4 q0 = ldg16(blk + 48 + 32 * p), q1 = ldg16(blk + 64 + 32 * p);
-  const uint8_t* du = xv.dig + u * kUnitDigitBytes;
-  const Digits32 dlo = load_digits32(du, 0), dhi = load_digits32(du, 32);
-  const int4 s4 = *reinterpret_cast<const int4*>(xv.sx + u * 4);
+  const uint4 hd = ld16<S>(blk);
+  const uint4 h0 = ld16<S>(blk + 16), h1 = ld16<S>(blk + 32);
+  const uint4 q0 = ld16<S>(blk + 48 + 32 * p), q1 = ld16<S>(blk + 64 + 32 * p);
   const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
   const uint32_t h[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
   const uint32_t g0 = 2 * p, g1 = 2 * p + 1;
@@ -356,32 +422,29 @@ QC_DEV float unit_q5k(const uint8_t* row, uint32_t u, const XView& xv) {
     lo[j] = (w[j] & 0x0f0f0f0fu) | (((h[j] >> g0) & 0x01010101u) << 4);
     hi[j] = ((w[j] >> 4) & 0x0f0f0f0fu) | (((h[j] >> g1) & 0x01010101u) << 4);
   }
-  const float qlo = idot32(lo, dlo), qhi = idot32(hi, dhi);
+  const float qlo = idot32(lo, ux, 0), qhi = idot32(hi, ux, 1);
   float sc0, m0, sc1, m1;
-  kq_scale_w(hd.y, hd.z, hd.w, g0, &sc0, &m0);
-  kq_scale_w(hd.y, hd.z, hd.w, g1, &sc1, &m1);
+  kq_scale_pair(hd.y, hd.z, hd.w, g0, &sc0, &m0, &sc1, &m1);
   const float d = h2f_bits(hd.x), dmin = h2f_bits(hd.x >> 16);
   const float r = sc0 * qlo + sc1 * qhi;
-  const float mm = m0 * (float)(s4.x + s4.y) + m1 * (float)(s4.z + s4.w);
-  return (d * r - dmin * mm) * xv.sb[b];
+  const float mm = m0 * (float)(ux.s.x + ux.s.y) + m1 * (float)(ux.s.z + ux.s.w);
+  return (d * r - dmin * mm) * ux.sb;
 }
 
 // Q6_K unit u = (block u/4, chunk c = (u/2)%2, half h = u%2): quarters 2h (elements
 // c*128+64h+t) and 2h+1 (c*128+64h+32+t), t < 32; four 16-element scale groups.
-QC_DEV float unit_q6k(const uint8_t* row, const __half* drow, uint32_t u, const XView& xv) {
+template <bool S>
+QC_DEV float unit_q6k(const uint8_t* row, const __half* drow, uint32_t u, const UnitX& ux) {
   const uint32_t b = u >> 2, c = (u >> 1) & 1, hh = u & 1;
   const uint8_t* blk = row + b * 208;
-  const uint4 l0 = ldg16(blk + c * 64), l1 = ldg16(blk + c * 64 + 16);        // quarter 2h: ql[c*64 + t]
-  const uint4 l2 = ldg16(blk + c * 64 + 32), l3 = ldg16(blk + c * 64 + 48);   // quarter 2h+1: ql[c*64+32+t]
-  const uint4 qa = ldg16(blk + 128 + c * 32), qb = ldg16(blk + 128 + c * 32 + 16);
-  const uint4 sc = ldg16(blk + 192);
-  const uint8_t* du = xv.dig + u * kUnitDigitBytes;
-  const Digits32 d0 = load_digits32(du, 0), d1 = load_digits32(du, 32);
-  const int4 s4 = *reinterpret_cast<const int4*>(xv.sx + u * 4);
+  const uint4 l0 = ld16<S>(blk + c * 64), l1 = ld16<S>(blk + c * 64 + 16);       // quarter 2h: ql[c*64 + t]
+  const uint4 l2 = ld16<S>(blk + c * 64 + 32), l3 = ld16<S>(blk + c * 64 + 48);  // quarter 2h+1: ql[c*64+32+t]
+  const uint4 qa = ld16<S>(blk + 128 + c * 32), qb = ld16<S>(blk + 128 + c * 32 + 16);
+  const uint4 sc = ld16<S>(blk + 192);
   const uint32_t la[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
   const uint32_t lb[8] = {l2.x, l2.y, l2.z, l2.w, l3.x, l3.y, l3.z, l3.w};
   const uint32_t qh[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-  const uint32_t ns = 4 * hh, s0 = 2 * (2 * hh), s1 = 2 * (2 * hh + 1);
+  const uint32_t ns = 4 * hh, s0 = 4 * hh, s1 = 4 * hh + 2;
   uint32_t ca[8], cb[8];
 #pragma unroll
   for (int j = 0; j < 8; j++) {
@@ -389,38 +452,34 @@ QC_DEV float unit_q6k(const uint8_t* row, const __half* drow, uint32_t u, const 
     cb[j] = ((lb[j] >> ns) & 0x0f0f0f0fu) | (((qh[j] >> s1) & 0x03030303u) << 4);
   }
   float qa0, qa1, qb0, qb1;
-  idot16x2(ca, d0, &qa0, &qa1);
-  idot16x2(cb, d1, &qb0, &qb1);
-  // scales: quarter q group t/16 -> sc[c*8 + 2q + t/16]
+  idot16x2(ca, ux, 0, &qa0, &qa1);
+  idot16x2(cb, ux, 1, &qb0, &qb1);
   // the four scales sit in bytes c*8 + 4h .. +3, i.e. in word 2c + h of the 16 scale bytes
   const uint32_t sw = (c ? (hh ? sc.w : sc.z) : (hh ? sc.y : sc.x));
   const float sa0 = (float)(int8_t)byte_of(sw, 0), sa1 = (float)(int8_t)byte_of(sw, 1);
   const float sb0 = (float)(int8_t)byte_of(sw, 2), sb1 = (float)(int8_t)byte_of(sw, 3);
   // sum (q - 32) x = sum q x - 32 sum x over each 16-element group
-  const float r = sa0 * (qa0 - 32.f * (float)s4.x) + sa1 * (qa1 - 32.f * (float)s4.y) +
-                  sb0 * (qb0 - 32.f * (float)s4.z) + sb1 * (qb1 - 32.f * (float)s4.w);
-  return h2f(drow[b]) * r * xv.sb[b];
+  const float r = sa0 * (qa0 - 32.f * (float)ux.s.x) + sa1 * (qa1 - 32.f * (float)ux.s.y) +
+                  sb0 * (qb0 - 32.f * (float)ux.s.z) + sb1 * (qb1 - 32.f * (float)ux.s.w);
+  return h2f(drow[b]) * r * ux.sb;
 }
 
 // Q8_0 unit u = blocks 2u and 2u+1.
-QC_DEV float unit_q80(const uint8_t* row, const __half* drow, uint32_t u, const XView& xv) {
+template <bool S>
+QC_DEV float unit_q80(const uint8_t* row, const __half* drow, uint32_t u, const UnitX& ux) {
   const uint8_t* blk = row + u * 64;
-  const uint4 a = ldg16(blk), b = ldg16(blk + 16), c = ldg16(blk + 32), e = ldg16(blk + 48);
-  const uint8_t* du = xv.dig + u * kUnitDigitBytes;
-  const Digits32 d0 = load_digits32(du, 0), d1 = load_digits32(du, 32);
+  const uint4 a = ld16<S>(blk), b = ld16<S>(blk + 16), c = ld16<S>(blk + 32), e = ld16<S>(blk + 48);
   const uint32_t w0[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
   const uint32_t w1[8] = {c.x, c.y, c.z, c.w, e.x, e.y, e.z, e.w};
-  const float q0 = idot32(w0, d0), q1 = idot32(w1, d1);
+  const float q0 = idot32(w0, ux, 0), q1 = idot32(w1, ux, 1);
   const __half2 dd = *reinterpret_cast<const __half2*>(drow + 2 * u);
-  return (__low2float(dd) * q0 + __high2float(dd) * q1) * xv.sb[u >> 2];
+  return (__low2float(dd) * q0 + __high2float(dd) * q1) * ux.sb;
 }
 
 // Q4_0 unit u = blocks 2u, 2u+1; byte t of a block holds elements t (low) and 16+t (high).
-QC_DEV float unit_q40(const uint8_t* row, const __half* drow, uint32_t u, const XView& xv) {
-  const uint4 a = ldg16(row + u * 32), b = ldg16(row + u * 32 + 16);
-  const uint8_t* du = xv.dig + u * kUnitDigitBytes;
-  const Digits32 d0 = load_digits32(du, 0), d1 = load_digits32(du, 32);
-  const int4 s4 = *reinterpret_cast<const int4*>(xv.sx + u * 4);
+template <bool S>
+QC_DEV float unit_q40(const uint8_t* row, const __half* drow, uint32_t u, const UnitX& ux) {
+  const uint4 a = ld16<S>(row + u * 32), b = ld16<S>(row + u * 32 + 16);
   const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wb[4] = {b.x, b.y, b.z, b.w};
   uint32_t c0[8], c1[8];
 #pragma unroll
@@ -430,20 +489,32 @@ QC_DEV float unit_q40(const uint8_t* row, const __half* drow, uint32_t u, const 
     c1[j] = wb[j] & 0x0f0f0f0fu;
     c1[j + 4] = (wb[j] >> 4) & 0x0f0f0f0fu;
   }
-  const float q0 = idot32(c0, d0), q1 = idot32(c1, d1);
+  const float q0 = idot32(c0, ux, 0), q1 = idot32(c1, ux, 1);
   const __half2 dd = *reinterpret_cast<const __half2*>(drow + 2 * u);
-  const float r0 = q0 - 8.f * (float)(s4.x + s4.y), r1 = q1 - 8.f * (float)(s4.z + s4.w);
-  return (__low2float(dd) * r0 + __high2float(dd) * r1) * xv.sb[u >> 2];
+  const float r0 = q0 - 8.f * (float)(ux.s.x + ux.s.y), r1 = q1 - 8.f * (float)(ux.s.z + ux.s.w);
+  return (__low2float(dd) * r0 + __high2float(dd) * r1) * ux.sb;
 }
 
-QC_DEV float unit_f16(const uint8_t* row, uint32_t u, const XView& xv) {
+// Float activations of one unit held in registers (F16/F32 matrices).
+struct UnitXF {
+  float4 f[16];
+};
+QC_DEV UnitXF load_unit_xf(const XView& xv, uint32_t u) {
+  UnitXF ux;
+  const float4* a = reinterpret_cast<const float4*>(xv.xf + u * kUnitFloats);
+#pragma unroll
+  for (int i = 0; i < 16; i++) ux.f[i] = a[i];
+  return ux;
+}
+
+template <bool S>
+QC_DEV float unit_f16(const uint8_t* row, uint32_t u, const UnitXF& ux) {
   const uint8_t* p = row + u * 128;
-  const float* x = xv.xf + u * kUnitFloats;
   float acc = 0.f;
 #pragma unroll
   for (int k = 0; k < 8; k++) {
-    const uint4 v = ldg16(p + 16 * k);
-    const float4 xa = *reinterpret_cast<const float4*>(x + 8 * k), xb = *reinterpret_cast<const float4*>(x + 8 * k + 4);
+    const uint4 v = ld16<S>(p + 16 * k);
+    const float4 xa = ux.f[2 * k], xb = ux.f[2 * k + 1];
     float2 f = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
     acc = fmaf(f.x, xa.x, acc);
     acc = fmaf(f.y, xa.y, acc);
@@ -460,55 +531,161 @@ QC_DEV float unit_f16(const uint8_t* row, uint32_t u, const XView& xv) {
   return acc;
 }
 
-QC_DEV float unit_f32(const uint8_t* row, uint32_t u, const XView& xv) {
+template <bool S>
+QC_DEV float unit_f32(const uint8_t* row, uint32_t u, const UnitXF& ux) {
   const uint8_t* p = row + u * 256;
-  const float* x = xv.xf + u * kUnitFloats;
   float acc = 0.f;
 #pragma unroll
   for (int k = 0; k < 16; k++) {
-    const uint4 v = ldg16(p + 16 * k);
-    const float4 xv4 = *reinterpret_cast<const float4*>(x + 4 * k);
-    acc = fmaf(__uint_as_float(v.x), xv4.x, acc);
-    acc = fmaf(__uint_as_float(v.y), xv4.y, acc);
-    acc = fmaf(__uint_as_float(v.z), xv4.z, acc);
-    acc = fmaf(__uint_as_float(v.w), xv4.w, acc);
+    const uint4 v = ld16<S>(p + 16 * k);
+    acc = fmaf(__uint_as_float(v.x), ux.f[k].x, acc);
+    acc = fmaf(__uint_as_float(v.y), ux.f[k].y, acc);
+    acc = fmaf(__uint_as_float(v.z), ux.f[k].z, acc);
+    acc = fmaf(__uint_as_float(v.w), ux.f[k].w, acc);
   }
   return acc;
 }
 
 template <uint32_t KIND>
-QC_DEV float unit_dot(const uint8_t* row, const __half* drow, uint32_t u, const XView& xv) {
-  if constexpr (KIND == Q4_K) return unit_q4k(row, u, xv);
-  else if constexpr (KIND == Q5_K) return unit_q5k(row, u, xv);
-  else if constexpr (KIND == Q6_K) return unit_q6k(row, drow, u, xv);
-  else if constexpr (KIND == Q8_0) return unit_q80(row, drow, u, xv);
-  else if constexpr (KIND == Q4_0) return unit_q40(row, drow, u, xv);
-  else if constexpr (KIND == F16) return unit_f16(row, u, xv);
-  else return unit_f32(row, u, xv);
+struct UnitXOf {
+  using type = UnitX;
+};
+template <>
+struct UnitXOf<F16> {
+  using type = UnitXF;
+};
+template <>
+struct UnitXOf<F32> {
+  using type = UnitXF;
+};
+
+template <uint32_t KIND>
+QC_DEV typename UnitXOf<KIND>::type load_x(const XView& xv, uint32_t u) {
+  if constexpr (KIND == F16 || KIND == F32) return load_unit_xf(xv, u);
+  else return load_unit_x(xv, u);
 }
 
-// This lane's partial of row `r` of expert `e`: units lane_in_row, +lpr, ... (the
-// caller sums the partials of the lpr lanes of the row).
-template <uint32_t KIND>
-QC_DEV float row_partial_k(const MatDesc& m, uint32_t e, uint32_t r, uint32_t lane_in_row, const XView& xv) {
-  const uint8_t* row = m.w + e * m.expert_stride + (uint64_t)r * m.row_stride;
-  const __half* drow = m.d ? m.d + e * m.d_expert_stride + (uint64_t)r * m.d_stride : nullptr;
-  float acc = 0.f;
+template <uint32_t KIND, bool S>
+QC_DEV float unit_dot(const uint8_t* row, const __half* drow, uint32_t u, const typename UnitXOf<KIND>::type& ux) {
+  if constexpr (KIND == Q4_K) return unit_q4k<S>(row, u, ux);
+  else if constexpr (KIND == Q5_K) return unit_q5k<S>(row, u, ux);
+  else if constexpr (KIND == Q6_K) return unit_q6k<S>(row, drow, u, ux);
+  else if constexpr (KIND == Q8_0) return unit_q80<S>(row, drow, u, ux);
+  else if constexpr (KIND == Q4_0) return unit_q40<S>(row, drow, u, ux);
+  else if constexpr (KIND == F16) return unit_f16<S>(row, u, ux);
+  else return unit_f32<S>(row, u, ux);
+}
+
+// ---------------------------------------------------------------------------
+// Warp-level matvec over rows [r0, r1) of a block.  Warp w takes row groups
+// (G = 32/lpr rows each) w, w+nw, ...; lane (row slot, lr) always handles units
+// lr, lr+lpr, ...  When a lane has one unit (upl == 1, the common case) its
+// activation data is loaded into registers once for all rows.  addr(r, &row,
+// &drow) gives the row pointers; emit(r, sum) runs on lane 0 of the row's group.
+template <uint32_t KIND, bool S, class Addr, class Emit>
+QC_DEV void warp_rows_k(const MatDesc& m, uint32_t r0, uint32_t r1, const XView& xv, Addr addr, Emit emit,
+                        uint32_t warp, uint32_t nw) {
+  const uint32_t lpr = m.lpr, G = 32 / lpr, lane = threadIdx.x & 31;
+  const uint32_t lr = lane % lpr, slot = lane / lpr, stride = nw * G;
+  if (m.upl == 1) {
+    const auto ux = load_x<KIND>(xv, lr);
 #pragma unroll 2
-  for (uint32_t k = 0; k < m.upl; k++) acc += unit_dot<KIND>(row, drow, lane_in_row + k * m.lpr, xv);
+    for (uint32_t b = r0 + warp * G; b < r1; b += stride) {
+      const uint32_t r = b + slot;
+      float acc = 0.f;
+      if (r < r1) {
+        const uint8_t* row;
+        const __half* drow;
+        addr(r, &row, &drow);
+        acc = unit_dot<KIND, S>(row, drow, lr, ux);
+      }
+      acc = group_sum(acc, lpr);
+      if (lr == 0 && r < r1) emit(r, acc);
+    }
+  } else {
+#pragma unroll 1
+    for (uint32_t b = r0 + warp * G; b < r1; b += stride) {
+      const uint32_t r = b + slot;
+      float acc = 0.f;
+      if (r < r1) {
+        const uint8_t* row;
+        const __half* drow;
+        addr(r, &row, &drow);
+#pragma unroll 1
+        for (uint32_t k = 0; k < m.upl; k++) {
+          const uint32_t u = lr + k * lpr;
+          acc += unit_dot<KIND, S>(row, drow, u, load_x<KIND>(xv, u));
+        }
+      }
+      acc = group_sum(acc, lpr);
+      if (lr == 0 && r < r1) emit(r, acc);
+    }
+  }
+}
+
+// All warps of the block (warp = threadIdx.x/32) or, with explicit arguments, one subset.
+template <bool S, class Addr, class Emit>
+QC_DEV void warp_rows(const MatDesc& m, uint32_t r0, uint32_t r1, const XView& xv, Addr addr, Emit emit,
+                      uint32_t warp = threadIdx.x >> 5, uint32_t nw = blockDim.x >> 5) {
+  switch (m.kind) {
+    case Q4_K: warp_rows_k<Q4_K, S>(m, r0, r1, xv, addr, emit, warp, nw); break;
+    case Q5_K: warp_rows_k<Q5_K, S>(m, r0, r1, xv, addr, emit, warp, nw); break;
+    case Q6_K: warp_rows_k<Q6_K, S>(m, r0, r1, xv, addr, emit, warp, nw); break;
+    case Q8_0: warp_rows_k<Q8_0, S>(m, r0, r1, xv, addr, emit, warp, nw); break;
+    case Q4_0: warp_rows_k<Q4_0, S>(m, r0, r1, xv, addr, emit, warp, nw); break;
+    case F16: warp_rows_k<F16, S>(m, r0, r1, xv, addr, emit, warp, nw); break;
+    default: warp_rows_k<F32, S>(m, r0, r1, xv, addr, emit, warp, nw); break;
+  }
+}
+// Rows of a matrix held in shared memory from row `rbase` on.
+struct SmemRows {
+  const MatDesc* m;
+  const uint8_t* base;
+  uint32_t rbase;
+  QC_DEV void operator()(uint32_t r, const uint8_t** row, const __half** drow) const {
+    *row = row_ptr(*m, base, r - rbase);
+    *drow = drow_ptr(*m, base, r - rbase);
+  }
+};
+
+// One row's partial for lane lr of its lpr-lane group (units lr, lr+lpr, ...).
+template <bool S>
+QC_DEV float row_partial(const MatDesc& m, const uint8_t* row, const __half* drow, uint32_t lr, const XView& xv) {
+  float acc = 0.f;
+  for (uint32_t k = 0; k < m.upl; k++) {
+    const uint32_t u = lr + k * m.lpr;
+    switch (m.kind) {
+      case Q4_K: acc += unit_q4k<S>(row, u, load_unit_x(xv, u)); break;
+      case Q5_K: acc += unit_q5k<S>(row, u, load_unit_x(xv, u)); break;
+      case Q6_K: acc += unit_q6k<S>(row, drow, u, load_unit_x(xv, u)); break;
+      case Q8_0: acc += unit_q80<S>(row, drow, u, load_unit_x(xv, u)); break;
+      case Q4_0: acc += unit_q40<S>(row, drow, u, load_unit_x(xv, u)); break;
+      case F16: acc += unit_f16<S>(row, u, load_unit_xf(xv, u)); break;
+      default: acc += unit_f32<S>(row, u, load_unit_xf(xv, u)); break;
+    }
+  }
   return acc;
 }
 
-QC_DEV float row_partial(const MatDesc& m, uint32_t e, uint32_t r, uint32_t lane_in_row, const XView& xv) {
-  switch (m.kind) {
-    case Q4_K: return row_partial_k<Q4_K>(m, e, r, lane_in_row, xv);
-    case Q5_K: return row_partial_k<Q5_K>(m, e, r, lane_in_row, xv);
-    case Q6_K: return row_partial_k<Q6_K>(m, e, r, lane_in_row, xv);
-    case Q8_0: return row_partial_k<Q8_0>(m, e, r, lane_in_row, xv);
-    case Q4_0: return row_partial_k<Q4_0>(m, e, r, lane_in_row, xv);
-    case F16: return row_partial_k<F16>(m, e, r, lane_in_row, xv);
-    default: return row_partial_k<F32>(m, e, r, lane_in_row, xv);
-  }
+// ---------------------------------------------------------------------------
+// Asynchronous global -> shared copies (cp.async, 16 bytes per request).
+QC_DEV void cp16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+QC_DEV void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+QC_DEV void cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+template <int N>
+QC_DEV void cp_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// Copy `bytes` (a multiple of 16; both addresses 16-byte aligned) with all threads of the block.
+QC_DEV void copy_async(uint8_t* dst, const uint8_t* src, uint64_t bytes) {
+  for (uint64_t o = threadIdx.x * 16ull; o < bytes; o += blockDim.x * 16ull) cp16(dst + o, src + o);
+}
+// Copy row groups [g0, g1) of expert e of m to dst.
+QC_DEV void copy_groups(uint8_t* dst, const MatDesc& m, uint32_t e, uint32_t g0, uint32_t g1) {
+  if (g1 > g0) copy_async(dst, expert_base(m, e) + (uint64_t)g0 * m.group_bytes, (uint64_t)(g1 - g0) * m.group_bytes);
 }
 
 }  // namespace qc

@@ -72,12 +72,12 @@ struct TensorIn {
 
 uint64_t align256(uint64_t v) { return (v + 255) & ~255ull; }
 
-// Device placement of one tensor: main plane, d plane, and (for vectors) an f32 copy.
+// Device placement of one tensor (8-row-group layout) and, for vectors, an f32 copy.
 struct Placed {
   const TensorIn* t = nullptr;
   uint64_t rows = 1, experts = 1, cols = 0;
   qc::DevLayout lay;
-  uint64_t off_main = 0, off_d = 0, off_f32 = 0;
+  uint64_t off = 0, off_f32 = 0;
   bool vector = false;
 };
 
@@ -97,21 +97,21 @@ class Uploader {
     cudaFree(buf_[0]);
     cudaFree(buf_[1]);
   }
-  // rows x raw_row bytes from host `src`, repacked for kind/cols into dst / dplane.
-  uint64_t put(const uint8_t* src, uint64_t rows, uint64_t raw_row, uint32_t kind, uint64_t cols, uint8_t* dst,
-               uint64_t row_stride, __half* dplane, uint64_t d_stride) {
+  // `n_rows` raw rows (all experts, expert-major; `rows` per expert) of `raw_row` bytes
+  // from host `src`, repacked into the 8-row-group layout at dst.
+  uint64_t put(const uint8_t* src, uint64_t n_rows, uint32_t rows, uint64_t raw_row, uint32_t kind, uint64_t cols,
+               uint8_t* dst, const qc::DevLayout& lay, uint64_t expert_stride) {
     const uint64_t per = cap_ / raw_row;
     uint64_t done = 0;
-    while (done < rows) {
-      const uint64_t n = rows - done < per ? rows - done : per;
+    while (done < n_rows) {
+      const uint64_t n = n_rows - done < per ? n_rows - done : per;
       uint8_t* b = buf_[k_++ & 1];
       QC_CK(cudaMemcpyAsync(b, src + done * raw_row, n * raw_row, cudaMemcpyHostToDevice, s_));
-      qc::launch_repack(b, n, raw_row, kind, cols, dst + done * row_stride, row_stride,
-                        dplane ? dplane + done * d_stride : nullptr, d_stride, s_);
+      qc::launch_repack(b, done, n, rows, raw_row, kind, cols, dst, lay, expert_stride, s_);
       QC_CK(cudaGetLastError());
       done += n;
     }
-    return rows * raw_row;
+    return n_rows * raw_row;
   }
 
  private:
@@ -121,21 +121,23 @@ class Uploader {
   unsigned k_ = 0;
 };
 
-qc::MatDesc make_desc(const Placed& p, uint8_t* base) {
+qc::MatDesc desc_of(uint32_t kind, uint64_t rows, uint64_t cols, const qc::DevLayout& lay, const uint8_t* w) {
   qc::MatDesc m{};
-  m.w = base + p.off_main;
-  m.d = p.lay.d_stride ? reinterpret_cast<const __half*>(base + p.off_d) : nullptr;
-  m.kind = p.t->kind;
-  m.rows = (uint32_t)p.rows;
-  m.cols = (uint32_t)p.cols;
-  m.units = p.lay.units;
-  m.lpr = p.lay.lpr;
-  m.upl = p.lay.upl;
-  m.row_stride = p.lay.row_stride;
-  m.d_stride = p.lay.d_stride;
-  m.expert_stride = p.rows * p.lay.row_stride;
-  m.d_expert_stride = p.rows * p.lay.d_stride;
+  m.w = w;
+  m.kind = kind;
+  m.rows = (uint32_t)rows;
+  m.cols = (uint32_t)cols;
+  m.units = lay.units;
+  m.lpr = lay.lpr;
+  m.upl = lay.upl;
+  m.main_bytes = (uint32_t)lay.main_bytes;
+  m.d_bytes = (uint32_t)lay.d_bytes;
+  m.group_bytes = (uint32_t)lay.group_bytes;
+  m.expert_stride = lay.expert_bytes(rows);
   return m;
+}
+qc::MatDesc make_desc(const Placed& p, uint8_t* base) {
+  return desc_of(p.t->kind, p.rows, p.cols, p.lay, base + p.off);
 }
 
 // Same matrix, processed with `lpr` lanes per row (a power of two dividing units).
@@ -163,6 +165,7 @@ struct qc_engine {
   const float* out_norm = nullptr;
   qc::Scratch sc{};
   qc::DecodeDims dims{};
+  qc::StepPlan plan{};
   uint32_t* d_gen = nullptr;
   cudaStream_t own = nullptr, stream = nullptr;
   cudaGraph_t graph = nullptr;
@@ -198,9 +201,10 @@ struct qc_engine {
                std::isfinite(c.theta) && c.theta > 0.f,
            "invalid Qwen3 MoE config");
     // limits of this engine's kernels (shared-memory tiles), beyond the reference's own checks
-    ensure(c.head_dim <= 256, "head_dim > 256 is not supported by the CUDA engine");
+    ensure(c.head_dim <= 256 && c.head_dim % 4 == 0, "the CUDA engine needs head_dim a multiple of 4, at most 256");
     ensure(c.heads / c.kvheads <= 64 && c.kvheads <= 64, "more than 64 query heads per KV head or KV heads");
     ensure(c.top <= 64, "more than 64 experts per token is not supported by the CUDA engine");
+    ensure(c.hidden <= 8192, "hidden size above 8192 is not supported by the CUDA engine");
   }
 
   void check_shape(const std::map<std::string, TensorIn>& t, const std::string& n, std::vector<uint64_t> shape) {
@@ -277,12 +281,9 @@ struct qc_engine {
       ensure(p.rows <= 0xffffffffull && p.cols <= 0xffffffffull, n + ": tensor too large");
       max_row = raw_row > max_row ? raw_row : max_row;
       p.lay = qc::dev_layout(ti.kind, p.cols);
-      p.off_main = off;
-      off = align256(off + p.lay.main_bytes(p.rows) * p.experts);
-      if (p.lay.d_stride) {
-        p.off_d = off;
-        off = align256(off + p.lay.d_bytes(p.rows) * p.experts);
-      }
+      ensure(p.lay.group_bytes <= 0xffffffffull, n + ": rows too wide");
+      p.off = off;
+      off = align256(off + p.lay.expert_bytes(p.rows) * p.experts);
       if (p.vector) {
         p.off_f32 = off;
         off = align256(off + p.cols * sizeof(float));
@@ -291,16 +292,15 @@ struct qc_engine {
     }
     weight_bytes = off;
     QC_CK(cudaMalloc(&d_weights, weight_bytes));
+    QC_CK(cudaMemsetAsync(d_weights, 0, weight_bytes, stream));  // padding rows and blocks read as zero
     {
       Uploader up(stream, max_row);
       for (const std::string& n : names) {
         const Placed& p = placed[n];
         uint64_t raw_row;
         qc::ggml_row_bytes(p.t->kind, p.cols, &raw_row);
-        stats.uploaded_bytes +=
-            up.put(p.t->data, p.rows * p.experts, raw_row, p.t->kind, p.cols, d_weights + p.off_main,
-                   p.lay.row_stride, p.lay.d_stride ? reinterpret_cast<__half*>(d_weights + p.off_d) : nullptr,
-                   p.lay.d_stride);
+        stats.uploaded_bytes += up.put(p.t->data, p.rows * p.experts, (uint32_t)p.rows, raw_row, p.t->kind, p.cols,
+                                       d_weights + p.off, p.lay, p.lay.expert_bytes(p.rows));
         if (p.vector) {
           qc::launch_dequant(make_desc(p, d_weights), 0, reinterpret_cast<float*>(d_weights + p.off_f32), stream);
           QC_CK(cudaGetLastError());
@@ -357,7 +357,7 @@ struct qc_engine {
     dims.ctx = context;
     dims.eps = cfg.eps;
     uint32_t nsplit = 32;
-    while ((context + nsplit - 1) / nsplit > 512) nsplit *= 2;
+    while ((context + nsplit - 1) / nsplit > 128) nsplit *= 2;
     dims.nsplit = nsplit;
     const uint64_t G = cfg.heads / cfg.kvheads, QD = (uint64_t)cfg.heads * D, KD = (uint64_t)cfg.kvheads * D;
     uint64_t so = 0;
@@ -366,7 +366,7 @@ struct qc_engine {
       so = align256(so + bytes);
       return o;
     };
-    const uint64_t o_x = take(cfg.hidden * 4), o_xn = take(cfg.hidden * 4), o_qkv = take((QD + 2 * KD) * 4);
+    const uint64_t o_x = take(cfg.hidden * 4), o_qkv = take((QD + 2 * KD) * 4);
     const uint64_t o_attn = take(QD * 4), o_part = take((uint64_t)cfg.kvheads * nsplit * G * (D + 2) * 4);
     const uint64_t o_rl = take(cfg.experts * 4), o_sel = take(cfg.top * 4), o_selw = take(cfg.top * 4);
     const uint64_t o_h = take((uint64_t)cfg.top * cfg.intermediate * 4), o_log = take((uint64_t)cfg.vocab * 4);
@@ -375,7 +375,6 @@ struct qc_engine {
     QC_CK(cudaMalloc(&d_scratch, so));
     QC_CK(cudaMemsetAsync(d_scratch, 0, so, stream));
     sc.x = reinterpret_cast<float*>(d_scratch + o_x);
-    sc.xn = reinterpret_cast<float*>(d_scratch + o_xn);
     sc.qkv = reinterpret_cast<float*>(d_scratch + o_qkv);
     sc.attn = reinterpret_cast<float*>(d_scratch + o_attn);
     sc.part = reinterpret_cast<float*>(d_scratch + o_part);
@@ -406,6 +405,9 @@ struct qc_engine {
     QC_CK(cudaEventCreate(&ev0));
     QC_CK(cudaEventCreate(&ev1));
     QC_CK(cudaStreamSynchronize(stream));
+    plan = qc::plan_step(step_args());
+    ensure(qc::step_smem_max(step_args(), plan) <= (size_t)kMaxSmem,
+           "model dimensions need more shared memory per block than the CUDA engine supports");
     capture();
   }
 
@@ -427,7 +429,7 @@ struct qc_engine {
     cudaStream_t cs;
     QC_CK(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
     QC_CK(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
-    qc::launch_step(step_args(), cs);
+    qc::launch_step(step_args(), plan, cs);
     cudaError_t le = cudaGetLastError();
     cudaError_t ce = cudaStreamEndCapture(cs, &graph);
     cudaStreamDestroy(cs);
@@ -474,7 +476,7 @@ struct qc_engine {
       QC_CK(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
       ProfCtx ctx{this, cudaSuccess};
       QC_CK(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
-      qc::launch_step(step_args(), cs, &qc_engine::prof_hook, &ctx);
+      qc::launch_step(step_args(), plan, cs, &qc_engine::prof_hook, &ctx);
       cudaError_t le = cudaGetLastError();
       cudaError_t ce = cudaStreamEndCapture(cs, &prof_graph);
       cudaStreamDestroy(cs);
@@ -657,6 +659,12 @@ int create_from(const qc::GgufFile& g, const uint8_t* base, uint32_t context, in
 
 }  // namespace
 
+#ifdef QC_TRACE
+namespace qc {
+cudaError_t trace_read(void* host, size_t bytes);
+}
+#endif
+
 extern "C" {
 
 const char* qc_last_error(void) { return g_last_error.c_str(); }
@@ -825,30 +833,18 @@ int qc_matrix_create(uint32_t kind, uint64_t rows, uint64_t cols, uint64_t exper
     std::unique_ptr<qc_matrix> m(new qc_matrix);
     m->device = device;
     const qc::DevLayout lay = qc::dev_layout(kind, cols);
-    const uint64_t main = align256(lay.main_bytes(rows) * experts), dp = align256(lay.d_bytes(rows) * experts);
-    m->bytes = main + dp;
+    ensure(lay.group_bytes <= 0xffffffffull, "rows too wide");
+    m->bytes = align256(lay.expert_bytes(rows) * experts);
     m->packed = len;
     m->experts = experts;
     QC_CK(cudaMalloc(&m->d, m->bytes));
+    QC_CK(cudaMemset(m->d, 0, m->bytes));
     {
       Uploader up(nullptr, raw_row, len);
-      up.put(blocks, rows * experts, raw_row, kind, cols, m->d, lay.row_stride,
-             lay.d_stride ? reinterpret_cast<__half*>(m->d + main) : nullptr, lay.d_stride);
+      up.put(blocks, rows * experts, (uint32_t)rows, raw_row, kind, cols, m->d, lay, lay.expert_bytes(rows));
     }
     QC_CK(cudaDeviceSynchronize());
-    qc::MatDesc& d = m->desc;
-    d.w = m->d;
-    d.d = lay.d_stride ? reinterpret_cast<const __half*>(m->d + main) : nullptr;
-    d.kind = kind;
-    d.rows = (uint32_t)rows;
-    d.cols = (uint32_t)cols;
-    d.units = lay.units;
-    d.lpr = lay.lpr;
-    d.upl = lay.upl;
-    d.row_stride = lay.row_stride;
-    d.d_stride = lay.d_stride;
-    d.expert_stride = rows * lay.row_stride;
-    d.d_expert_stride = rows * lay.d_stride;
+    m->desc = desc_of(kind, rows, cols, lay, m->d);
     *out = m.release();
   });
 }
@@ -883,6 +879,10 @@ int qc_matrix_bytes(const qc_matrix* m, uint64_t* device_bytes, uint64_t* packed
 }
 
 void qc_matrix_destroy(qc_matrix* m) { delete m; }
+
+#ifdef QC_TRACE
+int qc_trace_read(void* host, size_t bytes) { return qc::trace_read(host, bytes) == cudaSuccess ? 0 : 2; }
+#endif
 
 int qc_packed_matvec(uint32_t kind, uint64_t rows, uint64_t cols, const uint8_t* blocks, uint64_t len,
                      const float* x, float* y) {

@@ -4,6 +4,7 @@
 #include <stdint.h>
 
 #include "common.cuh"
+#include "layout.h"
 
 namespace qc {
 
@@ -41,7 +42,6 @@ struct DecodeDims {
 };
 struct Scratch {
   float* x;       // [hidden] residual stream
-  float* xn;      // [hidden] ffn-normalised x (router -> experts)
   float* qkv;     // [heads*D + 2*kvheads*D] raw projections
   float* attn;    // [heads*D] attention output
   float* part;    // [kvheads][nsplit][G][D + 2] attention partials
@@ -53,14 +53,28 @@ struct Scratch {
   const float2* rope;  // [ctx][D/2] (cos, sin)
 };
 
-void launch_repack(const uint8_t* src, uint64_t n_rows, uint64_t raw_row, uint32_t kind, uint64_t cols, uint8_t* dst,
-                   uint64_t row_stride, __half* dplane, uint64_t d_stride, cudaStream_t s);
+void launch_repack(const uint8_t* src, uint64_t flat0, uint64_t n_rows, uint32_t rows, uint64_t raw_row, uint32_t kind,
+                   uint64_t cols, uint8_t* dst, const DevLayout& l, uint64_t expert_stride, cudaStream_t s);
 void launch_dequant(const MatDesc& m, uint32_t e, float* out, cudaStream_t s);
 void launch_matvec(const MatDesc& m, uint32_t e, const float* x, float* y, int sms, cudaStream_t s);
 size_t matvec_smem(const MatDesc& m);
 cudaError_t matvec_prepare(int max_smem);
 
-// One decode step (all kernels of one token) enqueued on `s`.
+// ---- decode step ---------------------------------------------------------------------------
+constexpr uint32_t kMinChunk = 64;                // attention positions per split, at least
+constexpr uint32_t kWeightBudget = 160 * 1024;    // shared-memory weight bytes per block
+constexpr uint32_t kOutStageBudget = 48 * 1024;   // shared-memory bytes per vocab-projection stage
+
+// Positions per attention split held in shared memory, and the kernel's dynamic shared memory.
+__host__ __device__ inline uint32_t attn_cmax(const DecodeDims& d) {
+  const uint32_t c = (d.ctx + d.nsplit - 1) / d.nsplit;
+  return c < kMinChunk ? kMinChunk : c;
+}
+inline size_t attn_smem(const DecodeDims& d) {
+  const uint32_t G = d.heads / d.kvheads, c = attn_cmax(d), kp = d.head_dim + 4;
+  return (size_t)(2 * c * kp + G * kp + G * c + d.head_dim) * sizeof(float);
+}
+
 struct StepArgs {
   DecodeDims dims;
   Scratch sc;
@@ -71,11 +85,23 @@ struct StepArgs {
   const float* out_norm;
   int sms;
 };
+// Grid and per-block work of the per-layer kernels (the same for every layer).
+struct KernelSplit {
+  uint32_t grid, gper, wbytes;  // blocks, row groups per block, shared-memory weight bytes per block
+};
+struct StepPlan {
+  KernelSplit attn_in, oproj, router, gateup, down;
+  uint32_t gateup_bpe;        // gate/up blocks per selected expert
+  uint32_t out_grid, out_sg;  // vocab projection: blocks, groups per pipeline stage
+};
+StepPlan plan_step(const StepArgs& a);
+size_t step_smem_max(const StepArgs& a, const StepPlan& p);
+
 // Kernel kinds of a step, in launch order within a layer.
 enum StepKernel { K_EMBED = 0, K_ATTN_IN, K_ATTENTION, K_OPROJ, K_ROUTER, K_GATEUP, K_DOWN, K_OUTPUT, K_COUNT };
 // Called before each launch of a step with the kernel kind, and once more with K_COUNT after the last.
 typedef void (*StepHook)(void* ctx, int kind, cudaStream_t s);
-void launch_step(const StepArgs& a, cudaStream_t s, StepHook hook = nullptr, void* ctx = nullptr);
+void launch_step(const StepArgs& a, const StepPlan& p, cudaStream_t s, StepHook hook = nullptr, void* ctx = nullptr);
 inline uint32_t step_launches(uint32_t layers) { return 2 + 6 * layers; }
 cudaError_t decode_prepare(int max_smem);
 

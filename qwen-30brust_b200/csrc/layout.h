@@ -30,12 +30,16 @@ inline const char* ggml_row_bytes(uint32_t kind, uint64_t cols, uint64_t* out) {
 }
 
 // Device layout of a (rows x cols) matrix of `kind` (see MatDesc in common.cuh).
+// Rows are stored in groups of 8: [8 rows of blocks][8 rows of d values], so a
+// run of whole groups is one contiguous 16-byte-aligned span (8 * main_bytes and
+// 8 * d_bytes are multiples of 16 for every kind).  Row counts are padded to a
+// multiple of 8 with zero rows.
 struct DevLayout {
-  uint64_t row_stride = 0;  // bytes per row, main plane (multiple of 16)
-  uint64_t d_stride = 0;    // halves per row, d plane (0: no d plane)
+  uint64_t main_bytes = 0;   // block bytes of one row (multiple of 16)
+  uint64_t d_bytes = 0;      // d bytes of one row (0: no d values)
+  uint64_t group_bytes = 0;  // 8 * (main_bytes + d_bytes)
   uint32_t units = 0, lpr = 1, upl = 1;
-  uint64_t main_bytes(uint64_t rows) const { return rows * row_stride; }
-  uint64_t d_bytes(uint64_t rows) const { return rows * d_stride * 2; }
+  uint64_t expert_bytes(uint64_t rows) const { return (rows + 7) / 8 * group_bytes; }
 };
 
 // Every row is processed in units of 64 elements: units = ceil(cols / 64).
@@ -44,20 +48,20 @@ inline DevLayout dev_layout(uint32_t kind, uint64_t cols) {
   const uint64_t units = (cols + 63) / 64;
   l.units = (uint32_t)units;
   switch (kind) {
-    case 12: l.row_stride = cols / 256 * 144; break;
-    case 13: l.row_stride = cols / 256 * 176; break;
-    case 14: l.row_stride = cols / 256 * 208; l.d_stride = cols / 256; break;
-    case 8: l.row_stride = units * 64; l.d_stride = units * 2; break;  // two 32-blocks per unit
-    case 2: l.row_stride = units * 32; l.d_stride = units * 2; break;
-    case 1: l.row_stride = units * 128; break;
-    default: l.row_stride = units * 256; break;
+    case 12: l.main_bytes = cols / 256 * 144; break;
+    case 13: l.main_bytes = cols / 256 * 176; break;
+    case 14: l.main_bytes = cols / 256 * 208; l.d_bytes = cols / 256 * 2; break;
+    case 8: l.main_bytes = units * 64; l.d_bytes = units * 4; break;  // two 32-blocks per unit
+    case 2: l.main_bytes = units * 32; l.d_bytes = units * 4; break;
+    case 1: l.main_bytes = units * 128; break;
+    default: l.main_bytes = units * 256; break;
   }
+  l.group_bytes = 8 * (l.main_bytes + l.d_bytes);
   uint32_t lpr = 1;
   while (lpr < 32 && l.units % (lpr * 2) == 0) lpr *= 2;
   l.lpr = lpr;
   l.upl = l.units / lpr;
   return l;
 }
-
 
 }  // namespace qc

@@ -11,24 +11,29 @@
 namespace qc {
 
 // ---------------------------------------------------------------------------
-// Repack: raw GGUF rows (src, `n_rows` rows of `raw_row` bytes) into the device
-// layout.  One thread per block (quantized kinds) or per 16-byte chunk of the
-// padded output row (F16/F32).
-__global__ void k_repack(const uint8_t* __restrict__ src, uint64_t n_rows, uint64_t raw_row, uint32_t kind,
-                         uint64_t cols, uint8_t* __restrict__ dst, uint64_t row_stride, __half* __restrict__ dplane,
-                         uint64_t d_stride) {
-  uint64_t per_row, valid;  // output blocks (or 16-byte chunks) per row, and how many come from the source
+// Repack: flattened raw GGUF rows [flat0, flat0 + n_rows) of an expert stack
+// (`rows` rows per expert, `raw_row` bytes each, at src) into the 8-row-group
+// device layout at dst (expert 0 base).  One thread per output block (quantized
+// kinds) or per 16-byte chunk of the padded row (F16/F32).  Padding rows and
+// padding blocks are left as they are (the destination is zeroed beforehand).
+__global__ void k_repack(const uint8_t* __restrict__ src, uint64_t flat0, uint64_t n_rows, uint32_t rows,
+                         uint64_t raw_row, uint32_t kind, uint64_t cols, uint8_t* __restrict__ dst, uint32_t main_bytes,
+                         uint32_t d_bytes, uint32_t group_bytes, uint64_t expert_stride) {
+  uint64_t per_row;  // items per row
   switch (kind) {
-    case Q4_K: case Q5_K: case Q6_K: per_row = valid = cols / 256; break;
-    case Q8_0: case Q4_0: per_row = d_stride; valid = cols / 32; break;
-    default: per_row = row_stride / 16; valid = per_row; break;
+    case Q4_K: case Q5_K: case Q6_K: per_row = cols / 256; break;
+    case Q8_0: case Q4_0: per_row = cols / 32; break;
+    default: per_row = main_bytes / 16; break;
   }
   const uint64_t total = n_rows * per_row;
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
-    const uint64_t r = i / per_row, k = i % per_row;
-    const uint8_t* s = src + r * raw_row;
-    uint8_t* o = dst + r * row_stride;
-    const bool pad = k >= valid;
+    const uint64_t fr = i / per_row, k = i % per_row;
+    const uint64_t flat = flat0 + fr;
+    const uint32_t e = (uint32_t)(flat / rows), r = (uint32_t)(flat % rows);
+    const uint8_t* s = src + fr * raw_row;
+    uint8_t* g = dst + e * expert_stride + (uint64_t)(r >> 3) * group_bytes;
+    uint8_t* o = g + (r & 7) * main_bytes;
+    uint8_t* dd = g + 8 * main_bytes + (r & 7) * d_bytes;
     switch (kind) {
       case Q4_K:
         for (int j = 0; j < 144; j++) o[k * 144 + j] = s[k * 144 + j];
@@ -38,20 +43,21 @@ __global__ void k_repack(const uint8_t* __restrict__ src, uint64_t n_rows, uint6
         break;
       case Q6_K:
         for (int j = 0; j < 208; j++) o[k * 208 + j] = s[k * 210 + j];
-        dplane[r * d_stride + k] = __ushort_as_half((unsigned short)(s[k * 210 + 208] | (s[k * 210 + 209] << 8)));
+        dd[2 * k] = s[k * 210 + 208];
+        dd[2 * k + 1] = s[k * 210 + 209];
         break;
       case Q8_0:
-        for (int j = 0; j < 32; j++) o[k * 32 + j] = pad ? 0 : s[k * 34 + 2 + j];
-        dplane[r * d_stride + k] =
-            __ushort_as_half(pad ? (unsigned short)0 : (unsigned short)(s[k * 34] | (s[k * 34 + 1] << 8)));
+        for (int j = 0; j < 32; j++) o[k * 32 + j] = s[k * 34 + 2 + j];
+        dd[2 * k] = s[k * 34];
+        dd[2 * k + 1] = s[k * 34 + 1];
         break;
       case Q4_0:
-        for (int j = 0; j < 16; j++) o[k * 16 + j] = pad ? 0 : s[k * 18 + 2 + j];
-        dplane[r * d_stride + k] =
-            __ushort_as_half(pad ? (unsigned short)0 : (unsigned short)(s[k * 18] | (s[k * 18 + 1] << 8)));
+        for (int j = 0; j < 16; j++) o[k * 16 + j] = s[k * 18 + 2 + j];
+        dd[2 * k] = s[k * 18];
+        dd[2 * k + 1] = s[k * 18 + 1];
         break;
       default: {  // F16 / F32: 16-byte chunk k of the padded row
-        const uint64_t esz = kind == F16 ? 2 : 4, nbytes = cols * esz;
+        const uint64_t nbytes = cols * (kind == F16 ? 2 : 4);
         for (int j = 0; j < 16; j++) {
           const uint64_t b = k * 16 + j;
           o[b] = b < nbytes ? s[b] : 0;
@@ -64,63 +70,91 @@ __global__ void k_repack(const uint8_t* __restrict__ src, uint64_t n_rows, uint6
 // Bit-exact dequant of expert `e` (all rows) to out[r*cols + c] (reference quant.rs:36-80).
 __global__ void k_dequant(MatDesc m, uint32_t e, float* __restrict__ out) {
   const uint64_t total = (uint64_t)m.rows * m.cols;
+  const uint8_t* base = expert_base(m, e);
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
     const uint32_t r = (uint32_t)(i / m.cols), c = (uint32_t)(i % m.cols);
-    const uint8_t* row = m.w + e * m.expert_stride + (uint64_t)r * m.row_stride;
-    const __half* drow = m.d ? m.d + e * m.d_expert_stride + (uint64_t)r * m.d_stride : nullptr;
-    out[i] = dequant_one(m, row, drow, c);
+    out[i] = dequant_one(m, row_ptr(m, base, r), drow_ptr(m, base, r), c);
   }
 }
 
-// y = W_e x.  Each warp takes 32/lpr rows at a time; lpr lanes share a row.
+// y = W_e x, rows streamed through shared memory: each block takes a contiguous
+// run of 8-row groups and pipelines it in stages of `sg` groups (cp.async,
+// kStages deep); warps then walk the rows of a stage, lpr lanes per row.
+constexpr int kStages = 3;
+
 template <uint32_t KIND>
-__global__ void __launch_bounds__(256) k_matvec(MatDesc m, uint32_t e, const float* __restrict__ x,
-                                                float* __restrict__ y) {
+__global__ void __launch_bounds__(512) k_matvec(MatDesc m, uint32_t e, const float* __restrict__ x,
+                                                float* __restrict__ y, uint32_t sg) {
   extern __shared__ __align__(16) uint8_t smem[];
-  const XView xv = stage_x(smem, m.cols, m.units, uses_float_x(KIND), [&](uint32_t i) { return x[i]; });
-  const uint32_t lane = threadIdx.x & 31, lpr = m.lpr, G = 32 / lpr;
-  const uint32_t wpb = blockDim.x >> 5;
-  const uint32_t gw = blockIdx.x * wpb + (threadIdx.x >> 5), nw = gridDim.x * wpb;
-  for (uint32_t base = gw * G; base < m.rows; base += nw * G) {
-    const uint32_t r = base + lane / lpr, lr = lane % lpr;
-    float p = r < m.rows ? row_partial_k<KIND>(m, e, r, lr, xv) : 0.f;
-    p = group_sum(p, lpr);
-    if (lr == 0 && r < m.rows) y[r] = p;
+  const uint32_t groups = (m.rows + 7) / 8;
+  const uint32_t per = (groups + gridDim.x - 1) / gridDim.x;
+  const uint32_t g0 = min(groups, blockIdx.x * per), g1 = min(groups, g0 + per);
+  const uint32_t nst = (g1 - g0 + sg - 1) / sg;
+  const uint64_t stage_bytes = (uint64_t)sg * m.group_bytes;
+  uint8_t* buf = smem;
+  uint8_t* xmem = smem + kStages * stage_bytes;
+  for (uint32_t k = 0; k < kStages - 1; k++) {
+    if (k < nst) copy_groups(buf + (k % kStages) * stage_bytes, m, e, g0 + k * sg, min(g1, g0 + (k + 1) * sg));
+    cp_commit();
+  }
+  __shared__ float red[32];
+  stage_vectors<false>(xmem, 1, m.cols, m.units, uses_float_x(KIND), [&](uint32_t, uint32_t i) { return x[i]; },
+                       nullptr, 0.f, red);
+  const XView xv = xview_at(xmem, m.units, uses_float_x(KIND));
+  for (uint32_t k = 0; k < nst; k++) {
+    const uint32_t kn = k + kStages - 1;
+    if (kn < nst) copy_groups(buf + (kn % kStages) * stage_bytes, m, e, g0 + kn * sg, min(g1, g0 + (kn + 1) * sg));
+    cp_commit();
+    cp_wait<kStages - 1>();
+    __syncthreads();
+    const uint8_t* sb = buf + (k % kStages) * stage_bytes;
+    const uint32_t r0 = (g0 + k * sg) * 8, r1 = min(m.rows, min(g1, g0 + (k + 1) * sg) * 8);
+    warp_rows_k<KIND, true>(m, r0, r1, xv, SmemRows{&m, sb, r0}, [&](uint32_t r, float v) { y[r] = v; },
+                            threadIdx.x >> 5, blockDim.x >> 5);
+    __syncthreads();
   }
 }
 
 // ---------------------------------------------------------------------------
-void launch_repack(const uint8_t* src, uint64_t n_rows, uint64_t raw_row, uint32_t kind, uint64_t cols, uint8_t* dst,
-                   uint64_t row_stride, __half* dplane, uint64_t d_stride, cudaStream_t s) {
-  k_repack<<<148 * 8, 256, 0, s>>>(src, n_rows, raw_row, kind, cols, dst, row_stride, dplane, d_stride);
+void launch_repack(const uint8_t* src, uint64_t flat0, uint64_t n_rows, uint32_t rows, uint64_t raw_row, uint32_t kind,
+                   uint64_t cols, uint8_t* dst, const DevLayout& l, uint64_t expert_stride, cudaStream_t s) {
+  k_repack<<<148 * 8, 256, 0, s>>>(src, flat0, n_rows, rows, raw_row, kind, cols, dst, (uint32_t)l.main_bytes,
+                                   (uint32_t)l.d_bytes, (uint32_t)l.group_bytes, expert_stride);
 }
 
 void launch_dequant(const MatDesc& m, uint32_t e, float* out, cudaStream_t s) {
   k_dequant<<<148 * 8, 256, 0, s>>>(m, e, out);
 }
 
-uint32_t matvec_grid(const MatDesc& m, int sms) {
-  const uint32_t rows_per_block = 8 * (32 / m.lpr);
-  uint32_t need = (m.rows + rows_per_block - 1) / rows_per_block;
-  uint32_t cap = (uint32_t)sms * 8;
-  return need < cap ? need : cap;
+// Stage size in groups and total dynamic shared memory of k_matvec.
+static uint32_t matvec_stage_groups(const MatDesc& m) {
+  const uint64_t budget = 48 * 1024;
+  const uint64_t sg = budget / m.group_bytes;
+  return (uint32_t)(sg < 1 ? 1 : (sg > 8 ? 8 : sg));
+}
+
+size_t matvec_smem(const MatDesc& m) {
+  return (size_t)kStages * matvec_stage_groups(m) * m.group_bytes + xview_bytes(m.units, uses_float_x(m.kind));
 }
 
 void launch_matvec(const MatDesc& m, uint32_t e, const float* x, float* y, int sms, cudaStream_t s) {
-  const uint32_t grid = matvec_grid(m, sms);
+  const uint32_t groups = (m.rows + 7) / 8;
+  const uint32_t sg = matvec_stage_groups(m);
+  // enough blocks to cover the SMs, but each with at least one full stage of work
+  uint32_t grid = (groups + sg - 1) / sg;
+  grid = grid < (uint32_t)sms ? grid : (uint32_t)sms;
+  grid = grid < 1 ? 1 : grid;
   const size_t smem = matvec_smem(m);
   switch (m.kind) {
-    case Q4_K: k_matvec<Q4_K><<<grid, 256, smem, s>>>(m, e, x, y); break;
-    case Q5_K: k_matvec<Q5_K><<<grid, 256, smem, s>>>(m, e, x, y); break;
-    case Q6_K: k_matvec<Q6_K><<<grid, 256, smem, s>>>(m, e, x, y); break;
-    case Q8_0: k_matvec<Q8_0><<<grid, 256, smem, s>>>(m, e, x, y); break;
-    case Q4_0: k_matvec<Q4_0><<<grid, 256, smem, s>>>(m, e, x, y); break;
-    case F16: k_matvec<F16><<<grid, 256, smem, s>>>(m, e, x, y); break;
-    default: k_matvec<F32><<<grid, 256, smem, s>>>(m, e, x, y); break;
+    case Q4_K: k_matvec<Q4_K><<<grid, 512, smem, s>>>(m, e, x, y, sg); break;
+    case Q5_K: k_matvec<Q5_K><<<grid, 512, smem, s>>>(m, e, x, y, sg); break;
+    case Q6_K: k_matvec<Q6_K><<<grid, 512, smem, s>>>(m, e, x, y, sg); break;
+    case Q8_0: k_matvec<Q8_0><<<grid, 512, smem, s>>>(m, e, x, y, sg); break;
+    case Q4_0: k_matvec<Q4_0><<<grid, 512, smem, s>>>(m, e, x, y, sg); break;
+    case F16: k_matvec<F16><<<grid, 512, smem, s>>>(m, e, x, y, sg); break;
+    default: k_matvec<F32><<<grid, 512, smem, s>>>(m, e, x, y, sg); break;
   }
 }
-
-size_t matvec_smem(const MatDesc& m) { return xview_bytes(m.units, uses_float_x(m.kind)); }
 
 cudaError_t matvec_prepare(int max_smem) {
   cudaError_t err = cudaSuccess;
