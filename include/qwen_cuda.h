@@ -162,6 +162,18 @@ void qc_matrix_destroy(qc_matrix* m);
 int qc_packed_matvec(uint32_t kind, uint64_t rows, uint64_t cols, const uint8_t* blocks, uint64_t len,
                      const float* x, float* y);
 
+/* Allocation-free variant of qc_packed_matvec; it has no counterpart in the
+ * reference.  For callers that may not allocate device memory: a host whose
+ * own allocator has reserved the GPU's memory, or code that must not call
+ * cudaFree (it may synchronize the whole device).  All device working memory
+ * (raw blocks, the repacked matrix, x and y) lives in one static 32 MiB
+ * __device__ array per GPU, held until the process exits; larger matrices are
+ * rejected with QC_ERR_INVALID.  The first call on a device (the current one)
+ * looks up the array's address and sets kernel attributes — make it before any
+ * stream capture.  Calls share the array: calls that overlap on the GPU race. */
+int qc_packed_matvec_noalloc(uint32_t kind, uint64_t rows, uint64_t cols, const uint8_t* blocks, uint64_t len,
+                             const float* x, float* y);
+
 #ifdef __cplusplus
 }
 #endif

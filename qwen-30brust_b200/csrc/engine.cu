@@ -665,6 +665,11 @@ cudaError_t trace_read(void* host, size_t bytes);
 }
 #endif
 
+namespace qc {
+// Sets the thread-local message returned by qc_last_error() (used by noalloc.cu).
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+}  // namespace qc
+
 extern "C" {
 
 const char* qc_last_error(void) { return g_last_error.c_str(); }

@@ -27,7 +27,7 @@ EXPORTS = (
     "qc_last_error", "qc_engine_config", "qc_engine_set_stream", "qc_forward", "qc_forward_tokens",
     "qc_decode_greedy", "qc_decode_enqueue", "qc_sync", "qc_reset", "qc_position", "qc_get_stats",
     "qc_logits_device", "qc_row_bytes", "qc_matrix_create", "qc_matrix_matvec", "qc_matrix_dequant",
-    "qc_matrix_bytes", "qc_matrix_destroy", "qc_packed_matvec", "qc_profile_step",
+    "qc_matrix_bytes", "qc_matrix_destroy", "qc_packed_matvec", "qc_profile_step", "qc_packed_matvec_noalloc",
 )
 
 
@@ -108,6 +108,7 @@ def lib() -> C.CDLL:
         L.qc_matrix_destroy.restype = None
         L.qc_packed_matvec.argtypes = [u32, u64, u64, vp, u64, vp, vp]
         L.qc_profile_step.argtypes = [vp, C.POINTER(PhaseTimes)]
+        L.qc_packed_matvec_noalloc.argtypes = [u32, u64, u64, vp, u64, vp, vp]
         _lib = L
     return _lib
 
@@ -294,4 +295,16 @@ def packed_matvec(kind: int, rows: int, cols: int, blocks, x) -> np.ndarray:
     xx = np.ascontiguousarray(x, dtype=np.float32)
     y = np.empty(rows, dtype=np.float32)
     _global_check(lib().qc_packed_matvec(kind, rows, cols, b.ctypes.data, b.size, xx.ctypes.data, y.ctypes.data))
+    return y
+
+
+def packed_matvec_noalloc(kind: int, rows: int, cols: int, blocks, x) -> np.ndarray:
+    """qc_packed_matvec_noalloc: as packed_matvec, with no device allocation — for hosts
+    whose allocator owns the GPU's memory or that must not call cudaFree.  Working memory
+    is one static 32 MiB array per GPU shared by all calls (overlapping calls race)."""
+    b = _u8(blocks)
+    xx = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(rows, dtype=np.float32)
+    _global_check(lib().qc_packed_matvec_noalloc(kind, rows, cols, b.ctypes.data, b.size, xx.ctypes.data,
+                                                 y.ctypes.data))
     return y

@@ -1,0 +1,61 @@
+"""qc_packed_matvec_noalloc, the allocation-free packed matvec.
+
+It serves callers that may not allocate device memory (a host whose own
+allocator has reserved the GPU's memory, or code that must not call cudaFree,
+which may synchronize the device).  Its working memory is one static
+__device__ array per GPU shared by every call, so these tests check that two
+calls in a row — with different shapes before them, leaving other contents in
+the array — agree with qc_packed_matvec within the matvec tolerance, that the
+calls allocate nothing, and that oversized matrices are refused.  The file is
+named to run last.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+# (kind, rows, cols): formats with padding (Q8_0/Q4_0 odd block counts, F16/F32 odd
+# widths, row counts not a multiple of 8) after wider ones, so stale contents would show.
+CASES = [(1, 96, 1000), (12, 300, 512), (14, 64, 768), (8, 33, 96), (2, 65, 96), (1, 5, 40), (0, 70, 7),
+         (13, 17, 256)]
+
+
+def _check_rel(y, ref, what):
+    scale = float(np.abs(ref).max())
+    err = np.abs(y - ref)
+    assert err.max() <= 1e-4 * scale, f"{what}: vector rel {err.max() / scale:.3e}"
+    assert not (err > 1e-4 * np.abs(ref) + 1e-6 * scale).any(), what
+
+
+def test_noalloc_matches_packed_matvec_on_two_calls(cuda_engine, tools):
+    for kind, rows, cols in CASES:
+        blocks = tools.random_matrix(kind, rows, cols, seed=9, stream=kind * 1000 + rows, std=0.02)
+        for call in range(2):
+            x = tools.normal(9, 17 + call, cols)
+            ref = cuda_engine.packed_matvec(kind, rows, cols, blocks, x)
+            got = cuda_engine.packed_matvec_noalloc(kind, rows, cols, blocks, x)
+            _check_rel(got, ref, f"kind={kind} rows={rows} cols={cols} call={call}")
+
+
+def test_noalloc_allocates_nothing(cuda_engine, tools, torch_cuda):
+    torch = torch_cuda
+    kind, rows, cols = 12, 256, 2048
+    blocks = tools.random_matrix(kind, rows, cols, seed=3, stream=5, std=0.02)
+    x = tools.normal(3, 6, cols)
+    cuda_engine.packed_matvec_noalloc(kind, rows, cols, blocks, x)  # first call: per-device set-up
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(4):
+        cuda_engine.packed_matvec_noalloc(kind, rows, cols, blocks, x)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+
+
+def test_noalloc_refuses_matrices_beyond_its_scratch(cuda_engine):
+    rows, cols = 16384, 2048  # F16: 64 MiB of raw blocks alone
+    blocks = np.zeros(rows * cols * 2, dtype=np.uint8)
+    with pytest.raises(cuda_engine.QwenCudaError, match="at most"):
+        cuda_engine.packed_matvec_noalloc(1, rows, cols, blocks, np.zeros(cols, dtype=np.float32))
+    with pytest.raises(cuda_engine.QwenCudaError, match="shape mismatch"):
+        cuda_engine.packed_matvec_noalloc(12, 2, 256, np.zeros(144, dtype=np.uint8), np.zeros(256, dtype=np.float32))
