@@ -202,7 +202,9 @@ def run_ours(args) -> None:
     img, path = synth_image(T, spec, rank, world)
     t = time.time()
     eng = E.Engine(path if path is not None else img, CTX, device=local)
-    log(f"rank {rank}: engine up in {time.time() - t:.1f} s")
+    eng.set_decode_mode(args.decode_mode)
+    decode_path = eng.decode_path
+    log(f"rank {rank}: engine up in {time.time() - t:.1f} s; decode path {decode_path}")
     stream = torch.cuda.Stream()  # a real stream: NULL would mean the engine's own stream
     torch.cuda.set_stream(stream)
     eng.set_stream(stream.cuda_stream)
@@ -263,12 +265,18 @@ def run_ours(args) -> None:
         b = model_bytes(spec, T, pos0, args.steps)
         step_ms = ms / args.steps
         value = args.steps * world / (ms / 1e3)
-        # dominant kernel of the step by device time (per-kernel CUDA events in a captured step graph)
         kinds = [k for k in E.PHASES]
-        dom = max(kinds, key=lambda k: phases[k])
-        launches = 1 if dom in ("embed", "output") else spec.layers
-        dom_ms = phases[dom] / launches
-        dom_bytes = b["per_kernel"][dom]
+        if phases["launches"] == 1:
+            # the whole-token kernel is the step: its bytes are the token's, its duration the timed average
+            dom, dom_ms, dom_bytes = "token", step_ms, b["per_token"]
+            phases_ms = {"token": phases["token"]}
+        else:
+            # dominant kernel of the step by device time (per-kernel CUDA events in a captured step graph)
+            dom = max(kinds, key=lambda k: phases[k])
+            launches = 1 if dom in ("embed", "output") else spec.layers
+            dom_ms = phases[dom] / launches
+            dom_bytes = b["per_kernel"][dom]
+            phases_ms = {k: phases[k] for k in kinds}
         achieved = dom_bytes / (dom_ms / 1e3) / 1e9
         step_gbs = b["per_token"] / (step_ms / 1e3) / 1e9
         cpu = None
@@ -298,7 +306,9 @@ def run_ours(args) -> None:
             "roofline": {"kernel": f"k_{dom}", "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / pk["hbm_gbs"], "traffic": None,
                          "bytes_per_launch": dom_bytes, "ms_per_launch": dom_ms, "peak_source": pk["source"]},
-            "phases_ms": {k: phases[k] for k in kinds},
+            "phases_ms": phases_ms,
+            "decode_path": "whole-token kernel (1 launch per token)" if decode_path[0] == 0
+                           else f"per-phase kernels ({phases['launches']} launches per token)",
             "e2e": {"value": k2 * world / (ms_e2e / 1e3), "unit": "tok/s", "steps": k2,
                     "h2d_bytes_per_step": 4, "d2h_bytes_per_step": spec.vocab * 4 + 8,
                     "wall_tok_s": k2 / wall_e2e,
@@ -363,6 +373,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-tokens", type=int, default=2, help="tokens timed for the CPU baseline line")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode-mode", type=int, default=0, choices=[0, 1],
+                    help="0: whole-token kernel when the model fits it (default); 1: per-phase kernels")
     ap.add_argument("--ref-max-steps", type=int, default=8)
     args = ap.parse_args()
     if args.warmup < 3:

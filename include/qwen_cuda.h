@@ -133,9 +133,20 @@ int qc_get_stats(const qc_engine* e, qc_stats* out);
  * of the previous step (token 0 at position 0) and advances the position. */
 typedef struct qc_phase_times {
   double embed_ms, attn_in_ms, attention_ms, oproj_ms, router_ms, gateup_ms, down_ms, output_ms;
-  uint32_t launches; /* kernels in one step: 2 + 6*layers */
+  uint32_t launches; /* kernels in one step: 1 (whole-token kernel) or 2 + 6*layers (per-phase kernels) */
+  double token_ms;   /* the whole step; with the whole-token kernel the per-kernel fields stay 0 */
 } qc_phase_times;
 int qc_profile_step(qc_engine* e, qc_phase_times* out);
+
+/* Decode path (no counterpart in the reference, which has one CPU path per token).
+ * mode 0 (default): the whole-token persistent kernel, one launch per token,
+ * whenever the model's per-SM weight slices fit in shared memory, else the
+ * per-phase kernels; mode 1: always the per-phase kernels (2 + 6*layers
+ * launches per token).  Both compute the same forward. */
+int qc_engine_set_decode_mode(qc_engine* e, int mode);
+/* The path in use (0 whole-token kernel, 1 per-phase kernels) and, when the
+ * whole-token kernel cannot be used, why (`why` may be NULL; "" when it fits). */
+int qc_engine_decode_path(const qc_engine* e, int* path, const char** why);
 
 /* Device pointer of the logits of the latest step (vocab floats). */
 int qc_logits_device(const qc_engine* e, const float** out);

@@ -106,6 +106,25 @@ QC_DEV float block_sum(float v, float* red) {
   return t;
 }
 
+// Per-head RMSNorm + NeoX RoPE of one head vector held in shared memory by one warp.
+QC_DEV void head_norm_rope(float* v, const float* __restrict__ w, uint32_t D, float eps, const float2* __restrict__ cs) {
+  const uint32_t lane = threadIdx.x & 31;
+  float ss = 0.f;
+  for (uint32_t i = lane; i < D; i += 32) ss = fmaf(v[i], v[i], ss);
+  ss = warp_sum(ss);
+  const float s = 1.0f / sqrtf(ss / (float)D + eps);
+  for (uint32_t i = lane; i < D; i += 32) v[i] = __fmul_rn(v[i], __fmul_rn(s, w[i]));
+  __syncwarp();
+  // ops.rs:17-28: (a, b) -> (a c - b s, a s + b c) for pairs (i, i + D/2)
+  for (uint32_t i = lane; i < D / 2; i += 32) {
+    const float a = v[i], b = v[i + D / 2];
+    const float2 t = cs[i];
+    v[i] = __fsub_rn(__fmul_rn(a, t.x), __fmul_rn(b, t.y));
+    v[i + D / 2] = __fadd_rn(__fmul_rn(a, t.y), __fmul_rn(b, t.x));
+  }
+  __syncwarp();
+}
+
 // ---------------------------------------------------------------------------
 // Per-element dequant, bit-exact with reference quant.rs:36-80.  Products are
 // rounded separately (__fmul_rn / __fsub_rn) so the compiler cannot fuse

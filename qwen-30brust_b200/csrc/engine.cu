@@ -15,6 +15,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <cstddef>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -59,6 +60,7 @@ void prepare_device(int device) {
   if (device < 0 || device >= 64 || done[device]) return;
   QC_CK(qc::matvec_prepare(kMaxSmem));
   QC_CK(qc::decode_prepare(kMaxSmem));
+  QC_CK(qc::token_prepare(0));
   done[device] = true;
 }
 
@@ -166,6 +168,12 @@ struct qc_engine {
   qc::Scratch sc{};
   qc::DecodeDims dims{};
   qc::StepPlan plan{};
+  // whole-token kernel: its plan, exchange buffers and the device copy of `layers`
+  qc::TokenPlan tplan{};
+  const char* token_why = nullptr;  // why the model does not fit it (nullptr: it fits)
+  unsigned long long* d_ll = nullptr;
+  qc::LayerDev* d_layers = nullptr;
+  bool use_token = false;
   uint32_t* d_gen = nullptr;
   cudaStream_t own = nullptr, stream = nullptr;
   cudaGraph_t graph = nullptr;
@@ -190,6 +198,8 @@ struct qc_engine {
     cudaFree(d_weights);
     cudaFree(d_kv);
     cudaFree(d_scratch);
+    cudaFree(d_ll);
+    cudaFree(d_layers);
     if (own) cudaStreamDestroy(own);
   }
 
@@ -398,6 +408,7 @@ struct qc_engine {
     QC_CK(cudaMemcpyAsync(d_scratch + o_rope, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice,
                           stream));
     h_template = qc::DevState{};
+    h_template.seq = 1;  // exchange buffers start at tag 0
     h_template.gen_tokens = d_gen;
     h_template.gen_cap = context;
     QC_CK(cudaMemcpyAsync(d_state, &h_template, sizeof h_template, cudaMemcpyHostToDevice, stream));
@@ -405,9 +416,18 @@ struct qc_engine {
     QC_CK(cudaEventCreate(&ev0));
     QC_CK(cudaEventCreate(&ev1));
     QC_CK(cudaStreamSynchronize(stream));
+    QC_CK(cudaMalloc(&d_layers, layers.size() * sizeof(qc::LayerDev)));
+    QC_CK(cudaMemcpy(d_layers, layers.data(), layers.size() * sizeof(qc::LayerDev), cudaMemcpyHostToDevice));
     plan = qc::plan_step(step_args());
     ensure(qc::step_smem_max(step_args(), plan) <= (size_t)kMaxSmem,
            "model dimensions need more shared memory per block than the CUDA engine supports");
+    token_why = qc::plan_token(step_args(), 1 << 30, &tplan);
+    if (!token_why) {
+      const uint64_t n = tplan.ll_layer * cfg.layers;
+      QC_CK(cudaMalloc(&d_ll, n * sizeof(unsigned long long)));
+      QC_CK(cudaMemset(d_ll, 0, n * sizeof(unsigned long long)));  // tag 0: never a token's tag
+    }
+    use_token = !token_why;
     capture();
   }
 
@@ -417,6 +437,7 @@ struct qc_engine {
     a.sc = sc;
     a.st = d_state;
     a.layers = layers.data();
+    a.layers_dev = d_layers;
     a.n_layers = cfg.layers;
     a.embd = embd;
     a.out = out;
@@ -426,10 +447,25 @@ struct qc_engine {
   }
 
   void capture() {
+    if (use_token) {  // a device or driver that cannot capture the cooperative launch keeps the per-phase kernels
+      try {
+        capture_once();
+        return;
+      } catch (const ApiError&) {
+        cudaGetLastError();
+        token_why = "the cooperative whole-token launch could not be captured in a CUDA graph";
+        use_token = false;
+      }
+    }
+    capture_once();
+  }
+
+  void capture_once() {
     cudaStream_t cs;
     QC_CK(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
     QC_CK(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
-    qc::launch_step(step_args(), plan, cs);
+    if (use_token) qc::launch_token(step_args(), tplan, d_ll, true, cs);
+    else qc::launch_step(step_args(), plan, cs);
     cudaError_t le = cudaGetLastError();
     cudaError_t ce = cudaStreamEndCapture(cs, &graph);
     cudaStreamDestroy(cs);
@@ -438,11 +474,34 @@ struct qc_engine {
     QC_CK(cudaGraphInstantiate(&exec, graph, 0));
   }
 
+  // Decode path: 0 = the whole-token kernel when the model fits it, 1 = the per-phase kernels.
+  void set_mode(int mode) {
+    ensure(mode == 0 || mode == 1, "decode mode must be 0 (auto) or 1 (per-phase kernels)");
+    const bool want = mode == 0 && !token_why;
+    if (want == use_token) return;
+    QC_CK(cudaSetDevice(device));
+    QC_CK(cudaStreamSynchronize(stream));
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
+    exec = nullptr;
+    graph = nullptr;
+    if (prof_exec) cudaGraphExecDestroy(prof_exec);
+    if (prof_graph) cudaGraphDestroy(prof_graph);
+    prof_exec = nullptr;
+    prof_graph = nullptr;
+    for (cudaEvent_t ev : prof_ev) cudaEventDestroy(ev);
+    prof_ev.clear();
+    prof_kind.clear();
+    use_token = want;
+    capture();
+  }
+
   // ---- model.rs:202-216 ------------------------------------------------------------------
   void reset() {
     cudaSetDevice(device);
-    // any earlier asynchronous failure is reported by the caller; the reset itself must not throw past here
-    cudaMemcpyAsync(d_state, &h_template, sizeof h_template, cudaMemcpyHostToDevice, stream);
+    // any earlier asynchronous failure is reported by the caller; the reset itself must not throw past here.
+    // The token tag (DevState::seq, the last field) is kept.
+    cudaMemcpyAsync(d_state, &h_template, offsetof(qc::DevState, seq), cudaMemcpyHostToDevice, stream);
     cudaStreamSynchronize(stream);
     pos = 0;
   }
@@ -471,6 +530,20 @@ struct qc_engine {
   void profile(qc_phase_times* out) {
     ensure(pos < context, "context limit " + std::to_string(context) + " reached", QC_ERR_CONTEXT);
     QC_CK(cudaSetDevice(device));
+    if (use_token) {  // one kernel per token: its whole duration
+      *out = qc_phase_times{};
+      QC_CK(cudaEventRecord(ev0, stream));
+      QC_CK(cudaGraphLaunch(exec, stream));
+      QC_CK(cudaEventRecord(ev1, stream));
+      check_flags();
+      float ms = 0.f;
+      QC_CK(cudaEventElapsedTime(&ms, ev0, ev1));
+      out->token_ms = ms;
+      out->launches = 1;
+      pos += 1;
+      stats.tokens += 1;
+      return;
+    }
     if (!prof_exec) {
       cudaStream_t cs;
       QC_CK(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
@@ -494,6 +567,7 @@ struct qc_engine {
       float ms = 0.f;
       QC_CK(cudaEventElapsedTime(&ms, prof_ev[i], prof_ev[i + 1]));
       *slot[prof_kind[i]] += ms;
+      out->token_ms += ms;
     }
     out->launches = qc::step_launches(cfg.layers);
     pos += 1;
@@ -507,7 +581,9 @@ struct qc_engine {
   // Reads the sticky flags after `stream` is drained; a set flag is an error.
   void check_flags() {
     QC_CK(cudaMemcpyAsync(h_pinned + 2, &d_state->nonfinite, 8, cudaMemcpyDeviceToHost, stream));
+    QC_CK(cudaMemcpyAsync(h_pinned + 6, &d_state->abort, 4, cudaMemcpyDeviceToHost, stream));
     QC_CK(cudaStreamSynchronize(stream));
+    if (h_pinned[6]) throw ApiError(QC_ERR_CUDA, "decode kernel: a wait between thread blocks timed out");
     if (h_pinned[3]) throw ApiError(QC_ERR_TOKEN, "token outside vocabulary");
     if (h_pinned[2]) throw ApiError(QC_ERR_NONFINITE, "nonfinite model output");
   }
@@ -807,6 +883,21 @@ int qc_get_stats(const qc_engine* e, qc_stats* out) {
     *out = e->stats;
     out->weight_bytes = e->weight_bytes;
     out->kv_bytes = e->kv_bytes;
+  });
+}
+
+int qc_engine_set_decode_mode(qc_engine* e, int mode) {
+  return api(e, [&] {
+    ensure(e, "null engine");
+    e->set_mode(mode);
+  });
+}
+
+int qc_engine_decode_path(const qc_engine* e, int* path, const char** why) {
+  return api(const_cast<qc_engine*>(e), [&] {
+    ensure(e && path, "null argument");
+    *path = e->use_token ? 0 : 1;
+    if (why) *why = e->token_why ? e->token_why : "";
   });
 }
 

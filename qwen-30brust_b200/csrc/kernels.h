@@ -21,6 +21,10 @@ struct DevState {
   uint32_t attn_done[64];  // last-block counters, one per KV head
   uint32_t router_done;
   uint32_t output_done;
+  uint32_t abort;  // sticky: a wait of the whole-token kernel timed out
+  // Tag of the whole-token kernel's inter-block values: one per token, never
+  // reset (an engine reset keeps it, so values of earlier tokens never match).
+  uint32_t seq;
 };
 
 // Per-layer weights in the device layout.
@@ -33,6 +37,8 @@ struct LayerDev {
   float* kc;  // [kvheads][ctx][head_dim]
   float* vc;
 };
+
+static_assert(sizeof(LayerDev) % 16 == 0, "LayerDev is copied in 16-byte pieces");
 
 // Model dimensions and scratch buffers used by the decode kernels.
 struct DecodeDims {
@@ -79,7 +85,8 @@ struct StepArgs {
   DecodeDims dims;
   Scratch sc;
   DevState* st;
-  const LayerDev* layers;  // host array
+  const LayerDev* layers;      // host array
+  const LayerDev* layers_dev;  // the same array in device memory (whole-token kernel)
   uint32_t n_layers;
   MatDesc embd, out;
   const float* out_norm;
@@ -104,5 +111,25 @@ typedef void (*StepHook)(void* ctx, int kind, cudaStream_t s);
 void launch_step(const StepArgs& a, const StepPlan& p, cudaStream_t s, StepHook hook = nullptr, void* ctx = nullptr);
 inline uint32_t step_launches(uint32_t layers) { return 2 + 6 * layers; }
 cudaError_t decode_prepare(int max_smem);
+
+// ---- whole-token persistent kernel (token.cu) ---------------------------------------------
+constexpr uint32_t kMaxTokenLayers = 256;
+constexpr uint32_t kMaxTokenSlots = 12;  // vocab-projection pipeline stages
+
+// Work layout of the whole-token kernel: shared-memory regions and the offsets
+// (in 8-byte tagged values) of its per-layer exchange buffers.
+struct TokenPlan {
+  uint32_t nb;                          // thread blocks (one per SM)
+  uint32_t p_bytes, q_bytes;            // weight regions P and Q
+  uint32_t stage_off, misc_off, smem;   // staging area, small arrays, dynamic total
+  uint32_t smax;                        // attention splits per KV head, at most
+  uint32_t out_sg, nsp, nsq;            // vocab stage groups; stage slots in P and Q
+  uint64_t ll_qkv, ll_part, ll_attn, ll_xmid, ll_rl, ll_h, ll_xout, ll_layer;  // exchange buffer offsets
+};
+// Fills *p and returns nullptr if the model fits the whole-token kernel, else the reason it does not.
+const char* plan_token(const StepArgs& a, int max_smem, TokenPlan* p);
+// One token: the whole forward of StepArgs as one launch.  `ll` holds a.n_layers * p.ll_layer values.
+void launch_token(const StepArgs& a, const TokenPlan& p, unsigned long long* ll, bool cooperative, cudaStream_t s);
+cudaError_t token_prepare(int max_smem);
 
 }  // namespace qc

@@ -28,6 +28,7 @@ EXPORTS = (
     "qc_decode_greedy", "qc_decode_enqueue", "qc_sync", "qc_reset", "qc_position", "qc_get_stats",
     "qc_logits_device", "qc_row_bytes", "qc_matrix_create", "qc_matrix_matvec", "qc_matrix_dequant",
     "qc_matrix_bytes", "qc_matrix_destroy", "qc_packed_matvec", "qc_profile_step", "qc_packed_matvec_noalloc",
+    "qc_engine_set_decode_mode", "qc_engine_decode_path",
 )
 
 
@@ -56,7 +57,7 @@ PHASES = ("embed", "attn_in", "attention", "oproj", "router", "gateup", "down", 
 
 
 class PhaseTimes(C.Structure):
-    _fields_ = [(p + "_ms", C.c_double) for p in PHASES] + [("launches", C.c_uint32)]
+    _fields_ = [(p + "_ms", C.c_double) for p in PHASES] + [("launches", C.c_uint32), ("token_ms", C.c_double)]
 
 
 class Stats(C.Structure):
@@ -109,6 +110,8 @@ def lib() -> C.CDLL:
         L.qc_packed_matvec.argtypes = [u32, u64, u64, vp, u64, vp, vp]
         L.qc_profile_step.argtypes = [vp, C.POINTER(PhaseTimes)]
         L.qc_packed_matvec_noalloc.argtypes = [u32, u64, u64, vp, u64, vp, vp]
+        L.qc_engine_set_decode_mode.argtypes = [vp, C.c_int]
+        L.qc_engine_decode_path.argtypes = [vp, C.POINTER(C.c_int), C.POINTER(C.c_char_p)]
         _lib = L
     return _lib
 
@@ -232,7 +235,19 @@ class Engine:
         self._check(lib().qc_profile_step(self._h, C.byref(t)))
         out = {p: getattr(t, p + "_ms") for p in PHASES}
         out["launches"] = t.launches
+        out["token"] = t.token_ms
         return out
+
+    def set_decode_mode(self, mode: int) -> None:
+        """0: the whole-token kernel when the model fits it (default); 1: the per-phase kernels."""
+        self._check(lib().qc_engine_set_decode_mode(self._h, mode))
+
+    @property
+    def decode_path(self) -> tuple[int, str]:
+        """(0 whole-token kernel | 1 per-phase kernels, why the whole-token kernel is not used or "")."""
+        path, why = C.c_int(), C.c_char_p()
+        self._check(lib().qc_engine_decode_path(self._h, C.byref(path), C.byref(why)))
+        return path.value, (why.value or b"").decode()
 
     def logits_device_ptr(self) -> int:
         p = C.c_void_p()

@@ -14,11 +14,22 @@ from conftest import GOLDEN
 
 pytestmark = pytest.mark.gpu
 
+# decode paths: 0 = whole-token persistent kernel, 1 = per-phase kernels
+MODES = pytest.mark.parametrize("mode", [0, 1], ids=["token_kernel", "phase_kernels"])
 
-def test_f32_fixture_matches_reference_and_resets(cuda_engine):
+
+def _engine(cuda_engine, source, context, mode):
+    e = cuda_engine.Engine(source, context)
+    e.set_decode_mode(mode)
+    assert e.decode_path[0] == mode, e.decode_path
+    return e
+
+
+@MODES
+def test_f32_fixture_matches_reference_and_resets(cuda_engine, mode):
     """tests/model.rs:48-69 through qc_engine_open / qc_forward."""
     g = json.loads((GOLDEN / "tiny_f32_logits.json").read_text())
-    e = cuda_engine.Engine(GOLDEN / "tiny_f32.gguf", 4)
+    e = _engine(cuda_engine, GOLDEN / "tiny_f32.gguf", 4, mode)
     for tok, exp in zip(g["tokens"], g["expected_logits"]):
         got = e.forward(tok)
         assert np.abs(got - np.array(exp, dtype=np.float32)).max() < 2e-5
@@ -100,12 +111,13 @@ def test_engine_from_tensor_table(cuda_engine, oracle):
         cuda_engine.Engine.from_tensors(tensors, np.frombuffer(buf, dtype=np.uint8), bad, 4)
 
 
-def test_config1_tiny_quantized_logits_and_greedy(cuda_engine, oracle, tools):
+@MODES
+def test_config1_tiny_quantized_logits_and_greedy(cuda_engine, oracle, tools, mode):
     """16-token prompt, 32 greedy steps, logits compared at every step."""
     z = np.load(GOLDEN / "tiny_q_golden.npz")
     tokens, golden, n0 = z["tokens"], z["logits"], int(z["prompt_len"])
     img = tools.synth_gguf(tools.TINY)
-    e = cuda_engine.Engine(img, 64)
+    e = _engine(cuda_engine, img, 64, mode)
     m = oracle.Model(img, 64)
     worst = 0.0
     for p, tok in enumerate(tokens):
@@ -127,9 +139,10 @@ def test_config1_tiny_quantized_logits_and_greedy(cuda_engine, oracle, tools):
     np.testing.assert_allclose(last, golden[n0 + 31], atol=2e-2)
 
 
-def test_decode_enqueue_sync_and_limits(cuda_engine, tools):
+@MODES
+def test_decode_enqueue_sync_and_limits(cuda_engine, tools, mode):
     img = tools.synth_gguf(tools.TINY)
-    e = cuda_engine.Engine(img, 24)
+    e = _engine(cuda_engine, img, 24, mode)
     with pytest.raises(cuda_engine.QwenCudaError, match="previous forward"):
         e.decode_greedy(2)
     e.forward_tokens([1, 2, 3], want_logits=False)
@@ -149,10 +162,11 @@ def test_decode_enqueue_sync_and_limits(cuda_engine, tools):
     assert a.tolist() == b.tolist()
 
 
-def test_two_engines_are_independent(cuda_engine, tools):
+@MODES
+def test_two_engines_are_independent(cuda_engine, tools, mode):
     img = tools.synth_gguf(tools.TINY)
-    e1 = cuda_engine.Engine(img, 16)
-    e2 = cuda_engine.Engine(img, 16)
+    e1 = _engine(cuda_engine, img, 16, mode)
+    e2 = _engine(cuda_engine, img, 16, mode)
     l1 = e1.forward(5)
     e2.forward(7)
     l2 = e2.forward(5)
@@ -160,6 +174,43 @@ def test_two_engines_are_independent(cuda_engine, tools):
     l1b = e1.forward(5)
     assert np.array_equal(l1, l1b)
     assert not np.array_equal(l1, l2)
+
+
+def test_paths_agree_and_switch(cuda_engine, tools):
+    """Both decode paths give the same logits (up to fp32 reassociation) on one
+    engine, switching paths between tokens over one KV cache."""
+    img = tools.synth_gguf(tools.TINY)
+    a = _engine(cuda_engine, img, 128, 0)
+    b = _engine(cuda_engine, img, 128, 1)
+    assert a.decode_path == (0, "")
+    rng = np.random.default_rng(3)
+    for p, tok in enumerate(rng.integers(0, 512, 100).tolist()):
+        if p == 50:
+            a.set_decode_mode(1)
+        if p == 75:
+            a.set_decode_mode(0)
+        la, lb = a.forward(tok), b.forward(tok)
+        assert np.abs(la - lb).max() < 1e-4 * max(1.0, np.abs(lb).max()), p
+
+
+@MODES
+def test_long_context_split_attention(cuda_engine, oracle, tools, mode):
+    """16 KV heads and 1300 positions: the whole-token kernel splits each head's
+    positions over blocks (merge of split softmax states from position 64 on)
+    and, past 9 splits x 128 positions, runs several online-softmax steps per split."""
+    spec = tools.TINY.with_(heads=16, kvheads=16)
+    img = tools.synth_gguf(spec)
+    e = _engine(cuda_engine, img, 2048, mode)
+    m = oracle.Model(img, 2048)
+    toks = np.random.default_rng(4).integers(0, spec.vocab, 1300).tolist()
+    check = {0, 63, 64, 65, 200, 700, 1151, 1152, 1153, 1299}
+    for p, tok in enumerate(toks):
+        g = e.forward(tok, want_logits=p in check)
+        o = m.forward(tok)
+        if p in check:
+            err = float(np.abs(g - o).max())
+            assert err < 2e-2 and err < 1e-3 * max(1.0, float(np.abs(o).max())), (p, err)
+            assert int(np.argmax(g)) == oracle.sample_greedy(o), p
 
 
 @pytest.mark.slow
@@ -172,6 +223,7 @@ def test_config4_30b_greedy_matches_oracle(cuda_engine, oracle, tools):
     img = tools.synth_gguf(spec)
     prompt = np.random.default_rng(1).integers(0, spec.vocab, 8).tolist()
     e = cuda_engine.Engine(img, 4096)
+    assert e.decode_path == (0, ""), e.decode_path  # the 30B shape runs the whole-token kernel
     e.forward_tokens(prompt[:-1], want_logits=False)
     gpu_logits = [e.forward(prompt[-1])]
     toks = []
