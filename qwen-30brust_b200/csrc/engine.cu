@@ -738,6 +738,7 @@ int create_from(const qc::GgufFile& g, const uint8_t* base, uint32_t context, in
 #ifdef QC_TRACE
 namespace qc {
 cudaError_t trace_read(void* host, size_t bytes);
+cudaError_t token_trace_read(void* host, size_t bytes);
 }
 #endif
 
@@ -978,6 +979,7 @@ void qc_matrix_destroy(qc_matrix* m) { delete m; }
 
 #ifdef QC_TRACE
 int qc_trace_read(void* host, size_t bytes) { return qc::trace_read(host, bytes) == cudaSuccess ? 0 : 2; }
+int qc_token_trace_read(void* host, size_t bytes) { return qc::token_trace_read(host, bytes) == cudaSuccess ? 0 : 2; }
 #endif
 
 int qc_packed_matvec(uint32_t kind, uint64_t rows, uint64_t cols, const uint8_t* blocks, uint64_t len,

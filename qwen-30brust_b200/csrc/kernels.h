@@ -124,6 +124,8 @@ struct TokenPlan {
   uint32_t stage_off, misc_off, smem;   // staging area, small arrays, dynamic total
   uint32_t smax;                        // attention splits per KV head, at most
   uint32_t out_sg, nsp, nsq;            // vocab stage groups; stage slots in P and Q
+  uint32_t nsegs;                       // row-run descriptors in shared memory
+  uint32_t part_floats;                 // unit-group partial sums of the row engine
   uint64_t ll_qkv, ll_part, ll_attn, ll_xmid, ll_rl, ll_h, ll_xout, ll_layer;  // exchange buffer offsets
 };
 // Fills *p and returns nullptr if the model fits the whole-token kernel, else the reason it does not.

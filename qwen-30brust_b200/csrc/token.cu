@@ -67,7 +67,7 @@ struct TokenParams {
   uint32_t n_layers, hidden, heads, kvheads, D, experts, top, inter, vocab, ctx;
   float eps;
   uint32_t p_bytes, q_bytes, stage_off, misc_off;
-  uint32_t smax, out_sg, nsp, nsq;
+  uint32_t smax, out_sg, nsp, nsq, nsegs, part_floats;
 };
 
 // ---- primitives -----------------------------------------------------------------------------
@@ -102,6 +102,19 @@ QC_DEV unsigned long long ll_get(const unsigned long long* p) {
 }
 QC_DEV bool fresh(unsigned long long v, uint32_t seq) { return (uint32_t)(v >> 32) == seq; }
 QC_DEV float val(unsigned long long v) { return __uint_as_float((uint32_t)v); }
+
+// Phase timestamps of thread 0 of each block (diagnostic builds only): slots 0-15
+// and 20-31 for one layer, 16-19 for the vocab projection.
+#ifdef QC_TRACE
+__device__ unsigned long long g_ttrace[1024][32];
+QC_DEV void trace_at(bool on, int k) {
+  if (on && threadIdx.x == 0 && blockIdx.x < 1024) g_ttrace[blockIdx.x][k] = gtimer();
+}
+#else
+QC_DEV void trace_at(bool, int) {}
+#endif
+#define QC_TT(k) trace_at(l == 1, k)
+#define QC_TO(k) trace_at(true, 16 + (k))
 
 // Bounded polling: keep() is false once the wait must end, either because
 // another block gave up (abort set) or because kWaitNs passed (then it sets abort).
@@ -169,7 +182,7 @@ QC_DEV void ll_gather(const unsigned long long* src, uint32_t n, Dst dst, uint32
 template <bool RMS>
 QC_DEV void stage_ll(uint8_t* mem, uint32_t nv, uint32_t n, uint32_t units, bool with_float,
                      const unsigned long long* __restrict__ src, const float* __restrict__ w, float eps, float* red,
-                     uint32_t seq, DevState* st) {
+                     uint32_t seq, DevState* st, bool trace = false, int tslot = 0) {
   const uint32_t per = units4(units) * 64;
   const uint32_t total = nv * per, xb = xview_bytes(units, with_float);
   constexpr int P = 2;
@@ -203,6 +216,7 @@ QC_DEV void stage_ll(uint8_t* mem, uint32_t nv, uint32_t n, uint32_t units, bool
         }
       }
     } while (!ok && wt.keep(st));
+    trace_at(trace, tslot);
     if constexpr (RMS) {
       float ss = 0.f;
 #pragma unroll
@@ -257,68 +271,123 @@ QC_DEV void bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* b) {
 }
 QC_DEV void proxy_fence() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 QC_DEV void l2_prefetch(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+  bytes &= ~15u;
+  if (bytes) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+// A layer's norm vectors toward L2 (they are read element-wise by every block).
+QC_DEV void prefetch_vectors(const LayerDev& L, uint32_t hidden, uint32_t D) {
+  l2_prefetch(L.attn_norm, hidden * 4);
+  l2_prefetch(L.ffn_norm, hidden * 4);
+  l2_prefetch(L.q_norm, D * 4);
+  l2_prefetch(L.k_norm, D * 4);
 }
 
 // ---- row loops ----------------------------------------------------------------------------------
-// Destination of row results: v -> (add ? add[i] + v : v) into ll[i] (tagged) or out[i], i = r - r0.
-struct RowsOut {
+// A run of rows of one matrix held in shared memory: rows [r0, r1), row rbase at `base`.  Each
+// result v (plus add[i], i = r - r0) goes to ll[i] as a tagged value, or to out[i].
+struct Seg {
+  const uint8_t* base;
   const float* add;
   float* out;
   unsigned long long* ll;
-  uint32_t seq;
+  uint32_t r0, r1, rbase;
+  uint32_t main_bytes, d_bytes, group_bytes, kind;
 };
-template <uint32_t KIND>
-__device__ __noinline__ void rows_k(const MatDesc m, uint32_t r0, uint32_t r1, const XView xv, const uint8_t* base,
-                                    uint32_t rbase, const RowsOut o, uint32_t warp, uint32_t nw) {
-  warp_rows_k<KIND, true>(
-      m, r0, r1, xv,
-      [&](uint32_t r, const uint8_t** row, const __half** drow) {
-        *row = row_ptr(m, base, r - rbase);
-        *drow = drow_ptr(m, base, r - rbase);
-      },
-      [&](uint32_t r, float v) {
-        const uint32_t i = r - r0;
-        if (o.add) v = __fadd_rn(o.add[i], v);
-        if (o.ll) ll_put(o.ll + i, v, o.seq);
-        else o.out[i] = v;
-      },
-      warp, nw);
+__host__ __device__ inline Seg make_seg(const MatDesc& m, const uint8_t* base, uint32_t r0, uint32_t r1,
+                                        uint32_t rbase, const float* add, float* out, unsigned long long* ll) {
+  return Seg{base, add, out, ll, r0, r1, rbase, m.main_bytes, m.d_bytes, m.group_bytes, m.kind};
 }
-// Rows [r0, r1) of m held in shared memory from row rbase on, by warps (warp, warp + nw, ...) of a subset.
-QC_DEV void rows(const MatDesc& m, uint32_t r0, uint32_t r1, const XView& xv, const uint8_t* base, uint32_t rbase,
-                 const RowsOut& o, uint32_t warp = threadIdx.x >> 5, uint32_t nw = blockDim.x >> 5) {
-  if (r1 <= r0) return;
-  switch (m.kind) {
-    case Q4_K: rows_k<Q4_K>(m, r0, r1, xv, base, rbase, o, warp, nw); break;
-    case Q5_K: rows_k<Q5_K>(m, r0, r1, xv, base, rbase, o, warp, nw); break;
-    case Q6_K: rows_k<Q6_K>(m, r0, r1, xv, base, rbase, o, warp, nw); break;
-    case Q8_0: rows_k<Q8_0>(m, r0, r1, xv, base, rbase, o, warp, nw); break;
-    case Q4_0: rows_k<Q4_0>(m, r0, r1, xv, base, rbase, o, warp, nw); break;
-    case F16: rows_k<F16>(m, r0, r1, xv, base, rbase, o, warp, nw); break;
-    default: rows_k<F32>(m, r0, r1, xv, base, rbase, o, warp, nw); break;
-  }
+QC_DEV const uint8_t* seg_row(const Seg* q, uint32_t r) {
+  const uint32_t rr = r - q->rbase;
+  return q->base + (rr >> 3) * q->group_bytes + (rr & 7) * q->main_bytes;
+}
+QC_DEV const __half* seg_drow(const Seg* q, uint32_t r) {
+  const uint32_t rr = r - q->rbase;
+  return reinterpret_cast<const __half*>(q->base + (rr >> 3) * q->group_bytes + 8 * q->main_bytes + (rr & 7) * q->d_bytes);
+}
+QC_DEV void seg_emit(const Seg* q, uint32_t r, float v, uint32_t seq) {
+  const uint32_t i = r - q->r0;
+  if (q->add) v = __fadd_rn(q->add[i], v);
+  if (q->ll) ll_put(q->ll + i, v, seq);
+  else q->out[i] = v;
 }
 
-#ifdef QC_TRACE
-constexpr uint32_t kTraceLayer = 1;
-__device__ unsigned long long g_ttrace[1024][24];
-#define QC_TT(k)                                                                                   \
-  do {                                                                                             \
-    if (threadIdx.x == 0 && blockIdx.x < 1024 && l == kTraceLayer) g_ttrace[blockIdx.x][k] = gtimer(); \
-  } while (0)
-#define QC_TO(k)                                                                     \
-  do {                                                                               \
-    if (threadIdx.x == 0 && blockIdx.x < 1024) g_ttrace[blockIdx.x][16 + (k)] = gtimer(); \
-  } while (0)
-#else
-#define QC_TT(k) \
-  do {           \
-  } while (0)
-#define QC_TO(k) \
-  do {           \
-  } while (0)
-#endif
+// Rows of the runs sg[0..nseg) (one format; activation XView of `units` units), joint row index ri
+// in [0, R), R = total rows.  Warps split each row's units: a group of 8 lanes covers 8
+// consecutive units of one row, 4 rows per warp step, so a warp reads only its own 8 units of the
+// activation (once, broadcast to its 4 row slots) and every unit of the weights once.  The sum of
+// a row over unit group ug goes to part[ug * R + ri]; rows_finish adds the groups in order.
+QC_DEV uint32_t unit_groups(uint32_t units) { return (units + 7) / 8; }
+// (part[ug * Rtot + roff + ri] when these runs are a part of a larger table.)
+template <uint32_t KIND>
+__device__ __noinline__ void rows_us(const Seg* sg, uint32_t nseg, uint32_t units, const XView xv, float* part,
+                                     uint32_t Rtot, uint32_t roff, uint32_t warp, uint32_t nw) {
+  uint32_t R = 0;
+  for (uint32_t k = 0; k < nseg; k++) R += sg[k].r1 - sg[k].r0;
+  const uint32_t UG = unit_groups(units), lane = threadIdx.x & 31, rg = lane >> 3, j = lane & 7;
+  const uint32_t wpg = UG <= nw ? nw / UG : 1;
+  for (uint32_t ug = warp / wpg; ug < UG && warp < wpg * (UG <= nw ? UG : nw); ug += (UG <= nw ? UG : nw)) {
+    const uint32_t u = ug * 8 + j;
+    const bool uon = u < units;
+    const auto ux = load_x<KIND>(xv, uon ? u : 0);
+    uint32_t s = 0, first = 0;  // segment of ri; ri only grows
+    for (uint32_t rb = (warp % wpg) * 4; rb < R; rb += 4 * wpg) {  // the same trip count for the whole warp
+      const uint32_t ri = rb + rg;
+      float v = 0.f;
+      if (ri < R) {
+        while (ri >= first + sg[s].r1 - sg[s].r0) {
+          first += sg[s].r1 - sg[s].r0;
+          s++;
+        }
+        const Seg* q = sg + s;
+        const uint32_t r = q->r0 + ri - first;
+        if (uon) v = unit_dot<KIND, true>(seg_row(q, r), seg_drow(q, r), u, ux);
+      }
+      v += __shfl_xor_sync(0xffffffffu, v, 4);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      if (j == 0 && ri < R) part[ug * Rtot + roff + ri] = v;
+    }
+  }
+}
+// All runs of a table (consecutive runs of one format go to one call); no barrier inside.
+QC_DEV void run_rows(const Seg* sg, uint32_t nseg, uint32_t units, const XView& xv, float* part,
+                     uint32_t warp = threadIdx.x >> 5, uint32_t nw = blockDim.x >> 5) {
+  uint32_t Rtot = 0;
+  for (uint32_t k = 0; k < nseg; k++) Rtot += sg[k].r1 - sg[k].r0;
+  uint32_t roff = 0;
+  for (uint32_t i = 0; i < nseg;) {
+    uint32_t j = i + 1, R = sg[i].r1 - sg[i].r0;
+    while (j < nseg && sg[j].kind == sg[i].kind) R += sg[j].r1 - sg[j].r0, j++;
+    switch (sg[i].kind) {
+      case Q4_K: rows_us<Q4_K>(sg + i, j - i, units, xv, part, Rtot, roff, warp, nw); break;
+      case Q5_K: rows_us<Q5_K>(sg + i, j - i, units, xv, part, Rtot, roff, warp, nw); break;
+      case Q6_K: rows_us<Q6_K>(sg + i, j - i, units, xv, part, Rtot, roff, warp, nw); break;
+      case Q8_0: rows_us<Q8_0>(sg + i, j - i, units, xv, part, Rtot, roff, warp, nw); break;
+      case Q4_0: rows_us<Q4_0>(sg + i, j - i, units, xv, part, Rtot, roff, warp, nw); break;
+      case F16: rows_us<F16>(sg + i, j - i, units, xv, part, Rtot, roff, warp, nw); break;
+      default: rows_us<F32>(sg + i, j - i, units, xv, part, Rtot, roff, warp, nw); break;
+    }
+    roff += R;
+    i = j;
+  }
+}
+// After a barrier: row values (unit groups summed in order) to their runs, one thread per row.
+QC_DEV void rows_finish(const Seg* sg, uint32_t nseg, uint32_t units, const float* part, uint32_t seq) {
+  uint32_t R = 0;
+  for (uint32_t k = 0; k < nseg; k++) R += sg[k].r1 - sg[k].r0;
+  const uint32_t UG = unit_groups(units);
+  for (uint32_t ri = threadIdx.x; ri < R; ri += blockDim.x) {
+    uint32_t s = 0, first = 0;
+    while (ri >= first + sg[s].r1 - sg[s].r0) {
+      first += sg[s].r1 - sg[s].r0;
+      s++;
+    }
+    float v = 0.f;
+    for (uint32_t ug = 0; ug < UG; ug++) v += part[ug * R + ri];
+    seg_emit(sg + s, sg[s].r0 + ri - first, v, seq);
+  }
+}
 
 // Shared-memory bytes of the staging and small-array areas (host and device agree on these).
 struct AttnSmem {
@@ -354,13 +423,22 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
   const uint32_t nslots = T.nsp + T.nsq;
   const uint32_t E = T.experts, top = T.top, D = T.D, G = T.heads / T.kvheads, KP = D + 4;
   const uint32_t QD = T.heads * D, KD = T.kvheads * D;
-  // small arrays: [keys E][logits E][sel top][selw top][residual rows][row outputs]
+  // small arrays: [keys E4*4][logits E][sel top][selw top][segments nsegs][residual rows][row outputs]
+  const uint32_t E4 = (E + 3) / 4;
   uint8_t* mp = sm + T.misc_off;
-  unsigned long long* const key = reinterpret_cast<unsigned long long*>(mp);
-  float* const lg = reinterpret_cast<float*>(mp + up16(E * 8));
-  uint32_t* const sel = reinterpret_cast<uint32_t*>(mp + up16(E * 8) + up16(E * 4));
-  float* const selw = reinterpret_cast<float*>(mp + up16(E * 8) + up16(E * 4) + up16(top * 4));
-  float* const xres = reinterpret_cast<float*>(mp + up16(E * 8) + up16(E * 4) + 2 * up16(top * 4));
+  uint32_t* const key = reinterpret_cast<uint32_t*>(mp);
+  mp += E4 * 16;
+  float* const lg = reinterpret_cast<float*>(mp);
+  mp += up16(E * 4);
+  uint32_t* const sel = reinterpret_cast<uint32_t*>(mp);
+  mp += up16(top * 4);
+  float* const selw = reinterpret_cast<float*>(mp);
+  mp += up16(top * 4);
+  Seg* const segs = reinterpret_cast<Seg*>(mp);
+  mp += T.nsegs * sizeof(Seg);
+  float* const part = reinterpret_cast<float*>(mp);  // unit-group partial sums of the row engine
+  mp += up16(T.part_floats * 4);
+  float* const xres = reinterpret_cast<float*>(mp);
 
   if (tid < sizeof(LayerDev) / 16) cp16(reinterpret_cast<uint8_t*>(&Ld[0]) + 16 * tid,
                                         reinterpret_cast<const uint8_t*>(&T.layers[0]) + 16 * tid);
@@ -435,6 +513,7 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
   if (tid == 0) {
     issue_A(Ld[0]);
     issue_OR(Ld[0]);
+    prefetch_vectors(Ld[0], T.hidden, D);
   }
 
   // attention split of this token (the same for every layer)
@@ -463,25 +542,23 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
       cp16(reinterpret_cast<uint8_t*>(&Ld[(l + 1) & 1]) + 16 * tid,
            reinterpret_cast<const uint8_t*>(&T.layers[l + 1]) + 16 * tid);
     cp_commit();
-    if (att && tid == 0) {  // cached K/V rows of this split toward L2
-      const uint32_t te = min(at1, pos);
-      if (te > at0) {
-        const uint32_t bytes = (te - at0) * D * 4;
-        for (uint32_t o = 0; o < bytes; o += 16384) {
-          l2_prefetch(kc_h + (uint64_t)at0 * D + o / 4, min(16384u, bytes - o));
-          l2_prefetch(vc_h + (uint64_t)at0 * D + o / 4, min(16384u, bytes - o));
-        }
-      }
-    }
 
     // ---- P1: Q, K, V = W rms(x, attn_norm) --------------------------------------------------
     const bool flA = uses_float_x(L.q.kind) || uses_float_x(L.k.kind) || uses_float_x(L.v.kind);
+    if (tid == 0) {  // runs of Q, K and V rows (made visible by the staging barrier)
+      segs[0] = make_seg(L.q, rP, s.pq.b * 8, min(L.q.rows, s.pq.e * 8), s.pq.b * 8, nullptr, nullptr,
+                         LL + T.ll_qkv + s.pq.b * 8);
+      segs[1] = make_seg(L.k, rP + s.bq, s.pk.b * 8, min(L.k.rows, s.pk.e * 8), s.pk.b * 8, nullptr, nullptr,
+                         LL + T.ll_qkv + QD + s.pk.b * 8);
+      segs[2] = make_seg(L.v, rP + s.bq + s.bk, s.pv.b * 8, min(L.v.rows, s.pv.e * 8), s.pv.b * 8, nullptr, nullptr,
+                         LL + T.ll_qkv + QD + KD + s.pv.b * 8);
+    }
     if (l == 0)
       stage_vectors<true>(
           stg, 1, T.hidden, L.q.units, flA, [&](uint32_t, uint32_t i) { return dequant_one(T.embd, erow, edrow, i); },
           L.attn_norm, T.eps, red);
     else
-      stage_ll<true>(stg, 1, T.hidden, L.q.units, flA, Xin, L.attn_norm, T.eps, red, seq, st);
+      stage_ll<true>(stg, 1, T.hidden, L.q.units, flA, Xin, L.attn_norm, T.eps, red, seq, st, l == 1, 20);
     QC_TT(1);
     const XView xa = xview_at(stg, L.q.units, flA);
     if (s.bA) {
@@ -489,18 +566,9 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
       parP ^= 1;
     }
     QC_TT(2);
-    if (s.pq.n()) {
-      const uint32_t r0 = s.pq.b * 8, r1 = min(L.q.rows, s.pq.e * 8);
-      rows(L.q, r0, r1, xa, rP, r0, RowsOut{nullptr, nullptr, LL + T.ll_qkv + r0, seq});
-    }
-    if (s.pk.n()) {
-      const uint32_t r0 = s.pk.b * 8, r1 = min(L.k.rows, s.pk.e * 8);
-      rows(L.k, r0, r1, xa, rP + s.bq, r0, RowsOut{nullptr, nullptr, LL + T.ll_qkv + QD + r0, seq});
-    }
-    if (s.pv.n()) {
-      const uint32_t r0 = s.pv.b * 8, r1 = min(L.v.rows, s.pv.e * 8);
-      rows(L.v, r0, r1, xa, rP + s.bq + s.bk, r0, RowsOut{nullptr, nullptr, LL + T.ll_qkv + QD + KD + r0, seq});
-    }
+    run_rows(segs, 3, L.q.units, xa, part);
+    __syncthreads();
+    rows_finish(segs, 3, L.q.units, part, seq);
     __syncthreads();  // staging area reused below
     QC_TT(3);
 
@@ -512,12 +580,28 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
       float* const sc = vn + D;                         // [G][kSub] scores, then weights
       float* const mls = sc + G * kSub;                 // [G] running max, [G] running sum, [G] rescale
       const bool has_pos = at1 == time;
+      // cached K/V rows of each step go to region P (free between P1 and P5), rows of D floats
+      const uint32_t sub = min(kSub, T.p_bytes / (2 * D * 4));
+      float* const ks = reinterpret_cast<float*>(rP);
+      float* const vs = ks + sub * D;
+      auto issue_kv = [&](uint32_t tb) {  // thread 0; returns nothing, copies rows [tb, min(tb + sub, at1, pos))
+        const uint32_t te = min(min(tb + sub, at1), pos);
+        if (te <= tb) return;
+        const uint32_t bytes = (te - tb) * D * 4;
+        proxy_fence();
+        mb_expect(&mbar[0], 2 * bytes);
+        bulk_copy(ks, kc_h + (uint64_t)tb * D, bytes, &mbar[0]);
+        bulk_copy(vs, vc_h + (uint64_t)tb * D, bytes, &mbar[0]);
+      };
+      if (tid == 0) issue_kv(at0);
+      QC_TT(26);
       ll_gather(LL + T.ll_qkv + (uint64_t)ah * G * D, G * D,
                 [&](uint32_t i, float v) { qs[(i / D) * KP + i % D] = v; }, seq, st);
       if (has_pos) {
         ll_gather(LL + T.ll_qkv + QD + (uint64_t)ah * D, D, [&](uint32_t i, float v) { kn[i] = v; }, seq, st);
         ll_gather(LL + T.ll_qkv + QD + KD + (uint64_t)ah * D, D, [&](uint32_t i, float v) { vn[i] = v; }, seq, st);
       }
+      QC_TT(31);
       for (uint32_t g = tid; g < G; g += TNT) {
         mls[g] = -INFINITY;
         mls[G + g] = 0.f;
@@ -532,27 +616,72 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
         }
       }
       __syncthreads();
-      // online softmax over steps of kSub positions; thread (ag, ad4) accumulates 4 dims of head ag
+      QC_TT(24);
+      // online softmax over steps of `sub` positions
       const float sd = sqrtf((float)D);
-      const uint32_t nslot = G * (D / 4), ag = tid / (D / 4), ad4 = tid % (D / 4);
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (uint32_t tb = at0; tb < at1; tb += kSub) {
-        const uint32_t n = min(kSub, at1 - tb);
-        // s[g][t] = (q_g . k_t) / sqrt(D)  (ops.rs:84-91); thread per (t, g), t fastest
-        for (uint32_t i = tid; i < n * G; i += TNT) {
-          const uint32_t t = i % n, g = i / n;
-          const float* kr = tb + t == pos ? kn : kc_h + (uint64_t)(tb + t) * D;
-          const float4* k4 = reinterpret_cast<const float4*>(kr);
-          const float4* q4 = reinterpret_cast<const float4*>(qs + g * KP);
-          float p = 0.f;
-          for (uint32_t j = 0; j < D / 4; j++) {
-            const float4 a = k4[j], b = q4[j];
-            p = fmaf(a.x, b.x, p);
-            p = fmaf(a.y, b.y, p);
-            p = fmaf(a.z, b.z, p);
-            p = fmaf(a.w, b.w, p);
+      const uint32_t D4 = D / 4, vg = tid / D4, vd = tid % D4, h0 = 2 * vg, h1 = 2 * vg + 1;
+      float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
+      for (uint32_t tb = at0; tb < at1; tb += sub) {
+        const uint32_t n = min(sub, at1 - tb);
+        if (min(tb + n, pos) > tb) {  // cached rows of this step arrived
+          mb_wait(&mbar[0], parP, st);
+          parP ^= 1;
+        }
+        // s[g][t] = (q_g . k_t) / sqrt(D)  (ops.rs:84-91): a warp per position t, lanes over the
+        // head dimension, up to 8 query heads held in registers; the 8 partial dot products are
+        // summed across the warp by a halving exchange (9 shuffles), leaving head (lane >> 2) & 7
+        for (uint32_t gb = 0; gb < G; gb += 8) {
+          const uint32_t gn = min(8u, G - gb);
+          float4 qr[8][2];
+#pragma unroll
+          for (int g = 0; g < 8; g++)
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+              const uint32_t j = lane + 32 * i;
+              qr[g][i] = (g < (int)gn && j < D4) ? reinterpret_cast<const float4*>(qs + (gb + g) * KP)[j]
+                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+          for (uint32_t t = warp; t < n; t += nw) {
+            const float4* k4 = reinterpret_cast<const float4*>(tb + t == pos ? kn : ks + t * D);
+            float p[8];
+#pragma unroll
+            for (int g = 0; g < 8; g++) p[g] = 0.f;
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+              const uint32_t j = lane + 32 * i;
+              if (j < D4) {
+                const float4 a = k4[j];
+#pragma unroll
+                for (int g = 0; g < 8; g++) {
+                  p[g] = fmaf(a.x, qr[g][i].x, p[g]);
+                  p[g] = fmaf(a.y, qr[g][i].y, p[g]);
+                  p[g] = fmaf(a.z, qr[g][i].z, p[g]);
+                  p[g] = fmaf(a.w, qr[g][i].w, p[g]);
+                }
+              }
+            }
+            const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+            float h4[4], h2[2];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+              const float send = b4 ? p[k] : p[k + 4], keep = b4 ? p[k + 4] : p[k];
+              h4[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+            }
+#pragma unroll
+            for (int k = 0; k < 2; k++) {
+              const float send = b3 ? h4[k] : h4[k + 2], keep = b3 ? h4[k + 2] : h4[k];
+              h2[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+            }
+            float h1v;
+            {
+              const float send = b2 ? h2[0] : h2[1], keep = b2 ? h2[1] : h2[0];
+              h1v = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+            }
+            h1v += __shfl_xor_sync(0xffffffffu, h1v, 2);
+            h1v += __shfl_xor_sync(0xffffffffu, h1v, 1);
+            const uint32_t g = (lane >> 2) & 7;
+            if ((lane & 3) == 0 && g < gn) sc[(gb + g) * kSub + t] = h1v / sd;
           }
-          sc[g * kSub + t] = p / sd;
         }
         __syncthreads();
         for (uint32_t g = warp; g < G; g += nw) {
@@ -576,35 +705,51 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
           }
         }
         __syncthreads();
-        if (tid < nslot) {
-          const float f = mls[2 * G + ag];
-          acc.x *= f;
-          acc.y *= f;
-          acc.z *= f;
-          acc.w *= f;
+        // acc[h][4 dims] = sum_t p[h][t] v_t; thread (pair of heads h0 = 2 vg, h1 = h0 + 1; 4 dims vd)
+        if (h0 < G) {
+          const bool two = h1 < G;
+          const float f0 = mls[2 * G + h0], f1 = two ? mls[2 * G + h1] : 0.f;
+          acc0.x *= f0;
+          acc0.y *= f0;
+          acc0.z *= f0;
+          acc0.w *= f0;
+          acc1.x *= f1;
+          acc1.y *= f1;
+          acc1.z *= f1;
+          acc1.w *= f1;
+          const float* p0 = sc + h0 * kSub;
+          const float* p1 = sc + (two ? h1 : h0) * kSub;
           for (uint32_t t = 0; t < n; t++) {
-            const float p = sc[ag * kSub + t];
-            const float* vr = tb + t == pos ? vn : vc_h + (uint64_t)(tb + t) * D;
-            const float4 v = *reinterpret_cast<const float4*>(vr + 4 * ad4);
-            acc.x = fmaf(p, v.x, acc.x);
-            acc.y = fmaf(p, v.y, acc.y);
-            acc.z = fmaf(p, v.z, acc.z);
-            acc.w = fmaf(p, v.w, acc.w);
+            const float4 v = *reinterpret_cast<const float4*>((tb + t == pos ? vn : vs + t * D) + 4 * vd);
+            const float a = p0[t], b = two ? p1[t] : 0.f;
+            acc0.x = fmaf(a, v.x, acc0.x);
+            acc0.y = fmaf(a, v.y, acc0.y);
+            acc0.z = fmaf(a, v.z, acc0.z);
+            acc0.w = fmaf(a, v.w, acc0.w);
+            acc1.x = fmaf(b, v.x, acc1.x);
+            acc1.y = fmaf(b, v.y, acc1.y);
+            acc1.z = fmaf(b, v.z, acc1.z);
+            acc1.w = fmaf(b, v.w, acc1.w);
           }
         }
         __syncthreads();
+        if (tid == 0 && tb + sub < at1) issue_kv(tb + sub);
       }
-      if (tid < nslot) {
+      QC_TT(25);
+      for (uint32_t hh = 0; hh < 2; hh++) {
+        const uint32_t ag = h0 + hh;
+        if (h0 >= G || ag >= G) continue;
+        const float4 acc = hh ? acc1 : acc0;
         if (S == 1) {  // one split: normalize and publish the output directly
           const float inv = 1.f / mls[G + ag];
-          unsigned long long* o = LL + T.ll_attn + (uint64_t)(ah * G + ag) * D + 4 * ad4;
+          unsigned long long* o = LL + T.ll_attn + (uint64_t)(ah * G + ag) * D + 4 * vd;
           ll_put2(o, acc.x * inv, acc.y * inv, seq);
           ll_put2(o + 2, acc.z * inv, acc.w * inv, seq);
         } else {  // partial state [acc[D], m, l] of (head, split)
           unsigned long long* o = LL + T.ll_part + ((uint64_t)(ah * G + ag) * T.smax + as) * (D + 2);
-          ll_put2(o + 4 * ad4, acc.x, acc.y, seq);
-          ll_put2(o + 4 * ad4 + 2, acc.z, acc.w, seq);
-          if (ad4 == 0) ll_put2(o + D, mls[ag], mls[G + ag], seq);
+          ll_put2(o + 4 * vd, acc.x, acc.y, seq);
+          ll_put2(o + 4 * vd + 2, acc.z, acc.w, seq);
+          if (vd == 0) ll_put2(o + D, mls[ag], mls[G + ag], seq);
         }
       }
       if (S > 1) {  // this split merges query heads g = as, as + S, ... of its KV head
@@ -645,74 +790,111 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
     const uint32_t or0 = s.so.b * 8, or1 = min(L.o.rows, s.so.e * 8);
     for (uint32_t r = or0 + tid; r < or1; r += TNT)
       xres[r - or0] = l == 0 ? dequant_one(T.embd, erow, edrow, r) : ll_wait1(Xin + r, seq, st);
-    stage_ll<false>(stg, 1, QD, L.o.units, flO, LL + T.ll_attn, nullptr, 0.f, red, seq, st);
+    if (tid == 0) segs[0] = make_seg(L.o, rQ, or0, or1, or0, xres, nullptr, LL + T.ll_xmid + or0);
+    stage_ll<false>(stg, 1, QD, L.o.units, flO, LL + T.ll_attn, nullptr, 0.f, red, seq, st, l == 1, 21);
     QC_TT(5);
     if (s.bOR) {
       mb_wait(&mbar[1], parQ, st);
       parQ ^= 1;
     }
-    rows(L.o, or0, or1, xview_at(stg, L.o.units, flO), rQ, or0, RowsOut{xres, nullptr, LL + T.ll_xmid + or0, seq});
+    run_rows(segs, 1, L.o.units, xview_at(stg, L.o.units, flO), part);
+    __syncthreads();
+    rows_finish(segs, 1, L.o.units, part, seq);
     __syncthreads();
     QC_TT(6);
 
     // ---- P4: router logits of rms(x', ffn_norm) (the same vector feeds gate/up) ----------------
     const bool flR = uses_float_x(L.router.kind) || uses_float_x(L.gate.kind) || uses_float_x(L.up.kind);
-    stage_ll<true>(stg, 1, T.hidden, L.router.units, flR, LL + T.ll_xmid, L.ffn_norm, T.eps, red, seq, st);
+    if (tid == 0) {
+      const uint32_t r0 = s.sr.b * 8;
+      segs[0] = make_seg(L.router, rQ + s.bO, r0, min(L.router.rows, s.sr.e * 8), r0, nullptr, nullptr, LL + T.ll_rl + r0);
+    }
+    stage_ll<true>(stg, 1, T.hidden, L.router.units, flR, LL + T.ll_xmid, L.ffn_norm, T.eps, red, seq, st, l == 1, 22);
     const XView xf = xview_at(stg, L.router.units, flR);
     QC_TT(7);
-    {
-      const uint32_t r0 = s.sr.b * 8, r1 = min(L.router.rows, s.sr.e * 8);
-      rows(L.router, r0, r1, xf, rQ + s.bO, r0, RowsOut{nullptr, nullptr, LL + T.ll_rl + r0, seq});
-    }
+    run_rows(segs, 1, L.router.units, xf, part);
+    __syncthreads();
+    rows_finish(segs, 1, L.router.units, part, seq);
     QC_TT(8);
 
     // ---- P5: top-k with ties to the lower index + softmax over the kept logits, gate/up + SwiGLU
-    ll_gather(LL + T.ll_rl, E, [&](uint32_t i, float v) { lg[i] = v; }, seq, st);
+    ll_gather(LL + T.ll_rl, E, [&](uint32_t i, float v) {
+      lg[i] = v;
+      key[i] = total_key_u(v);
+    }, seq, st);
+    for (uint32_t e = E + tid; e < 4 * E4; e += TNT) key[e] = 0;  // below every real key: never counted
     __syncthreads();
-    for (uint32_t e = tid; e < E; e += TNT) key[e] = ((unsigned long long)total_key_u(lg[e]) << 32) | (0xffffffffu - e);
-    __syncthreads();
-    for (uint32_t e = tid; e < E; e += TNT) {
-      const unsigned long long ke = key[e];
-      uint32_t rank = 0;
-      for (uint32_t j = 0; j < E; j++) rank += key[j] > ke;
-      if (rank < top) sel[rank] = e;
-      if (c == 0 && !isfinite(lg[e])) atomicOr(&st->nonfinite, 1u);
-    }
-    __syncthreads();
-    if (tid == 0) {
-      float mx = -INFINITY;  // ops.rs:29-44, in selection order
-      for (uint32_t k = 0; k < top; k++) mx = fmaxf(mx, lg[sel[k]]);
-      float sum = 0.f;
-      for (uint32_t k = 0; k < top; k++) {
-        selw[k] = expf(lg[sel[k]] - mx);
-        sum = __fadd_rn(sum, selw[k]);
-      }
-      for (uint32_t k = 0; k < top; k++) selw[k] = selw[k] / sum;
-      // the selected experts' gate/up rows into P (Q/K/V consumed in P1), down rows into Q
-      proxy_fence();
-      const uint32_t gi = groups_of(L.gate.rows);
-      if (s.bGU) {
-        mb_expect(&mbar[0], s.bGU);
-        uint32_t off = 0;
-        for (uint32_t i = s.sg.b; i < s.sg.e;) {
-          const uint32_t slot = i / gi, g0 = i % gi, ng = min(gi - g0, s.sg.e - i), e = sel[slot];
-          bulk_copy(rP + off, L.gate.w + (uint64_t)e * L.gate.expert_stride + (uint64_t)g0 * L.gate.group_bytes,
-                    ng * L.gate.group_bytes, &mbar[0]);
-          off += ng * L.gate.group_bytes;
-          bulk_copy(rP + off, L.up.w + (uint64_t)e * L.up.expert_stride + (uint64_t)g0 * L.up.group_bytes,
-                    ng * L.up.group_bytes, &mbar[0]);
-          off += ng * L.up.group_bytes;
-          i += ng;
+    QC_TT(27);
+    {  // rank of each logit (ties to the lower index), 4 threads per expert reading 4 keys at a time
+      for (uint32_t base = 0; base < E; base += TNT / 4) {
+        const uint32_t e = base + tid / 4, part = tid % 4;
+        uint32_t rank = 0;
+        if (e < E) {
+          const uint32_t ke = key[e];
+          for (uint32_t i = part; i < E4; i += 4) {
+            const uint4 k4 = reinterpret_cast<const uint4*>(key)[i];
+            const uint32_t j = 4 * i;
+            rank += (k4.x > ke || (k4.x == ke && j < e)) + (k4.y > ke || (k4.y == ke && j + 1 < e)) +
+                    (k4.z > ke || (k4.z == ke && j + 2 < e)) + (k4.w > ke || (k4.w == ke && j + 3 < e));
+          }
+        }
+        rank += __shfl_xor_sync(0xffffffffu, rank, 1);
+        rank += __shfl_xor_sync(0xffffffffu, rank, 2);
+        if (e < E && part == 0) {
+          if (rank < top) sel[rank] = e;
+          if (c == 0 && !isfinite(lg[e])) atomicOr(&st->nonfinite, 1u);
         }
       }
-      if (s.bD) {
-        mb_expect(&mbar[1], s.bD);
-        const uint32_t per = s.sd.n() * L.down.group_bytes;
-        for (uint32_t k = 0; k < top; k++)
+    }
+    __syncthreads();
+    QC_TT(28);
+    if (warp == 0) {
+      // ops.rs:29-44 in selection order: max, exp, sequential sum, divide
+      float mx = -INFINITY;
+      for (uint32_t k = lane; k < top; k += 32) mx = fmaxf(mx, lg[sel[k]]);
+      mx = warp_max(mx);
+      for (uint32_t k = lane; k < top; k += 32) selw[k] = expf(lg[sel[k]] - mx);
+      __syncwarp();
+      if (lane == 0) {
+        float sum = 0.f;
+        for (uint32_t k = 0; k < top; k++) sum = __fadd_rn(sum, selw[k]);
+        red[1] = sum;
+      }
+      __syncwarp();
+      QC_TT(29);
+      const float sum = red[1];
+      // the selected experts' gate/up rows into P (Q/K/V and K/V rows consumed), down rows into Q
+      const uint32_t gi = groups_of(L.gate.rows);
+      uint32_t nruns = 0;
+      for (uint32_t i = s.sg.b; i < s.sg.e; nruns++) i += min(gi - i % gi, s.sg.e - i);
+      if (lane == 0) {
+        proxy_fence();
+        if (s.bGU) mb_expect(&mbar[0], s.bGU);
+        if (s.bD) mb_expect(&mbar[1], s.bD);
+      }
+      __syncwarp();
+      for (uint32_t q = lane; q < 2 * nruns + (s.bD ? top : 0); q += 32) {
+        if (q < 2 * nruns) {  // run q/2, gate (q even) or up
+          uint32_t i = s.sg.b, off = 0;
+          for (uint32_t r = 0; r < q / 2; r++) {
+            const uint32_t ng = min(gi - i % gi, s.sg.e - i);
+            off += ng * (L.gate.group_bytes + L.up.group_bytes);
+            i += ng;
+          }
+          const uint32_t g0 = i % gi, ng = min(gi - g0, s.sg.e - i), e = sel[i / gi];
+          const MatDesc& m = q & 1 ? L.up : L.gate;
+          bulk_copy(rP + off + (q & 1) * ng * L.gate.group_bytes,
+                    m.w + (uint64_t)e * m.expert_stride + (uint64_t)g0 * m.group_bytes, ng * m.group_bytes, &mbar[0]);
+        } else {
+          const uint32_t k = q - 2 * nruns, per = s.sd.n() * L.down.group_bytes;
           bulk_copy(rQ + k * per,
                     L.down.w + (uint64_t)sel[k] * L.down.expert_stride + (uint64_t)s.sd.b * L.down.group_bytes, per,
                     &mbar[1]);
+        }
       }
+      QC_TT(30);
+      __syncwarp();
+      for (uint32_t k = lane; k < top; k += 32) selw[k] = selw[k] / sum;
     }
     __syncthreads();
     QC_TT(9);
@@ -723,18 +905,26 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
       parP ^= 1;
     }
     QC_TT(10);
-    {
+    uint32_t nruns = 0;
+    if (tid == 0) {  // all gate runs, then all up runs (runs of one format go to one call)
       uint32_t off = 0;
-      for (uint32_t i = s.sg.b; i < s.sg.e;) {
+      for (uint32_t i = s.sg.b; i < s.sg.e; nruns++) {
         const uint32_t g0 = i % gi, ng = min(gi - g0, s.sg.e - i), it0 = i - s.sg.b;
         const uint32_t r0 = g0 * 8, r1 = min(L.gate.rows, (g0 + ng) * 8);
-        rows(L.gate, r0, r1, xf, rP + off, r0, RowsOut{nullptr, gout + it0 * 8, nullptr, 0});
+        segs[nruns] = make_seg(L.gate, rP + off, r0, r1, r0, nullptr, gout + it0 * 8, nullptr);
         off += ng * L.gate.group_bytes;
-        rows(L.up, r0, r1, xf, rP + off, r0, RowsOut{nullptr, gout + (nitem + it0) * 8, nullptr, 0});
+        segs[T.nsegs / 2 + nruns] = make_seg(L.up, rP + off, r0, r1, r0, nullptr, gout + (nitem + it0) * 8, nullptr);
         off += ng * L.up.group_bytes;
         i += ng;
       }
+      for (uint32_t k = 0; k < nruns; k++) segs[nruns + k] = segs[T.nsegs / 2 + k];
+      red[2] = __uint_as_float(nruns);
     }
+    __syncthreads();
+    nruns = __float_as_uint(red[2]);
+    run_rows(segs, 2 * nruns, L.gate.units, xf, part);
+    __syncthreads();
+    rows_finish(segs, 2 * nruns, L.gate.units, part, seq);
     __syncthreads();
     for (uint32_t idx = tid; idx < nitem * 8; idx += TNT) {
       const uint32_t i = s.sg.b + idx / 8, slot = i / gi, r = (i % gi) * 8 + idx % 8;
@@ -746,6 +936,7 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
     cp_wait_all();  // the next layer's descriptors
     __syncthreads();
     if (tid == 0) {  // region P is free: next layer's Q/K/V slice, or the first vocab stages
+      if (l + 1 < T.n_layers) prefetch_vectors(Ld[(l + 1) & 1], T.hidden, D);
       proxy_fence();
       if (l + 1 < T.n_layers) issue_A(Ld[(l + 1) & 1]);
       else
@@ -759,7 +950,12 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
     float* const dres = xres;           // [nd] x' rows of this block
     float* const dout = xres + nd;      // [top][nd]
     for (uint32_t r = dr0 + tid; r < dr1; r += TNT) dres[r - dr0] = ll_wait1(LL + T.ll_xmid + r, seq, st);
-    stage_ll<false>(stg, top, T.inter, L.down.units, flD, LL + T.ll_h, nullptr, 0.f, red, seq, st);
+    {
+      const uint32_t pbytes = s.sd.n() * L.down.group_bytes;
+      for (uint32_t k = tid; k < top; k += TNT)
+        segs[k] = make_seg(L.down, rQ + k * pbytes, dr0, dr1, dr0, nullptr, dout + k * nd, nullptr);
+    }
+    stage_ll<false>(stg, top, T.inter, L.down.units, flD, LL + T.ll_h, nullptr, 0.f, red, seq, st, l == 1, 23);
     QC_TT(12);
     const uint32_t xb = xview_bytes(L.down.units, flD);
     if (s.bD) {
@@ -767,12 +963,15 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
       parQ ^= 1;
     }
     QC_TT(13);
+    const uint32_t dpart = unit_groups(L.down.units) * (dr1 > dr0 ? dr1 - dr0 : 0);
     if (dr1 > dr0) {
-      const uint32_t per = nw >= top ? nw / top : 1, pbytes = s.sd.n() * L.down.group_bytes;
+      const uint32_t per = nw >= top ? nw / top : 1;
       for (uint32_t k = warp / per; k < top; k += nw / per)
-        rows(L.down, dr0, dr1, xview_at(stg + k * xb, L.down.units, flD), rQ + k * pbytes, dr0,
-             RowsOut{nullptr, dout + k * nd, nullptr, 0}, warp % per, per);
+        run_rows(segs + k, 1, L.down.units, xview_at(stg + k * xb, L.down.units, flD), part + k * dpart, warp % per,
+                 per);
     }
+    __syncthreads();
+    for (uint32_t k = 0; k < top; k++) rows_finish(segs + k, 1, L.down.units, part + k * dpart, seq);
     __syncthreads();
     for (uint32_t r = dr0 + tid; r < dr1; r += TNT) {
       float acc = 0.f;
@@ -883,13 +1082,12 @@ const char* plan_token(const StepArgs& a, int max_smem, TokenPlan* p) {
   t.nb = nb;
   t.smax = std::max(1u, std::min(nb / d.kvheads, (d.ctx + kMinChunk - 1) / kMinChunk));
   const uint32_t cap = std::min<uint32_t>(g_token_smem_cap, (uint32_t)max_smem);
-  uint32_t P = 0, Q = 0, stage = 0, res = 0, outs = 0;
+  uint32_t P = 0, Q = 0, stage = 0, res = 0, outs = 0, runs = 1, partf = 0;
   const AttnSmem as = attn_stage_bytes(G, D, t.smax);
   stage = std::max(as.attn, as.merge);
   for (uint32_t l = 0; l < a.n_layers; l++) {
     const LayerDev& L = a.layers[l];
-    if (L.q.units != L.k.units || L.q.units != L.v.units || L.q.lpr != L.k.lpr || L.q.lpr != L.v.lpr ||
-        L.router.units != L.gate.units || L.gate.units != L.up.units || L.gate.lpr != L.up.lpr ||
+    if (L.q.units != L.k.units || L.q.units != L.v.units || L.router.units != L.gate.units || L.gate.units != L.up.units ||
         L.gate.rows != d.inter || L.down.cols != d.inter || L.down.rows != d.hidden || L.o.rows != d.hidden)
       return "unexpected matrix shapes";
     const bool flA = uses_float_x(L.q.kind) || uses_float_x(L.k.kind) || uses_float_x(L.v.kind);
@@ -915,6 +1113,25 @@ const char* plan_token(const StepArgs& a, int max_smem, TokenPlan* p) {
       P = std::max(P, std::max(bA, bGU));
       Q = std::max(Q, std::max(bOR, bD));
       res = std::max(res, std::max(so.n() * 8, sd.n() * 8));
+      {  // unit-group partial sums of each phase's rows
+        auto ug = [](uint32_t units) { return (units + 7) / 8; };
+        uint32_t ra = 0;
+        for (int k = 0; k < 3; k++) {
+          const uint32_t lo = std::max(sa.b, seg0[k]), hi = std::min(sa.e, seg0[k] + segn[k]);
+          if (hi > lo) ra += (hi - lo) * 8;
+        }
+        partf = std::max(partf, ug(L.q.units) * ra);
+        partf = std::max(partf, ug(L.o.units) * so.n() * 8);
+        partf = std::max(partf, ug(L.router.units) * sr.n() * 8);
+        partf = std::max(partf, ug(L.gate.units) * 2 * sg.n() * 8);
+        partf = std::max(partf, d.top * ug(L.down.units) * sd.n() * 8);
+      }
+      {  // gate/up runs (one per selected expert the block's items touch)
+        const uint32_t gi = groups_of(L.gate.rows);
+        uint32_t n = 0;
+        for (uint32_t i = sg.b; i < sg.e; n++) i += std::min(gi - i % gi, sg.e - i);
+        runs = std::max(runs, n);
+      }
       outs = std::max(outs, std::max(2 * sg.n() * 8, (d.top + 1) * sd.n() * 8));
     }
   }
@@ -926,8 +1143,19 @@ const char* plan_token(const StepArgs& a, int max_smem, TokenPlan* p) {
   const uint32_t slot = sg * ogb;
   P = std::max(P, slot);
   Q = std::max(Q, slot);
+  // attention stages its cached K/V rows in P: at least 8 positions, up to kSub when room is left
+  const uint32_t kv_pos = 2 * D * 4;
+  P = std::max(P, 8 * kv_pos);
   P = up16(P);
   Q = up16(Q);
+  t.nsegs = std::max(std::max(3u, d.top), 2 * runs);
+  t.nsegs += t.nsegs & 1;
+  t.part_floats = partf;
+  const uint32_t misc = (d.experts + 3) / 4 * 16 + up16(d.experts * 4) + 2 * up16(d.top * 4) +
+                        t.nsegs * (uint32_t)sizeof(Seg) + up16(partf * 4) + up16(std::max(res, outs) * 4);
+  const uint32_t total = P + Q + up16(stage) + misc;
+  if (total > cap) return "the per-block weight slices and staging exceed the shared memory of one SM";
+  if (P < kSub * kv_pos) P += std::min(cap - total, kSub * kv_pos - P) & ~15u;
   t.out_sg = sg;
   t.nsp = std::min(P / slot, kMaxTokenSlots / 2);
   t.nsq = std::min(Q / slot, kMaxTokenSlots - t.nsp);
@@ -935,9 +1163,7 @@ const char* plan_token(const StepArgs& a, int max_smem, TokenPlan* p) {
   t.q_bytes = Q;
   t.stage_off = P + Q;
   t.misc_off = t.stage_off + up16(stage);
-  const uint32_t misc = up16(d.experts * 8) + up16(d.experts * 4) + 2 * up16(d.top * 4) + up16(std::max(res, outs) * 4);
   t.smem = t.misc_off + misc;
-  if (t.smem > cap) return "the per-block weight slices and staging exceed the shared memory of one SM";
   // exchange buffers (8-byte tagged values), each a multiple of 2 values
   auto ev = [](uint64_t n) { return (n + 1) & ~1ull; };
   const uint64_t QD = (uint64_t)d.heads * D, KD = (uint64_t)d.kvheads * D;
@@ -999,6 +1225,8 @@ void launch_token(const StepArgs& a, const TokenPlan& p, unsigned long long* ll,
   T.out_sg = p.out_sg;
   T.nsp = p.nsp;
   T.nsq = p.nsq;
+  T.nsegs = p.nsegs;
+  T.part_floats = p.part_floats;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.nb);
   cfg.blockDim = dim3(TNT);
