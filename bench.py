@@ -199,6 +199,8 @@ def run_ours(args) -> None:
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
     spec = T.QWEN3_30B_A3B
+    if args.layers:  # a shallower model of the same shapes: profiling runs only, not a bench line
+        spec = spec.with_(layers=args.layers)
     img, path = synth_image(T, spec, rank, world)
     t = time.time()
     eng = E.Engine(path if path is not None else img, CTX, device=local)
@@ -294,7 +296,8 @@ def run_ours(args) -> None:
             "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32 (activations, accumulate); Q4_K/Q6_K/F16/Q8_0 weights",
             "data": "synthetic: random-init N(0,0.02) weights quantized from seed 0; 512-token random prompt (seed 1)",
-            "config": {"workload": "BASELINE config 4: Qwen3-30B-A3B-shape decode, batch 1, greedy",
+            "config": {"workload": "BASELINE config 4: Qwen3-30B-A3B-shape decode, batch 1, greedy"
+                       if not args.layers else f"profiling run: config 4 shapes with {args.layers} layers (not a bench line)",
                        "layers": spec.layers, "hidden": spec.hidden, "heads": f"{spec.heads}q/{spec.kvheads}kv x {spec.head_dim}",
                        "experts": f"{spec.experts} top-{spec.top}", "intermediate": spec.intermediate,
                        "vocab": spec.vocab, "ctx": CTX, "prompt": PROMPT, "positions": [pos0, pos0 + args.steps - 1],
@@ -373,6 +376,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-tokens", type=int, default=2, help="tokens timed for the CPU baseline line")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="profiling only: the same model with this many layers (0 = all 48, the benchmark)")
     ap.add_argument("--decode-mode", type=int, default=0, choices=[0, 1],
                     help="0: whole-token kernel when the model fits it (default); 1: per-phase kernels")
     ap.add_argument("--ref-max-steps", type=int, default=8)
