@@ -438,10 +438,18 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
   mp += T.nsegs * sizeof(Seg);
   float* const part = reinterpret_cast<float*>(mp);  // unit-group partial sums of the row engine
   mp += up16(T.part_floats * 4);
+  float* const qnw = reinterpret_cast<float*>(mp);  // [D] q_norm of the layer
+  mp += up16(D * 4);
+  float* const knw = reinterpret_cast<float*>(mp);  // [D] k_norm of the layer
+  mp += up16(D * 4);
+  float* const ropes = reinterpret_cast<float*>(mp);  // [D/2] (cos, sin) of this token's position
+  mp += up16(D * 4);
   float* const xres = reinterpret_cast<float*>(mp);
 
   if (tid < sizeof(LayerDev) / 16) cp16(reinterpret_cast<uint8_t*>(&Ld[0]) + 16 * tid,
                                         reinterpret_cast<const uint8_t*>(&T.layers[0]) + 16 * tid);
+  for (uint32_t i = tid; i < D / 4; i += TNT)  // the RoPE row of this position (the same in every layer)
+    cp16(ropes + 4 * i, reinterpret_cast<const float*>(T.rope + (uint64_t)pos * (D / 2)) + 4 * i);
   cp_commit();
   if (tid == 0) {
     for (uint32_t i = 0; i < 2 + nslots; i++) mb_init(&mbar[i]);
@@ -522,10 +530,15 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
   S = S < 1 ? 1 : S;
   const uint32_t chunk = (time + S - 1) / S;
   S = (time + chunk - 1) / chunk;
-  const bool att = c < T.kvheads * S;
-  const uint32_t ah = att ? c / S : 0, as = att ? c % S : 0;
+  // blocks left over split the query heads of a KV head too: GS groups of GH heads
+  uint32_t GS = 1;
+  while (G % (2 * GS) == 0 && T.kvheads * S * GS * 2 <= nb) GS *= 2;
+  const uint32_t GH = G / GS;
+  const bool att = c < T.kvheads * S * GS;
+  const uint32_t ah = att ? c / (S * GS) : 0, ags = att ? (c / S) % GS : 0, as = att ? c % S : 0;
+  const uint32_t hq0 = ah * G + ags * GH;  // first query head of this block
   const uint32_t at0 = as * chunk, at1 = min(time, at0 + chunk);
-  const float2* const cs = T.rope + (uint64_t)pos * (D / 2);
+  const float2* const cs = reinterpret_cast<const float2*>(ropes);
   const uint8_t* const erow = row_ptr(T.embd, T.embd.w, token);
   const __half* const edrow = drow_ptr(T.embd, T.embd.w, token);
 
@@ -541,6 +554,9 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
     if (l + 1 < T.n_layers && tid < sizeof(LayerDev) / 16)
       cp16(reinterpret_cast<uint8_t*>(&Ld[(l + 1) & 1]) + 16 * tid,
            reinterpret_cast<const uint8_t*>(&T.layers[l + 1]) + 16 * tid);
+    if (att)  // this layer's QK-norm weights, read in P2 (the previous layer's copies are consumed)
+      for (uint32_t i = tid; i < D / 2; i += TNT) cp16(i < D / 4 ? qnw + 4 * i : knw + 4 * (i - D / 4),
+                                                      (i < D / 4 ? L.q_norm + 4 * i : L.k_norm + 4 * (i - D / 4)));
     cp_commit();
 
     // ---- P1: Q, K, V = W rms(x, attn_norm) --------------------------------------------------
@@ -574,11 +590,11 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
 
     // ---- P2: QK-norm, RoPE, KV append, split attention, merge --------------------------------
     if (att) {
-      float* const qs = reinterpret_cast<float*>(stg);  // [G][KP] query heads of this KV head
-      float* const kn = qs + G * KP;                    // [D] new key (normed, rotated)
+      float* const qs = reinterpret_cast<float*>(stg);  // [GH][KP] this block's query heads
+      float* const kn = qs + GH * KP;                   // [D] new key (normed, rotated)
       float* const vn = kn + D;                         // [D] new value
-      float* const sc = vn + D;                         // [G][kSub] scores, then weights
-      float* const mls = sc + G * kSub;                 // [G] running max, [G] running sum, [G] rescale
+      float* const sc = vn + D;                         // [GH][kSub] scores, then weights
+      float* const mls = sc + GH * kSub;                // [GH] running max, [GH] running sum, [GH] rescale
       const bool has_pos = at1 == time;
       // cached K/V rows of each step go to region P (free between P1 and P5), rows of D floats
       const uint32_t sub = min(kSub, T.p_bytes / (2 * D * 4));
@@ -595,31 +611,38 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
       };
       if (tid == 0) issue_kv(at0);
       QC_TT(26);
-      ll_gather(LL + T.ll_qkv + (uint64_t)ah * G * D, G * D,
+      ll_gather(LL + T.ll_qkv + (uint64_t)hq0 * D, GH * D,
                 [&](uint32_t i, float v) { qs[(i / D) * KP + i % D] = v; }, seq, st);
       if (has_pos) {
         ll_gather(LL + T.ll_qkv + QD + (uint64_t)ah * D, D, [&](uint32_t i, float v) { kn[i] = v; }, seq, st);
         ll_gather(LL + T.ll_qkv + QD + KD + (uint64_t)ah * D, D, [&](uint32_t i, float v) { vn[i] = v; }, seq, st);
       }
       QC_TT(31);
-      for (uint32_t g = tid; g < G; g += TNT) {
+      for (uint32_t g = tid; g < GH; g += TNT) {
         mls[g] = -INFINITY;
-        mls[G + g] = 0.f;
+        mls[GH + g] = 0.f;
       }
+      cp_wait_all();  // QK-norm weights
       __syncthreads();
-      for (uint32_t g = warp; g < G; g += nw) head_norm_rope(qs + g * KP, L.q_norm, D, T.eps, cs);
+      for (uint32_t g = warp; g < GH; g += nw) head_norm_rope(qs + g * KP, qnw, D, T.eps, cs);
       if (has_pos && warp == nw - 1) {  // model.rs:241-243: append k (normed, rotated) and v
-        head_norm_rope(kn, L.k_norm, D, T.eps, cs);
-        for (uint32_t i = lane; i < D; i += 32) {
-          kc_h[(uint64_t)pos * D + i] = kn[i];
-          vc_h[(uint64_t)pos * D + i] = vn[i];
-        }
+        head_norm_rope(kn, knw, D, T.eps, cs);
+        if (ags == 0)  // one of the GS blocks holding this position writes the cache
+          for (uint32_t i = lane; i < D; i += 32) {
+            kc_h[(uint64_t)pos * D + i] = kn[i];
+            vc_h[(uint64_t)pos * D + i] = vn[i];
+          }
       }
       __syncthreads();
       QC_TT(24);
       // online softmax over steps of `sub` positions
       const float sd = sqrtf((float)D);
-      const uint32_t D4 = D / 4, vg = tid / D4, vd = tid % D4, h0 = 2 * vg, h1 = 2 * vg + 1;
+      // value accumulation: thread (head pair vg, 4 dims vd, position phase vt) sums positions t = vt mod VT
+      const uint32_t D4 = D / 4, BT = (GH + 1) / 2 * D4;
+      uint32_t VT = 1;
+      while (VT * 2 * BT <= (uint32_t)TNT && VT < 16) VT *= 2;
+      const uint32_t vt = tid / BT, vr = tid % BT, vg = vr / D4, vd = vr % D4, h0 = 2 * vg, h1 = 2 * vg + 1;
+      const bool von = vt < VT && h0 < GH;
       float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
       for (uint32_t tb = at0; tb < at1; tb += sub) {
         const uint32_t n = min(sub, at1 - tb);
@@ -630,8 +653,8 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
         // s[g][t] = (q_g . k_t) / sqrt(D)  (ops.rs:84-91): a warp per position t, lanes over the
         // head dimension, up to 8 query heads held in registers; the 8 partial dot products are
         // summed across the warp by a halving exchange (9 shuffles), leaving head (lane >> 2) & 7
-        for (uint32_t gb = 0; gb < G; gb += 8) {
-          const uint32_t gn = min(8u, G - gb);
+        for (uint32_t gb = 0; gb < GH; gb += 8) {
+          const uint32_t gn = min(8u, GH - gb);
           float4 qr[8][2];
 #pragma unroll
           for (int g = 0; g < 8; g++)
@@ -684,7 +707,7 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
           }
         }
         __syncthreads();
-        for (uint32_t g = warp; g < G; g += nw) {
+        for (uint32_t g = warp; g < GH; g += nw) {
           float m = -INFINITY;
           for (uint32_t t = lane; t < n; t += 32) m = fmaxf(m, sc[g * kSub + t]);
           m = warp_max(m);
@@ -699,16 +722,16 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
           __syncwarp();
           if (lane == 0) {
             const float f = expf(mo - mn);
-            mls[2 * G + g] = f;
-            mls[G + g] = mls[G + g] * f + sum;
+            mls[2 * GH + g] = f;
+            mls[GH + g] = mls[GH + g] * f + sum;
             mls[g] = mn;
           }
         }
         __syncthreads();
         // acc[h][4 dims] = sum_t p[h][t] v_t; thread (pair of heads h0 = 2 vg, h1 = h0 + 1; 4 dims vd)
-        if (h0 < G) {
-          const bool two = h1 < G;
-          const float f0 = mls[2 * G + h0], f1 = two ? mls[2 * G + h1] : 0.f;
+        if (von) {
+          const bool two = h1 < GH;
+          const float f0 = mls[2 * GH + h0], f1 = two ? mls[2 * GH + h1] : 0.f;
           acc0.x *= f0;
           acc0.y *= f0;
           acc0.z *= f0;
@@ -719,7 +742,7 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
           acc1.w *= f1;
           const float* p0 = sc + h0 * kSub;
           const float* p1 = sc + (two ? h1 : h0) * kSub;
-          for (uint32_t t = 0; t < n; t++) {
+          for (uint32_t t = vt; t < n; t += VT) {
             const float4 v = *reinterpret_cast<const float4*>((tb + t == pos ? vn : vs + t * D) + 4 * vd);
             const float a = p0[t], b = two ? p1[t] : 0.f;
             acc0.x = fmaf(a, v.x, acc0.x);
@@ -735,29 +758,50 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
         __syncthreads();
         if (tid == 0 && tb + sub < at1) issue_kv(tb + sub);
       }
+      {  // partial sums of the position phases through region P (its K/V rows are consumed), in order
+        float4* const va = reinterpret_cast<float4*>(rP);  // [VT][BT][2]
+        if (von) {
+          va[(vt * BT + vr) * 2] = acc0;
+          va[(vt * BT + vr) * 2 + 1] = acc1;
+        }
+        __syncthreads();
+        if (von && vt == 0)
+          for (uint32_t k = 1; k < VT; k++) {
+            const float4 a = va[(k * BT + vr) * 2], b = va[(k * BT + vr) * 2 + 1];
+            acc0.x += a.x;
+            acc0.y += a.y;
+            acc0.z += a.z;
+            acc0.w += a.w;
+            acc1.x += b.x;
+            acc1.y += b.y;
+            acc1.z += b.z;
+            acc1.w += b.w;
+          }
+      }
       QC_TT(25);
-      for (uint32_t hh = 0; hh < 2; hh++) {
+      for (uint32_t hh = 0; hh < 2 && von && vt == 0; hh++) {
         const uint32_t ag = h0 + hh;
-        if (h0 >= G || ag >= G) continue;
+        if (ag >= GH) continue;
         const float4 acc = hh ? acc1 : acc0;
         if (S == 1) {  // one split: normalize and publish the output directly
-          const float inv = 1.f / mls[G + ag];
-          unsigned long long* o = LL + T.ll_attn + (uint64_t)(ah * G + ag) * D + 4 * vd;
+          const float inv = 1.f / mls[GH + ag];
+          unsigned long long* o = LL + T.ll_attn + (uint64_t)(hq0 + ag) * D + 4 * vd;
           ll_put2(o, acc.x * inv, acc.y * inv, seq);
           ll_put2(o + 2, acc.z * inv, acc.w * inv, seq);
         } else {  // partial state [acc[D], m, l] of (head, split)
-          unsigned long long* o = LL + T.ll_part + ((uint64_t)(ah * G + ag) * T.smax + as) * (D + 2);
+          unsigned long long* o = LL + T.ll_part + ((uint64_t)(hq0 + ag) * T.smax + as) * (D + 2);
           ll_put2(o + 4 * vd, acc.x, acc.y, seq);
           ll_put2(o + 4 * vd + 2, acc.z, acc.w, seq);
-          if (vd == 0) ll_put2(o + D, mls[ag], mls[G + ag], seq);
+          if (vd == 0) ll_put2(o + D, mls[ag], mls[GH + ag], seq);
         }
       }
-      if (S > 1) {  // this split merges query heads g = as, as + S, ... of its KV head
+      if (S > 1) {  // this split merges heads hq0 + as, hq0 + as + S, ... of its head group
         float* const pb = reinterpret_cast<float*>(stg);  // [S][D + 2]
         float* const fw = pb + S * (D + 2);               // [S]
-        for (uint32_t g = as; g < G; g += S) {
+        for (uint32_t gl = as; gl < GH; gl += S) {
+          const uint32_t g = hq0 + gl;
           __syncthreads();
-          ll_gather(LL + T.ll_part + (uint64_t)(ah * G + g) * T.smax * (D + 2), S * (D + 2),
+          ll_gather(LL + T.ll_part + (uint64_t)g * T.smax * (D + 2), S * (D + 2),
                     [&](uint32_t i, float v) { pb[i] = v; }, seq, st);
           __syncthreads();
           if (warp == 0) {
@@ -777,7 +821,7 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
           for (uint32_t d = tid; d < D; d += TNT) {
             float o = 0.f;
             for (uint32_t k = 0; k < S; k++) o = fmaf(pb[k * (D + 2) + d], fw[k], o);
-            ll_put(LL + T.ll_attn + (uint64_t)(ah * G + g) * D + d, o * red[0], seq);
+            ll_put(LL + T.ll_attn + (uint64_t)g * D + d, o * red[0], seq);
           }
         }
       }
@@ -1145,14 +1189,15 @@ const char* plan_token(const StepArgs& a, int max_smem, TokenPlan* p) {
   Q = std::max(Q, slot);
   // attention stages its cached K/V rows in P: at least 8 positions, up to kSub when room is left
   const uint32_t kv_pos = 2 * D * 4;
-  P = std::max(P, 8 * kv_pos);
+  P = std::max(std::max(P, 8 * kv_pos), 16384u);  // (also the attention's partial value sums)
   P = up16(P);
   Q = up16(Q);
   t.nsegs = std::max(std::max(3u, d.top), 2 * runs);
   t.nsegs += t.nsegs & 1;
   t.part_floats = partf;
   const uint32_t misc = (d.experts + 3) / 4 * 16 + up16(d.experts * 4) + 2 * up16(d.top * 4) +
-                        t.nsegs * (uint32_t)sizeof(Seg) + up16(partf * 4) + up16(std::max(res, outs) * 4);
+                        t.nsegs * (uint32_t)sizeof(Seg) + up16(partf * 4) + 3 * up16(D * 4) +
+                        up16(std::max(res, outs) * 4);
   const uint32_t total = P + Q + up16(stage) + misc;
   if (total > cap) return "the per-block weight slices and staging exceed the shared memory of one SM";
   if (P < kSub * kv_pos) P += std::min(cap - total, kSub * kv_pos - P) & ~15u;
