@@ -53,6 +53,11 @@ def peaks() -> dict:
     return {"hbm_gbs": 6650.0, "source": "fallback"}
 
 
+# DRAM bytes of one k_token launch from the ncu capture in profiles/k_token_4layer.md (4 layers):
+# 415.3 MB = 255.9 MB (vocab projection, logits) + 4 x 39.85 MB per layer; scaled by layer count.
+TOKEN_TRAFFIC_FIXED, TOKEN_TRAFFIC_PER_LAYER = 255.9e6, 39.85e6
+
+
 def model_bytes(spec, tools, pos_first: int, steps: int) -> dict:
     """Algorithmic bytes of one decode step (weights read once, KV read, KV row written)."""
     rb = tools.row_bytes
@@ -271,6 +276,7 @@ def run_ours(args) -> None:
         if phases["launches"] == 1:
             # the whole-token kernel is the step: its bytes are the token's, its duration the timed average
             dom, dom_ms, dom_bytes = "token", step_ms, b["per_token"]
+            traffic = TOKEN_TRAFFIC_FIXED + TOKEN_TRAFFIC_PER_LAYER * spec.layers
             phases_ms = {"token": phases["token"]}
         else:
             # dominant kernel of the step by device time (per-kernel CUDA events in a captured step graph)
@@ -279,6 +285,7 @@ def run_ours(args) -> None:
             dom_ms = phases[dom] / launches
             dom_bytes = b["per_kernel"][dom]
             phases_ms = {k: phases[k] for k in kinds}
+            traffic = None
         achieved = dom_bytes / (dom_ms / 1e3) / 1e9
         step_gbs = b["per_token"] / (step_ms / 1e3) / 1e9
         cpu = None
@@ -307,7 +314,8 @@ def run_ours(args) -> None:
                                     "frac": step_gbs / pk["hbm_gbs"], "roofline_tok_s": pk["hbm_gbs"] * 1e9 / b["per_token"],
                                     "peak_source": pk["source"]},
             "roofline": {"kernel": f"k_{dom}", "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                         "frac": achieved / pk["hbm_gbs"], "traffic": None,
+                         "frac": achieved / pk["hbm_gbs"], "traffic": traffic,
+                         "traffic_source": "ncu dram bytes of a 4-layer capture scaled by layers" if traffic else None,
                          "bytes_per_launch": dom_bytes, "ms_per_launch": dom_ms, "peak_source": pk["source"]},
             "phases_ms": phases_ms,
             "decode_path": "whole-token kernel (1 launch per token)" if decode_path[0] == 0
