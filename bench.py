@@ -14,8 +14,11 @@ all ranks; `e2e` is tok/s through qc_forward with the token copied in and the
 logits copied out (pinned host memory) every step, and the host picking the
 argmax, as the reference's chat loop does.  `--impl reference` times the
 reference's CPU path (the C++ restatement under oracle/, all host threads) on
-the same model.  With N > 1 each rank runs an independent replica (no
-collective on the data path yet): scaling "weak".
+the same model.  With N > 1 each rank runs an independent replica by default
+(scaling "weak"); with --ep the N ranks run ONE decode stream with the experts
+split over them (expert parallelism: each rank holds experts/N, partial MoE
+vectors exchanged over NVLink inside the token kernel), scaling "strong", and
+`value` is that stream's tok/s.
 """
 from __future__ import annotations
 
@@ -85,7 +88,7 @@ def model_bytes(spec, tools, pos_first: int, steps: int) -> dict:
         "embed": rb(spec.kind_embd, H) + H * 4,
     }
     return {"weights": weights, "kv_read": kv_read, "kv_write": L * kv_row, "per_token": weights + kv_read + L * kv_row,
-            "per_kernel": per_kernel}
+            "per_kernel": per_kernel, "experts": L * (gate_up_w + down_w)}
 
 
 class ClockSampler:
@@ -208,7 +211,14 @@ def run_ours(args) -> None:
         spec = spec.with_(layers=args.layers)
     img, path = synth_image(T, spec, rank, world)
     t = time.time()
-    eng = E.Engine(path if path is not None else img, CTX, device=local)
+    ep = world > 1 and args.ep
+    if ep:  # one stream over all ranks: this rank's experts, peers' exchange buffers over NVLink
+        src = img if img is not None else np.memmap(path, dtype=np.uint8, mode="r")
+        eng = E.Engine.expert_parallel(src, CTX, local, rank, world)
+        del src
+        E.connect_group(eng)
+    else:
+        eng = E.Engine(path if path is not None else img, CTX, device=local)
     eng.set_decode_mode(args.decode_mode)
     decode_path = eng.decode_path
     log(f"rank {rank}: engine up in {time.time() - t:.1f} s; decode path {decode_path}")
@@ -271,12 +281,15 @@ def run_ours(args) -> None:
         pk = peaks()
         b = model_bytes(spec, T, pos0, args.steps)
         step_ms = ms / args.steps
-        value = args.steps * world / (ms / 1e3)
+        streams = 1 if ep else world  # decode streams the job runs
+        if ep:  # per rank: replicated weights, KV and 1/world of the selected experts (uniform routing)
+            b = dict(b, per_token=b["per_token"] - b["experts"] * (1 - 1 / world))
+        value = args.steps * streams / (ms / 1e3)
         kinds = [k for k in E.PHASES]
         if phases["launches"] == 1:
             # the whole-token kernel is the step: its bytes are the token's, its duration the timed average
             dom, dom_ms, dom_bytes = "token", step_ms, b["per_token"]
-            traffic = TOKEN_TRAFFIC_FIXED + TOKEN_TRAFFIC_PER_LAYER * spec.layers
+            traffic = None if ep else TOKEN_TRAFFIC_FIXED + TOKEN_TRAFFIC_PER_LAYER * spec.layers  # 1-GPU capture
             phases_ms = {"token": phases["token"]}
         else:
             # dominant kernel of the step by device time (per-kernel CUDA events in a captured step graph)
@@ -300,7 +313,8 @@ def run_ours(args) -> None:
                              f"{ncores} threads, bit-identical to 1 thread; {cpu_model()}); {c['seconds']:.1f} s"}
         out = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
+            "scaling": "strong" if ep else "weak",
             "vs_baseline": None, "dtype": "f32 (activations, accumulate); Q4_K/Q6_K/F16/Q8_0 weights",
             "data": "synthetic: random-init N(0,0.02) weights quantized from seed 0; 512-token random prompt (seed 1)",
             "config": {"workload": "BASELINE config 4: Qwen3-30B-A3B-shape decode, batch 1, greedy"
@@ -308,9 +322,12 @@ def run_ours(args) -> None:
                        "layers": spec.layers, "hidden": spec.hidden, "heads": f"{spec.heads}q/{spec.kvheads}kv x {spec.head_dim}",
                        "experts": f"{spec.experts} top-{spec.top}", "intermediate": spec.intermediate,
                        "vocab": spec.vocab, "ctx": CTX, "prompt": PROMPT, "positions": [pos0, pos0 + args.steps - 1],
-                       "kv": "fp32", "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "kv": "fp32",
+                       "parallelism": (f"expert parallel x{world} (one stream)" if ep else f"replicas x{world}")
+                       if world > 1 else "single GPU",
                        "l2": "no flush: each step reads ~2.07 GB of weights and KV, > 126 MB L2"},
-            "hbm_roofline_decode": {"bytes_per_token": b["per_token"], "achieved_gbs": step_gbs, "peak_gbs": pk["hbm_gbs"],
+            "hbm_roofline_decode": {"bytes_per_token": b["per_token"],
+                                    "bytes_scope": "per rank (expert parallel)" if ep else "per stream", "achieved_gbs": step_gbs, "peak_gbs": pk["hbm_gbs"],
                                     "frac": step_gbs / pk["hbm_gbs"], "roofline_tok_s": pk["hbm_gbs"] * 1e9 / b["per_token"],
                                     "peak_source": pk["source"]},
             "roofline": {"kernel": f"k_{dom}", "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
@@ -320,7 +337,7 @@ def run_ours(args) -> None:
             "phases_ms": phases_ms,
             "decode_path": "whole-token kernel (1 launch per token)" if decode_path[0] == 0
                            else f"per-phase kernels ({phases['launches']} launches per token)",
-            "e2e": {"value": k2 * world / (ms_e2e / 1e3), "unit": "tok/s", "steps": k2,
+            "e2e": {"value": k2 * streams / (ms_e2e / 1e3), "unit": "tok/s", "steps": k2,
                     "h2d_bytes_per_step": 4, "d2h_bytes_per_step": spec.vocab * 4 + 8,
                     "wall_tok_s": k2 / wall_e2e,
                     "path": "qc_forward(token -> logits) per step + host argmax (reference chat loop, greedy)"},
@@ -389,6 +406,8 @@ def main():
     ap.add_argument("--decode-mode", type=int, default=0, choices=[0, 1],
                     help="0: whole-token kernel when the model fits it (default); 1: per-phase kernels")
     ap.add_argument("--ref-max-steps", type=int, default=8)
+    ap.add_argument("--ep", action="store_true",
+                    help="N > 1: one decode stream with the experts split over the ranks (expert parallelism)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

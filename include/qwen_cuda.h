@@ -89,6 +89,23 @@ int qc_engine_create(const qc_tensor_desc* tensors, size_t n_tensors, const uint
 /* Parse a GGUF image held in memory (gguf.rs:102-195, model.rs:21-90) and build the engine. */
 int qc_engine_create_gguf(const uint8_t* image, size_t len, uint32_t context, int device, qc_engine** out);
 
+/* Expert parallelism (no counterpart in the reference): as qc_engine_create_gguf, but this engine
+ * holds only experts [rank*E/world, (rank+1)*E/world) of the `world` ranks (world <= 8, one process
+ * and one GPU per rank) and replicates everything else.  Every rank computes the router and the
+ * top-k itself, runs the selected experts it holds, and adds its partial MoE vector straight into
+ * the other ranks' exchange buffers over NVLink (8-byte tagged values, system scope), so one token
+ * is one launch on every rank with no separate collective.  Before the first forward each rank
+ * exports a handle with qc_engine_ep_handle, the host gathers all `world` handles and device ids
+ * (rank order) and passes them to qc_engine_ep_connect on every rank.  All ranks must then run the
+ * same forward / decode calls in the same order; an error on one rank must be followed by
+ * qc_reset on every rank.  Ranks on the same GPU are refused. */
+int qc_engine_create_gguf_ep(const uint8_t* image, size_t len, uint32_t context, int device, uint32_t rank,
+                             uint32_t world, qc_engine** out);
+/* 64-byte CUDA IPC handle of this rank's exchange buffer and an id of its GPU (PCI location). */
+int qc_engine_ep_handle(qc_engine* e, void* handle, int* device_id);
+/* handles: world x 64 bytes, device_ids: world ints, both in rank order. */
+int qc_engine_ep_connect(qc_engine* e, const void* handles, const int* device_ids);
+
 /* Map a GGUF file read-only and build the engine (Gguf::open + Model::new). */
 int qc_engine_open(const char* path, uint32_t context, int device, qc_engine** out);
 

@@ -78,6 +78,7 @@ uint64_t align256(uint64_t v) { return (v + 255) & ~255ull; }
 struct Placed {
   const TensorIn* t = nullptr;
   uint64_t rows = 1, experts = 1, cols = 0;
+  uint64_t src_off = 0;  // byte offset of the first uploaded row in the tensor (expert shards)
   qc::DevLayout lay;
   uint64_t off = 0, off_f32 = 0;
   bool vector = false;
@@ -174,6 +175,12 @@ struct qc_engine {
   unsigned long long* d_ll = nullptr;
   qc::LayerDev* d_layers = nullptr;
   bool use_token = false;
+  // expert parallelism: this engine holds experts [e_lo, e_lo + e_n) of `ep_world` shards and adds its
+  // partial MoE vector into the peers' exchange buffers (CUDA IPC mappings)
+  uint32_t ep_rank = 0, ep_world = 1, e_lo = 0, e_n = 0;
+  bool ep_connected = false;
+  unsigned long long* peer_ll[8] = {};
+  unsigned long long** d_peers = nullptr;
   uint32_t* d_gen = nullptr;
   cudaStream_t own = nullptr, stream = nullptr;
   cudaGraph_t graph = nullptr;
@@ -198,6 +205,9 @@ struct qc_engine {
     cudaFree(d_weights);
     cudaFree(d_kv);
     cudaFree(d_scratch);
+    for (uint32_t q = 0; q < ep_world && q < 8; q++)
+      if (q != ep_rank && peer_ll[q]) cudaIpcCloseMemHandle(peer_ll[q]);
+    cudaFree(d_peers);
     cudaFree(d_ll);
     cudaFree(d_layers);
     if (own) cudaStreamDestroy(own);
@@ -251,10 +261,17 @@ struct qc_engine {
   }
 
   // ---- build ------------------------------------------------------------------------------
-  void build(const std::map<std::string, TensorIn>& t, const qc_config& c, uint32_t ctx, int dev) {
+  void build(const std::map<std::string, TensorIn>& t, const qc_config& c, uint32_t ctx, int dev, uint32_t rank = 0,
+             uint32_t world = 1) {
     cfg = c;
     validate_config(cfg);
     validate_tensors(t);
+    ensure(world >= 1 && world <= 8 && rank < world, "expert parallelism: need 1 <= world <= 8 and rank < world");
+    ensure(cfg.experts % world == 0, "expert parallelism: the expert count must be a multiple of the world size");
+    ep_rank = rank;
+    ep_world = world;
+    e_n = cfg.experts / world;
+    e_lo = rank * e_n;
     ensure(ctx > 0 && ctx <= cfg.max_context, "context must be in 1..=" + std::to_string(cfg.max_context));
     context = ctx;
     device = dev;
@@ -288,6 +305,10 @@ struct qc_engine {
       uint64_t raw_row;
       if (const char* e = qc::ggml_row_bytes(ti.kind, p.cols, &raw_row)) throw ApiError(QC_ERR_INVALID, n + ": " + e);
       ensure(ti.len == raw_row * p.rows * p.experts, n + ": tensor length does not match its shape");
+      if (p.experts > 1) {  // an expert stack: only this shard's experts are placed and uploaded
+        p.src_off = (uint64_t)e_lo * p.rows * raw_row;
+        p.experts = e_n;
+      }
       ensure(p.rows <= 0xffffffffull && p.cols <= 0xffffffffull, n + ": tensor too large");
       max_row = raw_row > max_row ? raw_row : max_row;
       p.lay = qc::dev_layout(ti.kind, p.cols);
@@ -309,8 +330,8 @@ struct qc_engine {
         const Placed& p = placed[n];
         uint64_t raw_row;
         qc::ggml_row_bytes(p.t->kind, p.cols, &raw_row);
-        stats.uploaded_bytes += up.put(p.t->data, p.rows * p.experts, (uint32_t)p.rows, raw_row, p.t->kind, p.cols,
-                                       d_weights + p.off, p.lay, p.lay.expert_bytes(p.rows));
+        stats.uploaded_bytes += up.put(p.t->data + p.src_off, p.rows * p.experts, (uint32_t)p.rows, raw_row, p.t->kind,
+                                       p.cols, d_weights + p.off, p.lay, p.lay.expert_bytes(p.rows));
         if (p.vector) {
           qc::launch_dequant(make_desc(p, d_weights), 0, reinterpret_cast<float*>(d_weights + p.off_f32), stream);
           QC_CK(cudaGetLastError());
@@ -422,13 +443,21 @@ struct qc_engine {
     ensure(qc::step_smem_max(step_args(), plan) <= (size_t)kMaxSmem,
            "model dimensions need more shared memory per block than the CUDA engine supports");
     token_why = qc::plan_token(step_args(), 1 << 30, &tplan);
+    ensure(world == 1 || !token_why,
+           std::string("expert parallelism needs the whole-token kernel: ") + (token_why ? token_why : ""));
+    QC_CK(cudaMalloc(&d_peers, 8 * sizeof(unsigned long long*)));
     if (!token_why) {
       const uint64_t n = tplan.ll_layer * cfg.layers;
       QC_CK(cudaMalloc(&d_ll, n * sizeof(unsigned long long)));
       QC_CK(cudaMemset(d_ll, 0, n * sizeof(unsigned long long)));  // tag 0: never a token's tag
     }
     use_token = !token_why;
-    capture();
+    ep_connected = world == 1;
+    if (world == 1) {
+      peer_ll[0] = d_ll;
+      QC_CK(cudaMemcpy(d_peers, peer_ll, 8 * sizeof(unsigned long long*), cudaMemcpyHostToDevice));
+      capture();
+    }
   }
 
   qc::StepArgs step_args() const {
@@ -439,6 +468,11 @@ struct qc_engine {
     a.layers = layers.data();
     a.layers_dev = d_layers;
     a.n_layers = cfg.layers;
+    a.ep_rank = ep_rank;
+    a.ep_world = ep_world;
+    a.e_lo = e_lo;
+    a.e_n = e_n;
+    a.peers = d_peers;
     a.embd = embd;
     a.out = out;
     a.out_norm = out_norm;
@@ -452,6 +486,7 @@ struct qc_engine {
         capture_once();
         return;
       } catch (const ApiError&) {
+        if (ep_world > 1) throw;  // the per-phase kernels have no expert-parallel form
         cudaGetLastError();
         token_why = "the cooperative whole-token launch could not be captured in a CUDA graph";
         use_token = false;
@@ -477,6 +512,7 @@ struct qc_engine {
   // Decode path: 0 = the whole-token kernel when the model fits it, 1 = the per-phase kernels.
   void set_mode(int mode) {
     ensure(mode == 0 || mode == 1, "decode mode must be 0 (auto) or 1 (per-phase kernels)");
+    ensure(mode == 0 || ep_world == 1, "an expert-parallel engine runs only the whole-token kernel");
     const bool want = mode == 0 && !token_why;
     if (want == use_token) return;
     QC_CK(cudaSetDevice(device));
@@ -493,6 +529,40 @@ struct qc_engine {
     prof_ev.clear();
     prof_kind.clear();
     use_token = want;
+    capture();
+  }
+
+  // ---- expert parallelism: exchange-buffer handles -------------------------------------------
+  void ep_handle(void* out_handle, int* pci) {
+    ensure(ep_world > 1, "not an expert-parallel engine");
+    QC_CK(cudaSetDevice(device));
+    cudaIpcMemHandle_t h;
+    QC_CK(cudaIpcGetMemHandle(&h, d_ll));
+    std::memcpy(out_handle, &h, sizeof h);
+    cudaDeviceProp prop;
+    QC_CK(cudaGetDeviceProperties(&prop, device));
+    *pci = prop.pciDomainID * 65536 + prop.pciBusID * 256 + prop.pciDeviceID;
+  }
+  void ep_connect(const uint8_t* handles, const int* pci) {
+    ensure(ep_world > 1, "not an expert-parallel engine");
+    ensure(!ep_connected, "expert-parallel engine already connected");
+    for (uint32_t a = 0; a < ep_world; a++)
+      for (uint32_t b = a + 1; b < ep_world; b++)
+        ensure(pci[a] != pci[b], "expert-parallel ranks must be on different GPUs");  // kernels wait on each other
+    QC_CK(cudaSetDevice(device));
+    for (uint32_t q = 0; q < ep_world; q++) {
+      if (q == ep_rank) {
+        peer_ll[q] = d_ll;
+        continue;
+      }
+      cudaIpcMemHandle_t h;
+      std::memcpy(&h, handles + 64 * q, sizeof h);
+      void* ptr = nullptr;
+      QC_CK(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+      peer_ll[q] = static_cast<unsigned long long*>(ptr);
+    }
+    QC_CK(cudaMemcpy(d_peers, peer_ll, 8 * sizeof(unsigned long long*), cudaMemcpyHostToDevice));
+    ep_connected = true;
     capture();
   }
 
@@ -529,6 +599,7 @@ struct qc_engine {
 
   void profile(qc_phase_times* out) {
     ensure(pos < context, "context limit " + std::to_string(context) + " reached", QC_ERR_CONTEXT);
+    ensure(ep_connected, "expert-parallel engine is not connected to its peers");
     QC_CK(cudaSetDevice(device));
     if (use_token) {  // one kernel per token: its whole duration
       *out = qc_phase_times{};
@@ -589,6 +660,7 @@ struct qc_engine {
   }
 
   void forward(uint32_t token, float* logits) {
+    ensure(ep_connected, "expert-parallel engine is not connected to its peers");
     ensure(pos < context, "context limit " + std::to_string(context) + " reached", QC_ERR_CONTEXT);
     ensure(token < cfg.vocab, "token outside vocabulary", QC_ERR_TOKEN);
     QC_CK(cudaSetDevice(device));
@@ -608,6 +680,7 @@ struct qc_engine {
   }
 
   void decode(uint32_t n, uint32_t* tokens_out, float* logits, bool wait) {
+    ensure(ep_connected, "expert-parallel engine is not connected to its peers");
     ensure(pos > 0, "greedy decode needs the logits of a previous forward");
     ensure((uint64_t)pos + n <= context, "prompt + max-tokens exceed --ctx", QC_ERR_CONTEXT);
     QC_CK(cudaSetDevice(device));
@@ -715,7 +788,8 @@ int api_forward(qc_engine* e, F&& f) {
   return rc;
 }
 
-int create_from(const qc::GgufFile& g, const uint8_t* base, uint32_t context, int device, qc_engine** out) {
+int create_from(const qc::GgufFile& g, const uint8_t* base, uint32_t context, int device, qc_engine** out,
+                uint32_t rank = 0, uint32_t world = 1) {
   std::unique_ptr<qc_engine> e(new qc_engine);
   const qc_config c = config_from(g);
   std::map<std::string, TensorIn> t;
@@ -728,7 +802,7 @@ int create_from(const qc::GgufFile& g, const uint8_t* base, uint32_t context, in
     ti.len = kv.second.len;
     t[kv.first] = ti;
   }
-  e->build(t, c, context, device);
+  e->build(t, c, context, device, rank, world);
   *out = e.release();
   return QC_OK;
 }
@@ -792,6 +866,31 @@ int qc_engine_create_gguf(const uint8_t* image, size_t len, uint32_t context, in
     qc::GgufFile g;
     g.parse(image, len);
     create_from(g, image, context, device, out);
+  });
+}
+
+int qc_engine_create_gguf_ep(const uint8_t* image, size_t len, uint32_t context, int device, uint32_t rank,
+                             uint32_t world, qc_engine** out) {
+  return api(nullptr, [&] {
+    ensure(out && (image || !len), "null argument");
+    *out = nullptr;
+    qc::GgufFile g;
+    g.parse(image, len);
+    create_from(g, image, context, device, out, rank, world);
+  });
+}
+
+int qc_engine_ep_handle(qc_engine* e, void* handle, int* device_id) {
+  return api(e, [&] {
+    ensure(e && handle && device_id, "null argument");
+    e->ep_handle(handle, device_id);
+  });
+}
+
+int qc_engine_ep_connect(qc_engine* e, const void* handles, const int* device_ids) {
+  return api(e, [&] {
+    ensure(e && handles && device_ids, "null argument");
+    e->ep_connect(static_cast<const uint8_t*>(handles), device_ids);
   });
 }
 

@@ -88,6 +88,9 @@ struct StepArgs {
   const LayerDev* layers;      // host array
   const LayerDev* layers_dev;  // the same array in device memory (whole-token kernel)
   uint32_t n_layers;
+  // expert parallelism (whole-token kernel): shard ep_rank of ep_world holds experts [e_lo, e_lo + e_n)
+  uint32_t ep_rank, ep_world, e_lo, e_n;
+  unsigned long long* const* peers;  // device array: exchange buffers of the ranks (own included)
   MatDesc embd, out;
   const float* out_norm;
   int sms;
@@ -126,7 +129,7 @@ struct TokenPlan {
   uint32_t out_sg, nsp, nsq;            // vocab stage groups; stage slots in P and Q
   uint32_t nsegs;                       // row-run descriptors in shared memory
   uint32_t part_floats;                 // unit-group partial sums of the row engine
-  uint64_t ll_qkv, ll_part, ll_attn, ll_xmid, ll_rl, ll_h, ll_xout, ll_layer;  // exchange buffer offsets
+  uint64_t ll_qkv, ll_part, ll_attn, ll_xmid, ll_rl, ll_h, ll_xout, ll_moe, ll_layer;  // exchange buffer offsets
 };
 // Fills *p and returns nullptr if the model fits the whole-token kernel, else the reason it does not.
 const char* plan_token(const StepArgs& a, int max_smem, TokenPlan* p);

@@ -68,6 +68,10 @@ struct TokenParams {
   float eps;
   uint32_t p_bytes, q_bytes, stage_off, misc_off;
   uint32_t smax, out_sg, nsp, nsq, nsegs, part_floats;
+  // expert parallelism: rank of world, local experts [e_lo, e_lo + e_n), ranks' exchange buffers
+  uint32_t world, rank, e_lo, e_n;
+  unsigned long long* const* peers;
+  uint64_t ll_moe;
 };
 
 // ---- primitives -----------------------------------------------------------------------------
@@ -98,6 +102,18 @@ QC_DEV void ll_get2(const unsigned long long* p, unsigned long long* a, unsigned
 QC_DEV unsigned long long ll_get(const unsigned long long* p) {
   unsigned long long v;
   asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// System-scope forms for the expert-parallel exchange: written by a peer GPU over NVLink.
+QC_DEV void ll_put_sys(unsigned long long* p, float v, uint32_t seq) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(tagged(v, seq)) : "memory");
+}
+QC_DEV void ll_get2_sys(const unsigned long long* p, unsigned long long* a, unsigned long long* b) {
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(*a), "=l"(*b) : "l"(p) : "memory");
+}
+QC_DEV unsigned long long ll_get_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 QC_DEV bool fresh(unsigned long long v, uint32_t seq) { return (uint32_t)(v >> 32) == seq; }
@@ -145,6 +161,15 @@ QC_DEV float ll_wait1(const unsigned long long* p, uint32_t seq, DevState* st) {
   return val(v);
 }
 
+// As ll_wait1 for a value that a peer GPU writes.
+QC_DEV float ll_wait1_sys(const unsigned long long* p, uint32_t seq, DevState* st) {
+  unsigned long long v;
+  Waiter w;
+  while (!fresh(v = ll_get_sys(p), seq) && w.keep(st)) {
+  }
+  return val(v);
+}
+
 // Tagged values [0, n) of src (16-byte aligned) into dst(i, value); each thread
 // polls up to 8 pairs at a time until all carry `seq`.  No barrier inside.
 template <class Dst>
@@ -182,7 +207,10 @@ QC_DEV void ll_gather(const unsigned long long* src, uint32_t n, Dst dst, uint32
 template <bool RMS>
 QC_DEV void stage_ll(uint8_t* mem, uint32_t nv, uint32_t n, uint32_t units, bool with_float,
                      const unsigned long long* __restrict__ src, const float* __restrict__ w, float eps, float* red,
-                     uint32_t seq, DevState* st, bool trace = false, int tslot = 0) {
+                     uint32_t seq, DevState* st, bool trace = false, int tslot = 0,
+                     const unsigned long long* add = nullptr, uint32_t nadd = 0) {
+  // (with nadd > 0, nv == 1 and each element is src[i] + add[0*n + i] + add[1*n + i] + ..., the adds
+  // written by peer GPUs and read at system scope, summed in order)
   const uint32_t per = units4(units) * 64;
   const uint32_t total = nv * per, xb = xview_bytes(units, with_float);
   constexpr int P = 2;
@@ -207,12 +235,21 @@ QC_DEV void stage_ll(uint8_t* mem, uint32_t nv, uint32_t n, uint32_t units, bool
 #pragma unroll
         for (int q = 0; q < 4; q++) {
           unsigned long long a = 0ull, b = 0ull;
+          float xa = 0.f, xb = 0.f;
           if (i0 < total && e + 2 * q < n) {  // n even: the whole pair is inside
             ll_get2(src + (uint64_t)j * n + e + 2 * q, &a, &b);
             ok &= fresh(a, seq) && fresh(b, seq);
+            xa = val(a);
+            xb = val(b);
+            for (uint32_t k = 0; k < nadd; k++) {
+              ll_get2_sys(add + (uint64_t)k * n + e + 2 * q, &a, &b);
+              ok &= fresh(a, seq) && fresh(b, seq);
+              xa = __fadd_rn(xa, val(a));
+              xb = __fadd_rn(xb, val(b));
+            }
           }
-          x[p][2 * q] = val(a);
-          x[p][2 * q + 1] = val(b);
+          x[p][2 * q] = xa;
+          x[p][2 * q + 1] = xb;
         }
       }
     } while (!ok && wt.keep(st));
@@ -427,6 +464,7 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
   const uint32_t E4 = (E + 3) / 4;
   uint8_t* mp = sm + T.misc_off;
   uint32_t* const key = reinterpret_cast<uint32_t*>(mp);
+  uint32_t* const lsl = key;  // after the ranking: the selected slots this rank holds
   mp += E4 * 16;
   float* const lg = reinterpret_cast<float*>(mp);
   mp += up16(E * 4);
@@ -459,6 +497,10 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
   __syncthreads();
   uint32_t parP = 0, parQ = 0;
   const uint32_t nbl = nb;
+  // The ranks' MoE partials alternate between two halves by step parity: a rank one step ahead
+  // writes the other half, and it can reach this half again only after every rank's previous
+  // kernel (the one reading it) has ended.
+  const uint64_t moe_half = T.ll_moe + (uint64_t)(seq & 1) * T.world * T.hidden;
 
   // ---- slices of this block (per layer; byte counts depend on the layer's formats) ----
   struct Slices {
@@ -546,7 +588,11 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
     const LayerDev& L = Ld[l & 1];
     const Slices s = slices(L);
     unsigned long long* const LL = T.ll + (uint64_t)l * T.ll_layer;
-    const unsigned long long* const Xin = l ? T.ll + (uint64_t)(l - 1) * T.ll_layer + T.ll_xout : nullptr;
+    // x of this layer: the previous layer's output (one rank), or its x' plus every rank's MoE partial
+    const bool ep = T.world > 1;
+    const unsigned long long* const Xin =
+        l ? T.ll + (uint64_t)(l - 1) * T.ll_layer + (ep ? T.ll_xmid : T.ll_xout) : nullptr;
+    const unsigned long long* const Xadd = l && ep ? T.ll + (uint64_t)(l - 1) * T.ll_layer + moe_half : nullptr;
     float* const kc_h = L.kc + (uint64_t)ah * T.ctx * D;
     float* const vc_h = L.vc + (uint64_t)ah * T.ctx * D;
     QC_TT(0);
@@ -574,7 +620,8 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
           stg, 1, T.hidden, L.q.units, flA, [&](uint32_t, uint32_t i) { return dequant_one(T.embd, erow, edrow, i); },
           L.attn_norm, T.eps, red);
     else
-      stage_ll<true>(stg, 1, T.hidden, L.q.units, flA, Xin, L.attn_norm, T.eps, red, seq, st, l == 1, 20);
+      stage_ll<true>(stg, 1, T.hidden, L.q.units, flA, Xin, L.attn_norm, T.eps, red, seq, st, l == 1, 20, Xadd,
+                     ep ? T.world : 0);
     QC_TT(1);
     const XView xa = xview_at(stg, L.q.units, flA);
     if (s.bA) {
@@ -833,7 +880,12 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
     const bool flO = uses_float_x(L.o.kind);
     const uint32_t or0 = s.so.b * 8, or1 = min(L.o.rows, s.so.e * 8);
     for (uint32_t r = or0 + tid; r < or1; r += TNT)
-      xres[r - or0] = l == 0 ? dequant_one(T.embd, erow, edrow, r) : ll_wait1(Xin + r, seq, st);
+      if (l == 0) xres[r - or0] = dequant_one(T.embd, erow, edrow, r);
+      else {
+        float v = ll_wait1(Xin + r, seq, st);
+        for (uint32_t q = 0; ep && q < T.world; q++) v = __fadd_rn(v, ll_wait1_sys(Xadd + (uint64_t)q * T.hidden + r, seq, st));
+        xres[r - or0] = v;
+      }
     if (tid == 0) segs[0] = make_seg(L.o, rQ, or0, or1, or0, xres, nullptr, LL + T.ll_xmid + or0);
     stage_ll<false>(stg, 1, QD, L.o.units, flO, LL + T.ll_attn, nullptr, 0.f, red, seq, st, l == 1, 21);
     QC_TT(5);
@@ -907,33 +959,45 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
       __syncwarp();
       QC_TT(29);
       const float sum = red[1];
-      // the selected experts' gate/up rows into P (Q/K/V and K/V rows consumed), down rows into Q
-      const uint32_t gi = groups_of(L.gate.rows);
-      uint32_t nruns = 0;
-      for (uint32_t i = s.sg.b; i < s.sg.e; nruns++) i += min(gi - i % gi, s.sg.e - i);
+      // the selected experts this rank holds (all of them on one rank), in selection order: lsl
       if (lane == 0) {
-        proxy_fence();
-        if (s.bGU) mb_expect(&mbar[0], s.bGU);
-        if (s.bD) mb_expect(&mbar[1], s.bD);
+        uint32_t n = 0;
+        for (uint32_t k = 0; k < top; k++)
+          if (sel[k] - T.e_lo < T.e_n) lsl[n++] = k;
+        red[3] = __uint_as_float(n);
       }
       __syncwarp();
-      for (uint32_t q = lane; q < 2 * nruns + (s.bD ? top : 0); q += 32) {
+      const uint32_t nl = __float_as_uint(red[3]);
+      const Span sgd = span_of(nl * groups_of(L.gate.rows), nbl, c);
+      const uint32_t bGU = sgd.n() * (L.gate.group_bytes + L.up.group_bytes), bD = nl * s.sd.n() * L.down.group_bytes;
+      // their gate/up rows into P (Q/K/V and K/V rows consumed), down rows into Q
+      const uint32_t gi = groups_of(L.gate.rows);
+      uint32_t nruns = 0;
+      for (uint32_t i = sgd.b; i < sgd.e; nruns++) i += min(gi - i % gi, sgd.e - i);
+      if (lane == 0) {
+        proxy_fence();
+        if (bGU) mb_expect(&mbar[0], bGU);
+        if (bD) mb_expect(&mbar[1], bD);
+      }
+      __syncwarp();
+      for (uint32_t q = lane; q < 2 * nruns + (bD ? nl : 0); q += 32) {
         if (q < 2 * nruns) {  // run q/2, gate (q even) or up
-          uint32_t i = s.sg.b, off = 0;
+          uint32_t i = sgd.b, off = 0;
           for (uint32_t r = 0; r < q / 2; r++) {
-            const uint32_t ng = min(gi - i % gi, s.sg.e - i);
+            const uint32_t ng = min(gi - i % gi, sgd.e - i);
             off += ng * (L.gate.group_bytes + L.up.group_bytes);
             i += ng;
           }
-          const uint32_t g0 = i % gi, ng = min(gi - g0, s.sg.e - i), e = sel[i / gi];
+          const uint32_t g0 = i % gi, ng = min(gi - g0, sgd.e - i), e = sel[lsl[i / gi]] - T.e_lo;
           const MatDesc& m = q & 1 ? L.up : L.gate;
           bulk_copy(rP + off + (q & 1) * ng * L.gate.group_bytes,
                     m.w + (uint64_t)e * m.expert_stride + (uint64_t)g0 * m.group_bytes, ng * m.group_bytes, &mbar[0]);
         } else {
           const uint32_t k = q - 2 * nruns, per = s.sd.n() * L.down.group_bytes;
           bulk_copy(rQ + k * per,
-                    L.down.w + (uint64_t)sel[k] * L.down.expert_stride + (uint64_t)s.sd.b * L.down.group_bytes, per,
-                    &mbar[1]);
+                    L.down.w + (uint64_t)(sel[lsl[k]] - T.e_lo) * L.down.expert_stride +
+                        (uint64_t)s.sd.b * L.down.group_bytes,
+                    per, &mbar[1]);
         }
       }
       QC_TT(30);
@@ -942,9 +1006,12 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
     }
     __syncthreads();
     QC_TT(9);
-    const uint32_t gi = groups_of(L.gate.rows), nitem = s.sg.n();
+    const uint32_t nl = __float_as_uint(red[3]);  // selected experts held here (top on one rank)
+    const Span sgd = span_of(nl * groups_of(L.gate.rows), nbl, c);
+    const uint32_t bGUd = sgd.n() * (L.gate.group_bytes + L.up.group_bytes), bDd = nl * s.sd.n() * L.down.group_bytes;
+    const uint32_t gi = groups_of(L.gate.rows), nitem = sgd.n();
     float* const gout = xres;  // [2][nitem * 8] gate then up results
-    if (s.bGU) {
+    if (bGUd) {
       mb_wait(&mbar[0], parP, st);
       parP ^= 1;
     }
@@ -952,8 +1019,8 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
     uint32_t nruns = 0;
     if (tid == 0) {  // all gate runs, then all up runs (runs of one format go to one call)
       uint32_t off = 0;
-      for (uint32_t i = s.sg.b; i < s.sg.e; nruns++) {
-        const uint32_t g0 = i % gi, ng = min(gi - g0, s.sg.e - i), it0 = i - s.sg.b;
+      for (uint32_t i = sgd.b; i < sgd.e; nruns++) {
+        const uint32_t g0 = i % gi, ng = min(gi - g0, sgd.e - i), it0 = i - sgd.b;
         const uint32_t r0 = g0 * 8, r1 = min(L.gate.rows, (g0 + ng) * 8);
         segs[nruns] = make_seg(L.gate, rP + off, r0, r1, r0, nullptr, gout + it0 * 8, nullptr);
         off += ng * L.gate.group_bytes;
@@ -971,7 +1038,7 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
     rows_finish(segs, 2 * nruns, L.gate.units, part, seq);
     __syncthreads();
     for (uint32_t idx = tid; idx < nitem * 8; idx += TNT) {
-      const uint32_t i = s.sg.b + idx / 8, slot = i / gi, r = (i % gi) * 8 + idx % 8;
+      const uint32_t i = sgd.b + idx / 8, slot = i / gi, r = (i % gi) * 8 + idx % 8;  // slot: index into lsl
       if (r < T.inter) {
         const float gv = gout[idx], uv = gout[nitem * 8 + idx];
         ll_put(LL + T.ll_h + (uint64_t)slot * T.inter + r, __fmul_rn(gv / (1.f + expf(-gv)), uv), seq);
@@ -996,31 +1063,34 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
     for (uint32_t r = dr0 + tid; r < dr1; r += TNT) dres[r - dr0] = ll_wait1(LL + T.ll_xmid + r, seq, st);
     {
       const uint32_t pbytes = s.sd.n() * L.down.group_bytes;
-      for (uint32_t k = tid; k < top; k += TNT)
+      for (uint32_t k = tid; k < nl; k += TNT)
         segs[k] = make_seg(L.down, rQ + k * pbytes, dr0, dr1, dr0, nullptr, dout + k * nd, nullptr);
     }
-    stage_ll<false>(stg, top, T.inter, L.down.units, flD, LL + T.ll_h, nullptr, 0.f, red, seq, st, l == 1, 23);
+    stage_ll<false>(stg, nl, T.inter, L.down.units, flD, LL + T.ll_h, nullptr, 0.f, red, seq, st, l == 1, 23);
     QC_TT(12);
     const uint32_t xb = xview_bytes(L.down.units, flD);
-    if (s.bD) {
+    if (bDd) {
       mb_wait(&mbar[1], parQ, st);
       parQ ^= 1;
     }
     QC_TT(13);
     const uint32_t dpart = unit_groups(L.down.units) * (dr1 > dr0 ? dr1 - dr0 : 0);
-    if (dr1 > dr0) {
-      const uint32_t per = nw >= top ? nw / top : 1;
-      for (uint32_t k = warp / per; k < top; k += nw / per)
+    if (dr1 > dr0 && nl) {
+      const uint32_t per = nw >= nl ? nw / nl : 1;
+      for (uint32_t k = warp / per; k < nl; k += nw / per)
         run_rows(segs + k, 1, L.down.units, xview_at(stg + k * xb, L.down.units, flD), part + k * dpart, warp % per,
                  per);
     }
     __syncthreads();
-    for (uint32_t k = 0; k < top; k++) rows_finish(segs + k, 1, L.down.units, part + k * dpart, seq);
+    for (uint32_t k = 0; k < nl; k++) rows_finish(segs + k, 1, L.down.units, part + k * dpart, seq);
     __syncthreads();
     for (uint32_t r = dr0 + tid; r < dr1; r += TNT) {
       float acc = 0.f;
-      for (uint32_t k = 0; k < top; k++) acc = __fadd_rn(acc, __fmul_rn(selw[k], dout[k * nd + r - dr0]));
-      ll_put(LL + T.ll_xout + r, __fadd_rn(dres[r - dr0], acc), seq);
+      for (uint32_t k = 0; k < nl; k++) acc = __fadd_rn(acc, __fmul_rn(selw[lsl[k]], dout[k * nd + r - dr0]));
+      if (!ep) ll_put(LL + T.ll_xout + r, __fadd_rn(dres[r - dr0], acc), seq);
+      else  // this rank's share of moe, into every rank's exchange buffer
+        for (uint32_t q = 0; q < T.world; q++)
+          ll_put_sys(T.peers[q] + (uint64_t)l * T.ll_layer + moe_half + (uint64_t)T.rank * T.hidden + r, acc, seq);
     }
     __syncthreads();
     if (tid == 0) {  // region Q is free: next layer's O + router slice, or the remaining vocab stages
@@ -1035,8 +1105,10 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
   // ---- logits = W_out rms(x, output_norm); finiteness; greedy argmax (ties to the lower index) --
   const MatDesc& mo = T.out;
   const bool flV = uses_float_x(mo.kind);
-  stage_ll<true>(stg, 1, T.hidden, mo.units, flV, T.ll + (uint64_t)(T.n_layers - 1) * T.ll_layer + T.ll_xout,
-                 T.out_norm, T.eps, red, seq, st);
+  stage_ll<true>(stg, 1, T.hidden, mo.units, flV,
+                 T.ll + (uint64_t)(T.n_layers - 1) * T.ll_layer + (T.world > 1 ? T.ll_xmid : T.ll_xout), T.out_norm,
+                 T.eps, red, seq, st, false, 0, T.world > 1 ? T.ll + (uint64_t)(T.n_layers - 1) * T.ll_layer + moe_half : nullptr,
+                 T.world > 1 ? T.world : 0);
   QC_TO(0);
   const XView xv = xview_at(stg, mo.units, flV);
   unsigned long long best = 0ull;
@@ -1227,6 +1299,8 @@ const char* plan_token(const StepArgs& a, int max_smem, TokenPlan* p) {
   o += ev((uint64_t)d.top * d.inter);
   t.ll_xout = o;
   o += ev(d.hidden);
+  t.ll_moe = o;  // [2][world][hidden] partial MoE vectors written by the ranks (expert parallelism)
+  o += a.ep_world > 1 ? ev(2ull * a.ep_world * d.hidden) : 0;
   t.ll_layer = o;
   *p = t;
   return nullptr;
@@ -1271,6 +1345,12 @@ void launch_token(const StepArgs& a, const TokenPlan& p, unsigned long long* ll,
   T.nsp = p.nsp;
   T.nsq = p.nsq;
   T.nsegs = p.nsegs;
+  T.world = a.ep_world ? a.ep_world : 1;
+  T.rank = a.ep_rank;
+  T.e_lo = a.e_lo;
+  T.e_n = a.e_n ? a.e_n : d.experts;
+  T.peers = a.peers;
+  T.ll_moe = p.ll_moe;
   T.part_floats = p.part_floats;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.nb);

@@ -28,8 +28,19 @@ EXPORTS = (
     "qc_decode_greedy", "qc_decode_enqueue", "qc_sync", "qc_reset", "qc_position", "qc_get_stats",
     "qc_logits_device", "qc_row_bytes", "qc_matrix_create", "qc_matrix_matvec", "qc_matrix_dequant",
     "qc_matrix_bytes", "qc_matrix_destroy", "qc_packed_matvec", "qc_profile_step", "qc_packed_matvec_noalloc",
-    "qc_engine_set_decode_mode", "qc_engine_decode_path",
+    "qc_engine_set_decode_mode", "qc_engine_decode_path", "qc_engine_create_gguf_ep", "qc_engine_ep_handle",
+    "qc_engine_ep_connect",
 )
+
+
+def connect_group(eng, group=None) -> None:
+    """Connect an expert-parallel engine to its peers: all-gather every rank's
+    ep_handle() over torch.distributed (any backend; rank order of `group`),
+    then Engine.connect.  Each rank of the group must call it."""
+    import torch.distributed as dist
+    allh = [None] * dist.get_world_size(group)
+    dist.all_gather_object(allh, eng.ep_handle(), group=group)
+    eng.connect(allh)
 
 
 class QwenCudaError(RuntimeError):
@@ -112,6 +123,9 @@ def lib() -> C.CDLL:
         L.qc_packed_matvec_noalloc.argtypes = [u32, u64, u64, vp, u64, vp, vp]
         L.qc_engine_set_decode_mode.argtypes = [vp, C.c_int]
         L.qc_engine_decode_path.argtypes = [vp, C.POINTER(C.c_int), C.POINTER(C.c_char_p)]
+        L.qc_engine_create_gguf_ep.argtypes = [vp, sz, u32, i, u32, u32, pp]
+        L.qc_engine_ep_handle.argtypes = [vp, vp, C.POINTER(C.c_int)]
+        L.qc_engine_ep_connect.argtypes = [vp, vp, vp]
         _lib = L
     return _lib
 
@@ -179,6 +193,39 @@ class Engine:
         self.vocab = cfg.vocab
         self.context = context
         return self
+
+    @classmethod
+    def expert_parallel(cls, image, context: int, device: int, rank: int, world: int):
+        """qc_engine_create_gguf_ep: this rank's share of the experts (one process and GPU per rank).
+
+        The engine is usable after connect() with every rank's handle."""
+        L = lib()
+        img = _u8(image)
+        h = C.c_void_p()
+        _global_check(L.qc_engine_create_gguf_ep(img.ctypes.data, img.size, context, device, rank, world,
+                                                 C.byref(h)))
+        self = cls.__new__(cls)
+        self._h = h
+        cfg = Config()
+        self._check(L.qc_engine_config(h, C.byref(cfg)))
+        self.config = cfg.as_dict()
+        self.vocab = cfg.vocab
+        self.context = context
+        self.rank, self.world = rank, world
+        return self
+
+    def ep_handle(self) -> tuple[bytes, int]:
+        """(64-byte IPC handle of this rank's exchange buffer, id of its GPU)."""
+        buf = (C.c_uint8 * 64)()
+        dev = C.c_int()
+        self._check(lib().qc_engine_ep_handle(self._h, buf, C.byref(dev)))
+        return bytes(buf), dev.value
+
+    def connect(self, handles: list[tuple[bytes, int]]) -> None:
+        """qc_engine_ep_connect with every rank's ep_handle() in rank order."""
+        hb = np.frombuffer(b"".join(h for h, _ in handles), dtype=np.uint8).copy()
+        ids = np.array([d for _, d in handles], dtype=np.int32)
+        self._check(lib().qc_engine_ep_connect(self._h, hb.ctypes.data, ids.ctypes.data))
 
     def _check(self, rc: int) -> None:
         if rc != OK:
