@@ -46,6 +46,7 @@ enum {
 
 typedef struct qc_engine qc_engine;
 typedef struct qc_matrix qc_matrix;
+typedef struct qc_sampler qc_sampler;
 
 /* Model hyper-parameters; same fields and meaning as model.rs:5-19 Config. */
 typedef struct qc_config {
@@ -138,6 +139,25 @@ int qc_decode_greedy(qc_engine* e, uint32_t n, uint32_t* tokens_out, float* logi
 /* As qc_decode_greedy, but only enqueues the n steps on the engine's stream and
  * returns; qc_sync waits and reports a non-finite output or a bad token. */
 int qc_decode_enqueue(qc_engine* e, uint32_t n);
+
+/* ---- Sampler (sampling.rs:3-65) on the device ---------------------------------------------------
+ * qc_sampler_create ~ Sampler::new(seed, temperature, top_k, top_p): "invalid sampling parameters"
+ * unless temperature is finite and >= 0 and 0 < top_p <= 1; top_k 0 = off.  The random source is
+ * rand 0.8's StdRng (ChaCha12 keyed by seed_from_u64), one keystream word per non-greedy draw.
+ * The sampler lives on `device` and is used with engines on that device. */
+int qc_sampler_create(uint64_t seed, float temperature, uint32_t top_k, float top_p, int device, qc_sampler** out);
+void qc_sampler_destroy(qc_sampler* s);
+/* Sampler::sample on n logits in DEVICE memory (stream: a cudaStream_t or NULL for the sampler's
+ * own); "invalid logits" (QC_ERR_INVALID) when empty or not all finite.  Errors: qc_last_error(). */
+int qc_sampler_sample(qc_sampler* s, const float* device_logits, uint32_t n, void* stream, uint32_t* token);
+/* The next n keystream words of the sampler's StdRng (advances it): reproducibility checks. */
+int qc_sampler_words(qc_sampler* s, uint32_t n, uint32_t* out);
+/* Sampler::sample on the logits of the engine's last step (no step is run). */
+int qc_engine_sample(qc_engine* e, qc_sampler* s, uint32_t* token);
+/* The chat loop with sampling (main.rs:261-282) on the device: n times, sample the current
+ * logits and feed the id to the next step.  tokens_out (n ids) and logits (of the last step) may
+ * be NULL.  Argument errors leave the engine as it was; a failed step resets it. */
+int qc_decode_sample(qc_engine* e, qc_sampler* s, uint32_t n, uint32_t* tokens_out, float* logits);
 int qc_sync(qc_engine* e);
 
 /* model.rs:202-208: clear the KV cache and set the position to 0. */

@@ -661,6 +661,103 @@ int guarded(F&& f) {
   }
 }
 
+// ---- sampling.rs:9-65 with its random source ------------------------------------------------
+// The reference draws from rand 0.8's StdRng seeded by SeedableRng::seed_from_u64.  Those crates
+// (rand 0.8.5's StdRng = rand_chacha 0.3 ChaCha12Rng; rand_core 0.6.4 seed_from_u64) are not in the
+// reference tree; their published algorithms are restated here:
+//  * seed_from_u64: a PCG32 step per 4 seed bytes (state = state * 6364136223846793005 +
+//    11634580027462260723, then the XSH-RR output of the new state, little-endian), 8 steps for the
+//    32-byte ChaCha key;
+//  * ChaCha12: the ChaCha block function (RFC 7539 quarter round) with 12 rounds over
+//    ["expand 32-byte k", key, 64-bit block counter (words 12-13), 64-bit stream id 0 (words 14-15)],
+//    the keystream read as consecutive little-endian u32 words from block 0;
+//  * gen::<f32>(): (next_u32 >> 8) * 2^-24.
+// The block function is pinned by the RFC 7539 block test vectors (20 rounds) in the tests; the
+// rest has no golden in the reference (its test checks determinism only), so sampled ids are
+// unpinned beyond greedy.
+static inline uint32_t rotl32(uint32_t v, int c) { return (v << c) | (v >> (32 - c)); }
+void chacha_block(const uint32_t in[16], int rounds, uint32_t out[16]) {
+  uint32_t x[16];
+  memcpy(x, in, sizeof x);
+  auto qr = [&](int a, int b, int c, int d) {
+    x[a] += x[b]; x[d] = rotl32(x[d] ^ x[a], 16);
+    x[c] += x[d]; x[b] = rotl32(x[b] ^ x[c], 12);
+    x[a] += x[b]; x[d] = rotl32(x[d] ^ x[a], 8);
+    x[c] += x[d]; x[b] = rotl32(x[b] ^ x[c], 7);
+  };
+  for (int r = 0; r < rounds; r += 2) {
+    qr(0, 4, 8, 12); qr(1, 5, 9, 13); qr(2, 6, 10, 14); qr(3, 7, 11, 15);
+    qr(0, 5, 10, 15); qr(1, 6, 11, 12); qr(2, 7, 8, 13); qr(3, 4, 9, 14);
+  }
+  for (int i = 0; i < 16; i++) out[i] = x[i] + in[i];
+}
+struct StdRngState {
+  uint32_t key[8];
+  uint64_t word = 0;  // position in the keystream, in u32 words
+  void seed_from_u64(uint64_t state) {
+    for (int i = 0; i < 8; i++) {
+      state = state * 6364136223846793005ull + 11634580027462260723ull;
+      const uint32_t xs = (uint32_t)(((state >> 18) ^ state) >> 27), rot = (uint32_t)(state >> 59);
+      key[i] = (xs >> rot) | (xs << ((32 - rot) & 31));
+    }
+    word = 0;
+  }
+  uint32_t next_u32() {
+    const uint64_t block = word / 16;
+    uint32_t in[16] = {0x61707865u, 0x3320646eu, 0x79622d32u, 0x6b206574u}, out[16];
+    memcpy(in + 4, key, 32);
+    in[12] = (uint32_t)block;
+    in[13] = (uint32_t)(block >> 32);
+    in[14] = in[15] = 0;
+    chacha_block(in, 12, out);
+    return out[word++ % 16];
+  }
+  float gen_f32() { return (float)(next_u32() >> 8) * (1.0f / 16777216.0f); }
+};
+struct Sampler {
+  StdRngState rng;
+  float temperature, top_p;
+  size_t top_k;
+};
+// sampling.rs:26-65.  Sums are sequential left folds in sorted order, as in the Rust source.
+uint32_t sample(Sampler& s, const float* logits, size_t n) {
+  ENSURE(n > 0, "invalid logits");
+  for (size_t i = 0; i < n; i++) ENSURE(std::isfinite(logits[i]), "invalid logits");
+  std::vector<uint32_t> ids(n);
+  for (size_t i = 0; i < n; i++) ids[i] = (uint32_t)i;
+  std::sort(ids.begin(), ids.end(), [&](uint32_t a, uint32_t b) {
+    int32_t ka = total_key(logits[a]), kb = total_key(logits[b]);
+    if (ka != kb) return ka > kb;
+    return a < b;
+  });
+  if (s.temperature == 0.f) return ids[0];
+  if (s.top_k > 0) ids.resize(std::min(s.top_k, ids.size()));
+  const float mx = logits[ids[0]];
+  std::vector<float> probs(ids.size());
+  for (size_t i = 0; i < ids.size(); i++) probs[i] = expf((logits[ids[i]] - mx) / s.temperature);
+  float total = 0.f;
+  for (float p : probs) total += p;
+  float cumulative = 0.f;
+  size_t keep = probs.size();
+  for (size_t i = 0; i < probs.size(); i++) {
+    cumulative += probs[i] / total;
+    if (cumulative >= s.top_p) {
+      keep = i + 1;
+      break;
+    }
+  }
+  probs.resize(keep);
+  ids.resize(keep);
+  float mass = 0.f;
+  for (float p : probs) mass += p;
+  float draw = s.rng.gen_f32() * mass;
+  for (size_t i = 0; i < keep; i++) {
+    if (draw < probs[i]) return ids[i];
+    draw -= probs[i];
+  }
+  return ids.back();
+}
+
 }  // namespace
 
 extern "C" {
@@ -718,6 +815,27 @@ int or_sample_greedy(const float* logits, size_t n, uint32_t* out) {
   });
 }
 
+void or_chacha_block(const uint32_t* in, int rounds, uint32_t* out) { chacha_block(in, rounds, out); }
+// sampling.rs:10-25 (Sampler::new): parameter checks, then StdRng::seed_from_u64(seed).
+void* or_sampler_new(uint64_t seed, float temperature, size_t top_k, float top_p) {
+  Sampler* out = nullptr;
+  int rc = guarded([&] {
+    ENSURE(std::isfinite(temperature) && temperature >= 0.f && std::isfinite(top_p) && top_p > 0.f && top_p <= 1.f,
+           "invalid sampling parameters");
+    out = new Sampler;
+    out->rng.seed_from_u64(seed);
+    out->temperature = temperature;
+    out->top_k = top_k;
+    out->top_p = top_p;
+  });
+  return rc == 0 ? out : nullptr;
+}
+int or_sampler_sample(void* h, const float* logits, size_t n, uint32_t* out) {
+  return guarded([&] { *out = sample(*static_cast<Sampler*>(h), logits, n); });
+}
+uint32_t or_sampler_next_u32(void* h) { return static_cast<Sampler*>(h)->rng.next_u32(); }
+void or_sampler_key(void* h, uint32_t* key8) { memcpy(key8, static_cast<Sampler*>(h)->rng.key, 32); }
+void or_sampler_free(void* h) { delete static_cast<Sampler*>(h); }
 void* or_model_open(const char* path, size_t context, int threads) {
   Model* out = nullptr;
   int rc = guarded([&] {

@@ -61,6 +61,17 @@ def lib() -> C.CDLL:
         L.or_gguf_check.argtypes = [vp, sz]
         L.or_f16_to_f32.argtypes = [C.c_uint16]
         L.or_f16_to_f32.restype = f32
+        L.or_chacha_block.argtypes = [C.POINTER(u32), C.c_int, C.POINTER(u32)]
+        L.or_chacha_block.restype = None
+        L.or_sampler_new.argtypes = [C.c_uint64, f32, sz, f32]
+        L.or_sampler_new.restype = vp
+        L.or_sampler_sample.argtypes = [vp, fp, sz, C.POINTER(u32)]
+        L.or_sampler_next_u32.argtypes = [vp]
+        L.or_sampler_next_u32.restype = u32
+        L.or_sampler_key.argtypes = [vp, C.POINTER(u32)]
+        L.or_sampler_key.restype = None
+        L.or_sampler_free.argtypes = [vp]
+        L.or_sampler_free.restype = None
         _lib = L
     return _lib
 
@@ -215,3 +226,40 @@ class Model:
             self.close()
         except Exception:
             pass
+
+
+def chacha_block(state16, rounds: int) -> np.ndarray:
+    """The ChaCha block function (input state of 16 words + state) with `rounds` rounds."""
+    a = np.ascontiguousarray(state16, dtype=np.uint32)
+    out = np.empty(16, dtype=np.uint32)
+    lib().or_chacha_block(a.ctypes.data_as(C.POINTER(C.c_uint32)), rounds, out.ctypes.data_as(C.POINTER(C.c_uint32)))
+    return out
+
+
+class Sampler:
+    """sampling.rs Sampler (StdRng = ChaCha12 seeded by seed_from_u64)."""
+
+    def __init__(self, seed: int, temperature: float, top_k: int, top_p: float):
+        h = lib().or_sampler_new(seed, temperature, top_k, top_p)
+        if not h:
+            raise OracleError(lib().or_last_error().decode())
+        self._h = h
+
+    def sample(self, logits) -> int:
+        ll = np.ascontiguousarray(logits, dtype=np.float32)
+        out = C.c_uint32()
+        _check(lib().or_sampler_sample(self._h, _fp(ll), ll.size, C.byref(out)))
+        return out.value
+
+    def next_u32(self) -> int:
+        return lib().or_sampler_next_u32(self._h)
+
+    def key(self) -> np.ndarray:
+        k = np.empty(8, dtype=np.uint32)
+        lib().or_sampler_key(self._h, k.ctypes.data_as(C.POINTER(C.c_uint32)))
+        return k
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().or_sampler_free(self._h)
+            self._h = None

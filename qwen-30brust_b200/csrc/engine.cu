@@ -15,6 +15,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <cmath>
 #include <cstddef>
 #include <cstring>
 #include <memory>
@@ -151,6 +152,32 @@ qc::MatDesc with_lpr(qc::MatDesc m, uint32_t lpr) {
 }
 
 }  // namespace
+
+// sampling.rs:3-8 Sampler: parameters and the StdRng state, resident on one device.
+struct qc_sampler {
+  int device = 0;
+  qc::SamplerDev* d = nullptr;
+  uint32_t* h = nullptr;  // pinned: [0] err, [1] token
+  cudaStream_t own = nullptr;
+  ~qc_sampler() {
+    cudaSetDevice(device);
+    if (own) cudaStreamDestroy(own);
+    cudaFreeHost(h);
+    cudaFree(d);
+  }
+  // Reads the sampled id and the sticky error after `st` drains; the error is cleared.
+  uint32_t finish(cudaStream_t st) {
+    static_assert(offsetof(qc::SamplerDev, token) == offsetof(qc::SamplerDev, err) + 4, "err, token adjacent");
+    QC_CK(cudaMemcpyAsync(h, &d->err, 8, cudaMemcpyDeviceToHost, st));
+    QC_CK(cudaStreamSynchronize(st));
+    if (h[0]) {
+      QC_CK(cudaMemsetAsync(&d->err, 0, 4, st));
+      QC_CK(cudaStreamSynchronize(st));
+      throw ApiError(QC_ERR_INVALID, "invalid logits");
+    }
+    return h[1];
+  }
+};
 
 struct qc_engine {
   int device = 0, sms = 148;
@@ -700,6 +727,35 @@ struct qc_engine {
     QC_CK(cudaEventElapsedTime(&ms, ev0, ev1));
     stats.matvec_ms += ms;
   }
+
+  // The chat loop with a sampler (main.rs:261-282): n times, sample the current logits on the
+  // device and feed the id to the next step; tokens_out gets the n sampled ids.
+  void decode_sample(qc_sampler* smp, uint32_t n, uint32_t* tokens_out, float* logits) {
+    ensure(ep_connected, "expert-parallel engine is not connected to its peers");
+    ensure(smp && smp->device == device, "the sampler lives on another device");
+    ensure(pos > 0, "sampling needs the logits of a previous forward");
+    ensure((uint64_t)pos + n <= context, "prompt + max-tokens exceed --ctx", QC_ERR_CONTEXT);
+    QC_CK(cudaSetDevice(device));
+    h_pinned[4] = 0;  // gen_count
+    QC_CK(cudaMemcpyAsync(&d_state->gen_count, h_pinned + 4, 4, cudaMemcpyHostToDevice, stream));
+    QC_CK(cudaEventRecord(ev0, stream));
+    for (uint32_t i = 0; i < n; i++) {
+      qc::launch_sample(sc.logits, cfg.vocab, smp->d, &d_state->token, stream);
+      QC_CK(cudaGetLastError());
+      launch_steps(1);
+    }
+    QC_CK(cudaEventRecord(ev1, stream));
+    pos += n;
+    stats.tokens += n;
+    stats.matvecs += ((5ull + 3ull * cfg.top) * cfg.layers + 1) * n;
+    if (tokens_out && n) QC_CK(cudaMemcpyAsync(tokens_out, d_gen, (size_t)n * 4, cudaMemcpyDeviceToHost, stream));
+    if (logits) QC_CK(cudaMemcpyAsync(logits, sc.logits, (size_t)cfg.vocab * 4, cudaMemcpyDeviceToHost, stream));
+    check_flags();
+    smp->finish(stream);
+    float ms = 0.f;
+    QC_CK(cudaEventElapsedTime(&ms, ev0, ev1));
+    stats.matvec_ms += ms;
+  }
 };
 
 struct qc_matrix {
@@ -957,6 +1013,82 @@ int qc_decode_greedy(qc_engine* e, uint32_t n, uint32_t* tokens_out, float* logi
 int qc_decode_enqueue(qc_engine* e, uint32_t n) {
   if (e && (e->pos == 0 || (uint64_t)e->pos + n > e->context)) return api(e, [&] { e->decode(n, nullptr, nullptr, false); });
   return api_forward(e, [&] { e->decode(n, nullptr, nullptr, false); });
+}
+
+// ---- sampling.rs ------------------------------------------------------------------------------
+int qc_sampler_create(uint64_t seed, float temperature, uint32_t top_k, float top_p, int device, qc_sampler** out) {
+  return api(nullptr, [&] {
+    ensure(out, "null argument");
+    *out = nullptr;
+    ensure(std::isfinite(temperature) && temperature >= 0.f && std::isfinite(top_p) && top_p > 0.f && top_p <= 1.f,
+           "invalid sampling parameters");  // sampling.rs:11-19
+    std::unique_ptr<qc_sampler> smp(new qc_sampler);
+    smp->device = device;
+    QC_CK(cudaSetDevice(device));
+    qc::SamplerDev init{};
+    // rand_core 0.6.4 SeedableRng::seed_from_u64: one PCG32 step (XSH-RR output) per 4 key bytes
+    uint64_t state = seed;
+    for (int i = 0; i < 8; i++) {
+      state = state * 6364136223846793005ull + 11634580027462260723ull;
+      const uint32_t xs = (uint32_t)(((state >> 18) ^ state) >> 27), rot = (uint32_t)(state >> 59);
+      init.key[i] = (xs >> rot) | (xs << ((32 - rot) & 31));
+    }
+    init.temperature = temperature;
+    init.top_k = top_k;
+    init.top_p = top_p;
+    QC_CK(cudaMalloc(&smp->d, sizeof init));
+    QC_CK(cudaMemcpy(smp->d, &init, sizeof init, cudaMemcpyHostToDevice));
+    QC_CK(cudaMallocHost(&smp->h, 16));
+    QC_CK(cudaStreamCreateWithFlags(&smp->own, cudaStreamNonBlocking));
+    *out = smp.release();
+  });
+}
+
+void qc_sampler_destroy(qc_sampler* s) { delete s; }
+
+int qc_sampler_sample(qc_sampler* s, const float* logits, uint32_t n, void* stream, uint32_t* token) {
+  return api(nullptr, [&] {
+    ensure(s && token && (logits || !n), "null argument");
+    QC_CK(cudaSetDevice(s->device));
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : s->own;
+    if (n == 0) throw ApiError(QC_ERR_INVALID, "invalid logits");
+    qc::launch_sample(logits, n, s->d, nullptr, st);
+    QC_CK(cudaGetLastError());
+    *token = s->finish(st);
+  });
+}
+
+int qc_sampler_words(qc_sampler* s, uint32_t n, uint32_t* out) {
+  return api(nullptr, [&] {
+    ensure(s && (out || !n), "null argument");
+    QC_CK(cudaSetDevice(s->device));
+    uint32_t* d = nullptr;
+    QC_CK(cudaMalloc(&d, (size_t)(n ? n : 1) * 4));
+    qc::launch_sampler_words(s->d, n, d, s->own);
+    cudaError_t r = cudaGetLastError();
+    if (r == cudaSuccess) r = cudaMemcpyAsync(out, d, (size_t)n * 4, cudaMemcpyDeviceToHost, s->own);
+    if (r == cudaSuccess) r = cudaStreamSynchronize(s->own);
+    cudaFree(d);
+    QC_CK(r);
+  });
+}
+
+int qc_engine_sample(qc_engine* e, qc_sampler* s, uint32_t* token) {
+  return api(e, [&] {
+    ensure(e && s && token, "null argument");
+    ensure(s->device == e->device, "the sampler lives on another device");
+    ensure(e->pos > 0, "sampling needs the logits of a previous forward");
+    QC_CK(cudaSetDevice(e->device));
+    qc::launch_sample(e->sc.logits, e->cfg.vocab, s->d, nullptr, e->stream);
+    QC_CK(cudaGetLastError());
+    *token = s->finish(e->stream);
+  });
+}
+
+int qc_decode_sample(qc_engine* e, qc_sampler* s, uint32_t n, uint32_t* tokens_out, float* logits) {
+  if (e && (e->pos == 0 || (uint64_t)e->pos + n > e->context || !s))  // argument errors: no reset
+    return api(e, [&] { e->decode_sample(s, n, tokens_out, logits); });
+  return api_forward(e, [&] { e->decode_sample(s, n, tokens_out, logits); });
 }
 
 int qc_sync(qc_engine* e) {

@@ -137,4 +137,18 @@ const char* plan_token(const StepArgs& a, int max_smem, TokenPlan* p);
 void launch_token(const StepArgs& a, const TokenPlan& p, unsigned long long* ll, bool cooperative, cudaStream_t s);
 cudaError_t token_prepare(int max_smem);
 
+// Device state of one sampler (sampling.rs:3-8): the StdRng keystream position and the parameters.
+struct SamplerDev {
+  uint32_t key[8];          // ChaCha12 key (from seed_from_u64)
+  unsigned long long word;  // next keystream word
+  float temperature, top_p;
+  uint32_t top_k;           // 0 = off
+  uint32_t err;             // sticky: the logits held a non-finite value
+  uint32_t token;           // the last sampled id
+};
+// Sampler::sample on n device logits: one block; the id goes to s->token and, if given, *token_dst.
+void launch_sample(const float* logits, uint32_t n, SamplerDev* s, uint32_t* token_dst, cudaStream_t st);
+// n keystream words of the sampler (advancing it), for reproducibility checks.
+void launch_sampler_words(SamplerDev* s, uint32_t n, uint32_t* out, cudaStream_t st);
+
 }  // namespace qc

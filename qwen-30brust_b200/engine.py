@@ -29,7 +29,8 @@ EXPORTS = (
     "qc_logits_device", "qc_row_bytes", "qc_matrix_create", "qc_matrix_matvec", "qc_matrix_dequant",
     "qc_matrix_bytes", "qc_matrix_destroy", "qc_packed_matvec", "qc_profile_step", "qc_packed_matvec_noalloc",
     "qc_engine_set_decode_mode", "qc_engine_decode_path", "qc_engine_create_gguf_ep", "qc_engine_ep_handle",
-    "qc_engine_ep_connect",
+    "qc_engine_ep_connect", "qc_sampler_create", "qc_sampler_destroy", "qc_sampler_sample", "qc_sampler_words",
+    "qc_engine_sample", "qc_decode_sample",
 )
 
 
@@ -126,6 +127,13 @@ def lib() -> C.CDLL:
         L.qc_engine_create_gguf_ep.argtypes = [vp, sz, u32, i, u32, u32, pp]
         L.qc_engine_ep_handle.argtypes = [vp, vp, C.POINTER(C.c_int)]
         L.qc_engine_ep_connect.argtypes = [vp, vp, vp]
+        L.qc_sampler_create.argtypes = [u64, C.c_float, u32, C.c_float, i, pp]
+        L.qc_sampler_destroy.argtypes = [vp]
+        L.qc_sampler_destroy.restype = None
+        L.qc_sampler_sample.argtypes = [vp, vp, u32, vp, C.POINTER(u32)]
+        L.qc_sampler_words.argtypes = [vp, u32, vp]
+        L.qc_engine_sample.argtypes = [vp, vp, C.POINTER(u32)]
+        L.qc_decode_sample.argtypes = [vp, vp, u32, vp, vp]
         _lib = L
     return _lib
 
@@ -145,6 +153,37 @@ def _u8(a) -> np.ndarray:
     if isinstance(a, (bytes, bytearray)):
         return np.frombuffer(bytes(a), dtype=np.uint8)
     return np.ascontiguousarray(a, dtype=np.uint8)
+
+
+class Sampler:
+    """sampling.rs Sampler on the device (qc_sampler_*): Sampler(seed, temperature, top_k, top_p)."""
+
+    def __init__(self, seed: int, temperature: float, top_k: int, top_p: float, device: int = 0):
+        h = C.c_void_p()
+        _global_check(lib().qc_sampler_create(seed, temperature, top_k, top_p, device, C.byref(h)))
+        self._h = h
+
+    def sample_device(self, logits_ptr: int, n: int, stream_ptr: int | None = None) -> int:
+        """Sampler::sample on n float32 logits at a device address."""
+        t = C.c_uint32()
+        _global_check(lib().qc_sampler_sample(self._h, logits_ptr, n, stream_ptr, C.byref(t)))
+        return t.value
+
+    def words(self, n: int) -> np.ndarray:
+        out = np.empty(max(n, 1), dtype=np.uint32)
+        _global_check(lib().qc_sampler_words(self._h, n, out.ctypes.data))
+        return out[:n]
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().qc_sampler_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class Engine:
@@ -295,6 +334,20 @@ class Engine:
         path, why = C.c_int(), C.c_char_p()
         self._check(lib().qc_engine_decode_path(self._h, C.byref(path), C.byref(why)))
         return path.value, (why.value or b"").decode()
+
+    def sample(self, sampler: "Sampler") -> int:
+        """qc_engine_sample: Sampler::sample on the logits of the last step."""
+        t = C.c_uint32()
+        self._check(lib().qc_engine_sample(self._h, sampler._h, C.byref(t)))
+        return t.value
+
+    def decode_sample(self, sampler: "Sampler", n: int, want_logits: bool = False):
+        """qc_decode_sample: n (sample, step) pairs on the device; returns the n sampled ids."""
+        toks = np.empty(max(n, 1), dtype=np.uint32)
+        out = np.empty(self.vocab, dtype=np.float32) if want_logits else None
+        self._check(lib().qc_decode_sample(self._h, sampler._h, n, toks.ctypes.data,
+                                           out.ctypes.data if out is not None else None))
+        return toks[:n], out
 
     def logits_device_ptr(self) -> int:
         p = C.c_void_p()

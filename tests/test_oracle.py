@@ -131,3 +131,75 @@ def test_config1_quantized_model_matches_numpy_reference(oracle, tools):
         np.testing.assert_allclose(got, logits[p], rtol=2e-4, atol=2e-5)
         if p + 1 < len(tokens) and p + 1 >= n0:
             assert oracle.sample_greedy(got) == tokens[p + 1]
+
+
+# ---- sampling.rs with its random source ------------------------------------------------------
+
+def _rfc_state(key_bytes, counter, nonce_bytes):
+    w = np.frombuffer(bytes(key_bytes), dtype="<u4")
+    n = np.frombuffer(bytes(nonce_bytes), dtype="<u4")
+    return np.array([0x61707865, 0x3320646E, 0x79622D32, 0x6B206574, *w, counter, *n], dtype=np.uint32)
+
+
+def test_chacha_block_matches_rfc7539_vectors(oracle):
+    """The ChaCha block function against RFC 7539's published block vectors (20 rounds):
+    section 2.3.2 (key 00..1f, counter 1, nonce 00 00 00 09 00 00 00 4a 00 00 00 00) and
+    appendix A.1 test vector 1 (all-zero key, nonce and counter)."""
+    st = _rfc_state(range(32), 1, [0, 0, 0, 9, 0, 0, 0, 0x4A, 0, 0, 0, 0])
+    got = oracle.chacha_block(st, 20)
+    want = [0xE4E7F110, 0x15593BD1, 0x1FDD0F50, 0xC47120A3, 0xC7F4D1C7, 0x0368C033, 0x9AAA2204, 0x4E6CD4C3,
+            0x466482D2, 0x09AA9F07, 0x05D7C214, 0xA2028BD9, 0xD19C12B5, 0xB94E16DE, 0xE883D0CB, 0x4E3C50A2]
+    assert got.tolist() == want
+    z = oracle.chacha_block(_rfc_state([0] * 32, 0, [0] * 12), 20)
+    assert z.astype("<u4").tobytes().hex() == (
+        "76b8e0ada0f13d90405d6ae55386bd28bdd219b8a08ded1aa836efcc8b770dc7"
+        "da41597c5157488d7724e03fb8d84a376a43b8f41518a11cc387b669b2ee6586")
+
+
+def test_sampler_seed_and_greedy(oracle):
+    """tests/core.rs:28-42: greedy picks the argmax, NaN logits and bad parameters are errors,
+    and two samplers with one seed draw the same ids."""
+    s = oracle.Sampler(42, 0.0, 0, 1.0)
+    assert s.sample([0.0, 4.0, 2.0]) == 1
+    with pytest.raises(oracle.OracleError, match="invalid logits"):
+        s.sample([float("nan")])
+    with pytest.raises(oracle.OracleError, match="invalid sampling parameters"):
+        oracle.Sampler(1, 1.0, 1, 0.0)
+    for bad in [(-1.0, 0, 0.5), (float("inf"), 0, 0.5), (1.0, 0, 1.5), (1.0, 0, float("nan"))]:
+        with pytest.raises(oracle.OracleError, match="invalid sampling parameters"):
+            oracle.Sampler(1, *bad)
+    a, b = oracle.Sampler(77, 1.0, 0, 1.0), oracle.Sampler(77, 1.0, 0, 1.0)
+    for _ in range(40):
+        assert a.sample([1.0, 2.0, 3.0]) == b.sample([1.0, 2.0, 3.0])
+
+
+def test_sampler_rules(oracle):
+    """top_k 1 and a tiny top_p keep only the argmax; the draw follows the kept probabilities
+    (exp(l - max) / T, renormalised) and consumes one keystream word per non-greedy sample."""
+    rng = np.random.default_rng(5)
+    logits = rng.normal(size=300).astype(np.float32)
+    top = int(np.argmax(logits))
+    for args in [(0.8, 1, 1.0), (0.8, 0, 1e-6), (2.0, 1, 0.5)]:
+        s = oracle.Sampler(9, *args)
+        assert all(s.sample(logits) == top for _ in range(20))
+    # two ids with probabilities 1/4 and 3/4 at T = 1
+    s = oracle.Sampler(3, 1.0, 0, 1.0)
+    ids = [s.sample([0.0, math.log(3.0)]) for _ in range(4000)]
+    assert abs(np.mean(ids) - 0.75) < 0.03
+    # one word per draw: a sampler that drew k times is k words ahead of a fresh one
+    s, t = oracle.Sampler(11, 0.7, 20, 0.9), oracle.Sampler(11, 0.7, 20, 0.9)
+    for _ in range(5):
+        s.sample(logits)
+    for _ in range(5):
+        t.next_u32()
+    assert s.next_u32() == t.next_u32()
+    # the draw against the kept prefix: u * mass picks the first id whose running sum exceeds it
+    s, w = oracle.Sampler(21, 0.7, 50, 0.8), oracle.Sampler(21, 0.7, 50, 0.8)
+    order = sorted(range(logits.size), key=lambda i: (-float(logits[i]), i))[:50]
+    p = np.exp((logits[order] - logits[order[0]]) / np.float32(0.7)).astype(np.float32)
+    keep = int(np.searchsorted(np.cumsum(p / p.sum()), 0.8) + 1)
+    for _ in range(50):
+        u = (w.next_u32() >> 8) / 16777216.0
+        draw = u * float(p[:keep].sum())
+        want = order[min(int(np.searchsorted(np.cumsum(p[:keep]), draw, side="right")), keep - 1)]
+        assert s.sample(logits) == want
