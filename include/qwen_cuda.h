@@ -140,6 +140,16 @@ int qc_decode_greedy(qc_engine* e, uint32_t n, uint32_t* tokens_out, float* logi
  * returns; qc_sync waits and reports a non-finite output or a bad token. */
 int qc_decode_enqueue(qc_engine* e, uint32_t n);
 
+/* The MoE half of layer `layer` (model.rs:245-287: RMSNorm(ffn_norm), router, top-k, expert
+ * SwiGLU, weighted combine, residual) for n_tokens independent token vectors at once.
+ * x, out: n_tokens x hidden floats in host memory.  path 1 runs the per-token decode kernels
+ * once per token (matvecs); path 2 the batched kernels: tokens grouped per expert, gate/up and
+ * down as tcgen05 tensor-core GEMMs (Q4_K gate/up and Q6_K down only).  device_ms (may be NULL)
+ * receives the device time of the layer, copies excluded.  The KV cache and position are not
+ * touched.  Not available on expert-parallel engines. */
+int qc_moe_layer(qc_engine* e, uint32_t layer, const float* x, uint32_t n_tokens, float* out, int path,
+                 float* device_ms);
+
 /* ---- Sampler (sampling.rs:3-65) on the device ---------------------------------------------------
  * qc_sampler_create ~ Sampler::new(seed, temperature, top_k, top_p): "invalid sampling parameters"
  * unless temperature is finite and >= 0 and 0 < top_p <= 1; top_k 0 = off.  The random source is

@@ -625,21 +625,8 @@ static Split split_groups(uint32_t groups, uint32_t group_bytes, uint32_t blocks
   return {(groups + gper - 1) / gper, gper};
 }
 
-StepPlan plan_step(const StepArgs& a) {
-  StepPlan p{};
-  const DecodeDims& d = a.dims;
-  const uint32_t sms = (uint32_t)a.sms;
-  const LayerDev& L = a.layers[0];
-  {  // attn_in: the group space of Q, K and V
-    const uint32_t gb = std::max(L.q.group_bytes, std::max(L.k.group_bytes, L.v.group_bytes));
-    const uint32_t groups = (L.q.rows + 7) / 8 + (L.k.rows + 7) / 8 + (L.v.rows + 7) / 8;
-    const Split s = split_groups(groups, gb, sms, kWeightBudget);
-    p.attn_in = {s.grid, s.gper, s.gper * gb};
-  }
-  {
-    const Split s = split_groups((L.o.rows + 7) / 8, L.o.group_bytes, sms, kWeightBudget);
-    p.oproj = {s.grid, s.gper, s.gper * L.o.group_bytes};
-  }
+// Router, gate/up and down splits (the MoE kernels).
+static void plan_moe_part(StepPlan& p, const DecodeDims& d, const LayerDev& L, uint32_t sms) {
   {
     const Split s = split_groups((L.router.rows + 7) / 8, L.router.group_bytes, sms, kWeightBudget);
     p.router = {s.grid, s.gper, s.gper * L.router.group_bytes};
@@ -656,6 +643,30 @@ StepPlan plan_step(const StepArgs& a) {
     const Split s = split_groups((L.down.rows + 7) / 8, gb, sms, kWeightBudget);
     p.down = {s.grid, s.gper, s.gper * gb};
   }
+}
+
+StepPlan plan_moe(const DecodeDims& d, const LayerDev& L, int sms) {
+  StepPlan p{};
+  plan_moe_part(p, d, L, (uint32_t)sms);
+  return p;
+}
+
+StepPlan plan_step(const StepArgs& a) {
+  StepPlan p{};
+  const DecodeDims& d = a.dims;
+  const uint32_t sms = (uint32_t)a.sms;
+  const LayerDev& L = a.layers[0];
+  {  // attn_in: the group space of Q, K and V
+    const uint32_t gb = std::max(L.q.group_bytes, std::max(L.k.group_bytes, L.v.group_bytes));
+    const uint32_t groups = (L.q.rows + 7) / 8 + (L.k.rows + 7) / 8 + (L.v.rows + 7) / 8;
+    const Split s = split_groups(groups, gb, sms, kWeightBudget);
+    p.attn_in = {s.grid, s.gper, s.gper * gb};
+  }
+  {
+    const Split s = split_groups((L.o.rows + 7) / 8, L.o.group_bytes, sms, kWeightBudget);
+    p.oproj = {s.grid, s.gper, s.gper * L.o.group_bytes};
+  }
+  plan_moe_part(p, d, L, sms);
   {
     const uint32_t sg = std::max(1u, std::min(8u, kOutStageBudget / a.out.group_bytes));
     p.out_sg = sg;
@@ -726,6 +737,16 @@ void launch_step(const StepArgs& a, const StepPlan& p, cudaStream_t s, StepHook 
   launch(k_output, dim3(p.out_grid), smem_output(a, p), s, a.out, c.x, a.out_norm, d.hidden, d.eps, c.logits, a.st,
          p.out_sg);
   H(K_COUNT);
+}
+
+void launch_moe_token(const DecodeDims& d, const StepPlan& p, const LayerDev& L, const Scratch& c, DevState* st,
+                      cudaStream_t s) {
+  launch(k_router, dim3(p.router.grid), smem_router(L, p), s, L.router, c.x, L.ffn_norm, d.hidden, d.eps, d.top,
+         c.rlogit, c.sel, c.selw, st, p.router.gper, p.router.wbytes);
+  launch(k_gateup, dim3(p.gateup.grid), smem_gateup(L, p), s, L.gate, L.up, c.x, L.ffn_norm, d.hidden, d.eps, c.sel,
+         c.h, p.gateup_bpe, p.gateup.gper, p.gateup.wbytes);
+  launch(k_down, dim3(p.down.grid), smem_down(L, p, d.top), s, L.down, c.h, d.top, c.sel, c.selw, c.x, p.down.gper,
+         p.down.wbytes);
 }
 
 #ifdef QC_TRACE

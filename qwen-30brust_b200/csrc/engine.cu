@@ -62,6 +62,7 @@ void prepare_device(int device) {
   QC_CK(qc::matvec_prepare(kMaxSmem));
   QC_CK(qc::decode_prepare(kMaxSmem));
   QC_CK(qc::token_prepare(0));
+  QC_CK(qc::moe_prepare());
   done[device] = true;
 }
 
@@ -236,6 +237,7 @@ struct qc_engine {
       if (q != ep_rank && peer_ll[q]) cudaIpcCloseMemHandle(peer_ll[q]);
     cudaFree(d_peers);
     cudaFree(d_ll);
+    cudaFree(d_moe);
     cudaFree(d_layers);
     if (own) cudaStreamDestroy(own);
   }
@@ -728,6 +730,130 @@ struct qc_engine {
     stats.matvec_ms += ms;
   }
 
+  // ---- the MoE half of one layer for a batch of tokens --------------------------------------
+  uint8_t* d_moe = nullptr;  // scratch of moe_cap tokens
+  uint32_t moe_cap = 0;
+  std::vector<float> moe_sw;  // per layer: power-of-two weight scales (gate/up, down); 0 = not yet measured
+
+  qc::MoeArgs moe_args(uint32_t layer, uint32_t T) {
+    const qc::LayerDev& L = layers[layer];
+    qc::MoeArgs a{};
+    a.router = L.router;
+    a.gate = L.gate;
+    a.up = L.up;
+    a.down = L.down;
+    a.ffn_norm = L.ffn_norm;
+    a.H = cfg.hidden;
+    a.I = cfg.intermediate;
+    a.E = cfg.experts;
+    a.top = cfg.top;
+    a.T = T;
+    a.eps = cfg.eps;
+    const uint64_t P = (uint64_t)moe_cap * cfg.top;
+    uint64_t o = 0;
+    auto take = [&](uint64_t bytes) {
+      uint8_t* p = d_moe + o;
+      o = align256(o + bytes);
+      return p;
+    };
+    a.h = reinterpret_cast<float*>(take((uint64_t)moe_cap * cfg.hidden * 4));
+    a.hscale = reinterpret_cast<float*>(take(moe_cap * 4));
+    a.sel = reinterpret_cast<uint32_t*>(take(P * 4));
+    a.selw = reinterpret_cast<float*>(take(P * 4));
+    a.cnt = reinterpret_cast<uint32_t*>(take(cfg.experts * 4));
+    a.off = reinterpret_cast<uint32_t*>(take(cfg.experts * 4));
+    a.ptok = reinterpret_cast<uint32_t*>(take(P * 4));
+    a.ppair = reinterpret_cast<uint32_t*>(take(P * 4));
+    a.gu = reinterpret_cast<float*>(take(P * cfg.intermediate * 4));
+    a.gumax = reinterpret_cast<uint32_t*>(take(P * 4));
+    a.y = reinterpret_cast<float*>(take(P * cfg.hidden * 4));
+    a.err = reinterpret_cast<uint32_t*>(take(4));
+    // inputs and outputs of the call follow the scratch
+    return a;
+  }
+  uint64_t moe_bytes(uint32_t cap) const {
+    const uint64_t P = (uint64_t)cap * cfg.top;
+    auto al = [](uint64_t b) { return align256(b); };
+    return al((uint64_t)cap * cfg.hidden * 4) + al(cap * 4) + 2 * al(P * 4) + 2 * al(cfg.experts * 4) +
+           2 * al(P * 4) + al(P * cfg.intermediate * 4) + al(P * 4) + al(P * cfg.hidden * 4) + al(4) +
+           2 * al((uint64_t)cap * cfg.hidden * 4);
+  }
+
+  // x, out: [T][hidden] host arrays.  path 1: the per-token decode kernels (router, gate/up, down)
+  // once per token; path 2: the batched tensor-core kernels.  *ms: device time of the layer.
+  void moe_layer(uint32_t layer, const float* x, uint32_t T, float* out, int path, float* ms) {
+    ensure(layer < cfg.layers, "layer index out of range");
+    ensure(T > 0 && x && out, "empty batch");
+    ensure(path == 1 || path == 2, "MoE path must be 1 (per-token kernels) or 2 (tensor cores)");
+    ensure(ep_world == 1, "an expert-parallel engine holds only its own experts");
+    QC_CK(cudaSetDevice(device));
+    if (T > moe_cap) {
+      QC_CK(cudaStreamSynchronize(stream));
+      cudaFree(d_moe);
+      d_moe = nullptr;
+      moe_cap = 0;
+      QC_CK(cudaMalloc(&d_moe, moe_bytes(T)));
+      moe_cap = T;
+    }
+    qc::MoeArgs a = moe_args(layer, T);
+    const uint64_t xbytes = (uint64_t)T * cfg.hidden * 4;
+    float* d_x = reinterpret_cast<float*>(d_moe + moe_bytes(moe_cap) - 2 * align256((uint64_t)moe_cap * cfg.hidden * 4));
+    float* d_out = d_x + align256((uint64_t)moe_cap * cfg.hidden * 4) / 4;
+    QC_CK(cudaMemcpyAsync(d_x, x, xbytes, cudaMemcpyHostToDevice, stream));
+    if (path == 2) {
+      if (const char* why = qc::moe_tc_supported(a)) throw ApiError(QC_ERR_INVALID, why);
+      if (moe_sw.empty()) moe_sw.assign(2 * cfg.layers, 0.f);
+      if (moe_sw[2 * layer] == 0.f) {  // bounds of |w| from the block scales, once per layer
+        uint32_t* b = a.err;
+        uint32_t hb[2] = {0, 0};
+        QC_CK(cudaMemsetAsync(b, 0, 4, stream));
+        qc::launch_moe_wbound(a.gate, cfg.experts, b, stream);
+        qc::launch_moe_wbound(a.up, cfg.experts, b, stream);
+        QC_CK(cudaMemcpyAsync(&hb[0], b, 4, cudaMemcpyDeviceToHost, stream));
+        QC_CK(cudaMemsetAsync(b, 0, 4, stream));
+        qc::launch_moe_wbound(a.down, cfg.experts, b, stream);
+        QC_CK(cudaMemcpyAsync(&hb[1], b, 4, cudaMemcpyDeviceToHost, stream));
+        QC_CK(cudaStreamSynchronize(stream));
+        for (int i = 0; i < 2; i++) {
+          float bound;
+          std::memcpy(&bound, &hb[i], 4);
+          int ex = 0;
+          std::frexp(bound > 0.f ? bound : 1.f, &ex);
+          moe_sw[2 * layer + i] = std::ldexp(1.f, 14 - ex);
+        }
+      }
+      a.sw_gu = moe_sw[2 * layer];
+      a.sw_down = moe_sw[2 * layer + 1];
+      QC_CK(cudaMemsetAsync(a.err, 0, 4, stream));
+      QC_CK(cudaEventRecord(ev0, stream));
+      qc::launch_moe_tc(a, d_x, d_out, stream);
+      QC_CK(cudaGetLastError());
+      QC_CK(cudaEventRecord(ev1, stream));
+      uint32_t herr = 0;
+      QC_CK(cudaMemcpyAsync(&herr, a.err, 4, cudaMemcpyDeviceToHost, stream));
+      QC_CK(cudaStreamSynchronize(stream));
+      if (herr & 2) throw ApiError(QC_ERR_CUDA, "MoE tensor-core kernel: a wait timed out");
+      if (herr & 1) throw ApiError(QC_ERR_NONFINITE, "non-finite router logits");
+    } else {
+      const qc::LayerDev& L = layers[layer];
+      QC_CK(cudaEventRecord(ev0, stream));
+      for (uint32_t t = 0; t < T; t++) {
+        QC_CK(cudaMemcpyAsync(sc.x, d_x + (uint64_t)t * cfg.hidden, cfg.hidden * 4, cudaMemcpyDeviceToDevice, stream));
+        qc::launch_moe_token(dims, plan, L, sc, d_state, stream);
+        QC_CK(cudaGetLastError());
+        QC_CK(cudaMemcpyAsync(d_out + (uint64_t)t * cfg.hidden, sc.x, cfg.hidden * 4, cudaMemcpyDeviceToDevice, stream));
+      }
+      QC_CK(cudaEventRecord(ev1, stream));
+      QC_CK(cudaStreamSynchronize(stream));
+      check_flags();
+    }
+    QC_CK(cudaMemcpyAsync(out, d_out, xbytes, cudaMemcpyDeviceToHost, stream));
+    QC_CK(cudaStreamSynchronize(stream));
+    float t_ms = 0.f;
+    QC_CK(cudaEventElapsedTime(&t_ms, ev0, ev1));
+    if (ms) *ms = t_ms;
+  }
+
   // The chat loop with a sampler (main.rs:261-282): n times, sample the current logits on the
   // device and feed the id to the next step; tokens_out gets the n sampled ids.
   void decode_sample(qc_sampler* smp, uint32_t n, uint32_t* tokens_out, float* logits) {
@@ -1130,6 +1256,14 @@ int qc_engine_decode_path(const qc_engine* e, int* path, const char** why) {
     ensure(e && path, "null argument");
     *path = e->use_token ? 0 : 1;
     if (why) *why = e->token_why ? e->token_why : "";
+  });
+}
+
+int qc_moe_layer(qc_engine* e, uint32_t layer, const float* x, uint32_t n_tokens, float* out, int path,
+                 float* device_ms) {
+  return api(e, [&] {
+    ensure(e, "null engine");
+    e->moe_layer(layer, x, n_tokens, out, path, device_ms);
   });
 }
 

@@ -137,6 +137,38 @@ const char* plan_token(const StepArgs& a, int max_smem, TokenPlan* p);
 void launch_token(const StepArgs& a, const TokenPlan& p, unsigned long long* ll, bool cooperative, cudaStream_t s);
 cudaError_t token_prepare(int max_smem);
 
+// The MoE half of one layer for a batch of tokens (moe.cu).
+struct MoeArgs {
+  MatDesc router, gate, up, down;  // one layer's router and expert stacks, device layout
+  const float* ffn_norm;
+  uint32_t H, I, E, top, T;
+  float eps;
+  float sw_gu, sw_down;  // power-of-two weight scales of the fp16 hi/lo split
+  // scratch
+  float* h;          // [T][H] normalized inputs
+  float* hscale;     // [T] power-of-two scale of each token's h
+  uint32_t* sel;     // [T][top] selected experts, selection order
+  float* selw;       // [T][top] their weights
+  uint32_t* cnt;     // [E] pairs per expert
+  uint32_t* off;     // [E] first grouped pair of each expert
+  uint32_t* ptok;    // [T*top] grouped pairs: token
+  uint32_t* ppair;   // [T*top] grouped pairs: pair id t*top + slot
+  float* gu;         // [T*top][I] SwiGLU outputs by pair id
+  uint32_t* gumax;   // [T*top] bits of max |gu| by pair id
+  float* y;          // [T*top][H] down outputs by pair id
+  uint32_t* err;     // bit 0: non-finite router logit; bit 1: a tensor-core wait timed out
+};
+const char* moe_tc_supported(const MoeArgs& a);
+size_t moe_gemm_smem();
+cudaError_t moe_prepare();
+void launch_moe_wbound(const MatDesc& m, uint32_t experts, uint32_t* out, cudaStream_t s);
+// x [T][H] -> out [T][H]: route, plan, tensor-core gate/up + SwiGLU, down, combine.
+void launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStream_t s);
+// The per-token MoE kernels of the decode step (router, gate/up, down) on the vector c.x, in place.
+StepPlan plan_moe(const DecodeDims& d, const LayerDev& L, int sms);
+void launch_moe_token(const DecodeDims& d, const StepPlan& p, const LayerDev& L, const Scratch& c, DevState* st,
+                      cudaStream_t s);
+
 // Device state of one sampler (sampling.rs:3-8): the StdRng keystream position and the parameters.
 struct SamplerDev {
   uint32_t key[8];          // ChaCha12 key (from seed_from_u64)

@@ -1,0 +1,491 @@
+// The MoE half of a layer (model.rs:245-287) for a batch of T tokens at once, on the 5th-generation
+// tensor cores.
+//
+//   k_moe_route    per token: RMSNorm(ffn_norm), router matvec (F16), top-k with ties to the lower
+//                  index, softmax over the kept logits in selection order (ops.rs:3-15, 29-56)
+//   k_moe_plan     the (token, slot) pairs grouped by expert, tokens ascending within an expert
+//   k_moe_gemm<0>  per (expert, 64-row tile): gate and up rows of the expert times its tokens'
+//                  normalized inputs, then SwiGLU  g / (1 + exp(-g)) * u  (model.rs:259-274)
+//   k_moe_gemm<1>  per (expert, 128-row tile): down rows times the expert's SwiGLU outputs
+//   k_moe_combine  x + (w_0 y_0 + w_1 y_1 + ...) in selection order (model.rs:275-287)
+//
+// Tensor-core GEMM (tcgen05.mma, kind::f16, fp32 accumulator in TMEM, M = 128, N = tokens padded
+// to 16): each weight is dequantized exactly as quant.rs does (separately rounded products),
+// scaled by a power of two and split into two fp16 values hi + lo; each activation likewise
+// (power-of-two scale per token).  hi*hi + hi*lo + lo*hi is accumulated by three MMAs per K step,
+// so a product keeps ~22 significant bits and the only other rounding is the fp32 accumulation:
+// results stay within the matvec tolerance of the reference's f32 fold.  Operands are written by
+// the CTA's threads straight into the canonical no-swizzle K-major shared-memory layout (8-row x
+// 16-byte core matrices) in two stages, so dequantization of K step k+1 overlaps the MMAs of
+// step k; one thread issues the MMAs and commits them to the stage's mbarrier.
+#include <cuda_fp16.h>
+
+#include "kernels.h"
+
+namespace qc {
+namespace {
+
+constexpr int kMT = 256;          // threads of a GEMM CTA
+constexpr uint32_t kKS = 64;      // K elements per stage
+constexpr uint32_t kNMax = 128;   // tokens per accumulator pass
+constexpr uint32_t kAStage = 128 * kKS * 2;         // one fp16 plane of A per stage: 16 KB
+constexpr uint32_t kBStage = kNMax * kKS * 2;       // one fp16 plane of B per stage (N = 128): 16 KB
+constexpr uint32_t kStage = 2 * kAStage + 2 * kBStage;
+constexpr uint32_t kTmemCols = 128;
+constexpr unsigned long long kWaitNs = 2000000000ull;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// Canonical K-major layout without swizzle: 16-byte chunk kc (8 fp16 along K) of row r.
+__device__ __forceinline__ uint32_t kmajor_off(uint32_t r, uint32_t kc, uint32_t rows) {
+  return kc * rows * 16 + (r >> 3) * 128 + (r & 7) * 16;
+}
+// Shared-memory matrix descriptor: start, leading byte offset (between K chunks), stride byte offset
+// (between 8-row groups), descriptor version 1, no swizzle.
+__device__ __forceinline__ unsigned long long sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return (unsigned long long)((addr >> 4) & 0x3fff) | ((unsigned long long)((lbo >> 4) & 0x3fff) << 16) |
+         ((unsigned long long)((sbo >> 4) & 0x3fff) << 32) | (1ull << 46);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* m) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(m)) : "memory");
+}
+__device__ __forceinline__ unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// Wait (at most 2 s) for the phase with the given parity; false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* m, uint32_t parity) {
+  const uint32_t a = smem_u32(m);
+  const unsigned long long t0 = now_ns();
+  for (uint32_t i = 0;; i++) {
+    uint32_t ok;
+    asm volatile(
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((i & 255) == 255 && now_ns() - t0 > kWaitNs) return false;
+  }
+}
+
+__device__ __forceinline__ float pow2_scale(float maxabs) {  // 2^k with maxabs * 2^k < 2^14
+  if (!(maxabs > 0.f) || !isfinite(maxabs)) return 1.f;
+  int ex;
+  frexpf(maxabs, &ex);  // maxabs < 2^ex
+  return ldexpf(1.f, 14 - ex);
+}
+
+__device__ __forceinline__ void split8(const float (&v)[8], float s, uint4* hi, uint4* lo) {
+  __half h[8], l[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const float x = v[j] * s;  // power of two: exact
+    h[j] = __float2half_rn(x);
+    l[j] = __float2half_rn(x - __half2float(h[j]));  // exact difference
+  }
+  *hi = *reinterpret_cast<const uint4*>(h);
+  *lo = *reinterpret_cast<const uint4*>(l);
+}
+
+// ---- per-token routing ---------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_moe_route(MoeArgs a, const float* __restrict__ x) {
+  __shared__ float red[32];
+  __shared__ float lg[1024];
+  const uint32_t t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float* xr = x + (uint64_t)t * a.H;
+  float ss = 0.f;
+  for (uint32_t i = tid; i < a.H; i += 256) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
+  ss = block_sum(ss, red);
+  // ops.rs:3-15: s = 1 / sqrt(sum / n + eps); x_i * (s * w_i)
+  const float s = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)a.H), a.eps)));
+  float* hr = a.h + (uint64_t)t * a.H;
+  float mx = 0.f;
+  for (uint32_t i = tid; i < a.H; i += 256) {
+    const float v = __fmul_rn(xr[i], __fmul_rn(s, a.ffn_norm[i]));
+    hr[i] = v;
+    mx = fmaxf(mx, fabsf(v));
+  }
+  mx = warp_max(mx);
+  __syncthreads();
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  if (tid == 0) {
+    float m = 0.f;
+    for (int w = 0; w < 8; w++) m = fmaxf(m, red[w]);
+    a.hscale[t] = pow2_scale(m);
+  }
+  // router logits: one warp per expert row (F16)
+  for (uint32_t e = warp; e < a.E; e += 8) {
+    const __half* wr = reinterpret_cast<const __half*>(row_ptr(a.router, a.router.w, e));
+    float acc = 0.f;
+    for (uint32_t i = lane; i < a.H; i += 32) acc = __fadd_rn(acc, __fmul_rn(__half2float(wr[i]), hr[i]));
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      lg[e] = acc;
+      if (!isfinite(acc)) atomicOr(a.err, 1u);
+    }
+  }
+  __syncthreads();
+  // rank of each logit (ties to the lower index); the top ranks are the selection, in order
+  for (uint32_t e = tid; e < a.E; e += 256) {
+    const uint32_t ke = total_key_u(lg[e]);
+    uint32_t rank = 0;
+    for (uint32_t j = 0; j < a.E; j++) {
+      const uint32_t kj = total_key_u(lg[j]);
+      rank += kj > ke || (kj == ke && j < e);
+    }
+    if (rank < a.top) a.sel[(uint64_t)t * a.top + rank] = e;
+  }
+  __syncthreads();
+  if (tid == 0) {  // ops.rs:29-44 over the kept logits, in selection order
+    const uint32_t* sl = a.sel + (uint64_t)t * a.top;
+    float* w = a.selw + (uint64_t)t * a.top;
+    float m = -INFINITY;
+    for (uint32_t k = 0; k < a.top; k++) m = fmaxf(m, lg[sl[k]]);
+    float sum = 0.f;
+    for (uint32_t k = 0; k < a.top; k++) {
+      w[k] = expf(__fsub_rn(lg[sl[k]], m));
+      sum = __fadd_rn(sum, w[k]);
+    }
+    for (uint32_t k = 0; k < a.top; k++) w[k] = __fdiv_rn(w[k], sum);
+  }
+}
+
+// ---- pairs grouped by expert ---------------------------------------------------------------
+__global__ void __launch_bounds__(1024) k_moe_plan(MoeArgs a) {
+  __shared__ uint32_t cnt[1024], off[1025];
+  const uint32_t tid = threadIdx.x, P = a.T * a.top;
+  for (uint32_t e = tid; e < a.E; e += 1024) cnt[e] = 0;
+  __syncthreads();
+  for (uint32_t p = tid; p < P; p += 1024) atomicAdd(&cnt[a.sel[p]], 1u);
+  __syncthreads();
+  if (tid == 0) {
+    off[0] = 0;
+    for (uint32_t e = 0; e < a.E; e++) off[e + 1] = off[e] + cnt[e];
+  }
+  __syncthreads();
+  for (uint32_t e = tid; e < a.E; e += 1024) {
+    a.cnt[e] = cnt[e];
+    a.off[e] = off[e];
+  }
+  for (uint32_t p = tid; p < P; p += 1024) {
+    const uint32_t e = a.sel[p];
+    uint32_t before = 0;
+    for (uint32_t q = 0; q < p; q++) before += a.sel[q] == e;
+    const uint32_t pos = off[e] + before;
+    a.ptok[pos] = p / a.top;
+    a.ppair[pos] = p;
+    a.gumax[p] = 0;
+  }
+}
+
+// ---- A operand producers: 8 consecutive weights of one row, dequantized as quant.rs does ----
+// Q4_K (quant.rs:50-62): row r of expert e, elements [k, k + 8) (k a multiple of 8).
+__device__ __forceinline__ void dq8_q4k(const MatDesc& m, uint32_t e, uint32_t r, uint32_t k, float (&w)[8]) {
+  const uint8_t* b = row_ptr(m, expert_base(m, e), r) + (k >> 8) * 144;
+  const uint32_t i = k & 255, g = i >> 5;
+  int sc, mn;
+  kq_scale(b + 4, (int)g, &sc, &mn);
+  const float d = h2f_bits(b[0] | (b[1] << 8)), dmin = h2f_bits(b[2] | (b[3] << 8));
+  const float ds = __fmul_rn(d, (float)sc), dm = __fmul_rn(dmin, (float)mn);
+  const uint2 q = *reinterpret_cast<const uint2*>(b + 16 + (i >> 6) * 32 + (i & 31));
+  const uint32_t sh = (g & 1) * 4;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const uint32_t byte = ((j < 4 ? q.x : q.y) >> (8 * (j & 3))) & 0xffu;
+    w[j] = __fsub_rn(__fmul_rn(ds, (float)((byte >> sh) & 15u)), dm);
+  }
+}
+// Q6_K (quant.rs:63-77) in the device layout (208-byte blocks, d values after the 8 rows).
+__device__ __forceinline__ void dq8_q6k(const MatDesc& m, uint32_t e, uint32_t r, uint32_t k, float (&w)[8]) {
+  const uint8_t* base = expert_base(m, e);
+  const uint8_t* b = row_ptr(m, base, r) + (k >> 8) * 208;
+  const uint32_t i = k & 255, chunk = i >> 7, j = i & 127, quarter = j >> 5, lane = j & 31;
+  const uint2 lo = *reinterpret_cast<const uint2*>(b + chunk * 64 + (quarter & 1) * 32 + lane);
+  const uint2 hi = *reinterpret_cast<const uint2*>(b + 128 + chunk * 32 + lane);
+  const float sc = (float)(int8_t)b[192 + chunk * 8 + quarter * 2 + lane / 16];
+  const float ds = __fmul_rn(__half2float(drow_ptr(m, base, r)[k >> 8]), sc);
+  const uint32_t sl = (quarter >> 1) * 4, shh = quarter * 2;
+#pragma unroll
+  for (int t = 0; t < 8; t++) {
+    const uint32_t l = ((t < 4 ? lo.x : lo.y) >> (8 * (t & 3))) & 0xffu;
+    const uint32_t h = ((t < 4 ? hi.x : hi.y) >> (8 * (t & 3))) & 0xffu;
+    const int q = (int)(((l >> sl) & 15u) | (((h >> shh) & 3u) << 4)) - 32;
+    w[t] = __fmul_rn(ds, (float)q);
+  }
+}
+
+// ---- grouped GEMM on the tensor cores --------------------------------------------------------
+// MODE 0: A rows 0-63 = gate rows [64 tile, +64), rows 64-127 = up rows; K = H; B = h of the tokens.
+// MODE 1: A rows = down rows [128 tile, +128); K = I; B = SwiGLU outputs of the pairs.
+template <int MODE>
+__global__ void __launch_bounds__(kMT, 1) k_moe_gemm(MoeArgs a) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  __shared__ __align__(8) uint64_t mbar[2];
+  __shared__ uint32_t tmem_base;
+  __shared__ float bscale[kNMax];
+  __shared__ uint32_t bpair[kNMax], btok[kNMax];
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t e = blockIdx.y, tile = blockIdx.x;
+  const uint32_t n_all = a.cnt[e];
+  if (n_all == 0) return;
+  const MatDesc& mA = MODE == 0 ? a.gate : a.down;
+  const uint32_t K = MODE == 0 ? a.H : a.I, KS = K / kKS;
+  const float sw = MODE == 0 ? a.sw_gu : a.sw_down;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 0) {
+    mbar_init(&mbar[0]);
+    mbar_init(&mbar[1]);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_base;
+  uint32_t issued[2] = {0, 0};
+  bool ok = true;
+
+  for (uint32_t n0 = 0; n0 < n_all && ok; n0 += kNMax) {
+    const uint32_t nn = min(kNMax, n_all - n0), N = max(16u, (nn + 15) & ~15u);
+    for (uint32_t n = tid; n < N; n += kMT) {
+      if (n < nn) {
+        const uint32_t pos = a.off[e] + n0 + n;
+        bpair[n] = a.ppair[pos];
+        btok[n] = a.ptok[pos];
+        bscale[n] = MODE == 0 ? a.hscale[btok[n]] : pow2_scale(__uint_as_float(a.gumax[bpair[n]]));
+      } else {
+        bpair[n] = btok[n] = 0xffffffffu;
+        bscale[n] = 0.f;
+      }
+    }
+    __syncthreads();
+    // instruction descriptor: f32 accumulator, f16 A and B, both K-major, N, M = 128
+    const uint32_t idesc = (1u << 4) | ((N >> 3) << 17) | ((128u >> 4) << 24);
+    for (uint32_t ks = 0; ks < KS; ks++) {
+      const uint32_t s = ks & 1;
+      if (issued[s] && !mbar_wait(&mbar[s], (issued[s] - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      uint8_t* st = sm + s * kStage;
+      uint8_t *ahi = st, *alo = st + kAStage, *bhi = st + 2 * kAStage, *blo = bhi + kBStage;
+      const uint32_t k0 = ks * kKS;
+      {  // A: thread -> row tid/2, chunks 4*(tid&1) .. +3 (one quant.rs sub-block / quarter)
+        const uint32_t r = tid >> 1, kc0 = (tid & 1) * 4;
+        bool valid;
+        uint32_t row;
+        const MatDesc* m;
+        if (MODE == 0) {
+          m = r < 64 ? &a.gate : &a.up;
+          row = tile * 64 + (r & 63);
+          valid = row < a.I;
+        } else {
+          m = &a.down;
+          row = tile * 128 + r;
+          valid = row < a.H;
+        }
+#pragma unroll
+        for (uint32_t c = 0; c < 4; c++) {
+          const uint32_t kc = kc0 + c;
+          float w[8];
+          if (valid) {
+            if (MODE == 0) dq8_q4k(*m, e, row, k0 + kc * 8, w);
+            else dq8_q6k(*m, e, row, k0 + kc * 8, w);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; j++) w[j] = 0.f;
+          }
+          uint4 h, l;
+          split8(w, sw, &h, &l);
+          *reinterpret_cast<uint4*>(ahi + kmajor_off(r, kc, 128)) = h;
+          *reinterpret_cast<uint4*>(alo + kmajor_off(r, kc, 128)) = l;
+        }
+      }
+      for (uint32_t it = tid; it < N * 8; it += kMT) {  // B: (token n, chunk kc)
+        const uint32_t n = it >> 3, kc = it & 7;
+        float v[8];
+        if (n < nn) {
+          const float* src = MODE == 0 ? a.h + (uint64_t)btok[n] * a.H + k0 + kc * 8
+                                       : a.gu + (uint64_t)bpair[n] * a.I + k0 + kc * 8;
+          const float4 x0 = *reinterpret_cast<const float4*>(src), x1 = *reinterpret_cast<const float4*>(src + 4);
+          v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
+          v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; j++) v[j] = 0.f;
+        }
+        uint4 h, l;
+        split8(v, n < nn ? bscale[n] : 0.f, &h, &l);
+        *reinterpret_cast<uint4*>(bhi + kmajor_off(n, kc, N)) = h;
+        *reinterpret_cast<uint4*>(blo + kmajor_off(n, kc, N)) = l;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncthreads();
+      if (tid == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t a_hi = smem_u32(ahi), a_lo = smem_u32(alo), b_hi = smem_u32(bhi), b_lo = smem_u32(blo);
+#pragma unroll
+        for (uint32_t j = 0; j < kKS / 16; j++) {  // K = 16 per MMA: chunks 2j, 2j+1
+          const unsigned long long dah = sdesc(a_hi + 2 * j * 128 * 16, 128 * 16, 128);
+          const unsigned long long dal = sdesc(a_lo + 2 * j * 128 * 16, 128 * 16, 128);
+          const unsigned long long dbh = sdesc(b_hi + 2 * j * N * 16, N * 16, 128);
+          const unsigned long long dbl = sdesc(b_lo + 2 * j * N * 16, N * 16, 128);
+          const uint32_t acc0 = (ks > 0 || j > 0) ? 1u : 0u;
+          asm volatile(
+              "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+              "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem),
+              "l"(dah), "l"(dbh), "r"(idesc), "r"(acc0)
+              : "memory");
+          asm volatile(
+              "{\n.reg .pred p;\nsetp.ne.b32 p, 1, 0;\n"
+              "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem),
+              "l"(dah), "l"(dbl), "r"(idesc)
+              : "memory");
+          asm volatile(
+              "{\n.reg .pred p;\nsetp.ne.b32 p, 1, 0;\n"
+              "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem),
+              "l"(dal), "l"(dbh), "r"(idesc)
+              : "memory");
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         smem_u32(&mbar[s]))
+                     : "memory");
+      }
+      issued[s]++;
+    }
+    if (!ok) break;
+    {  // the last commit covers every MMA issued before it
+      const uint32_t s = (KS - 1) & 1;
+      if (!mbar_wait(&mbar[s], (issued[s] - 1) & 1)) {
+        ok = false;
+        break;
+      }
+    }
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    // epilogue: warp q < 4 reads TMEM lanes 32q..32q+31 (rows), N columns (tokens)
+    float* E = reinterpret_cast<float*>(sm);  // [128][N + 1]
+    if (warp < 4) {
+      const uint32_t r = warp * 32 + lane;
+      for (uint32_t c0 = 0; c0 < N; c0 += 16) {
+        uint32_t v[16];
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+            "%14, %15}, [%16];"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+            : "r"(tmem + ((warp * 32u) << 16) + c0));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+          const uint32_t n = c0 + j;
+          E[r * (N + 1) + n] = n < nn ? __uint_as_float(v[j]) / (sw * bscale[n]) : 0.f;
+        }
+      }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (MODE == 0) {
+      for (uint32_t it = tid; it < 64 * nn; it += kMT) {
+        const uint32_t n = it / 64, j = it % 64, row = tile * 64 + j;
+        if (row < a.I) {
+          const float g = E[j * (N + 1) + n], u = E[(64 + j) * (N + 1) + n];
+          const float act = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u);
+          a.gu[(uint64_t)bpair[n] * a.I + row] = act;
+          atomicMax(&a.gumax[bpair[n]], __float_as_uint(fabsf(act)));
+        }
+      }
+    } else {
+      for (uint32_t it = tid; it < 128 * nn; it += kMT) {
+        const uint32_t n = it / 128, r = it % 128, row = tile * 128 + r;
+        if (row < a.H) a.y[(uint64_t)bpair[n] * a.H + row] = E[r * (N + 1) + n];
+      }
+    }
+    __syncthreads();
+  }
+  if (!ok && tid == 0) atomicOr(a.err, 2u);
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (!ok) {  // let MMAs still in flight finish before the accumulator is released
+    for (uint32_t s = 0; s < 2; s++)
+      if (issued[s]) mbar_wait(&mbar[s], (issued[s] - 1) & 1);
+  }
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+}
+
+// ---- combine in selection order + residual ---------------------------------------------------
+__global__ void __launch_bounds__(256) k_moe_combine(MoeArgs a, const float* __restrict__ x, float* __restrict__ out) {
+  const uint32_t t = blockIdx.x;
+  for (uint32_t r = threadIdx.x; r < a.H; r += 256) {
+    float acc = 0.f;
+    for (uint32_t k = 0; k < a.top; k++) {
+      const uint32_t p = t * a.top + k;
+      acc = __fadd_rn(acc, __fmul_rn(a.selw[p], a.y[(uint64_t)p * a.H + r]));
+    }
+    out[(uint64_t)t * a.H + r] = __fadd_rn(x[(uint64_t)t * a.H + r], acc);
+  }
+}
+
+// Upper bound of |w| over a Q4_K or Q6_K expert stack, from the block scales (atomic max of bits).
+__global__ void k_moe_wbound(MatDesc m, uint32_t experts, uint32_t* out) {
+  const uint32_t blocks = m.cols / 256;
+  const uint64_t n = (uint64_t)experts * m.rows * blocks;
+  float mx = 0.f;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t e = (uint32_t)(i / ((uint64_t)m.rows * blocks)), rem = (uint32_t)(i % ((uint64_t)m.rows * blocks));
+    const uint32_t r = rem / blocks, sb = rem % blocks;
+    const uint8_t* base = expert_base(m, e);
+    if (m.kind == Q4_K) {
+      const uint8_t* b = row_ptr(m, base, r) + sb * 144;
+      const float d = fabsf(h2f_bits(b[0] | (b[1] << 8))), dmin = fabsf(h2f_bits(b[2] | (b[3] << 8)));
+      mx = fmaxf(mx, d * 63.f * 15.f + dmin * 63.f);
+    } else {
+      mx = fmaxf(mx, fabsf(__half2float(drow_ptr(m, base, r)[sb])) * 128.f * 32.f);
+    }
+  }
+  mx = warp_max(mx);
+  if ((threadIdx.x & 31) == 0 && isfinite(mx)) atomicMax(out, __float_as_uint(mx));
+}
+
+}  // namespace
+
+const char* moe_tc_supported(const MoeArgs& a) {
+  if (a.gate.kind != Q4_K || a.up.kind != Q4_K || a.down.kind != Q6_K)
+    return "the tensor-core MoE path takes Q4_K gate/up and Q6_K down experts";
+  if (a.H % kKS || a.I % kKS) return "the tensor-core MoE path needs hidden and intermediate sizes in multiples of 64";
+  if (a.router.kind != F16) return "the batched MoE path takes an F16 router";
+  if (a.E > 1024) return "the batched MoE path takes at most 1024 experts";
+  return nullptr;
+}
+
+size_t moe_gemm_smem() { return 2 * (size_t)kStage; }
+
+cudaError_t moe_prepare() {
+  cudaError_t e = cudaFuncSetAttribute(k_moe_gemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)moe_gemm_smem());
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_moe_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)moe_gemm_smem());
+  return e;
+}
+
+void launch_moe_wbound(const MatDesc& m, uint32_t experts, uint32_t* out, cudaStream_t s) {
+  k_moe_wbound<<<296, 256, 0, s>>>(m, experts, out);
+}
+
+void launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStream_t s) {
+  k_moe_route<<<a.T, 256, 0, s>>>(a, x);
+  k_moe_plan<<<1, 1024, 0, s>>>(a);
+  k_moe_gemm<0><<<dim3((a.I + 63) / 64, a.E), kMT, moe_gemm_smem(), s>>>(a);
+  k_moe_gemm<1><<<dim3((a.H + 127) / 128, a.E), kMT, moe_gemm_smem(), s>>>(a);
+  k_moe_combine<<<a.T, 256, 0, s>>>(a, x, out);
+}
+
+}  // namespace qc

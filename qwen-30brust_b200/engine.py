@@ -30,7 +30,7 @@ EXPORTS = (
     "qc_matrix_bytes", "qc_matrix_destroy", "qc_packed_matvec", "qc_profile_step", "qc_packed_matvec_noalloc",
     "qc_engine_set_decode_mode", "qc_engine_decode_path", "qc_engine_create_gguf_ep", "qc_engine_ep_handle",
     "qc_engine_ep_connect", "qc_sampler_create", "qc_sampler_destroy", "qc_sampler_sample", "qc_sampler_words",
-    "qc_engine_sample", "qc_decode_sample",
+    "qc_engine_sample", "qc_decode_sample", "qc_moe_layer",
 )
 
 
@@ -134,6 +134,7 @@ def lib() -> C.CDLL:
         L.qc_sampler_words.argtypes = [vp, u32, vp]
         L.qc_engine_sample.argtypes = [vp, vp, C.POINTER(u32)]
         L.qc_decode_sample.argtypes = [vp, vp, u32, vp, vp]
+        L.qc_moe_layer.argtypes = [vp, u32, vp, u32, vp, i, C.POINTER(C.c_float)]
         _lib = L
     return _lib
 
@@ -348,6 +349,16 @@ class Engine:
         self._check(lib().qc_decode_sample(self._h, sampler._h, n, toks.ctypes.data,
                                            out.ctypes.data if out is not None else None))
         return toks[:n], out
+
+    def moe_layer(self, layer: int, x, path: int) -> tuple[np.ndarray, float]:
+        """qc_moe_layer: the MoE half of `layer` for a batch of token vectors x [T][hidden].
+        path 1: per-token decode kernels; path 2: tensor-core grouped GEMMs.  Returns (out, device ms)."""
+        xx = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty_like(xx)
+        ms = C.c_float()
+        self._check(lib().qc_moe_layer(self._h, layer, xx.ctypes.data, xx.shape[0], out.ctypes.data, path,
+                                       C.byref(ms)))
+        return out, ms.value
 
     def logits_device_ptr(self) -> int:
         p = C.c_void_p()

@@ -162,3 +162,69 @@ def f16_to_f32(v: int) -> float:
 
 def f32_to_f16(v: float) -> int:
     return lib().qct_f32_to_f16(v)
+
+
+def gguf_table(buf) -> tuple[dict, list, int]:
+    """Walk a GGUF image's header (gguf.rs:102-195 layout): (metadata scalars and strings,
+    [(name, dims, kind, offset relative to the data start)], data start)."""
+    import struct
+    buf = bytes(buf) if not isinstance(buf, (bytes, bytearray)) else buf
+    pos = 8
+    nt, nk = struct.unpack_from("<QQ", buf, pos)
+    pos += 16
+
+    def rstr(p):
+        n, = struct.unpack_from("<Q", buf, p)
+        return buf[p + 8:p + 8 + n].decode(), p + 8 + n
+
+    sizes = {0: 1, 1: 1, 2: 2, 3: 2, 4: 4, 5: 4, 6: 4, 7: 1, 10: 8, 11: 8, 12: 8}
+    meta = {}
+    for _ in range(nk):
+        k, pos = rstr(pos)
+        t, = struct.unpack_from("<I", buf, pos)
+        pos += 4
+        if t == 8:
+            meta[k], pos = rstr(pos)
+        elif t == 9:
+            it, n = struct.unpack_from("<IQ", buf, pos)
+            pos += 12
+            for _ in range(n):
+                if it == 8:
+                    _, pos = rstr(pos)
+                else:
+                    pos += sizes[it]
+        else:
+            meta[k] = struct.unpack_from("<" + {4: "I", 6: "f"}.get(t, "I"), buf, pos)[0]
+            pos += sizes[t]
+    infos = []
+    for _ in range(nt):
+        name, pos = rstr(pos)
+        nd, = struct.unpack_from("<I", buf, pos)
+        pos += 4
+        dims = list(struct.unpack_from("<" + "Q" * nd, buf, pos))
+        pos += 8 * nd
+        kind, off = struct.unpack_from("<IQ", buf, pos)
+        pos += 12
+        infos.append((name, dims, kind, off))
+    start = (pos + 31) // 32 * 32
+    return meta, infos, start
+
+
+def tensor_view(img: np.ndarray, name: str) -> tuple[np.ndarray, int, list]:
+    """(the bytes of tensor `name` inside a GGUF image, as a writable view; kind; dims)."""
+    _, infos, start = gguf_table(img[:1 << 22].tobytes() if img.size > (1 << 22) else img.tobytes())
+    for n, dims, kind, off in infos:
+        if n == name:
+            nbytes = row_bytes(kind, dims[0]) * int(np.prod(dims[1:], dtype=np.int64))
+            return img[start + off:start + off + nbytes], kind, dims
+    raise KeyError(name)
+
+
+def skew_router(img: np.ndarray, layer: int, s: float) -> None:
+    """Scale row e of an F16 router (ffn_gate_inp) by (e + 1)^-s, in place: larger rows win the
+    top-k more often, so the expert load falls off with the expert index (Zipf-like)."""
+    v, kind, dims = tensor_view(img, f"blk.{layer}.ffn_gate_inp.weight")
+    assert kind == F16
+    w = v.view(np.float16).reshape(dims[1], dims[0])
+    g = (np.arange(dims[1], dtype=np.float64) + 1.0) ** -s
+    w[:] = (w.astype(np.float64) * g[:, None]).astype(np.float16)

@@ -49,46 +49,9 @@ def test_f32_fixture_matches_reference_and_resets(cuda_engine, mode):
 
 
 def _tensor_table(buf: bytes):
-    """Minimal GGUF table walk (gguf.rs layout) producing qc_tensor_desc fields."""
-    pos = 8
-    nt, nk = struct.unpack_from("<QQ", buf, pos)
-    pos += 16
-
-    def rstr(p):
-        n, = struct.unpack_from("<Q", buf, p)
-        return buf[p + 8:p + 8 + n].decode(), p + 8 + n
-
-    sizes = {0: 1, 1: 1, 2: 2, 3: 2, 4: 4, 5: 4, 6: 4, 7: 1, 10: 8, 11: 8, 12: 8}
-    meta = {}
-    for _ in range(nk):
-        k, pos = rstr(pos)
-        t, = struct.unpack_from("<I", buf, pos)
-        pos += 4
-        if t == 8:
-            meta[k], pos = rstr(pos)
-        elif t == 9:
-            it, n = struct.unpack_from("<IQ", buf, pos)
-            pos += 12
-            for _ in range(n):
-                if it == 8:
-                    _, pos = rstr(pos)
-                else:
-                    pos += sizes[it]
-        else:
-            meta[k] = struct.unpack_from("<" + {4: "I", 6: "f"}.get(t, "I"), buf, pos)[0]
-            pos += sizes[t]
-    infos = []
-    for _ in range(nt):
-        name, pos = rstr(pos)
-        nd, = struct.unpack_from("<I", buf, pos)
-        pos += 4
-        dims = list(struct.unpack_from("<" + "Q" * nd, buf, pos))
-        pos += 8 * nd
-        kind, off = struct.unpack_from("<IQ", buf, pos)
-        pos += 12
-        infos.append((name, dims, kind, off))
-    start = (pos + 31) // 32 * 32
-    return meta, infos, start
+    """GGUF table walk (gguf.rs layout) producing qc_tensor_desc fields."""
+    from qwen30brust_b200 import tools
+    return tools.gguf_table(buf)
 
 
 def test_engine_from_tensor_table(cuda_engine, oracle):
