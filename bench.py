@@ -393,6 +393,64 @@ def run_reference(args) -> None:
     }), flush=True)
 
 
+def run_moe_layer(args) -> None:
+    """one Qwen3-30B-A3B MoE layer for T in {1, 8, 32, 128} tokens, per-token
+    decode kernels (path 1, matvecs) against tcgen05 grouped GEMMs (path 2); Zipf-skewed router."""
+    import torch
+    from qwen30brust_b200 import engine as E, tools as T
+    spec = T.QWEN3_30B_A3B.with_(layers=1, vocab=512)
+    img = T.synth_gguf(spec)
+    T.skew_router(img, 0, 1.1)
+    eng = E.Engine(img, 16)
+    H, I, NE, top = spec.hidden, spec.intermediate, spec.experts, spec.top
+    rv, _, _ = T.tensor_view(img, "blk.0.ffn_gate_inp.weight")
+    router = np.frombuffer(rv.tobytes(), dtype=np.float16).reshape(NE, H).astype(np.float64)
+    norm = np.frombuffer(T.tensor_view(img, "blk.0.ffn_norm.weight")[0].tobytes(), dtype=np.float32)
+    gate_b, down_b = T.row_bytes(T.Q4_K, H) * I, T.row_bytes(T.Q6_K, I) * H
+    expert_bytes = 2 * gate_b + down_b
+    rng = np.random.default_rng(7)
+    sampler = ClockSampler(0)
+    rows, load = [], np.zeros(NE, dtype=np.int64)
+    with sampler:
+        for tokens in (1, 8, 32, 128):
+            x = rng.normal(size=(tokens, H)).astype(np.float32)
+            h = x / np.sqrt((x.astype(np.float64) ** 2).mean(axis=1, keepdims=True) + spec.eps) * norm
+            sel = np.argsort(-(h @ router.T), axis=1, kind="stable")[:, :top]  # workload statistic only
+            distinct = len(np.unique(sel))
+            np.add.at(load, sel.ravel(), 1)
+            res = {"tokens": tokens, "distinct_experts": distinct, "tokens_per_expert": tokens * top / distinct}
+            byts = NE * H * 2 + distinct * expert_bytes
+            flops = 2 * tokens * top * 3 * H * I
+            for path in (1, 2):
+                for _ in range(args.warmup):
+                    eng.moe_layer(0, x, path)
+                ms = sorted(eng.moe_layer(0, x, path)[1] for _ in range(args.steps))
+                med = ms[len(ms) // 2]
+                res[f"path{path}"] = {"ms": med, "tok_s": tokens / (med / 1e3), "gbs": byts / (med / 1e3) / 1e9,
+                                      "tflops": flops / (med / 1e3) / 1e12}
+            res["bytes"], res["flops"] = byts, flops
+            res["speedup_tc"] = res["path1"]["ms"] / res["path2"]["ms"]
+            rows.append(res)
+            log(f"T={tokens}: distinct {distinct}, per-token kernels {res['path1']['ms']:.3f} ms, "
+                f"tensor cores {res['path2']['ms']:.3f} ms")
+    cross = next((r["tokens_per_expert"] for r in rows if r["speedup_tc"] > 1.0), None)
+    ranked = np.sort(load)[::-1]
+    top_share = ranked[: max(1, NE // 16)].sum() / max(1, ranked.sum())
+    out = {
+        "metric": "MoE layer tokens/s (BASELINE config 3), per-token decode kernels vs tcgen05 grouped GEMMs",
+        "unit": "tok/s", "higher_is_better": True, "steps": args.steps, "warmup": args.warmup,
+        "dtype": "f32 activations; Q4_K gate/up, Q6_K down, F16 router; tensor path fp16 hi/lo split, fp32 accumulate",
+        "data": "synthetic: N(0,0.02) weights (seed 0), router row e scaled by (e+1)^-1.1, hidden N(0,1) (seed 7)",
+        "config": {"workload": "BASELINE config 3: one Qwen3-30B-A3B MoE layer", "hidden": H, "experts": NE,
+                   "top": top, "intermediate": I, "timing": "device time of qc_moe_layer, median of steps"},
+        "results": rows,
+        "crossover_tokens_per_expert": cross,
+        "load_share_top_8_experts": float(top_share),
+        "clocks": sampler.summary(),
+    }
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -406,12 +464,16 @@ def main():
     ap.add_argument("--decode-mode", type=int, default=0, choices=[0, 1],
                     help="0: whole-token kernel when the model fits it (default); 1: per-phase kernels")
     ap.add_argument("--ref-max-steps", type=int, default=8)
+    ap.add_argument("--config", type=int, default=4, choices=[3, 4],
+                    help="3: the MoE-layer study (per-token kernels vs tensor cores); 4: the decode bench")
     ap.add_argument("--ep", action="store_true",
                     help="N > 1: one decode stream with the experts split over the ranks (expert parallelism)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
-    if args.impl == "reference":
+    if args.config == 3:
+        run_moe_layer(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
