@@ -78,16 +78,20 @@ __device__ __forceinline__ float pow2_scale(float maxabs) {  // 2^k with maxabs 
   return ldexpf(1.f, 14 - ex);
 }
 
+// v * s (s a power of two: exact) as fp16 hi + lo, two values per conversion.
 __device__ __forceinline__ void split8(const float (&v)[8], float s, uint4* hi, uint4* lo) {
-  __half h[8], l[8];
+  uint32_t h[4], l[4];
 #pragma unroll
-  for (int j = 0; j < 8; j++) {
-    const float x = v[j] * s;  // power of two: exact
-    h[j] = __float2half_rn(x);
-    l[j] = __float2half_rn(x - __half2float(h[j]));  // exact difference
+  for (int j = 0; j < 4; j++) {
+    const float x0 = v[2 * j] * s, x1 = v[2 * j + 1] * s;
+    const __half2 hh = __floats2half2_rn(x0, x1);
+    const float2 back = __half22float2(hh);
+    const __half2 ll = __floats2half2_rn(x0 - back.x, x1 - back.y);  // exact differences
+    h[j] = *reinterpret_cast<const uint32_t*>(&hh);
+    l[j] = *reinterpret_cast<const uint32_t*>(&ll);
   }
-  *hi = *reinterpret_cast<const uint4*>(h);
-  *lo = *reinterpret_cast<const uint4*>(l);
+  *hi = make_uint4(h[0], h[1], h[2], h[3]);
+  *lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
 // ---- per-token routing ---------------------------------------------------------------------
@@ -182,39 +186,125 @@ __global__ void __launch_bounds__(1024) k_moe_plan(MoeArgs a) {
   }
 }
 
-// ---- A operand producers: 8 consecutive weights of one row, dequantized as quant.rs does ----
-// Q4_K (quant.rs:50-62): row r of expert e, elements [k, k + 8) (k a multiple of 8).
-__device__ __forceinline__ void dq8_q4k(const MatDesc& m, uint32_t e, uint32_t r, uint32_t k, float (&w)[8]) {
-  const uint8_t* b = row_ptr(m, expert_base(m, e), r) + (k >> 8) * 144;
-  const uint32_t i = k & 255, g = i >> 5;
-  int sc, mn;
-  kq_scale(b + 4, (int)g, &sc, &mn);
-  const float d = h2f_bits(b[0] | (b[1] << 8)), dmin = h2f_bits(b[2] | (b[3] << 8));
-  const float ds = __fmul_rn(d, (float)sc), dm = __fmul_rn(dmin, (float)mn);
-  const uint2 q = *reinterpret_cast<const uint2*>(b + 16 + (i >> 6) * 32 + (i & 31));
-  const uint32_t sh = (g & 1) * 4;
+// ---- A and B operands of one K step, fetched one step ahead -------------------------------------
+// A: thread -> row tid/2 of the tile, chunks 4*(tid&1) .. +3 of the step (8 weights each, one
+// quant.rs sub-block of Q4_K / one quarter of Q6_K).  The raw bytes of step k+1 are loaded into
+// registers while step k is decoded and multiplied.
+struct ARaw {
+  uint4 r[5];  // Q4_K: header (d, dmin, 12 scale bytes), 32 qs bytes.  Q6_K: 16 scale bytes, 32 ql, 32 qh
+  uint32_t d;  // Q6_K: f16 bits of d
+};
+
+template <int MODE>
+__device__ __forceinline__ bool a_row(const MoeArgs& a, uint32_t tile, uint32_t r, const MatDesc** m, uint32_t* row) {
+  if (MODE == 0) {
+    *m = r < 64 ? &a.gate : &a.up;
+    *row = tile * 64 + (r & 63);
+    return *row < a.I;
+  }
+  *m = &a.down;
+  *row = tile * 128 + r;
+  return *row < a.H;
+}
+
+template <int MODE>
+__device__ __forceinline__ void fetch_a(const MoeArgs& a, uint32_t e, uint32_t tile, uint32_t k0, ARaw& w) {
+  const uint32_t r = threadIdx.x >> 1, kc0 = (threadIdx.x & 1) * 4;
+  const MatDesc* m;
+  uint32_t row;
+  if (!a_row<MODE>(a, tile, r, &m, &row)) {
 #pragma unroll
-  for (int j = 0; j < 8; j++) {
-    const uint32_t byte = ((j < 4 ? q.x : q.y) >> (8 * (j & 3))) & 0xffu;
-    w[j] = __fsub_rn(__fmul_rn(ds, (float)((byte >> sh) & 15u)), dm);
+    for (int i = 0; i < 5; i++) w.r[i] = make_uint4(0, 0, 0, 0);
+    w.d = 0;
+    return;
+  }
+  const uint8_t* base = expert_base(*m, e);
+  const uint32_t i0 = k0 & 255;
+  if (MODE == 0) {
+    const uint8_t* b = row_ptr(*m, base, row) + (k0 >> 8) * 144;
+    w.r[0] = ldg16(b);
+    w.r[1] = ldg16(b + 16 + (i0 >> 6) * 32);
+    w.r[2] = ldg16(b + 32 + (i0 >> 6) * 32);
+  } else {
+    const uint8_t* b = row_ptr(*m, base, row) + (k0 >> 8) * 208;
+    const uint32_t chunk = i0 >> 7, quarter = ((i0 & 127) >> 5) + kc0 / 4;
+    w.r[0] = ldg16(b + 192);
+    w.r[1] = ldg16(b + chunk * 64 + (quarter & 1) * 32);
+    w.r[2] = ldg16(b + chunk * 64 + (quarter & 1) * 32 + 16);
+    w.r[3] = ldg16(b + 128 + chunk * 32);
+    w.r[4] = ldg16(b + 128 + chunk * 32 + 16);
+    w.d = __ldg(reinterpret_cast<const unsigned short*>(drow_ptr(*m, base, row)) + (k0 >> 8));
   }
 }
-// Q6_K (quant.rs:63-77) in the device layout (208-byte blocks, d values after the 8 rows).
-__device__ __forceinline__ void dq8_q6k(const MatDesc& m, uint32_t e, uint32_t r, uint32_t k, float (&w)[8]) {
-  const uint8_t* base = expert_base(m, e);
-  const uint8_t* b = row_ptr(m, base, r) + (k >> 8) * 208;
-  const uint32_t i = k & 255, chunk = i >> 7, j = i & 127, quarter = j >> 5, lane = j & 31;
-  const uint2 lo = *reinterpret_cast<const uint2*>(b + chunk * 64 + (quarter & 1) * 32 + lane);
-  const uint2 hi = *reinterpret_cast<const uint2*>(b + 128 + chunk * 32 + lane);
-  const float sc = (float)(int8_t)b[192 + chunk * 8 + quarter * 2 + lane / 16];
-  const float ds = __fmul_rn(__half2float(drow_ptr(m, base, r)[k >> 8]), sc);
-  const uint32_t sl = (quarter >> 1) * 4, shh = quarter * 2;
+
+__device__ __forceinline__ uint32_t word_of(const uint4& v, uint32_t i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+__device__ __forceinline__ uint32_t byte_in(const uint4& v, uint32_t i) { return (word_of(v, i >> 2) >> (8 * (i & 3))) & 0xffu; }
+
+// Chunk c (0..3) of the thread's A work for step k0: 8 weights, quant.rs arithmetic.
+// The products are those of quant.rs times sw (a power of two, so the roundings are the same).
+template <int MODE>
+__device__ __forceinline__ void decode_a(const ARaw& w, uint32_t k0, uint32_t c, float sw, float (&out)[8]) {
+  const uint32_t kc0 = (threadIdx.x & 1) * 4, i0 = k0 & 255;
+  if (MODE == 0) {
+    const uint32_t g = (i0 >> 5) + kc0 / 4;
+    const uint4 h = w.r[0];
+    int sc, mn;
+    if (g < 4) {
+      sc = byte_in(h, 4 + g) & 63;
+      mn = byte_in(h, 8 + g) & 63;
+    } else {
+      sc = (byte_in(h, 8 + g) & 15) | ((byte_in(h, g) >> 6) << 4);
+      mn = (byte_in(h, 8 + g) >> 4) | ((byte_in(h, 4 + g) >> 6) << 4);
+    }
+    const float d = h2f_bits(h.x), dmin = h2f_bits(h.x >> 16);
+    const float ds = __fmul_rn(d, (float)sc) * sw, dm = __fmul_rn(dmin, (float)mn) * sw;
+    const uint4& q = c < 2 ? w.r[1] : w.r[2];
+    const uint32_t lo = word_of(q, (c & 1) * 2), hi = word_of(q, (c & 1) * 2 + 1), sh = (g & 1) * 4;
 #pragma unroll
-  for (int t = 0; t < 8; t++) {
-    const uint32_t l = ((t < 4 ? lo.x : lo.y) >> (8 * (t & 3))) & 0xffu;
-    const uint32_t h = ((t < 4 ? hi.x : hi.y) >> (8 * (t & 3))) & 0xffu;
-    const int q = (int)(((l >> sl) & 15u) | (((h >> shh) & 3u) << 4)) - 32;
-    w[t] = __fmul_rn(ds, (float)q);
+    for (int j = 0; j < 8; j++) {
+      const uint32_t byte = ((j < 4 ? lo : hi) >> (8 * (j & 3))) & 0xffu;
+      out[j] = __fsub_rn(__fmul_rn(ds, (float)((byte >> sh) & 15u)), dm);
+    }
+  } else {
+    const uint32_t chunk = i0 >> 7, quarter = ((i0 & 127) >> 5) + kc0 / 4;
+    const float sc = (float)(int8_t)byte_in(w.r[0], chunk * 8 + quarter * 2 + c / 2);
+    const float ds = __fmul_rn(h2f_bits(w.d), sc) * sw;
+    const uint4& L = c < 2 ? w.r[1] : w.r[2];
+    const uint4& Hh = c < 2 ? w.r[3] : w.r[4];
+    const uint32_t l0 = word_of(L, (c & 1) * 2), l1 = word_of(L, (c & 1) * 2 + 1);
+    const uint32_t h0 = word_of(Hh, (c & 1) * 2), h1 = word_of(Hh, (c & 1) * 2 + 1);
+    const uint32_t sl = (quarter >> 1) * 4, shh = quarter * 2;
+#pragma unroll
+    for (int t = 0; t < 8; t++) {
+      const uint32_t l = ((t < 4 ? l0 : l1) >> (8 * (t & 3))) & 0xffu;
+      const uint32_t h = ((t < 4 ? h0 : h1) >> (8 * (t & 3))) & 0xffu;
+      const int q = (int)(((l >> sl) & 15u) | (((h >> shh) & 3u) << 4)) - 32;
+      out[t] = __fmul_rn(ds, (float)q);
+    }
+  }
+}
+
+// B: items (token n, chunk kc) it = tid + 256 j, j < 4 (N * 8 <= 1024).
+struct BRaw {
+  float4 v[4][2];
+};
+
+template <int MODE>
+__device__ __forceinline__ void fetch_b(const MoeArgs& a, const uint32_t* btok, const uint32_t* bpair, uint32_t nn,
+                                        uint32_t N, uint32_t k0, BRaw& b) {
+#pragma unroll
+  for (uint32_t j = 0; j < 4; j++) {
+    const uint32_t it = threadIdx.x + kMT * j, n = it >> 3, kc = it & 7;
+    if (it < N * 8 && n < nn) {
+      const float* src = MODE == 0 ? a.h + (uint64_t)btok[n] * a.H + k0 + kc * 8
+                                   : a.gu + (uint64_t)bpair[n] * a.I + k0 + kc * 8;
+      b.v[j][0] = *reinterpret_cast<const float4*>(src);
+      b.v[j][1] = *reinterpret_cast<const float4*>(src + 4);
+    } else {
+      b.v[j][0] = b.v[j][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
   }
 }
 
@@ -270,63 +360,48 @@ __global__ void __launch_bounds__(kMT, 1) k_moe_gemm(MoeArgs a) {
     __syncthreads();
     // instruction descriptor: f32 accumulator, f16 A and B, both K-major, N, M = 128
     const uint32_t idesc = (1u << 4) | ((N >> 3) << 17) | ((128u >> 4) << 24);
+    ARaw anx;
+    BRaw bnx;
+    fetch_a<MODE>(a, e, tile, 0, anx);
+    fetch_b<MODE>(a, btok, bpair, nn, N, 0, bnx);
     for (uint32_t ks = 0; ks < KS; ks++) {
       const uint32_t s = ks & 1;
+      const ARaw acur = anx;
+      const BRaw bcur = bnx;
+      const uint32_t k0 = ks * kKS;
+      if (ks + 1 < KS) {  // the next step's bytes are in flight during this step
+        fetch_a<MODE>(a, e, tile, k0 + kKS, anx);
+        fetch_b<MODE>(a, btok, bpair, nn, N, k0 + kKS, bnx);
+      }
       if (issued[s] && !mbar_wait(&mbar[s], (issued[s] - 1) & 1)) {
         ok = false;
         break;
       }
       uint8_t* st = sm + s * kStage;
       uint8_t *ahi = st, *alo = st + kAStage, *bhi = st + 2 * kAStage, *blo = bhi + kBStage;
-      const uint32_t k0 = ks * kKS;
-      {  // A: thread -> row tid/2, chunks 4*(tid&1) .. +3 (one quant.rs sub-block / quarter)
+      {
         const uint32_t r = tid >> 1, kc0 = (tid & 1) * 4;
-        bool valid;
-        uint32_t row;
-        const MatDesc* m;
-        if (MODE == 0) {
-          m = r < 64 ? &a.gate : &a.up;
-          row = tile * 64 + (r & 63);
-          valid = row < a.I;
-        } else {
-          m = &a.down;
-          row = tile * 128 + r;
-          valid = row < a.H;
-        }
 #pragma unroll
         for (uint32_t c = 0; c < 4; c++) {
-          const uint32_t kc = kc0 + c;
           float w[8];
-          if (valid) {
-            if (MODE == 0) dq8_q4k(*m, e, row, k0 + kc * 8, w);
-            else dq8_q6k(*m, e, row, k0 + kc * 8, w);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 8; j++) w[j] = 0.f;
-          }
+          decode_a<MODE>(acur, k0, c, sw, w);
           uint4 h, l;
-          split8(w, sw, &h, &l);
-          *reinterpret_cast<uint4*>(ahi + kmajor_off(r, kc, 128)) = h;
-          *reinterpret_cast<uint4*>(alo + kmajor_off(r, kc, 128)) = l;
+          split8(w, 1.f, &h, &l);
+          *reinterpret_cast<uint4*>(ahi + kmajor_off(r, kc0 + c, 128)) = h;
+          *reinterpret_cast<uint4*>(alo + kmajor_off(r, kc0 + c, 128)) = l;
         }
       }
-      for (uint32_t it = tid; it < N * 8; it += kMT) {  // B: (token n, chunk kc)
-        const uint32_t n = it >> 3, kc = it & 7;
-        float v[8];
-        if (n < nn) {
-          const float* src = MODE == 0 ? a.h + (uint64_t)btok[n] * a.H + k0 + kc * 8
-                                       : a.gu + (uint64_t)bpair[n] * a.I + k0 + kc * 8;
-          const float4 x0 = *reinterpret_cast<const float4*>(src), x1 = *reinterpret_cast<const float4*>(src + 4);
-          v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
-          v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
-        } else {
 #pragma unroll
-          for (int j = 0; j < 8; j++) v[j] = 0.f;
+      for (uint32_t j = 0; j < 4; j++) {
+        const uint32_t it = tid + kMT * j, n = it >> 3, kc = it & 7;
+        if (it < N * 8) {
+          const float v[8] = {bcur.v[j][0].x, bcur.v[j][0].y, bcur.v[j][0].z, bcur.v[j][0].w,
+                              bcur.v[j][1].x, bcur.v[j][1].y, bcur.v[j][1].z, bcur.v[j][1].w};
+          uint4 h, l;
+          split8(v, n < nn ? bscale[n] : 0.f, &h, &l);
+          *reinterpret_cast<uint4*>(bhi + kmajor_off(n, kc, N)) = h;
+          *reinterpret_cast<uint4*>(blo + kmajor_off(n, kc, N)) = l;
         }
-        uint4 h, l;
-        split8(v, n < nn ? bscale[n] : 0.f, &h, &l);
-        *reinterpret_cast<uint4*>(bhi + kmajor_off(n, kc, N)) = h;
-        *reinterpret_cast<uint4*>(blo + kmajor_off(n, kc, N)) = l;
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncthreads();
