@@ -41,6 +41,7 @@ namespace qc {
 namespace {
 
 constexpr int TNT = 512;
+constexpr uint32_t kTokMinChunk = 32;  // attention positions per split of the whole-token kernel, at least
 constexpr uint32_t kSub = 128;                        // attention positions per online-softmax step
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
 
@@ -426,6 +427,30 @@ QC_DEV void rows_finish(const Seg* sg, uint32_t nseg, uint32_t units, const floa
   }
 }
 
+// Position splits S and query-head groups GS of the attention for `time` positions: every
+// (KV head, split, group) is one block.  The cost model is the per-block work: the score loop
+// takes the same time for up to 8 query heads (a warp per position holds 8 in registers), the
+// value sums grow with heads x positions, and each split adds a merge input.
+__host__ __device__ inline void attn_split(uint32_t time, uint32_t G, uint32_t kvheads, uint32_t nb, uint32_t smax,
+                                           uint32_t* S_out, uint32_t* GS_out, uint32_t* chunk_out) {
+  uint32_t best = 0xffffffffu;
+  for (uint32_t gs = 1; gs <= G && G % gs == 0; gs *= 2) {
+    if (kvheads * gs > nb) break;
+    uint32_t s = min(min(smax, nb / (kvheads * gs)), (time + kTokMinChunk - 1) / kTokMinChunk);
+    s = s < 1 ? 1 : s;
+    const uint32_t chunk = (time + s - 1) / s;
+    s = (time + chunk - 1) / chunk;
+    const uint32_t gh = G / gs;
+    const uint32_t cost = chunk * ((gh + 7) / 8) * 4 + chunk * gh + (s > 1 ? 8 * s : 0);
+    if (cost < best) {
+      best = cost;
+      *S_out = s;
+      *GS_out = gs;
+      *chunk_out = chunk;
+    }
+  }
+}
+
 // Shared-memory bytes of the staging and small-array areas (host and device agree on these).
 struct AttnSmem {
   uint32_t attn, merge;
@@ -566,15 +591,11 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
     prefetch_vectors(Ld[0], T.hidden, D);
   }
 
-  // attention split of this token (the same for every layer)
+  // attention split of this token (the same for every layer): S position ranges of `chunk`
+  // positions times GS groups of GH query heads per KV head, at most one block each
   const uint32_t time = pos + 1;
-  uint32_t S = min(T.smax, (time + kMinChunk - 1) / kMinChunk);
-  S = S < 1 ? 1 : S;
-  const uint32_t chunk = (time + S - 1) / S;
-  S = (time + chunk - 1) / chunk;
-  // blocks left over split the query heads of a KV head too: GS groups of GH heads
-  uint32_t GS = 1;
-  while (G % (2 * GS) == 0 && T.kvheads * S * GS * 2 <= nb) GS *= 2;
+  uint32_t S = 1, GS = 1, chunk = time;
+  attn_split(time, G, T.kvheads, nb, T.smax, &S, &GS, &chunk);
   const uint32_t GH = G / GS;
   const bool att = c < T.kvheads * S * GS;
   const uint32_t ah = att ? c / (S * GS) : 0, ags = att ? (c / S) % GS : 0, as = att ? c % S : 0;
@@ -1082,7 +1103,16 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
                  per);
     }
     __syncthreads();
-    for (uint32_t k = 0; k < nl; k++) rows_finish(segs + k, 1, L.down.units, part + k * dpart, seq);
+    {  // every (expert, row) pair at once: unit groups summed in order into dout
+      const uint32_t R = dr1 > dr0 ? dr1 - dr0 : 0, UG = unit_groups(L.down.units);
+      for (uint32_t i = tid; i < nl * R; i += TNT) {
+        const uint32_t k = i / R, ri = i % R;
+        const float* pp = part + k * dpart + ri;
+        float v = 0.f;
+        for (uint32_t ug = 0; ug < UG; ug++) v += pp[ug * R];
+        dout[k * nd + ri] = v;
+      }
+    }
     __syncthreads();
     for (uint32_t r = dr0 + tid; r < dr1; r += TNT) {
       float acc = 0.f;
@@ -1196,7 +1226,7 @@ const char* plan_token(const StepArgs& a, int max_smem, TokenPlan* p) {
   if (d.hidden % 2 || (d.heads * D) % 2 || d.inter % 2) return "hidden, heads*head_dim and the expert width must be even";
   TokenPlan t{};
   t.nb = nb;
-  t.smax = std::max(1u, std::min(nb / d.kvheads, (d.ctx + kMinChunk - 1) / kMinChunk));
+  t.smax = std::max(1u, std::min(nb / d.kvheads, (d.ctx + kTokMinChunk - 1) / kTokMinChunk));
   const uint32_t cap = std::min<uint32_t>(g_token_smem_cap, (uint32_t)max_smem);
   uint32_t P = 0, Q = 0, stage = 0, res = 0, outs = 0, runs = 1, partf = 0;
   const AttnSmem as = attn_stage_bytes(G, D, t.smax);
