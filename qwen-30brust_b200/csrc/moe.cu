@@ -16,8 +16,9 @@
 // so a product keeps ~22 significant bits and the only other rounding is the fp32 accumulation:
 // results stay within the matvec tolerance of the reference's f32 fold.  Operands are written by
 // the CTA's threads straight into the canonical no-swizzle K-major shared-memory layout (8-row x
-// 16-byte core matrices) in two stages, so dequantization of K step k+1 overlaps the MMAs of
-// step k; one thread issues the MMAs and commits them to the stage's mbarrier.
+// 16-byte core matrices) in two stages of K = 32, so dequantization of K step k+1 overlaps the
+// MMAs of step k (two CTAs per SM); one thread issues the MMAs and commits them to the stage's
+// mbarrier.  The bytes of the next K step are fetched into registers during the current one.
 #include <cuda_fp16.h>
 
 #include "kernels.h"
@@ -26,11 +27,16 @@ namespace qc {
 namespace {
 
 constexpr int kMT = 256;          // threads of a GEMM CTA
-constexpr uint32_t kKS = 64;      // K elements per stage
+constexpr uint32_t kKS = 32;      // K elements per stage
+constexpr uint32_t kKC = kKS / 8;  // 16-byte chunks of a row per stage
+constexpr uint32_t kCPT = kKC / 2;  // A chunks per thread (two threads per row)
 constexpr uint32_t kNMax = 128;   // tokens per accumulator pass
-constexpr uint32_t kAStage = 128 * kKS * 2;         // one fp16 plane of A per stage: 16 KB
-constexpr uint32_t kBStage = kNMax * kKS * 2;       // one fp16 plane of B per stage (N = 128): 16 KB
+constexpr uint32_t kBPT = kNMax * kKC / kMT;  // B chunks per thread, at most
+constexpr uint32_t kAStage = 128 * kKS * 2;         // one fp16 plane of A per stage: 8 KB
+constexpr uint32_t kBStage = kNMax * kKS * 2;       // one fp16 plane of B per stage (N = 128): 8 KB
 constexpr uint32_t kStage = 2 * kAStage + 2 * kBStage;
+constexpr uint32_t kEpiBytes = 128 * (kNMax + 1) * 4;  // the epilogue's [128][N + 1] floats
+constexpr uint32_t kSmem = 2 * kStage > kEpiBytes ? 2 * kStage : kEpiBytes;
 constexpr uint32_t kTmemCols = 128;
 constexpr unsigned long long kWaitNs = 2000000000ull;
 
@@ -191,8 +197,10 @@ __global__ void __launch_bounds__(1024) k_moe_plan(MoeArgs a) {
 // quant.rs sub-block of Q4_K / one quarter of Q6_K).  The raw bytes of step k+1 are loaded into
 // registers while step k is decoded and multiplied.
 struct ARaw {
-  uint4 r[5];  // Q4_K: header (d, dmin, 12 scale bytes), 32 qs bytes.  Q6_K: 16 scale bytes, 32 ql, 32 qh
-  uint32_t d;  // Q6_K: f16 bits of d
+  uint4 hdr;            // Q4_K: d, dmin, 12 scale bytes.  Q6_K: the 16 scale bytes
+  uint4 q[kCPT / 2];    // Q4_K: qs bytes of the chunks.  Q6_K: ql bytes
+  uint4 h[kCPT / 2];    // Q6_K: qh bytes
+  uint32_t d;           // Q6_K: f16 bits of d
 };
 
 template <int MODE>
@@ -209,30 +217,32 @@ __device__ __forceinline__ bool a_row(const MoeArgs& a, uint32_t tile, uint32_t 
 
 template <int MODE>
 __device__ __forceinline__ void fetch_a(const MoeArgs& a, uint32_t e, uint32_t tile, uint32_t k0, ARaw& w) {
-  const uint32_t r = threadIdx.x >> 1, kc0 = (threadIdx.x & 1) * 4;
+  const uint32_t r = threadIdx.x >> 1, kc0 = (threadIdx.x & 1) * kCPT;
   const MatDesc* m;
   uint32_t row;
   if (!a_row<MODE>(a, tile, r, &m, &row)) {
+    w.hdr = make_uint4(0, 0, 0, 0);
 #pragma unroll
-    for (int i = 0; i < 5; i++) w.r[i] = make_uint4(0, 0, 0, 0);
+    for (uint32_t u = 0; u < kCPT / 2; u++) w.q[u] = w.h[u] = make_uint4(0, 0, 0, 0);
     w.d = 0;
     return;
   }
   const uint8_t* base = expert_base(*m, e);
-  const uint32_t i0 = k0 & 255;
-  if (MODE == 0) {
+  const uint32_t i = (k0 & 255) + 8 * kc0;  // first element of the thread's chunks in the super-block
+  if (MODE == 0) {  // the chunks share one sub-block: 8 * kCPT consecutive qs bytes
     const uint8_t* b = row_ptr(*m, base, row) + (k0 >> 8) * 144;
-    w.r[0] = ldg16(b);
-    w.r[1] = ldg16(b + 16 + (i0 >> 6) * 32);
-    w.r[2] = ldg16(b + 32 + (i0 >> 6) * 32);
-  } else {
+    w.hdr = ldg16(b);
+#pragma unroll
+    for (uint32_t u = 0; u < kCPT / 2; u++) w.q[u] = ldg16(b + 16 + (i >> 6) * 32 + (i & 31) + 16 * u);
+  } else {  // ... one quarter: 8 * kCPT consecutive ql and qh bytes
     const uint8_t* b = row_ptr(*m, base, row) + (k0 >> 8) * 208;
-    const uint32_t chunk = i0 >> 7, quarter = ((i0 & 127) >> 5) + kc0 / 4;
-    w.r[0] = ldg16(b + 192);
-    w.r[1] = ldg16(b + chunk * 64 + (quarter & 1) * 32);
-    w.r[2] = ldg16(b + chunk * 64 + (quarter & 1) * 32 + 16);
-    w.r[3] = ldg16(b + 128 + chunk * 32);
-    w.r[4] = ldg16(b + 128 + chunk * 32 + 16);
+    const uint32_t chunk = i >> 7, quarter = (i & 127) >> 5, lane = i & 31;
+    w.hdr = ldg16(b + 192);
+#pragma unroll
+    for (uint32_t u = 0; u < kCPT / 2; u++) {
+      w.q[u] = ldg16(b + chunk * 64 + (quarter & 1) * 32 + lane + 16 * u);
+      w.h[u] = ldg16(b + 128 + chunk * 32 + lane + 16 * u);
+    }
     w.d = __ldg(reinterpret_cast<const unsigned short*>(drow_ptr(*m, base, row)) + (k0 >> 8));
   }
 }
@@ -242,14 +252,16 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, uint32_t i) {
 }
 __device__ __forceinline__ uint32_t byte_in(const uint4& v, uint32_t i) { return (word_of(v, i >> 2) >> (8 * (i & 3))) & 0xffu; }
 
-// Chunk c (0..3) of the thread's A work for step k0: 8 weights, quant.rs arithmetic.
+// Chunk c (< kCPT) of the thread's A work for step k0: 8 weights, quant.rs arithmetic.
 // The products are those of quant.rs times sw (a power of two, so the roundings are the same).
 template <int MODE>
 __device__ __forceinline__ void decode_a(const ARaw& w, uint32_t k0, uint32_t c, float sw, float (&out)[8]) {
-  const uint32_t kc0 = (threadIdx.x & 1) * 4, i0 = k0 & 255;
+  const uint32_t kc0 = (threadIdx.x & 1) * kCPT, i = (k0 & 255) + 8 * (kc0 + c);
+  const uint4& q = w.q[c / 2];
+  const uint32_t lo = word_of(q, (c & 1) * 2), hi = word_of(q, (c & 1) * 2 + 1);
   if (MODE == 0) {
-    const uint32_t g = (i0 >> 5) + kc0 / 4;
-    const uint4 h = w.r[0];
+    const uint32_t g = i >> 5;
+    const uint4 h = w.hdr;
     int sc, mn;
     if (g < 4) {
       sc = byte_in(h, 4 + g) & 63;
@@ -260,44 +272,41 @@ __device__ __forceinline__ void decode_a(const ARaw& w, uint32_t k0, uint32_t c,
     }
     const float d = h2f_bits(h.x), dmin = h2f_bits(h.x >> 16);
     const float ds = __fmul_rn(d, (float)sc) * sw, dm = __fmul_rn(dmin, (float)mn) * sw;
-    const uint4& q = c < 2 ? w.r[1] : w.r[2];
-    const uint32_t lo = word_of(q, (c & 1) * 2), hi = word_of(q, (c & 1) * 2 + 1), sh = (g & 1) * 4;
+    const uint32_t sh = (g & 1) * 4;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
       const uint32_t byte = ((j < 4 ? lo : hi) >> (8 * (j & 3))) & 0xffu;
       out[j] = __fsub_rn(__fmul_rn(ds, (float)((byte >> sh) & 15u)), dm);
     }
   } else {
-    const uint32_t chunk = i0 >> 7, quarter = ((i0 & 127) >> 5) + kc0 / 4;
-    const float sc = (float)(int8_t)byte_in(w.r[0], chunk * 8 + quarter * 2 + c / 2);
+    const uint32_t chunk = i >> 7, quarter = (i & 127) >> 5, lane = i & 31;
+    const float sc = (float)(int8_t)byte_in(w.hdr, chunk * 8 + quarter * 2 + lane / 16);
     const float ds = __fmul_rn(h2f_bits(w.d), sc) * sw;
-    const uint4& L = c < 2 ? w.r[1] : w.r[2];
-    const uint4& Hh = c < 2 ? w.r[3] : w.r[4];
-    const uint32_t l0 = word_of(L, (c & 1) * 2), l1 = word_of(L, (c & 1) * 2 + 1);
+    const uint4& Hh = w.h[c / 2];
     const uint32_t h0 = word_of(Hh, (c & 1) * 2), h1 = word_of(Hh, (c & 1) * 2 + 1);
     const uint32_t sl = (quarter >> 1) * 4, shh = quarter * 2;
 #pragma unroll
     for (int t = 0; t < 8; t++) {
-      const uint32_t l = ((t < 4 ? l0 : l1) >> (8 * (t & 3))) & 0xffu;
+      const uint32_t l = ((t < 4 ? lo : hi) >> (8 * (t & 3))) & 0xffu;
       const uint32_t h = ((t < 4 ? h0 : h1) >> (8 * (t & 3))) & 0xffu;
-      const int q = (int)(((l >> sl) & 15u) | (((h >> shh) & 3u) << 4)) - 32;
-      out[t] = __fmul_rn(ds, (float)q);
+      const int qv = (int)(((l >> sl) & 15u) | (((h >> shh) & 3u) << 4)) - 32;
+      out[t] = __fmul_rn(ds, (float)qv);
     }
   }
 }
 
-// B: items (token n, chunk kc) it = tid + 256 j, j < 4 (N * 8 <= 1024).
+// B: items (token n, chunk kc) it = tid + 256 j, j < kBPT (N * kKC items).
 struct BRaw {
-  float4 v[4][2];
+  float4 v[kBPT][2];
 };
 
 template <int MODE>
 __device__ __forceinline__ void fetch_b(const MoeArgs& a, const uint32_t* btok, const uint32_t* bpair, uint32_t nn,
                                         uint32_t N, uint32_t k0, BRaw& b) {
 #pragma unroll
-  for (uint32_t j = 0; j < 4; j++) {
-    const uint32_t it = threadIdx.x + kMT * j, n = it >> 3, kc = it & 7;
-    if (it < N * 8 && n < nn) {
+  for (uint32_t j = 0; j < kBPT; j++) {
+    const uint32_t it = threadIdx.x + kMT * j, n = it / kKC, kc = it % kKC;
+    if (it < N * kKC && n < nn) {
       const float* src = MODE == 0 ? a.h + (uint64_t)btok[n] * a.H + k0 + kc * 8
                                    : a.gu + (uint64_t)bpair[n] * a.I + k0 + kc * 8;
       b.v[j][0] = *reinterpret_cast<const float4*>(src);
@@ -312,7 +321,7 @@ __device__ __forceinline__ void fetch_b(const MoeArgs& a, const uint32_t* btok, 
 // MODE 0: A rows 0-63 = gate rows [64 tile, +64), rows 64-127 = up rows; K = H; B = h of the tokens.
 // MODE 1: A rows = down rows [128 tile, +128); K = I; B = SwiGLU outputs of the pairs.
 template <int MODE>
-__global__ void __launch_bounds__(kMT, 1) k_moe_gemm(MoeArgs a) {
+__global__ void __launch_bounds__(kMT, 2) k_moe_gemm(MoeArgs a) {
   extern __shared__ __align__(128) uint8_t sm[];
   __shared__ __align__(8) uint64_t mbar[2];
   __shared__ uint32_t tmem_base;
@@ -380,9 +389,9 @@ __global__ void __launch_bounds__(kMT, 1) k_moe_gemm(MoeArgs a) {
       uint8_t* st = sm + s * kStage;
       uint8_t *ahi = st, *alo = st + kAStage, *bhi = st + 2 * kAStage, *blo = bhi + kBStage;
       {
-        const uint32_t r = tid >> 1, kc0 = (tid & 1) * 4;
+        const uint32_t r = tid >> 1, kc0 = (tid & 1) * kCPT;
 #pragma unroll
-        for (uint32_t c = 0; c < 4; c++) {
+        for (uint32_t c = 0; c < kCPT; c++) {
           float w[8];
           decode_a<MODE>(acur, k0, c, sw, w);
           uint4 h, l;
@@ -392,9 +401,9 @@ __global__ void __launch_bounds__(kMT, 1) k_moe_gemm(MoeArgs a) {
         }
       }
 #pragma unroll
-      for (uint32_t j = 0; j < 4; j++) {
-        const uint32_t it = tid + kMT * j, n = it >> 3, kc = it & 7;
-        if (it < N * 8) {
+      for (uint32_t j = 0; j < kBPT; j++) {
+        const uint32_t it = tid + kMT * j, n = it / kKC, kc = it % kKC;
+        if (it < N * kKC) {
           const float v[8] = {bcur.v[j][0].x, bcur.v[j][0].y, bcur.v[j][0].z, bcur.v[j][0].w,
                               bcur.v[j][1].x, bcur.v[j][1].y, bcur.v[j][1].z, bcur.v[j][1].w};
           uint4 h, l;
@@ -536,13 +545,13 @@ __global__ void k_moe_wbound(MatDesc m, uint32_t experts, uint32_t* out) {
 const char* moe_tc_supported(const MoeArgs& a) {
   if (a.gate.kind != Q4_K || a.up.kind != Q4_K || a.down.kind != Q6_K)
     return "the tensor-core MoE path takes Q4_K gate/up and Q6_K down experts";
-  if (a.H % kKS || a.I % kKS) return "the tensor-core MoE path needs hidden and intermediate sizes in multiples of 64";
+  if (a.H % 64 || a.I % 64) return "the tensor-core MoE path needs hidden and intermediate sizes in multiples of 64";
   if (a.router.kind != F16) return "the batched MoE path takes an F16 router";
   if (a.E > 1024) return "the batched MoE path takes at most 1024 experts";
   return nullptr;
 }
 
-size_t moe_gemm_smem() { return 2 * (size_t)kStage; }
+size_t moe_gemm_smem() { return kSmem; }
 
 cudaError_t moe_prepare() {
   cudaError_t e = cudaFuncSetAttribute(k_moe_gemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)moe_gemm_smem());
