@@ -57,8 +57,8 @@ def peaks() -> dict:
 
 
 # DRAM bytes of one k_token launch from the ncu capture in profiles/k_token_4layer.md (4 layers):
-# 415.3 MB = 255.9 MB (vocab projection, logits) + 4 x 39.85 MB per layer; scaled by layer count.
-TOKEN_TRAFFIC_FIXED, TOKEN_TRAFFIC_PER_LAYER = 255.9e6, 39.85e6
+# 414.3 MB = 255.9 MB (vocab projection, logits) + 4 x 39.6 MB per layer; scaled by layer count.
+TOKEN_TRAFFIC_FIXED, TOKEN_TRAFFIC_PER_LAYER = 255.9e6, 39.6e6
 
 
 def model_bytes(spec, tools, pos_first: int, steps: int) -> dict:
