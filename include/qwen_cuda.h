@@ -98,8 +98,10 @@ int qc_engine_create_gguf(const uint8_t* image, size_t len, uint32_t context, in
  * is one launch on every rank with no separate collective.  Before the first forward each rank
  * exports a handle with qc_engine_ep_handle, the host gathers all `world` handles and device ids
  * (rank order) and passes them to qc_engine_ep_connect on every rank.  All ranks must then run the
- * same forward / decode calls in the same order; an error on one rank must be followed by
- * qc_reset on every rank.  Ranks on the same GPU are refused. */
+ * same forward / decode calls in the same order.  If one rank stops, the others' next step ends
+ * with QC_ERR_CUDA ("a wait between thread blocks timed out", after 2 s) and resets them; after
+ * any error the ranks' token tags no longer agree, so every rank must be destroyed and created
+ * again.  Ranks on the same GPU are refused. */
 int qc_engine_create_gguf_ep(const uint8_t* image, size_t len, uint32_t context, int device, uint32_t rank,
                              uint32_t world, qc_engine** out);
 /* 64-byte CUDA IPC handle of this rank's exchange buffer and an id of its GPU (PCI location). */

@@ -97,3 +97,48 @@ def test_expert_parallel_refusals(cuda_engine, tools):
     single = E(img, 16)
     with pytest.raises(cuda_engine.QwenCudaError, match="not an expert-parallel engine"):
         single.ep_handle()
+
+
+def test_peer_gone_times_out_and_gpu_stays_usable(cuda_engine):
+    """A rank that stops between steps: the other rank's next token ends with the timeout error
+    within a few seconds (bounded waits of 2 s, no GPU fault), its position resets, and the GPU
+    still runs a fresh engine.  Host-side failure only; no NCCL, plain peer stores."""
+    if _gpus() < 2:
+        pytest.skip("needs 2 GPUs")
+    import _ep_worker
+    ctx = mp.get_context("spawn")
+    up = ctx.Queue()
+    downs = [ctx.Queue() for _ in range(2)]
+    procs = [ctx.Process(target=_ep_worker.run_peer_gone, args=(r, 2, up, downs[r], [3, 1, 4]))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        handles, synced, done = {}, set(), {}
+        while len(done) < 2:
+            kind, rank, payload = up.get(timeout=300)
+            assert kind != "error", f"rank {rank}:\n{payload}"
+            if kind == "handle":
+                handles[rank] = payload
+                if len(handles) == 2:
+                    for q in downs:
+                        q.put([handles[r] for r in range(2)])
+            elif kind == "synced":
+                synced.add(rank)
+                if len(synced) == 2:
+                    downs[0].put("go")
+            else:
+                done[rank] = payload
+                if rank == 0:
+                    downs[1].put("finish")
+        for p in procs:
+            p.join(timeout=60)
+    finally:
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+    code, msg, seconds, pos, fresh_ok = done[0]
+    assert code == cuda_engine.ERR_CUDA and "timed out" in msg, (code, msg)
+    assert seconds < 30, seconds
+    assert pos == 0  # a failed forward resets the cache, as model.rs:210-216 does
+    assert fresh_ok
