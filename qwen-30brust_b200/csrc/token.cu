@@ -172,10 +172,12 @@ QC_DEV float ll_wait1_sys(const unsigned long long* p, uint32_t seq, DevState* s
 }
 
 // Tagged values [0, n) of src (16-byte aligned) into dst(i, value); each thread
-// polls up to 8 pairs at a time until all carry `seq`.  No barrier inside.
+// polls up to 2 pairs at a time until all carry `seq`.  No barrier inside.  (Small unroll
+// factors here and in stage_ll keep the kernel's code path per layer short: instruction fetch
+// is its largest stall, and B = 2 / P = 1 measured 6% faster than B = 8 / P = 2.)
 template <class Dst>
 QC_DEV void ll_gather(const unsigned long long* src, uint32_t n, Dst dst, uint32_t seq, DevState* st) {
-  constexpr int B = 8;
+  constexpr int B = 2;
   for (uint32_t base = 0; base < n; base += 2 * B * blockDim.x) {
     unsigned long long a[B], b[B];
     Waiter w;
@@ -214,7 +216,7 @@ QC_DEV void stage_ll(uint8_t* mem, uint32_t nv, uint32_t n, uint32_t units, bool
   // written by peer GPUs and read at system scope, summed in order)
   const uint32_t per = units4(units) * 64;
   const uint32_t total = nv * per, xb = xview_bytes(units, with_float);
-  constexpr int P = 2;
+  constexpr int P = 1;
   for (uint32_t base = 0; base < total; base += P * blockDim.x * 8) {
     float x[P][8], ww[P][8];
     if constexpr (RMS) {
