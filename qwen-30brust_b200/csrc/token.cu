@@ -431,7 +431,7 @@ QC_DEV void rows_finish(const Seg* sg, uint32_t nseg, uint32_t units, const floa
 
 // Position splits S and query-head groups GS of the attention for `time` positions: every
 // (KV head, split, group) is one block.  The cost model is the per-block work: the score loop
-// takes the same time for up to 8 query heads (a warp per position holds 8 in registers), the
+// takes the same time for up to 4 query heads (a warp per position holds 4 in registers), the
 // value sums grow with heads x positions, and each split adds a merge input.
 __host__ __device__ inline void attn_split(uint32_t time, uint32_t G, uint32_t kvheads, uint32_t nb, uint32_t smax,
                                            uint32_t* S_out, uint32_t* GS_out, uint32_t* chunk_out) {
@@ -443,7 +443,7 @@ __host__ __device__ inline void attn_split(uint32_t time, uint32_t G, uint32_t k
     const uint32_t chunk = (time + s - 1) / s;
     s = (time + chunk - 1) / chunk;
     const uint32_t gh = G / gs;
-    const uint32_t cost = chunk * ((gh + 7) / 8) * 4 + chunk * gh + (s > 1 ? 8 * s : 0);
+    const uint32_t cost = chunk * ((gh + 3) / 4) * 4 + chunk * gh + (s > 1 ? 8 * s : 0);
     if (cost < best) {
       best = cost;
       *S_out = s;
@@ -721,13 +721,13 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
           parP ^= 1;
         }
         // s[g][t] = (q_g . k_t) / sqrt(D)  (ops.rs:84-91): a warp per position t, lanes over the
-        // head dimension, up to 8 query heads held in registers; the 8 partial dot products are
-        // summed across the warp by a halving exchange (9 shuffles), leaving head (lane >> 2) & 7
-        for (uint32_t gb = 0; gb < GH; gb += 8) {
-          const uint32_t gn = min(8u, GH - gb);
-          float4 qr[8][2];
+        // head dimension, 4 query heads at a time held in registers; the 4 partial dot products
+        // are summed across the warp by a halving exchange (6 shuffles), leaving head (lane >> 3) & 3
+        for (uint32_t gb = 0; gb < GH; gb += 4) {
+          const uint32_t gn = min(4u, GH - gb);
+          float4 qr[4][2];
 #pragma unroll
-          for (int g = 0; g < 8; g++)
+          for (int g = 0; g < 4; g++)
 #pragma unroll
             for (int i = 0; i < 2; i++) {
               const uint32_t j = lane + 32 * i;
@@ -736,16 +736,16 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
             }
           for (uint32_t t = warp; t < n; t += nw) {
             const float4* k4 = reinterpret_cast<const float4*>(tb + t == pos ? kn : ks + t * D);
-            float p[8];
+            float p[4];
 #pragma unroll
-            for (int g = 0; g < 8; g++) p[g] = 0.f;
+            for (int g = 0; g < 4; g++) p[g] = 0.f;
 #pragma unroll
             for (int i = 0; i < 2; i++) {
               const uint32_t j = lane + 32 * i;
               if (j < D4) {
                 const float4 a = k4[j];
 #pragma unroll
-                for (int g = 0; g < 8; g++) {
+                for (int g = 0; g < 4; g++) {
                   p[g] = fmaf(a.x, qr[g][i].x, p[g]);
                   p[g] = fmaf(a.y, qr[g][i].y, p[g]);
                   p[g] = fmaf(a.z, qr[g][i].z, p[g]);
@@ -753,27 +753,24 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
                 }
               }
             }
-            const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
-            float h4[4], h2[2];
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-              const float send = b4 ? p[k] : p[k + 4], keep = b4 ? p[k + 4] : p[k];
-              h4[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-            }
+            // halving exchange: 4 partial sums per lane -> head (lane >> 3) & 3 summed over the warp
+            const bool b4 = lane & 16, b3 = lane & 8;
+            float h2[2];
 #pragma unroll
             for (int k = 0; k < 2; k++) {
-              const float send = b3 ? h4[k] : h4[k + 2], keep = b3 ? h4[k + 2] : h4[k];
-              h2[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+              const float send = b4 ? p[k] : p[k + 2], keep = b4 ? p[k + 2] : p[k];
+              h2[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
             }
             float h1v;
             {
-              const float send = b2 ? h2[0] : h2[1], keep = b2 ? h2[1] : h2[0];
-              h1v = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+              const float send = b3 ? h2[0] : h2[1], keep = b3 ? h2[1] : h2[0];
+              h1v = keep + __shfl_xor_sync(0xffffffffu, send, 8);
             }
+            h1v += __shfl_xor_sync(0xffffffffu, h1v, 4);
             h1v += __shfl_xor_sync(0xffffffffu, h1v, 2);
             h1v += __shfl_xor_sync(0xffffffffu, h1v, 1);
-            const uint32_t g = (lane >> 2) & 7;
-            if ((lane & 3) == 0 && g < gn) sc[(gb + g) * kSub + t] = h1v / sd;
+            const uint32_t g = (lane >> 3) & 3;
+            if ((lane & 7) == 0 && g < gn) sc[(gb + g) * kSub + t] = h1v / sd;
           }
         }
         __syncthreads();
