@@ -238,22 +238,22 @@ QC_DEV void stage_ll(uint8_t* mem, uint32_t nv, uint32_t n, uint32_t units, bool
 #pragma unroll
         for (int q = 0; q < 4; q++) {
           unsigned long long a = 0ull, b = 0ull;
-          float xa = 0.f, xb = 0.f;
           if (i0 < total && e + 2 * q < n) {  // n even: the whole pair is inside
             ll_get2(src + (uint64_t)j * n + e + 2 * q, &a, &b);
             ok &= fresh(a, seq) && fresh(b, seq);
-            xa = val(a);
-            xb = val(b);
-            for (uint32_t k = 0; k < nadd; k++) {
-              ll_get2_sys(add + (uint64_t)k * n + e + 2 * q, &a, &b);
-              ok &= fresh(a, seq) && fresh(b, seq);
-              xa = __fadd_rn(xa, val(a));
-              xb = __fadd_rn(xb, val(b));
-            }
           }
-          x[p][2 * q] = xa;
-          x[p][2 * q + 1] = xb;
+          x[p][2 * q] = val(a);
+          x[p][2 * q + 1] = val(b);
         }
+        if (nadd && i0 < total)  // (expert parallelism) the peers' vectors, added in order
+          for (uint32_t q = 0; q < 8 && e + q < n; q += 2)
+            for (uint32_t k = 0; k < nadd; k++) {
+              unsigned long long a, b;
+              ll_get2_sys(add + (uint64_t)k * n + e + q, &a, &b);
+              ok &= fresh(a, seq) && fresh(b, seq);
+              x[p][q] = __fadd_rn(x[p][q], val(a));
+              x[p][q + 1] = __fadd_rn(x[p][q + 1], val(b));
+            }
       }
     } while (!ok && wt.keep(st));
     trace_at(trace, tslot);
@@ -694,16 +694,14 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
       }
       cp_wait_all();  // QK-norm weights
       __syncthreads();
-      for (uint32_t g = warp; g < GH; g += nw) head_norm_rope(qs + g * KP, qnw, D, T.eps, cs);
-      if (has_pos && warp == nw - 1) {  // model.rs:241-243: append k (normed, rotated) and v
-        head_norm_rope(kn, knw, D, T.eps, cs);
-        if (ags == 0)  // one of the GS blocks holding this position writes the cache
-          for (uint32_t i = lane; i < D; i += 32) {
-            kc_h[(uint64_t)pos * D + i] = kn[i];
-            vc_h[(uint64_t)pos * D + i] = vn[i];
-          }
-      }
+      for (uint32_t g = warp; g < GH + (has_pos ? 1u : 0u); g += nw)  // the query heads, then the new key
+        head_norm_rope(g < GH ? qs + g * KP : kn, g < GH ? qnw : knw, D, T.eps, cs);
       __syncthreads();
+      if (has_pos && ags == 0 && warp == 0)  // model.rs:241-243: append k (normed, rotated) and v; one
+        for (uint32_t i = lane; i < D; i += 32) {  // of the GS blocks holding this position writes the cache
+          kc_h[(uint64_t)pos * D + i] = kn[i];
+          vc_h[(uint64_t)pos * D + i] = vn[i];
+        }
       QC_TT(24);
       // online softmax over steps of `sub` positions
       const float sd = sqrtf((float)D);
