@@ -8,17 +8,22 @@ prompt (seed 1) prefilled before timing; weights per step (~2 GB) exceed the
 126 MB L2, so no flush is needed between steps.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--config 2|3|4] [--replicas]
 
 Prints one JSON line on rank 0.  `value` is device-resident decode tok/s over
 all ranks; `e2e` is tok/s through qc_forward with the token copied in and the
 logits copied out (pinned host memory) every step, and the host picking the
-argmax, as the reference's chat loop does.  `--impl reference` times the
-reference's CPU path (the C++ restatement under oracle/, all host threads) on
-the same model.  With N > 1 each rank runs an independent replica by default
-(scaling "weak"); with --ep the N ranks run ONE decode stream with the experts
-split over them (expert parallelism: each rank holds experts/N, partial MoE
-vectors exchanged over NVLink inside the token kernel), scaling "strong", and
-`value` is that stream's tok/s.
+argmax, as the reference's chat loop does.  With N > 1 the N ranks run ONE
+decode stream with the experts split over them (expert parallelism: each rank
+holds experts/N, partial MoE vectors exchanged over NVLink inside the token
+kernel; scaling "strong"); --replicas runs N independent streams instead.
+At N = 1 the line also carries BASELINE config 2 (`matvec`: every isolated
+matvec shape, event-timed GB/s with > 126 MB of distinct weights rotated past
+L2) and config 3 (`moe_layer`: one MoE layer at 1-128 tokens, per-token kernels
+against the tcgen05 grouped GEMMs), and the CPU baseline (the reference's CPU
+path, 1 thread and all host threads).  `--impl reference` times the reference's
+CPU path (the C++ restatement under oracle/, all host threads) on the same
+model, at the same positions and step count.
 """
 from __future__ import annotations
 
@@ -56,8 +61,9 @@ def peaks() -> dict:
     return {"hbm_gbs": 6650.0, "source": "fallback"}
 
 
-# DRAM bytes of one k_token launch from the ncu capture in profiles/k_token_4layer.md (4 layers):
-# 414.3 MB = 255.9 MB (vocab projection, logits) + 4 x 39.6 MB per layer; scaled by layer count.
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one k_token launch, from an ncu capture of
+# `bench.py --layers 4` (4 layers of the same shapes): fixed part (vocab projection, logits) + per layer;
+# a 48-layer token is scaled by the layer count (traffic grows in proportion to the layers).
 TOKEN_TRAFFIC_FIXED, TOKEN_TRAFFIC_PER_LAYER = 255.9e6, 39.6e6
 
 
@@ -158,18 +164,141 @@ def cpu_model() -> str:
 
 
 def cpu_decode(img, tokens: list[int], threads: int) -> dict:
-    """The reference's CPU path (oracle restatement, row-parallel over `threads`) on `tokens`."""
+    """The reference's CPU path (oracle restatement, row-parallel over `threads`, every element
+    decoded per use as backend.rs:28-52 does) on `tokens`; the first token is untimed (page-in)."""
     from oracle import oracle as O
     if not O.LIB_PATH.exists():
         O.build()
     m = O.Model(img, CTX, threads=threads)
-    m.forward(tokens[0])  # first token outside the timing (page-in of the 20 GB image)
+    m.forward(tokens[0])
     t0 = time.perf_counter()
     for t in tokens[1:]:
         m.forward(t)
     dt = time.perf_counter() - t0
     m.close()
     return {"tok_s": (len(tokens) - 1) / dt, "seconds": dt, "tokens": len(tokens) - 1}
+
+
+def cpu_baseline(img, prompt, ncores: int, tokens_all: int) -> dict:
+    """CPU baseline of the main line: 1 thread (the reference's own CPU path is single-threaded,
+    backend.rs:40-48) over 1 token and all host threads over `tokens_all` tokens, positions 1.."""
+    toks = [int(x) for x in prompt[:tokens_all + 1]]
+    one = cpu_decode(img, toks[:2], 1)
+    allc = cpu_decode(img, toks, ncores)
+    return {"value": allc["tok_s"], "unit": "tok/s", "cores": ncores, "kind": "port",
+            "single_thread": {"value": one["tok_s"], "unit": "tok/s", "cores": 1, "seconds": one["seconds"],
+                              "tokens": one["tokens"]},
+            "sample": f"{allc['tokens']} decode tokens at positions 1..{allc['tokens']} of the same 30B-shape "
+                      f"model over {ncores} threads ({allc['seconds']:.1f} s), and 1 token at position 1 on 1 "
+                      f"thread ({one['seconds']:.1f} s): C++ restatement of backend.rs Cpu::matvec (per-element "
+                      f"decode, sequential f32 folds) + ops.rs + model.rs, row-parallel, bit-identical for any "
+                      f"thread count; {cpu_model()}"}
+
+
+# BASELINE config 2: (name, GGML kind, rows, cols) of every isolated matvec shape; each shape's Q8_0
+# variant follows.
+def matvec_shapes(T) -> list:
+    base = [("q_proj", T.Q4_K, 4096, 2048), ("kv_proj", T.Q4_K, 512, 2048), ("o_proj", T.Q4_K, 2048, 4096),
+            ("gate_up", T.Q4_K, 768, 2048), ("gate_up_q5k", T.Q5_K, 768, 2048), ("down", T.Q6_K, 2048, 768),
+            ("router", T.F16, 128, 2048), ("vocab", T.Q6_K, 151936, 2048)]
+    q8 = [(n + "_q8_0", T.Q8_0, r, c) for n, k, r, c in base if k != T.Q5_K]
+    return base + q8
+
+
+def matvec_study(T, E, torch, steps: int, warmup: int, only: str | None = None, rotate: int = 512 << 20) -> dict:
+    """y = W x for every shape through qc_matrix_matvec, x ~ N(0,1), W ~ N(0,0.02)
+    quantized from seed 0.  Each shape is uploaded as `copies` stacked matrices (>= 512 MB of distinct
+    weights, so L2 serves no repeat) and one CUDA graph launches the kernel once per copy; the graph is
+    replayed `steps` times between CUDA events.  GB/s = algorithmic bytes (packed W + 4 cols + 4 rows)
+    per launch / the average launch time (inter-kernel gaps inside the graph included)."""
+    pk = peaks()
+    stream = torch.cuda.Stream()
+    out = []
+    for name, kind, rows, cols in matvec_shapes(T):
+        if only and name != only:
+            continue
+        blocks = T.random_matrix(kind, rows, cols, seed=0, stream=T.stream_of(name))
+        packed = blocks.size
+        copies = int(min(1024, max(2, -(-rotate // packed))))
+        m = E.Matrix(kind, rows, cols, np.tile(blocks, copies), experts=copies)
+        del blocks
+        g = torch.Generator(device="cuda").manual_seed(1)
+        x = torch.randn(cols, device="cuda", dtype=torch.float32, generator=g)
+        y = torch.empty(rows, device="cuda", dtype=torch.float32)
+        with torch.cuda.stream(stream):
+            m.matvec(x.data_ptr(), y.data_ptr(), stream.cuda_stream, expert=0)  # outside capture: first launch
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(copies):
+                m.matvec(x.data_ptr(), y.data_ptr(), stream.cuda_stream, expert=i)
+        for _ in range(warmup):
+            graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(steps):
+                graph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (steps * copies)
+        alg = packed + 4 * cols + 4 * rows
+        gbs = alg / (us * 1e-6) / 1e9
+        out.append({"shape": name, "kind": T.KIND_NAMES[kind], "rows": rows, "cols": cols, "packed_bytes": packed,
+                    "bytes_per_launch": alg, "us_per_launch": us, "gbs": gbs, "frac": gbs / pk["hbm_gbs"],
+                    "copies_rotated": copies})
+        log(f"matvec {name:>14} {T.KIND_NAMES[kind]:>5} {rows}x{cols}: {us:8.2f} us  {gbs:7.1f} GB/s "
+            f"({gbs / pk['hbm_gbs']:.3f} of peak)")
+        del graph, m
+    return {"results": out, "peak_gbs": pk["hbm_gbs"], "peak_source": pk["source"],
+            "timing": f"CUDA events around {steps} replays of a graph of one launch per rotated copy; "
+                      f"L2 defeated by >= {rotate >> 20} MB of distinct weights per shape"}
+
+
+def moe_study(T, E, steps: int, warmup: int) -> dict:
+    """BASELINE config 3: one Qwen3-30B-A3B MoE layer for T in {1, 8, 32, 128} tokens, per-token
+    decode kernels (path 1, matvecs) against tcgen05 grouped GEMMs (path 2); Zipf-skewed router."""
+    spec = T.QWEN3_30B_A3B.with_(layers=1, vocab=512)
+    img = T.synth_gguf(spec)
+    T.skew_router(img, 0, 1.1)
+    eng = E.Engine(img, 16)
+    H, I, NE, top = spec.hidden, spec.intermediate, spec.experts, spec.top
+    rv, _, _ = T.tensor_view(img, "blk.0.ffn_gate_inp.weight")
+    router = np.frombuffer(rv.tobytes(), dtype=np.float16).reshape(NE, H).astype(np.float64)
+    norm = np.frombuffer(T.tensor_view(img, "blk.0.ffn_norm.weight")[0].tobytes(), dtype=np.float32)
+    gate_b, down_b = T.row_bytes(T.Q4_K, H) * I, T.row_bytes(T.Q6_K, I) * H
+    expert_bytes = 2 * gate_b + down_b
+    rng = np.random.default_rng(7)
+    rows, load = [], np.zeros(NE, dtype=np.int64)
+    for tokens in (1, 8, 32, 128):
+        x = rng.normal(size=(tokens, H)).astype(np.float32)
+        h = x / np.sqrt((x.astype(np.float64) ** 2).mean(axis=1, keepdims=True) + spec.eps) * norm
+        sel = np.argsort(-(h @ router.T), axis=1, kind="stable")[:, :top]  # workload statistic only
+        distinct = len(np.unique(sel))
+        np.add.at(load, sel.ravel(), 1)
+        res = {"tokens": tokens, "distinct_experts": distinct, "tokens_per_expert": tokens * top / distinct}
+        byts = NE * H * 2 + distinct * expert_bytes
+        flops = 2 * tokens * top * 3 * H * I
+        for path in (1, 2):
+            for _ in range(warmup):
+                eng.moe_layer(0, x, path)
+            ms = sorted(eng.moe_layer(0, x, path)[1] for _ in range(steps))
+            med = ms[len(ms) // 2]
+            res[f"path{path}"] = {"ms": med, "tok_s": tokens / (med / 1e3), "gbs": byts / (med / 1e3) / 1e9,
+                                  "tflops": flops / (med / 1e3) / 1e12}
+        res["bytes"], res["flops"] = byts, flops
+        res["speedup_tc"] = res["path1"]["ms"] / res["path2"]["ms"]
+        rows.append(res)
+        log(f"moe T={tokens}: distinct {distinct}, per-token kernels {res['path1']['ms']:.3f} ms, "
+            f"tensor cores {res['path2']['ms']:.3f} ms")
+    eng.close()
+    cross = next((r["tokens_per_expert"] for r in rows if r["speedup_tc"] > 1.0), None)
+    ranked = np.sort(load)[::-1]
+    return {"results": rows, "crossover_tokens_per_expert": cross,
+            "load_share_top_8_experts": float(ranked[: max(1, NE // 16)].sum() / max(1, ranked.sum())),
+            "timing": "device time of qc_moe_layer (CUDA events), median of steps",
+            "data": "synthetic: N(0,0.02) weights (seed 0), router row e scaled by (e+1)^-1.1, hidden N(0,1) (seed 7)"}
 
 
 def synth_image(tools, spec, rank: int, world: int):
@@ -211,7 +340,7 @@ def run_ours(args) -> None:
         spec = spec.with_(layers=args.layers)
     img, path = synth_image(T, spec, rank, world)
     t = time.time()
-    ep = world > 1 and args.ep
+    ep = world > 1 and not args.replicas
     if ep:  # one stream over all ranks: this rank's experts, peers' exchange buffers over NVLink
         src = img if img is not None else np.memmap(path, dtype=np.uint8, mode="r")
         eng = E.Engine.expert_parallel(src, CTX, local, rank, world)
@@ -276,6 +405,15 @@ def run_ours(args) -> None:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
     ms, ms_e2e = times.tolist()
     eng.close()
+    studies = {}
+    if world == 1 and not args.layers and not args.no_studies:  # BASELINE configs 2 and 3 beside the decode line
+        for key, fn in (("matvec", lambda: matvec_study(T, E, torch, steps=5, warmup=3)),
+                        ("moe_layer", lambda: moe_study(T, E, steps=7, warmup=3))):
+            try:
+                studies[key] = fn()
+            except Exception as exc:  # a failed study must not cost the decode line; it is reported instead
+                log(f"{key} study failed: {exc!r}")
+                studies[key] = {"error": repr(exc)}
 
     if rank == 0:
         pk = peaks()
@@ -302,15 +440,9 @@ def run_ours(args) -> None:
         achieved = dom_bytes / (dom_ms / 1e3) / 1e9
         step_gbs = b["per_token"] / (step_ms / 1e3) / 1e9
         cpu = None
-        if not args.no_cpu_baseline:
-            ncores = cpu_cores()
-            toks = [int(x) for x in prompt[:args.cpu_tokens + 1]]
+        if not args.no_cpu_baseline and world == 1:
             src = img if img is not None else np.fromfile(path, dtype=np.uint8)
-            c = cpu_decode(src, toks, ncores)
-            cpu = {"value": c["tok_s"], "unit": "tok/s", "cores": ncores, "kind": "port",
-                   "sample": f"{c['tokens']} decode tokens at positions 1..{c['tokens']} of the same 30B-shape model "
-                             f"(C++ restatement of backend.rs Cpu::matvec + ops.rs + model.rs, row-parallel over "
-                             f"{ncores} threads, bit-identical to 1 thread; {cpu_model()}); {c['seconds']:.1f} s"}
+            cpu = cpu_baseline(src, prompt, cpu_cores(), args.cpu_tokens)
         out = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
@@ -345,6 +477,12 @@ def run_ours(args) -> None:
             "gpu_launches": phases["launches"] * args.steps,
             "clocks": sampler.summary(),
         }
+        if ep:  # what crosses NVLink: every rank stores its partial MoE vector into every rank, per layer
+            out["expert_parallel"] = {"ranks": world, "experts_per_rank": spec.experts // world,
+                                      "weight_bytes_per_token_per_rank": b["per_token"],
+                                      "exchange_bytes_per_token_per_rank": spec.layers * world * spec.hidden * 8,
+                                      "exchange": "8-byte tagged f32 peer stores inside k_token, one per layer"}
+        out.update(studies)
         print(json.dumps(out), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -358,97 +496,83 @@ def run_ours(args) -> None:
 
 
 def run_reference(args) -> None:
-    """The reference's own CPU path (its C++ restatement, all host threads), same metric and config."""
+    """The reference's own CPU path (its C++ restatement, all host threads), same metric, model and
+    positions as the repo arm: the 512-token prompt and the repo arm's warm-up and profiled steps
+    are prefilled (untimed, layer-major, bit-identical to token-by-token forwards), then `warmup`
+    untimed and `steps` timed decode tokens at the repo arm's positions, each a full forward of
+    the reference's per-element-decode path."""
     rank = int(os.environ.get("RANK", 0))
     if rank != 0:
         return
     from qwen30brust_b200 import tools as T
-    spec = T.QWEN3_30B_A3B
-    img = T.synth_gguf(spec)
-    ncores = cpu_cores()
-    # bounded: each step is one full token of the 30B model on the CPU; cap the timed steps
-    steps = max(1, min(args.steps, args.ref_max_steps))
-    prompt = np.random.default_rng(1).integers(0, spec.vocab, steps + args.warmup + 1).tolist()
     from oracle import oracle as O
     if not O.LIB_PATH.exists():
         O.build()
-    m = O.Model(img, CTX, threads=ncores)
-    for t in prompt[:args.warmup + 1]:
-        m.forward(int(t))
+    spec = T.QWEN3_30B_A3B
+    img = T.synth_gguf(spec)
+    ncores = cpu_cores()
+    steps = max(1, min(args.steps, args.ref_max_steps))  # bounded: each step is ~1.5 s of CPU work
+    prompt = np.random.default_rng(1).integers(0, spec.vocab, PROMPT).astype(np.uint32)
+    # the repo arm times positions PROMPT + warmup + 1 ..: it runs the prompt, `warmup` greedy steps
+    # and one profiled step first.  Here: the prompt and one more token prefilled (untimed), then
+    # `warmup` untimed steps, so the timed steps run at the same positions.
+    m = O.Model(img, CTX, threads=ncores, fast=True)
     t0 = time.perf_counter()
-    for t in prompt[args.warmup + 1:]:
-        m.forward(int(t))
+    m.prefill(np.concatenate([prompt, prompt[-1:]]))
+    prefill_s = time.perf_counter() - t0
+    m.set_fast(False)  # timed steps: every element decoded per use, as Cpu::matvec (backend.rs:28-52)
+    tok = int(prompt[0])
+    for _ in range(args.warmup):
+        tok = O.sample_greedy(m.forward(tok))
+    pos0 = m.position
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        tok = O.sample_greedy(m.forward(tok))
     dt = time.perf_counter() - t0
     value = steps / dt
-    sample = (f"{steps} decode tokens (positions {args.warmup + 1}..{args.warmup + steps}) of the 30B-shape model; "
-              f"C++ restatement of the reference CPU path, row-parallel over {ncores} threads; {cpu_model()}")
+    sample = (f"{steps} greedy decode tokens at positions {pos0}..{pos0 + steps - 1} of the 30B-shape model after a "
+              f"{PROMPT}-token prompt (prefilled untimed in {prefill_s:.0f} s) and {args.warmup} untimed steps; C++ "
+              f"restatement of the reference CPU path (per-element decode, sequential f32 folds), row-parallel over "
+              f"{ncores} threads; {cpu_model()}")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": 0, "steps": steps,
         "warmup": args.warmup, "ms_per_step": dt / steps * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic: random-init N(0,0.02) weights quantized from seed 0",
-        "config": {"workload": "BASELINE config 4: Qwen3-30B-A3B-shape decode, batch 1, greedy", "ctx": CTX},
+        "data": "synthetic: random-init N(0,0.02) weights quantized from seed 0; 512-token random prompt (seed 1)",
+        "config": {"workload": "BASELINE config 4: Qwen3-30B-A3B-shape decode, batch 1, greedy", "ctx": CTX,
+                   "prompt": PROMPT, "positions": [pos0, pos0 + steps - 1]},
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": ncores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
 
-def run_moe_layer(args) -> None:
-    """BASELINE config 3: one Qwen3-30B-A3B MoE layer for T in {1, 8, 32, 128} tokens, per-token
-    decode kernels (path 1, matvecs) against tcgen05 grouped GEMMs (path 2); Zipf-skewed router."""
+def run_matvec(args) -> None:
+    """BASELINE config 2 alone (`--config 2`, optionally one `--shape`): the matvec study's JSON line."""
     import torch
     from qwen30brust_b200 import engine as E, tools as T
-    spec = T.QWEN3_30B_A3B.with_(layers=1, vocab=512)
-    img = T.synth_gguf(spec)
-    T.skew_router(img, 0, 1.1)
-    eng = E.Engine(img, 16)
-    H, I, NE, top = spec.hidden, spec.intermediate, spec.experts, spec.top
-    rv, _, _ = T.tensor_view(img, "blk.0.ffn_gate_inp.weight")
-    router = np.frombuffer(rv.tobytes(), dtype=np.float16).reshape(NE, H).astype(np.float64)
-    norm = np.frombuffer(T.tensor_view(img, "blk.0.ffn_norm.weight")[0].tobytes(), dtype=np.float32)
-    gate_b, down_b = T.row_bytes(T.Q4_K, H) * I, T.row_bytes(T.Q6_K, I) * H
-    expert_bytes = 2 * gate_b + down_b
-    rng = np.random.default_rng(7)
+    torch.cuda.set_device(0)
     sampler = ClockSampler(0)
-    rows, load = [], np.zeros(NE, dtype=np.int64)
     with sampler:
-        for tokens in (1, 8, 32, 128):
-            x = rng.normal(size=(tokens, H)).astype(np.float32)
-            h = x / np.sqrt((x.astype(np.float64) ** 2).mean(axis=1, keepdims=True) + spec.eps) * norm
-            sel = np.argsort(-(h @ router.T), axis=1, kind="stable")[:, :top]  # workload statistic only
-            distinct = len(np.unique(sel))
-            np.add.at(load, sel.ravel(), 1)
-            res = {"tokens": tokens, "distinct_experts": distinct, "tokens_per_expert": tokens * top / distinct}
-            byts = NE * H * 2 + distinct * expert_bytes
-            flops = 2 * tokens * top * 3 * H * I
-            for path in (1, 2):
-                for _ in range(args.warmup):
-                    eng.moe_layer(0, x, path)
-                ms = sorted(eng.moe_layer(0, x, path)[1] for _ in range(args.steps))
-                med = ms[len(ms) // 2]
-                res[f"path{path}"] = {"ms": med, "tok_s": tokens / (med / 1e3), "gbs": byts / (med / 1e3) / 1e9,
-                                      "tflops": flops / (med / 1e3) / 1e12}
-            res["bytes"], res["flops"] = byts, flops
-            res["speedup_tc"] = res["path1"]["ms"] / res["path2"]["ms"]
-            rows.append(res)
-            log(f"T={tokens}: distinct {distinct}, per-token kernels {res['path1']['ms']:.3f} ms, "
-                f"tensor cores {res['path2']['ms']:.3f} ms")
-    cross = next((r["tokens_per_expert"] for r in rows if r["speedup_tc"] > 1.0), None)
-    ranked = np.sort(load)[::-1]
-    top_share = ranked[: max(1, NE // 16)].sum() / max(1, ranked.sum())
-    out = {
+        res = matvec_study(T, E, torch, args.steps, args.warmup, only=args.shape)
+    print(json.dumps({"metric": "matvec HBM GB/s (BASELINE config 2)", "unit": "GB/s", "higher_is_better": True,
+                      "steps": args.steps, "warmup": args.warmup, "dtype": "f32 x and y; GGML weights",
+                      "data": "synthetic: W ~ N(0,0.02) quantized from seed 0, x ~ N(0,1)",
+                      "config": {"workload": "BASELINE config 2: isolated matvecs at Qwen3-30B-A3B shapes"},
+                      **res, "clocks": sampler.summary()}), flush=True)
+
+
+def run_moe_layer(args) -> None:
+    """BASELINE config 3 alone (`--config 3`): the MoE-layer study's JSON line."""
+    from qwen30brust_b200 import engine as E, tools as T
+    sampler = ClockSampler(0)
+    with sampler:
+        res = moe_study(T, E, args.steps, args.warmup)
+    print(json.dumps({
         "metric": "MoE layer tokens/s (BASELINE config 3), per-token decode kernels vs tcgen05 grouped GEMMs",
         "unit": "tok/s", "higher_is_better": True, "steps": args.steps, "warmup": args.warmup,
         "dtype": "f32 activations; Q4_K gate/up, Q6_K down, F16 router; tensor path fp16 hi/lo split, fp32 accumulate",
-        "data": "synthetic: N(0,0.02) weights (seed 0), router row e scaled by (e+1)^-1.1, hidden N(0,1) (seed 7)",
-        "config": {"workload": "BASELINE config 3: one Qwen3-30B-A3B MoE layer", "hidden": H, "experts": NE,
-                   "top": top, "intermediate": I, "timing": "device time of qc_moe_layer, median of steps"},
-        "results": rows,
-        "crossover_tokens_per_expert": cross,
-        "load_share_top_8_experts": float(top_share),
-        "clocks": sampler.summary(),
-    }
-    print(json.dumps(out), flush=True)
+        "config": {"workload": "BASELINE config 3: one Qwen3-30B-A3B MoE layer", "experts": 128, "top": 8},
+        **res, "clocks": sampler.summary()}), flush=True)
 
 
 def main():
@@ -457,21 +581,25 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-tokens", type=int, default=2, help="tokens timed for the CPU baseline line")
+    ap.add_argument("--cpu-tokens", type=int, default=4, help="tokens timed on all host threads for the CPU baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-studies", action="store_true", help="skip the config 2 / config 3 objects of the main line")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: the same model with this many layers (0 = all 48, the benchmark)")
     ap.add_argument("--decode-mode", type=int, default=0, choices=[0, 1],
                     help="0: whole-token kernel when the model fits it (default); 1: per-phase kernels")
-    ap.add_argument("--ref-max-steps", type=int, default=8)
-    ap.add_argument("--config", type=int, default=4, choices=[3, 4],
-                    help="3: the MoE-layer study (per-token kernels vs tensor cores); 4: the decode bench")
-    ap.add_argument("--ep", action="store_true",
-                    help="N > 1: one decode stream with the experts split over the ranks (expert parallelism)")
+    ap.add_argument("--ref-max-steps", type=int, default=32)
+    ap.add_argument("--config", type=int, default=4, choices=[2, 3, 4],
+                    help="2: matvec study; 3: MoE-layer study; 4: the decode bench (default)")
+    ap.add_argument("--shape", default=None, help="--config 2: one shape only (e.g. q_proj, vocab)")
+    ap.add_argument("--replicas", action="store_true",
+                    help="N > 1: N independent decode streams instead of one expert-parallel stream")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
-    if args.config == 3:
+    if args.config == 2:
+        run_matvec(args)
+    elif args.config == 3:
         run_moe_layer(args)
     elif args.impl == "reference":
         run_reference(args)

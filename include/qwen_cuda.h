@@ -227,10 +227,13 @@ int qc_packed_matvec(uint32_t kind, uint64_t rows, uint64_t cols, const uint8_t*
  * own allocator has reserved the GPU's memory, or code that must not call
  * cudaFree (it may synchronize the whole device).  All device working memory
  * (raw blocks, the repacked matrix, x and y) lives in one static 32 MiB
- * __device__ array per GPU, held until the process exits; larger matrices are
- * rejected with QC_ERR_INVALID.  The first call on a device (the current one)
- * looks up the array's address and sets kernel attributes — make it before any
- * stream capture.  Calls share the array: calls that overlap on the GPU race. */
+ * __device__ array per GPU; larger matrices are rejected with QC_ERR_INVALID.
+ * CUDA loads device code lazily, so the 32 MiB are reserved on a device at the
+ * first call there (the current device), which also looks up the array's
+ * address and sets kernel attributes: make that first call on each device
+ * before the host's allocator claims the GPU's memory and before any stream
+ * capture.  The array is then held until the process exits.  Calls share the
+ * array: calls that overlap on the GPU race. */
 int qc_packed_matvec_noalloc(uint32_t kind, uint64_t rows, uint64_t cols, const uint8_t* blocks, uint64_t len,
                              const float* x, float* y);
 

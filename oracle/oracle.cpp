@@ -30,30 +30,109 @@
 #include <sys/mman.h>
 #include <sys/stat.h>
 #include <unistd.h>
+#include <condition_variable>
+#include <exception>
+#include <functional>
+#include <mutex>
 #include <thread>
 
 namespace {
 
 thread_local std::string g_err;
 
-// Row-parallel loop over [0, n) on `threads` std::threads (0 = all hardware
-// threads).  Each index is computed by exactly one thread with the same
-// sequential arithmetic, so results do not depend on the thread count.
+// Row-parallel loop over [0, n) on `threads` worker threads (0 = all hardware threads).  Each
+// index is computed by exactly one thread with the same sequential arithmetic, so results do not
+// depend on the thread count.  The workers persist between calls (a pool), so the many small
+// matvecs of one token do not pay a thread start each.
+class Pool {
+ public:
+  static Pool& get() {
+    static Pool p;
+    return p;
+  }
+  // Runs f(i) for i in [0, n) on min(nt, n) threads (the caller is one of them).
+  void run(size_t n, size_t nt, const std::function<void(size_t)>& f) {
+    std::lock_guard<std::mutex> serial(call_mu_);  // one parallel loop at a time
+    nt = std::min(nt, n);
+    if (nt <= 1) {
+      for (size_t i = 0; i < n; i++) f(i);
+      return;
+    }
+    grow(nt - 1);
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      job_ = &f;
+      n_ = n;
+      nt_ = nt;
+      pending_ = nt - 1;
+      gen_++;
+    }
+    cv_.notify_all();
+    slice(0);
+    std::unique_lock<std::mutex> lk(mu_);
+    done_cv_.wait(lk, [&] { return pending_ == 0; });
+    job_ = nullptr;
+    if (err_) {  // the first failure of any slice, raised on the calling thread
+      std::exception_ptr e = err_;
+      err_ = nullptr;
+      std::rethrow_exception(e);
+    }
+  }
+  ~Pool() {
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      stop_ = true;
+      gen_++;
+    }
+    cv_.notify_all();
+    for (auto& t : workers_) t.join();
+  }
+
+ private:
+  void slice(size_t t) {
+    const size_t lo = n_ * t / nt_, hi = n_ * (t + 1) / nt_;
+    try {
+      for (size_t i = lo; i < hi; i++) (*job_)(i);
+    } catch (...) {
+      std::lock_guard<std::mutex> lk(err_mu_);
+      if (!err_) err_ = std::current_exception();
+    }
+  }
+  void grow(size_t want) {
+    while (workers_.size() < want) {
+      const size_t id = workers_.size() + 1;  // slice index of this worker
+      workers_.emplace_back([this, id] {
+        uint64_t seen = 0;
+        for (;;) {
+          {
+            std::unique_lock<std::mutex> lk(mu_);
+            cv_.wait(lk, [&] { return gen_ != seen; });
+            seen = gen_;
+            if (stop_) return;
+            if (id >= nt_) continue;  // not needed by this loop
+          }
+          slice(id);
+          std::lock_guard<std::mutex> lk(mu_);
+          if (--pending_ == 0) done_cv_.notify_one();
+        }
+      });
+    }
+  }
+  std::mutex call_mu_, mu_, err_mu_;
+  std::exception_ptr err_;
+  std::condition_variable cv_, done_cv_;
+  std::vector<std::thread> workers_;
+  const std::function<void(size_t)>* job_ = nullptr;
+  size_t n_ = 0, nt_ = 1, pending_ = 0;
+  uint64_t gen_ = 0;
+  bool stop_ = false;
+};
+
 template <class F>
 void parallel_for(size_t n, int threads, F&& f) {
   size_t nt = threads > 0 ? (size_t)threads : std::max(1u, std::thread::hardware_concurrency());
-  nt = std::min(nt, n ? n : 1);
-  if (nt <= 1) {
-    for (size_t i = 0; i < n; i++) f(i);
-    return;
-  }
-  std::vector<std::thread> pool;
-  for (size_t t = 0; t < nt; t++)
-    pool.emplace_back([&, t] {
-      size_t lo = n * t / nt, hi = n * (t + 1) / nt;
-      for (size_t i = lo; i < hi; i++) f(i);
-    });
-  for (auto& th : pool) th.join();
+  const std::function<void(size_t)> fn = [&](size_t i) { f(i); };
+  Pool::get().run(n, nt, fn);
 }
 
 struct Fail {
@@ -181,15 +260,130 @@ float value(const uint8_t* b, uint32_t kind, size_t col) {
 // Rust's `Iterator::sum::<f32>()` is a sequential left fold that starts from -0.0.
 constexpr float kSumInit = -0.0f;
 
-// backend.rs:112-136 — y[r] = sequential f32 fold of x[i] * value(row, i).
+// All values of block `k` of a row (elements k*block .. +block), each computed with exactly the
+// operations value() uses for it (quant.rs:36-80); only the per-block factors (d * sc, dmin * m,
+// d * scale) are computed once per block or sub-block instead of once per element, which gives the
+// same f32 results.  Used by the fast matvec below.
+void decode_block(const uint8_t* b, uint32_t kind, size_t k, float* out) {
+  switch (kind) {
+    case 2: {
+      const size_t p = k * 18;
+      const float d = h(b, p);
+      for (size_t i = 0; i < 32; i++) {
+        const uint8_t q = (uint8_t)((b[p + 2 + i % 16] >> (i < 16 ? 0 : 4)) & 15);
+        out[i] = d * (float)((int)q - 8);
+      }
+      return;
+    }
+    case 8: {
+      const size_t p = k * 34;
+      const float d = h(b, p);
+      for (size_t i = 0; i < 32; i++) out[i] = d * (float)(int8_t)b[p + 2 + i];
+      return;
+    }
+    case 12:
+    case 13: {
+      const size_t size = kind == 12 ? 144 : 176, p = k * size, qs = p + (kind == 12 ? 16 : 48);
+      const float d = h(b, p), dmin = h(b, p + 2);
+      for (size_t g = 0; g < 8; g++) {
+        uint8_t s, m;
+        scale(b + p + 4, g, &s, &m);
+        const float ds = d * (float)s, c = dmin * (float)m;
+        for (size_t t = 0; t < 32; t++) {
+          const size_t i = g * 32 + t;
+          uint8_t q = (uint8_t)((b[qs + (i / 64) * 32 + i % 32] >> ((g % 2) * 4)) & 15);
+          if (kind == 13 && (b[p + 16 + i % 32] & (1u << g)) != 0) q += 16;
+          out[i] = ds * (float)q - c;
+        }
+      }
+      return;
+    }
+    case 14: {
+      const size_t p = k * 210;
+      const float d = h(b, p + 208);
+      for (size_t i = 0; i < 256; i++) {
+        const size_t chunk = i / 128, j = i % 128, quarter = j / 32, lane = j % 32;
+        const uint8_t low = b[p + chunk * 64 + (quarter % 2) * 32 + lane];
+        const uint8_t lo = (uint8_t)((low >> ((quarter / 2) * 4)) & 15);
+        const uint8_t hi = (uint8_t)((b[p + 128 + chunk * 32 + lane] >> (quarter * 2)) & 3);
+        const int q = (int)(lo | (hi << 4)) - 32;
+        out[i] = (d * (float)(int8_t)b[p + 192 + chunk * 8 + quarter * 2 + lane / 16]) * (float)q;
+      }
+      return;
+    }
+    default:
+      out[0] = value(b, kind, k);
+  }
+}
+
+// backend.rs:28-52 (Cpu::matvec) — y[r] = sequential f32 fold of x[i] * value(row, i), each element
+// decoded by value() as the reference does.  With `fast`, the same folds over values decoded a
+// block at a time (decode_block), four rows interleaved per thread: identical results, for tests
+// that need many tokens of a large model.
 void matvec(const uint8_t* data, uint32_t kind, size_t rows, size_t cols, const float* x, float* y,
+            int threads, bool fast = false) {
+  size_t rb = row_bytes(kind, cols);
+  if (!fast) {
+    parallel_for(rows, threads, [&](size_t r) {
+      const uint8_t* b = data + r * rb;
+      float acc = kSumInit;
+      for (size_t i = 0; i < cols; i++) acc = acc + x[i] * value(b, kind, i);
+      y[r] = acc;
+    });
+    return;
+  }
+  size_t block, bytes;
+  layout(kind, &block, &bytes);
+  const size_t nq = (rows + 3) / 4;
+  parallel_for(nq, threads, [&](size_t qi) {
+    const size_t r0 = qi * 4, nr = std::min<size_t>(4, rows - r0);
+    float acc[4] = {kSumInit, kSumInit, kSumInit, kSumInit};
+    float v[4][256];
+    for (size_t k = 0; k < cols / block; k++) {
+      for (size_t j = 0; j < nr; j++) decode_block(data + (r0 + j) * rb, kind, k, v[j]);
+      const float* xx = x + k * block;
+      if (nr == 4) {
+        for (size_t i = 0; i < block; i++) {
+          acc[0] = acc[0] + xx[i] * v[0][i];
+          acc[1] = acc[1] + xx[i] * v[1][i];
+          acc[2] = acc[2] + xx[i] * v[2][i];
+          acc[3] = acc[3] + xx[i] * v[3][i];
+        }
+      } else {
+        for (size_t j = 0; j < nr; j++)
+          for (size_t i = 0; i < block; i++) acc[j] = acc[j] + xx[i] * v[j][i];
+      }
+    }
+    for (size_t j = 0; j < nr; j++) y[r0 + j] = acc[j];
+  });
+}
+
+// Y[t][r] for n input vectors X[t] (t < n): the same sequential fold per (t, r) as matvec, each
+// row decoded once (decode_block) and applied to kTile vectors at a time (independent folds, so
+// the compiler runs them side by side in vector registers).  Used by Model::prefill.
+constexpr size_t kTile = 32;
+void matmul(const uint8_t* data, uint32_t kind, size_t rows, size_t cols, const float* X, size_t n, float* Y,
             int threads) {
   size_t rb = row_bytes(kind, cols);
+  size_t block, bytes;
+  layout(kind, &block, &bytes);
+  // X transposed in tiles: XT[tile][i][k] = X[tile * kTile + k][i] (0 past n)
+  const size_t tiles = (n + kTile - 1) / kTile;
+  std::vector<float> XT(tiles * cols * kTile, 0.f);
+  for (size_t t = 0; t < n; t++)
+    for (size_t i = 0; i < cols; i++) XT[(t / kTile) * cols * kTile + i * kTile + t % kTile] = X[t * cols + i];
   parallel_for(rows, threads, [&](size_t r) {
+    std::vector<float> w(cols);
     const uint8_t* b = data + r * rb;
-    float acc = kSumInit;
-    for (size_t i = 0; i < cols; i++) acc = acc + x[i] * value(b, kind, i);
-    y[r] = acc;
+    for (size_t k = 0; k < cols / block; k++) decode_block(b, kind, k, w.data() + k * block);
+    for (size_t tile = 0; tile < tiles; tile++) {
+      float acc[kTile];
+      for (size_t k = 0; k < kTile; k++) acc[k] = kSumInit;
+      const float* xt = XT.data() + tile * cols * kTile;
+      for (size_t i = 0; i < cols; i++)
+        for (size_t k = 0; k < kTile; k++) acc[k] = acc[k] + xt[i * kTile + k] * w[i];
+      for (size_t k = 0; k < kTile && tile * kTile + k < n; k++) Y[(tile * kTile + k) * rows + r] = acc[k];
+    }
   });
 }
 
@@ -255,13 +449,14 @@ void route(const float* logits, size_t n, size_t top, uint32_t* ids, float* weig
 }
 // ops.rs:57-98 — GQA causal attention over the whole cache, layout [t][kvhead][d].
 void attention(const float* q, const float* k, const float* v, size_t heads, size_t kvheads, size_t d,
-               size_t time, float* out) {
+               size_t time, float* out, int threads = 1) {
   ENSURE(kvheads > 0 && heads > 0 && d > 0 && heads % kvheads == 0, "attention shape mismatch");
   ENSURE(time > 0, "empty KV cache");
   for (size_t i = 0; i < heads * d; i++) out[i] = 0.f;
-  std::vector<float> scores(time);
   float sd = sqrtf((float)d);
-  for (size_t hh = 0; hh < heads; hh++) {
+  // heads are independent: one thread computes each head with the reference's arithmetic
+  parallel_for(heads, time * d >= (1u << 16) ? threads : 1, [&](size_t hh) {
+    std::vector<float> scores(time);
     size_t kh = hh / (heads / kvheads);
     const float* qs = q + hh * d;
     for (size_t t = 0; t < time; t++) {
@@ -276,7 +471,7 @@ void attention(const float* q, const float* k, const float* v, size_t heads, siz
       const float* vr = v + (t * kvheads + kh) * d;
       for (size_t j = 0; j < d; j++) out[hh * d + j] += sc * vr[j];
     }
-  }
+  });
 }
 
 // ---------------------------------------------------------------- gguf.rs
@@ -554,9 +749,10 @@ struct Model {
   std::vector<float> output_norm;
   size_t position = 0, context = 0;
   int threads = 0;
+  bool fast = false;  // block-decoding matvec (same results, for long test runs)
   uint64_t matvecs = 0;
 
-  // backend.rs:141-159 + Cpu::matvec
+  // backend.rs:57-75 (backend::matrix: rank check, expert slice) + Cpu::matvec
   std::vector<float> mv(const std::string& name, long expert, const std::vector<float>& x) {
     const Tensor& t = g->tensor(name);
     ENSURE(t.dims.size() == (expert >= 0 ? 3u : 2u), "matrix rank mismatch: " + name);
@@ -566,7 +762,7 @@ struct Model {
     ENSURE(expert < 0 || e < t.dims[2], "expert out of bounds");
     ENSURE(cols == x.size(), "matvec shape mismatch " + name);
     std::vector<float> y(rows);
-    matvec(g->data(t) + e * len, t.kind, rows, cols, x.data(), y.data(), threads);
+    matvec(g->data(t) + e * len, t.kind, rows, cols, x.data(), y.data(), threads, fast);
     matvecs++;
     return y;
   }
@@ -575,7 +771,10 @@ struct Model {
     for (auto& v : vv) v.clear();
     position = 0;
   }
-  std::vector<float> forward_inner(uint32_t token) {  // model.rs:217-302
+  // model.rs:217-302.  With want_logits false the output projection (model.rs:289-301) is skipped
+  // and an empty vector returned: a test-speed shortcut for prompt tokens whose logits nobody reads
+  // (the KV cache and position advance exactly as in the full forward).
+  std::vector<float> forward_inner(uint32_t token, bool want_logits = true) {
     ENSURE(position < context, "context limit " + std::to_string(context) + " reached");
     ENSURE(token < c.vocab, "token outside vocabulary");
     std::vector<float> x = g->row("token_embd.weight", token);
@@ -596,7 +795,7 @@ struct Model {
       size_t time = kk[i].size() / (c.kvheads * D);
       std::vector<float> a(c.heads * D);
       ENSURE(q.size() == c.heads * D, "attention shape mismatch");
-      attention(q.data(), kk[i].data(), vv[i].data(), c.heads, c.kvheads, D, time, a.data());
+      attention(q.data(), kk[i].data(), vv[i].data(), c.heads, c.kvheads, D, time, a.data(), threads);
       std::vector<float> o = mv(base + ".attn_output.weight", -1, a);
       for (size_t j = 0; j < x.size(); j++) x[j] += o[j];
       xn = x;
@@ -618,12 +817,105 @@ struct Model {
       }
       for (size_t j = 0; j < x.size(); j++) x[j] += moe[j];
     }
+    if (!want_logits) {
+      position++;
+      return {};
+    }
     rms(x.data(), output_norm.data(), x.size(), c.eps);
     const char* out = g->tensors.count("output.weight") ? "output.weight" : "token_embd.weight";
     std::vector<float> logits = mv(out, -1, x);
     for (float f : logits) ENSURE(std::isfinite(f), "nonfinite model output");
     position++;
     return logits;
+  }
+
+  // forward_inner(token, false) for each of n tokens, computed layer by layer over all of them:
+  // token t's layer-l step needs only the layer-l keys and values of tokens <= t, so this order
+  // gives the same results as n sequential forwards, with each weight row decoded once per layer
+  // instead of once per token.  Test and benchmark set-up only (a long prompt before the
+  // positions a test checks); errors are raised before any state changes.
+  void prefill(const uint32_t* toks, size_t n) {
+    ENSURE(position + n <= context, "context limit " + std::to_string(context) + " reached");
+    for (size_t t = 0; t < n; t++) ENSURE(toks[t] < c.vocab, "token outside vocabulary");
+    if (n == 0) return;
+    const size_t H = c.hidden, D = c.head_dim, QD = c.heads * D, KD = c.kvheads * D;
+    std::vector<float> X(n * H), XN(n * H);
+    for (size_t t = 0; t < n; t++) {
+      std::vector<float> e = g->row("token_embd.weight", toks[t]);
+      std::copy(e.begin(), e.end(), X.begin() + t * H);
+    }
+    auto mm = [&](const std::string& name, long expert, const float* in, size_t nin, size_t cols, float* out) {
+      const Tensor& t = g->tensor(name);
+      size_t rows = t.dims[1], len = row_bytes(t.kind, t.dims[0]) * rows;
+      ENSURE(t.dims[0] == cols, "matvec shape mismatch " + name);
+      matmul(g->data(t) + (expert >= 0 ? (size_t)expert : 0) * len, t.kind, rows, cols, in, nin, out, threads);
+      matvecs += nin;
+      return rows;
+    };
+    for (size_t i = 0; i < c.layers; i++) {
+      std::string base = "blk." + std::to_string(i);
+      XN = X;
+      for (size_t t = 0; t < n; t++) rms(XN.data() + t * H, norms[i][0].data(), H, c.eps);
+      std::vector<float> q(n * QD), k(n * KD), v(n * KD);
+      mm(base + ".attn_q.weight", -1, XN.data(), n, H, q.data());
+      mm(base + ".attn_k.weight", -1, XN.data(), n, H, k.data());
+      mm(base + ".attn_v.weight", -1, XN.data(), n, H, v.data());
+      for (size_t t = 0; t < n; t++) {
+        float* qt = q.data() + t * QD;
+        float* kt = k.data() + t * KD;
+        for (size_t o = 0; o + D <= QD; o += D) rms(qt + o, norms[i][1].data(), D, c.eps);
+        for (size_t o = 0; o + D <= KD; o += D) rms(kt + o, norms[i][2].data(), D, c.eps);
+        rope(qt, QD, D, position + t, c.theta);
+        rope(kt, KD, D, position + t, c.theta);
+        kk[i].insert(kk[i].end(), kt, kt + KD);
+        vv[i].insert(vv[i].end(), v.data() + t * KD, v.data() + (t + 1) * KD);
+      }
+      std::vector<float> a(n * QD, 0.f), o(n * H);
+      for (size_t t = 0; t < n; t++)
+        attention(q.data() + t * QD, kk[i].data(), vv[i].data(), c.heads, c.kvheads, D, position + t + 1,
+                  a.data() + t * QD, threads);
+      mm(base + ".attn_output.weight", -1, a.data(), n, QD, o.data());
+      for (size_t j = 0; j < n * H; j++) X[j] += o[j];
+      XN = X;
+      for (size_t t = 0; t < n; t++) rms(XN.data() + t * H, norms[i][3].data(), H, c.eps);
+      std::vector<float> rl(n * c.experts);
+      mm(base + ".ffn_gate_inp.weight", -1, XN.data(), n, H, rl.data());
+      std::vector<uint32_t> ids(n * c.top);
+      std::vector<float> w(n * c.top);
+      for (size_t t = 0; t < n; t++)
+        route(rl.data() + t * c.experts, c.experts, c.top, ids.data() + t * c.top, w.data() + t * c.top);
+      // every (token, slot) pair of an expert at once; down[t][s] kept for the combine in slot order
+      const size_t I = c.intermediate;
+      std::vector<float> down(n * c.top * H);
+      for (uint32_t e = 0; e < c.experts; e++) {
+        std::vector<size_t> pairs;
+        for (size_t p = 0; p < n * c.top; p++)
+          if (ids[p] == e) pairs.push_back(p);
+        if (pairs.empty()) continue;
+        const size_t np = pairs.size();
+        std::vector<float> xin(np * H), gate(np * I), up(np * I), dn(np * H);
+        for (size_t j = 0; j < np; j++)
+          std::copy(XN.begin() + (pairs[j] / c.top) * H, XN.begin() + (pairs[j] / c.top + 1) * H, xin.begin() + j * H);
+        mm(base + ".ffn_gate_exps.weight", e, xin.data(), np, H, gate.data());
+        mm(base + ".ffn_up_exps.weight", e, xin.data(), np, H, up.data());
+        for (size_t j = 0; j < np * I; j++) {
+          float gg = gate[j];
+          gate[j] = (gg / (1.f + expf(-gg))) * up[j];
+        }
+        mm(base + ".ffn_down_exps.weight", e, gate.data(), np, I, dn.data());
+        for (size_t j = 0; j < np; j++) std::copy(dn.begin() + j * H, dn.begin() + (j + 1) * H, down.begin() + pairs[j] * H);
+      }
+      for (size_t t = 0; t < n; t++) {
+        std::vector<float> moe(H, 0.f);
+        for (size_t s2 = 0; s2 < c.top; s2++) {
+          const float ws = w[t * c.top + s2];
+          const float* d = down.data() + (t * c.top + s2) * H;
+          for (size_t j = 0; j < H; j++) moe[j] += ws * d[j];
+        }
+        for (size_t j = 0; j < H; j++) X[t * H + j] += moe[j];
+      }
+    }
+    position += n;
   }
 };
 
@@ -793,6 +1085,14 @@ int or_matvec(const uint8_t* data, size_t len, uint32_t kind, size_t rows, size_
     matvec(data, kind, rows, cols, x, y, threads);
   });
 }
+// The block-decoding form of or_matvec (identical results).
+int or_matvec_fast(const uint8_t* data, size_t len, uint32_t kind, size_t rows, size_t cols, const float* x,
+                   float* y, int threads) {
+  return guarded([&] {
+    ENSURE(rows > 0 && len >= row_bytes(kind, cols) * rows, "matvec shape mismatch");
+    matvec(data, kind, rows, cols, x, y, threads, true);
+  });
+}
 int or_rms(float* x, const float* w, size_t n, float eps) { return guarded([&] { rms(x, w, n, eps); }); }
 void or_rope(float* x, size_t n, size_t head, size_t pos, float theta) { rope(x, n, head, pos, theta); }
 int or_softmax(float* x, size_t n) { return guarded([&] { softmax(x, n); }); }
@@ -871,19 +1171,29 @@ void* or_model_from_memory(const uint8_t* buf, size_t len, size_t context, int t
   });
   return rc == 0 ? out : nullptr;
 }
-// model.rs:210-216 — on error the cache and position are reset.
+// model.rs:210-216 — on error the cache and position are reset.  logits == NULL skips the output
+// projection (see forward_inner).
 int or_model_forward(void* h, uint32_t token, float* logits) {
   Model* m = (Model*)h;
   std::vector<float> out;
-  int rc = guarded([&] { out = m->forward_inner(token); });
+  int rc = guarded([&] { out = m->forward_inner(token, logits != nullptr); });
   if (rc) {
     m->reset();
     return rc;
   }
-  memcpy(logits, out.data(), out.size() * sizeof(float));
+  if (logits) memcpy(logits, out.data(), out.size() * sizeof(float));
   return 0;
 }
+// n forwards without logits (Model::prefill); on error the cache and position are reset.
+int or_model_prefill(void* h, const uint32_t* tokens, size_t n) {
+  Model* m = (Model*)h;
+  int rc = guarded([&] { m->prefill(tokens, n); });
+  if (rc) m->reset();
+  return rc;
+}
 void or_model_reset(void* h) { ((Model*)h)->reset(); }
+// Fast (block-decoding) matvecs on or off; results are identical either way.
+void or_model_set_fast(void* h, int fast) { ((Model*)h)->fast = fast != 0; }
 size_t or_model_position(void* h) { return ((Model*)h)->position; }
 uint64_t or_model_matvecs(void* h) { return ((Model*)h)->matvecs; }
 // hidden, layers, heads, kvheads, head_dim, experts, top, intermediate, vocab, max_context

@@ -52,6 +52,10 @@ def lib() -> C.CDLL:
         L.or_model_from_memory.restype = vp
         L.or_model_forward.argtypes = [vp, u32, fp]
         L.or_model_reset.argtypes = [vp]
+        L.or_model_prefill.argtypes = [vp, C.POINTER(u32), sz]
+        L.or_model_set_fast.argtypes = [vp, C.c_int]
+        L.or_model_set_fast.restype = None
+        L.or_matvec_fast.argtypes = [vp, sz, u32, sz, sz, fp, fp, C.c_int]
         L.or_model_position.argtypes = [vp]
         L.or_model_position.restype = sz
         L.or_model_matvecs.argtypes = [vp]
@@ -121,12 +125,14 @@ def decode_rows(blocks: np.ndarray, kind: int, rows: int, cols: int) -> np.ndarr
     return out
 
 
-def matvec(blocks: np.ndarray, kind: int, rows: int, cols: int, x, threads: int = 0) -> np.ndarray:
+def matvec(blocks: np.ndarray, kind: int, rows: int, cols: int, x, threads: int = 0, fast: bool = False) -> np.ndarray:
+    """backend.rs Cpu::matvec; `fast` decodes a block at a time (identical results, faster)."""
     b = np.ascontiguousarray(blocks, dtype=np.uint8)
     xx = _f32(x)
     assert xx.size == cols
     y = np.empty(rows, dtype=np.float32)
-    _check(lib().or_matvec(b.ctypes.data, b.size, kind, rows, cols, _fp(xx), _fp(y), threads))
+    fn = lib().or_matvec_fast if fast else lib().or_matvec
+    _check(fn(b.ctypes.data, b.size, kind, rows, cols, _fp(xx), _fp(y), threads))
     return y
 
 
@@ -183,7 +189,9 @@ CONFIG_KEYS = ("hidden", "layers", "heads", "kvheads", "head_dim", "experts", "t
 class Model:
     """model.rs Model with the Cpu backend: `forward(token) -> logits`, reset on error."""
 
-    def __init__(self, source: str | os.PathLike | np.ndarray, context: int, threads: int = 0):
+    def __init__(self, source: str | os.PathLike | np.ndarray, context: int, threads: int = 0, fast: bool = False):
+        """`fast`: block-decoding matvecs, bit-identical to the reference's per-element decode
+        (the default, which the CPU baseline times); for tests that run many tokens."""
         L = lib()
         self._buf = None
         if isinstance(source, np.ndarray):
@@ -199,11 +207,27 @@ class Model:
         L.or_model_config(h, v, _fp(et))
         self.config = dict(zip(CONFIG_KEYS, list(v)))
         self.config["eps"], self.config["theta"] = float(et[0]), float(et[1])
+        L.or_model_set_fast(h, 1 if fast else 0)
 
-    def forward(self, token: int) -> np.ndarray:
+    def forward(self, token: int, want_logits: bool = True) -> np.ndarray | None:
+        """One token; with want_logits False the output projection is skipped (returns None)."""
+        if not want_logits:
+            _check(lib().or_model_forward(self._h, token, None))
+            return None
         out = np.empty(self.config["vocab"], dtype=np.float32)
         _check(lib().or_model_forward(self._h, token, _fp(out)))
         return out
+
+    def set_fast(self, fast: bool) -> None:
+        """Block-decoding (True) or per-element (False, the reference's way) matvecs from now on."""
+        lib().or_model_set_fast(self._h, 1 if fast else 0)
+
+    def prefill(self, tokens) -> None:
+        """Forwards of `tokens` without logits, computed layer by layer over all of them (each
+        weight row decoded once per layer): the same KV cache and position as one forward per
+        token, much faster.  Test and benchmark set-up only."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        _check(lib().or_model_prefill(self._h, t.ctypes.data_as(C.POINTER(C.c_uint32)), t.size))
 
     def reset(self) -> None:
         lib().or_model_reset(self._h)

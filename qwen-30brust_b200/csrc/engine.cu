@@ -63,6 +63,7 @@ void prepare_device(int device) {
   QC_CK(qc::decode_prepare(kMaxSmem));
   QC_CK(qc::token_prepare(0));
   QC_CK(qc::moe_prepare());
+  QC_CK(qc::sample_prepare());
   done[device] = true;
 }
 
@@ -866,8 +867,7 @@ struct qc_engine {
     QC_CK(cudaMemcpyAsync(&d_state->gen_count, h_pinned + 4, 4, cudaMemcpyHostToDevice, stream));
     QC_CK(cudaEventRecord(ev0, stream));
     for (uint32_t i = 0; i < n; i++) {
-      qc::launch_sample(sc.logits, cfg.vocab, smp->d, &d_state->token, stream);
-      QC_CK(cudaGetLastError());
+      QC_CK(qc::launch_sample(sc.logits, cfg.vocab, smp->d, &d_state->token, stream));
       launch_steps(1);
     }
     QC_CK(cudaEventRecord(ev1, stream));
@@ -1151,6 +1151,7 @@ int qc_sampler_create(uint64_t seed, float temperature, uint32_t top_k, float to
     std::unique_ptr<qc_sampler> smp(new qc_sampler);
     smp->device = device;
     QC_CK(cudaSetDevice(device));
+    prepare_device(device);
     qc::SamplerDev init{};
     // rand_core 0.6.4 SeedableRng::seed_from_u64: one PCG32 step (XSH-RR output) per 4 key bytes
     uint64_t state = seed;
@@ -1178,8 +1179,7 @@ int qc_sampler_sample(qc_sampler* s, const float* logits, uint32_t n, void* stre
     QC_CK(cudaSetDevice(s->device));
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : s->own;
     if (n == 0) throw ApiError(QC_ERR_INVALID, "invalid logits");
-    qc::launch_sample(logits, n, s->d, nullptr, st);
-    QC_CK(cudaGetLastError());
+    QC_CK(qc::launch_sample(logits, n, s->d, nullptr, st));
     *token = s->finish(st);
   });
 }
@@ -1205,8 +1205,7 @@ int qc_engine_sample(qc_engine* e, qc_sampler* s, uint32_t* token) {
     ensure(s->device == e->device, "the sampler lives on another device");
     ensure(e->pos > 0, "sampling needs the logits of a previous forward");
     QC_CK(cudaSetDevice(e->device));
-    qc::launch_sample(e->sc.logits, e->cfg.vocab, s->d, nullptr, e->stream);
-    QC_CK(cudaGetLastError());
+    QC_CK(qc::launch_sample(e->sc.logits, e->cfg.vocab, s->d, nullptr, e->stream));
     *token = s->finish(e->stream);
   });
 }

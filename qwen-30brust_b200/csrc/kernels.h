@@ -179,7 +179,9 @@ struct SamplerDev {
   uint32_t token;           // the last sampled id
 };
 // Sampler::sample on n device logits: one block; the id goes to s->token and, if given, *token_dst.
-void launch_sample(const float* logits, uint32_t n, SamplerDev* s, uint32_t* token_dst, cudaStream_t st);
+// Once per device (the dynamic shared-memory attribute of the sampler kernel), before launch_sample.
+cudaError_t sample_prepare();
+cudaError_t launch_sample(const float* logits, uint32_t n, SamplerDev* s, uint32_t* token_dst, cudaStream_t st);
 // n keystream words of the sampler (advancing it), for reproducibility checks.
 void launch_sampler_words(SamplerDev* s, uint32_t n, uint32_t* out, cudaStream_t st);
 

@@ -7,14 +7,20 @@
 // further cudaMalloc fails, or fragments a pool it manages), or code that must
 // not call cudaFree because it may synchronize the whole device.  This variant
 // keeps all of that working memory in one file-scope __device__ array of
-// kScratchBytes (32 MiB), which every GPU that loads the library holds until
-// the process exits.
+// kScratchBytes (32 MiB).
 //
 // Use:
-//   * The first call on a device (the current device, cudaGetDevice) looks up
-//     the array's device address with cudaGetSymbolAddress and sets the matvec
-//     kernels' shared-memory attribute; make that first call before any stream
-//     capture on that device.
+//   * CUDA loads a library's device code lazily (the default since CUDA 12.2),
+//     so the array is reserved on a device when this file's code is first
+//     loaded there: at the first call on that device, which looks up the
+//     array's device address with cudaGetSymbolAddress (that lookup loads the
+//     code) and sets the matvec kernels' shared-memory attribute.  From then on
+//     the device holds the array until the process exits.  A host whose own
+//     allocator claims the GPU's memory must therefore make one call on each
+//     device before that allocator reserves its pool (with eager loading,
+//     CUDA_MODULE_LOADING=EAGER, the array is reserved when the library's
+//     context is created instead).  Make that first call before any stream
+//     capture on the device as well.
 //   * Every call reuses the same array and leaves its contents behind: the call
 //     zeroes the part that must start at zero (the padding of the repacked
 //     matrix) itself.  Calls that overlap on the GPU — from several host

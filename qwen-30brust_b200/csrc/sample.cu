@@ -338,10 +338,15 @@ __global__ void k_sampler_words(SamplerDev* s, uint32_t n, uint32_t* out) {
 
 }  // namespace
 
-void launch_sample(const float* logits, uint32_t n, SamplerDev* s, uint32_t* token_dst, cudaStream_t st) {
-  constexpr int smem = kExact * 12;
-  if (cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return;
-  k_sample<<<1, kST, smem, st>>>(logits, n, s, token_dst);
+constexpr int kSampleSmem = kExact * 12;
+
+cudaError_t sample_prepare() {
+  return cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, kSampleSmem);
+}
+
+cudaError_t launch_sample(const float* logits, uint32_t n, SamplerDev* s, uint32_t* token_dst, cudaStream_t st) {
+  k_sample<<<1, kST, kSampleSmem, st>>>(logits, n, s, token_dst);
+  return cudaGetLastError();
 }
 
 void launch_sampler_words(SamplerDev* s, uint32_t n, uint32_t* out, cudaStream_t st) {

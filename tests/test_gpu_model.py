@@ -205,3 +205,76 @@ def test_config4_30b_greedy_matches_oracle(cuda_engine, oracle, tools):
         assert oracle.sample_greedy(lo) == toks[step], (step, top2[1] - top2[0], err)
         assert err < 2e-2, (step, err)
         lo = m.forward(toks[step])
+
+
+def _attn_split(time, G, kvheads, nb, smax, min_chunk=32):
+    """The whole-token kernel's choice of (position splits, query-head groups) for `time`
+    attended positions, restated from its cost model so the test can aim at every choice."""
+    best, out = None, None
+    gs = 1
+    while gs <= G and G % gs == 0 and kvheads * gs <= nb:
+        s = max(1, min(min(smax, nb // (kvheads * gs)), (time + min_chunk - 1) // min_chunk))
+        chunk = (time + s - 1) // s
+        s = (time + chunk - 1) // chunk
+        gh = G // gs
+        cost = chunk * ((gh + 3) // 4) * 4 + chunk * gh + (8 * s if s > 1 else 0)
+        if best is None or cost < best:
+            best, out = cost, (s, gs)
+        gs *= 2
+    return out
+
+
+@pytest.mark.slow
+def test_bench_shape_attention_splits_and_greedy_match_oracle(cuda_engine, oracle, tools, torch_cuda):
+    """The configuration the decode bench times, checked against the oracle: the 30B-A3B shapes
+    (32 query / 4 KV heads x 128, 128 experts top-8, expert width 768, vocab 151,936, Q4_K/Q6_K/
+    F16 mix) with 2 layers so the CPU oracle keeps up, over the whole 4096-position context.
+    A 512-token random prompt, then 32 greedy steps (tokens identical, logits within max-abs
+    2e-2 and top-1 at every step), then random tokens to position 4095 with logits compared
+    where the attention's (splits, head groups) choice changes, around the bench's positions
+    517-644, and at every multiple of 256 up to the last position, so every split the kernel
+    takes at this shape (up to 18 splits x 2 head groups, several online-softmax steps per split
+    past ~1900 positions) is compared.  Both decode paths run in lockstep on the same tokens."""
+    spec = tools.QWEN3_30B_A3B.with_(layers=2)
+    img = tools.synth_gguf(spec)
+    ctx = 4096
+    engines = [_engine(cuda_engine, img, ctx, mode) for mode in (0, 1)]
+    m = oracle.Model(img, ctx, fast=True)
+    nb = torch_cuda.cuda.get_device_properties(0).multi_processor_count
+    G, kv = spec.heads // spec.kvheads, spec.kvheads
+    smax = max(1, min(nb // kv, (ctx + 31) // 32))
+    splits = [_attn_split(t, G, kv, nb, smax) for t in range(1, ctx + 1)]
+    check = {p for p in range(1, ctx) if p >= 500 and splits[p] != splits[p - 1]}  # position p: time p + 1
+    check |= {p - 1 for p in check} | set(range(511, 545)) | {580, 600, 644} | set(range(767, ctx, 256)) | {ctx - 1}
+    assert {splits[p] for p in check} >= {splits[p] for p in range(511, ctx)}
+    rng = np.random.default_rng(11)
+    prompt = rng.integers(0, spec.vocab, 512).tolist()
+    tail = rng.integers(0, spec.vocab, ctx).tolist()
+
+    pending = []  # tokens the engines have run and the oracle has not yet
+
+    def step(tok, p, want):
+        outs = [e.forward(tok, want_logits=want) for e in engines]
+        if not want:
+            pending.append(tok)
+            return None
+        m.prefill(pending)  # the oracle catches up layer-major (same results as token by token)
+        pending.clear()
+        o = m.forward(tok)
+        for mode, g in enumerate(outs):
+            err = float(np.abs(g - o).max())
+            assert err < 2e-2, (mode, p, err)
+            assert int(np.argmax(g)) == oracle.sample_greedy(o), (mode, p)
+        return o
+
+    for p, tok in enumerate(prompt):
+        o = step(tok, p, p in check or p == len(prompt) - 1)
+    for k in range(32):  # greedy from the oracle's argmax; the engines must pick the same ids
+        p = len(prompt) + k
+        o = step(oracle.sample_greedy(o), p, True)
+    for p in range(len(prompt) + 32, ctx):
+        step(tail[p], p, p in check)
+    assert ctx - 1 in check and not pending
+    assert all(e.position == ctx for e in engines) and m.position == ctx
+    for e in engines:
+        e.close()

@@ -203,3 +203,47 @@ def test_sampler_rules(oracle):
         draw = u * float(p[:keep].sum())
         want = order[min(int(np.searchsorted(np.cumsum(p[:keep]), draw, side="right")), keep - 1)]
         assert s.sample(logits) == want
+
+
+def test_fast_matvec_and_model_are_bit_identical(oracle, tools):
+    """The block-decoding matvec (used by long GPU parity runs) gives the same f32 results as the
+    per-element decode the reference performs (backend.rs:28-52), for every format, and a model
+    run with it gives the same logits, including after forwards that skip the output projection."""
+    for kind in KINDS:
+        cols = 512 if kind in (12, 13, 14) else 96
+        rows = 37
+        blocks = tools.random_matrix(kind, rows, cols, seed=4, stream=kind + 1, std=0.02)
+        x = tools.normal(4, 99 + kind, cols)
+        a = oracle.matvec(blocks, kind, rows, cols, x)
+        b = oracle.matvec(blocks, kind, rows, cols, x, fast=True)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), kind
+        c = oracle.matvec(blocks, kind, rows, cols, x, threads=3, fast=True)
+        assert np.array_equal(a.view(np.uint32), c.view(np.uint32)), kind
+    img = tools.synth_gguf(tools.TINY)
+    slow, fast = oracle.Model(img, 64), oracle.Model(img, 64, fast=True)
+    for p, tok in enumerate([5, 9, 300, 7, 42, 11]):
+        want = p % 3 == 2
+        a, b = slow.forward(tok), fast.forward(tok, want_logits=want)
+        assert (b is None) != want
+        if want:
+            assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), p
+    assert slow.position == fast.position == 6
+
+
+def test_prefill_equals_sequential_forwards(oracle, tools):
+    """Model::prefill (layer-major over a prompt, each weight row decoded once per layer) leaves the
+    same KV cache and position as one forward per token: the next logits are bit-identical."""
+    img = tools.synth_gguf(tools.TINY)
+    toks = np.random.default_rng(2).integers(0, tools.TINY.vocab, 45).tolist()
+    a, b = oracle.Model(img, 64), oracle.Model(img, 64, fast=True)
+    for t in toks[:40]:
+        a.forward(t, want_logits=False)
+    b.prefill(toks[:17])
+    b.prefill(toks[17:40])
+    assert a.position == b.position == 40
+    for t in toks[40:]:
+        la, lb = a.forward(t), b.forward(t)
+        assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+    with pytest.raises(oracle.OracleError, match="context limit"):
+        b.prefill(list(range(30)))
+    assert b.position == 0  # reset on error, as forward
