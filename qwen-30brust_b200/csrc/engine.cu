@@ -158,14 +158,33 @@ qc::MatDesc with_lpr(qc::MatDesc m, uint32_t lpr) {
 // sampling.rs:3-8 Sampler: parameters and the StdRng state, resident on one device.
 struct qc_sampler {
   int device = 0;
+  uint32_t top_k = 0;
   qc::SamplerDev* d = nullptr;
   uint32_t* h = nullptr;  // pinned: [0] err, [1] token
   cudaStream_t own = nullptr;
+  void* scratch = nullptr;  // sort and fold arrays of sets larger than shared memory
+  uint32_t scratch_n = 0;
   ~qc_sampler() {
     cudaSetDevice(device);
     if (own) cudaStreamDestroy(own);
     cudaFreeHost(h);
     cudaFree(d);
+    cudaFree(scratch);
+  }
+  // Scratch for a sample over n ids (none when the top-k set fits the kernel's shared memory);
+  // allocated before the first such sample and kept for later ones.
+  qc::SampleScratch scratch_for(uint32_t n) {
+    const uint32_t set = top_k > 0 && top_k < n ? top_k : n;
+    if (set <= qc::sample_exact_max()) return qc::SampleScratch{};
+    if (n > scratch_n) {
+      QC_CK(cudaDeviceSynchronize());  // an earlier sample may still use the old arrays
+      cudaFree(scratch);
+      scratch = nullptr;
+      scratch_n = 0;
+      QC_CK(cudaMalloc(&scratch, qc::sample_scratch_bytes(n)));
+      scratch_n = n;
+    }
+    return qc::sample_scratch_at(scratch, n);
   }
   // Reads the sampled id and the sticky error after `st` drains; the error is cleared.
   uint32_t finish(cudaStream_t st) {
@@ -865,9 +884,10 @@ struct qc_engine {
     QC_CK(cudaSetDevice(device));
     h_pinned[4] = 0;  // gen_count
     QC_CK(cudaMemcpyAsync(&d_state->gen_count, h_pinned + 4, 4, cudaMemcpyHostToDevice, stream));
+    const qc::SampleScratch scr = smp->scratch_for(cfg.vocab);
     QC_CK(cudaEventRecord(ev0, stream));
     for (uint32_t i = 0; i < n; i++) {
-      QC_CK(qc::launch_sample(sc.logits, cfg.vocab, smp->d, &d_state->token, stream));
+      QC_CK(qc::launch_sample(sc.logits, cfg.vocab, smp->d, &d_state->token, scr, stream));
       launch_steps(1);
     }
     QC_CK(cudaEventRecord(ev1, stream));
@@ -1150,6 +1170,7 @@ int qc_sampler_create(uint64_t seed, float temperature, uint32_t top_k, float to
            "invalid sampling parameters");  // sampling.rs:11-19
     std::unique_ptr<qc_sampler> smp(new qc_sampler);
     smp->device = device;
+    smp->top_k = top_k;
     QC_CK(cudaSetDevice(device));
     prepare_device(device);
     qc::SamplerDev init{};
@@ -1179,7 +1200,7 @@ int qc_sampler_sample(qc_sampler* s, const float* logits, uint32_t n, void* stre
     QC_CK(cudaSetDevice(s->device));
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : s->own;
     if (n == 0) throw ApiError(QC_ERR_INVALID, "invalid logits");
-    QC_CK(qc::launch_sample(logits, n, s->d, nullptr, st));
+    QC_CK(qc::launch_sample(logits, n, s->d, nullptr, s->scratch_for(n), st));
     *token = s->finish(st);
   });
 }
@@ -1205,7 +1226,7 @@ int qc_engine_sample(qc_engine* e, qc_sampler* s, uint32_t* token) {
     ensure(s->device == e->device, "the sampler lives on another device");
     ensure(e->pos > 0, "sampling needs the logits of a previous forward");
     QC_CK(cudaSetDevice(e->device));
-    QC_CK(qc::launch_sample(e->sc.logits, e->cfg.vocab, s->d, nullptr, e->stream));
+    QC_CK(qc::launch_sample(e->sc.logits, e->cfg.vocab, s->d, nullptr, s->scratch_for(e->cfg.vocab), e->stream));
     *token = s->finish(e->stream);
   });
 }

@@ -179,9 +179,24 @@ struct SamplerDev {
   uint32_t token;           // the last sampled id
 };
 // Sampler::sample on n device logits: one block; the id goes to s->token and, if given, *token_dst.
+// Device scratch of a sample over more than sample_exact_max() ids (a set too large for shared
+// memory): the sort's ping-pong (key, index) arrays and the probabilities, their quotients by the
+// total and the total's running sums, n words each (sample_scratch_bytes(n) in all).
+struct SampleScratch {
+  uint32_t *key0, *key1, *idx0, *idx1;
+  float *p, *q, *run;
+};
+inline size_t sample_scratch_bytes(uint32_t n) { return (size_t)n * 4 * 7; }
+inline SampleScratch sample_scratch_at(void* base, uint32_t n) {
+  uint32_t* w = static_cast<uint32_t*>(base);
+  return SampleScratch{w, w + n, w + 2 * (size_t)n, w + 3 * (size_t)n, reinterpret_cast<float*>(w + 4 * (size_t)n),
+                       reinterpret_cast<float*>(w + 5 * (size_t)n), reinterpret_cast<float*>(w + 6 * (size_t)n)};
+}
+uint32_t sample_exact_max();
 // Once per device (the dynamic shared-memory attribute of the sampler kernel), before launch_sample.
 cudaError_t sample_prepare();
-cudaError_t launch_sample(const float* logits, uint32_t n, SamplerDev* s, uint32_t* token_dst, cudaStream_t st);
+cudaError_t launch_sample(const float* logits, uint32_t n, SamplerDev* s, uint32_t* token_dst,
+                          const SampleScratch& scr, cudaStream_t st);
 // n keystream words of the sampler (advancing it), for reproducibility checks.
 void launch_sampler_words(SamplerDev* s, uint32_t n, uint32_t* out, cudaStream_t st);
 

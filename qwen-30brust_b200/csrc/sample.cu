@@ -7,12 +7,14 @@
 //  * sets of at most kExact ids are gathered, sorted (bitonic) and then run through the reference's
 //    own sequential f32 arithmetic by one thread: max-subtracted exp / temperature, total, the
 //    cumulative top-p cut, the draw and the subtract loop, with the same roundings;
-//  * larger sets (top_k 0 over a 151,936-token vocabulary) use the same order and rules in exact
-//    2^-40 fixed point: the total, the top-p boundary (first id whose cumulative mass reaches
-//    top_p * total) and the drawn id (first id whose cumulative mass exceeds draw * kept mass) are
-//    each a radix select by mass.  Integer sums make the result independent of thread timing; it
-//    can differ from the reference's f32 running sums only when the draw or the cut falls within
-//    their rounding of a boundary.
+//  * larger sets (top_k 0 over a 151,936-token vocabulary) are put in the same order by a stable
+//    single-block LSD radix sort of all n (key, index) pairs in device scratch, and one warp then
+//    runs the reference's sequential f32 folds over them (total with its running sums, cumulative
+//    top-p cut, draw, subtract loop): the same values and roundings as the reference, so the same
+//    id, at the cost of three dependent chains of up to n additions (~0.3 ms each at n = 151,936).
+//  * exp((l - max) / T) is exp in double rounded once to f32 (correctly rounded except in rare
+//    double-rounding cases), so it agrees with the host libm's f32 exp wherever that is within
+//    half an ulp.
 // The random source is rand 0.8's StdRng: ChaCha12 keyed by rand_core's seed_from_u64 (PCG32),
 // words consumed in keystream order, gen::<f32>() = (word >> 8) * 2^-24.
 #include "kernels.h"
@@ -22,12 +24,17 @@ namespace {
 
 constexpr int kST = 1024;
 constexpr uint32_t kExact = 16384;  // (key, index) and probability of each: 12 B in shared memory
-constexpr double kFix = 1099511627776.0;  // 2^40
+constexpr int kSortE = 16;           // radix sort: elements per thread per tile (tile = kST * kSortE)
+
+// exp(x) for the probabilities: double exp rounded once to f32.
+__device__ __forceinline__ float exp_f32(float x) { return __double2float_rn(exp((double)x)); }
 
 __device__ __forceinline__ uint32_t order_key(float f) {  // f32::total_cmp order as unsigned
   const uint32_t u = __float_as_uint(f);
   return u ^ ((u >> 31) ? 0xffffffffu : 0x80000000u);
 }
+
+__device__ __forceinline__ uint32_t warp_of() { return threadIdx.x >> 5; }
 
 __device__ __forceinline__ uint32_t rotl(uint32_t v, int c) { return __funnelshift_l(v, v, c); }
 
@@ -69,6 +76,7 @@ struct Found {
 
 struct Shared {
   unsigned long long hist[256];
+  uint32_t offs[256];
   unsigned long long red[33];
   Found found;
   uint32_t sel_b, count, token;
@@ -204,8 +212,100 @@ __device__ __forceinline__ bool ahead_or_at(uint32_t i, uint32_t k, const Found&
   return k > f.key || (k == f.key && i <= f.idx);
 }
 
+// All n ids in (key descending, index ascending) order: a stable LSD radix sort of the inverted key
+// (4 passes of 8 bits) from index order.  Each pass counts the digits, then walks tiles of
+// kST * kSortE ids: warp w takes 32 * kSortE consecutive ids in rounds of 32, ranks each id among
+// the same digit in its warp (match_any; earlier rounds counted in cnt[w][digit]), and after a
+// scan of the warps' counts per digit every id lands at offs[digit] + (ids of that digit in
+// earlier warps) + its rank: index order is kept within each digit.  Result in key[1], idx[1].
+// cnt: [32][256] words of shared memory.
+__device__ void sort_desc(const float* __restrict__ lg, uint32_t n, uint32_t* const key[2], uint32_t* const idx[2],
+                          uint32_t* cnt, Shared& sh) {
+  const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t lt = (1u << lane) - 1u;
+  for (int pass = 0; pass < 4; pass++) {
+    const int shf = 8 * pass;
+    const uint32_t* ks = pass ? key[(pass - 1) & 1] : nullptr;  // pass 0 reads the logits
+    const uint32_t* is = pass ? idx[(pass - 1) & 1] : nullptr;
+    uint32_t* kd = key[pass & 1];
+    uint32_t* id = idx[pass & 1];
+    auto kget = [&](uint32_t j) { return ks ? ks[j] : ~order_key(lg[j]); };
+    auto iget = [&](uint32_t j) { return is ? is[j] : j; };
+    for (uint32_t b = tid; b < 256; b += kST) sh.offs[b] = 0;
+    for (uint32_t b = tid; b < 32 * 256; b += kST) cnt[b] = 0;
+    __syncthreads();
+    for (uint32_t j = tid; j < n; j += kST) atomicAdd(&sh.offs[(kget(j) >> shf) & 255u], 1u);
+    __syncthreads();
+    if (tid == 0) {  // exclusive scan of the digit counts
+      uint32_t run = 0;
+      for (int b = 0; b < 256; b++) {
+        const uint32_t c = sh.offs[b];
+        sh.offs[b] = run;
+        run += c;
+      }
+    }
+    __syncthreads();
+    for (uint32_t base = 0; base < n; base += kST * kSortE) {
+      const uint32_t w0 = base + warp * 32 * kSortE;
+      uint32_t rank[kSortE];
+#pragma unroll
+      for (int e = 0; e < kSortE; e++) {
+        const uint32_t j = w0 + e * 32 + lane;
+        const uint32_t d = j < n ? (kget(j) >> shf) & 255u : 256u + lane;  // past n: a class of its own
+        const uint32_t m = __match_any_sync(0xffffffffu, d);
+        uint32_t r = 0;
+        if (d < 256) r = cnt[warp * 256 + d];
+        __syncwarp();
+        if (d < 256 && (m & lt) == 0) cnt[warp * 256 + d] = r + __popc(m);  // the group's first lane
+        __syncwarp();
+        rank[e] = r + __popc(m & lt);
+      }
+      __syncthreads();
+      if (tid < 256) {  // per digit: the warps' counts become their starting positions
+        uint32_t run = sh.offs[tid];
+        for (int w = 0; w < 32; w++) {
+          const uint32_t c = cnt[w * 256 + tid];
+          cnt[w * 256 + tid] = run;
+          run += c;
+        }
+        sh.offs[tid] = run;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int e = 0; e < kSortE; e++) {
+        const uint32_t j = w0 + e * 32 + lane;
+        if (j < n) {
+          const uint32_t k = kget(j);
+          const uint32_t pos = cnt[warp * 256 + ((k >> shf) & 255u)] + rank[e];
+          kd[pos] = k;
+          id[pos] = iget(j);
+        }
+      }
+      __syncthreads();
+      for (uint32_t b = tid; b < 32 * 256; b += kST) cnt[b] = 0;
+      __syncthreads();
+    }
+  }
+}
+
+// The reference's running f32 sum over v[0..n) (sampling.rs:44, 53): every lane of the calling warp
+// holds the same value; the running sums go to run[j] when run is not null.
+__device__ float warp_fold(const float* __restrict__ v, uint32_t n, float* run) {
+  const uint32_t lane = threadIdx.x & 31;
+  float acc = 0.f;
+  for (uint32_t b = 0; b < n; b += 32) {
+    const float x = b + lane < n ? v[b + lane] : 0.f;
+    const uint32_t m = min(32u, n - b);
+    for (uint32_t k = 0; k < m; k++) {
+      acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, x, k));
+      if (run && lane == k) run[b + k] = acc;
+    }
+  }
+  return acc;
+}
+
 __global__ void __launch_bounds__(kST) k_sample(const float* __restrict__ lg, uint32_t n, SamplerDev* s,
-                                                uint32_t* token_dst) {
+                                                uint32_t* token_dst, SampleScratch scr) {
   __shared__ Shared sh;
   extern __shared__ __align__(16) unsigned char dyn[];
   const uint32_t tid = threadIdx.x;
@@ -235,7 +335,7 @@ __global__ void __launch_bounds__(kST) k_sample(const float* __restrict__ lg, ui
     const float mx = lg[amax];
     const uint32_t Kset = s->top_k > 0 && s->top_k < n ? s->top_k : n;
     Found fk{0u, 0xffffffffu, 0, 0};  // last id of the top-k set (everything when Kset == n)
-    if (Kset < n) fk = select_first(lg, n, Kset, [](uint32_t, uint32_t) { return 1ull; }, sh);
+    if (Kset < n && Kset <= kExact) fk = select_first(lg, n, Kset, [](uint32_t, uint32_t) { return 1ull; }, sh);
     if (Kset <= kExact) {
       // gather the set, sort it, then the reference's arithmetic on one thread
       if (tid == 0) sh.count = 0;
@@ -269,7 +369,7 @@ __global__ void __launch_bounds__(kST) k_sample(const float* __restrict__ lg, ui
           __syncthreads();
         }
       for (uint32_t j = tid; j < K; j += kST)
-        probs[j] = expf(__fdiv_rn(__fsub_rn(lg[(uint32_t)ck[j]], mx), temp));
+        probs[j] = exp_f32(__fdiv_rn(__fsub_rn(lg[(uint32_t)ck[j]], mx), temp));
       __syncthreads();
       if (tid == 0) {
         float total = 0.f;
@@ -299,30 +399,62 @@ __global__ void __launch_bounds__(kST) k_sample(const float* __restrict__ lg, ui
       __syncthreads();
       token = sh.token;
     } else {
-      // exact fixed-point masses: w = round(exp((l - max) / T) * 2^40) inside the top-k set
-      auto fix = [&](uint32_t i) {
-        return (unsigned long long)__double2ull_rn((double)expf(__fdiv_rn(__fsub_rn(lg[i], mx), temp)) * kFix);
-      };
-      auto in_k = [&](uint32_t i, uint32_t k) { return ahead_or_at(i, k, fk) ? fix(i) : 0ull; };
-      unsigned long long tot = 0;
-      for (uint32_t i = tid; i < n; i += kST) tot += in_k(i, order_key(lg[i]));
-      tot = block_sum(tot, sh);
-      // top-p: the first id whose cumulative mass reaches top_p * total
-      unsigned long long tp = (unsigned long long)ceil((double)top_p * (double)tot);
-      tp = tp < 1 ? 1 : (tp > tot ? tot : tp);
-      const Found fp = select_first(lg, n, tp, in_k, sh);
-      const unsigned long long kept = fp.before + fp.w;
-      // the draw: the first kept id whose cumulative mass exceeds u * kept
-      if (tid == 0) sh.red[0] = next_word(s) >> 8;
+      // all n ids sorted in scratch; the top-k set is the first Kset of them (sampling.rs:32-39)
+      uint32_t* const key[2] = {scr.key0, scr.key1};
+      uint32_t* const idx[2] = {scr.idx0, scr.idx1};
+      sort_desc(lg, n, key, idx, reinterpret_cast<uint32_t*>(dyn), sh);
+      const uint32_t K = Kset, *const ids = scr.idx1;
+      for (uint32_t j = tid; j < K; j += kST) scr.p[j] = exp_f32(__fdiv_rn(__fsub_rn(lg[ids[j]], mx), temp));
       __syncthreads();
-      const unsigned long long u = sh.red[0];
+      if (warp_of() == 0) {  // the total, keeping its running sums
+        const float t = warp_fold(scr.p, K, scr.run);
+        if ((tid & 31) == 0) sh.red[0] = __float_as_uint(t);
+      }
       __syncthreads();
-      const unsigned long long lo = u * kept, hi = __umul64hi(u, kept);
-      const unsigned long long d = (hi << 40) | (lo >> 24);  // floor(u * kept / 2^24) < kept
-      const Found fd = select_first(lg, n, d + 1, [&](uint32_t i, uint32_t k) {
-        return ahead_or_at(i, k, fp) ? in_k(i, k) : 0ull;
-      }, sh);
-      token = fd.idx;
+      const float total = __uint_as_float((uint32_t)sh.red[0]);
+      for (uint32_t j = tid; j < K; j += kST) scr.q[j] = __fdiv_rn(scr.p[j], total);
+      __syncthreads();
+      if (warp_of() == 0) {
+        const uint32_t lane = tid & 31;
+        // top-p: the first j whose cumulative sum of p / total reaches top_p (sampling.rs:45-52)
+        float cum = 0.f;
+        uint32_t keep = K;
+        for (uint32_t b = 0; b < K && keep == K; b += 32) {
+          const float x = b + lane < K ? scr.q[b + lane] : 0.f;
+          const uint32_t m = min(32u, K - b);
+          for (uint32_t k = 0; k < m; k++) {
+            cum = __fadd_rn(cum, __shfl_sync(0xffffffffu, x, k));
+            if (cum >= top_p) {
+              keep = b + k + 1;
+              break;
+            }
+          }
+        }
+        // the kept mass is the total's running sum at keep - 1 (the same fold, truncated)
+        const float mass = scr.run[keep - 1];
+        uint32_t word = 0;
+        if (lane == 0) word = next_word(s);
+        word = __shfl_sync(0xffffffffu, word, 0);
+        float draw = __fmul_rn((float)(word >> 8) * (1.0f / 16777216.0f), mass);
+        uint32_t pick = ids[keep - 1];
+        bool done = false;
+        for (uint32_t b = 0; b < keep && !done; b += 32) {  // sampling.rs:56-63
+          const float x = b + lane < keep ? scr.p[b + lane] : 0.f;
+          const uint32_t m = min(32u, keep - b);
+          for (uint32_t k = 0; k < m; k++) {
+            const float pk = __shfl_sync(0xffffffffu, x, k);
+            if (draw < pk) {
+              pick = ids[b + k];
+              done = true;
+              break;
+            }
+            draw = __fsub_rn(draw, pk);
+          }
+        }
+        if (lane == 0) sh.token = pick;
+      }
+      __syncthreads();
+      token = sh.token;
     }
   }
   if (tid == 0) {
@@ -338,14 +470,18 @@ __global__ void k_sampler_words(SamplerDev* s, uint32_t n, uint32_t* out) {
 
 }  // namespace
 
-constexpr int kSampleSmem = kExact * 12;
+constexpr int kSampleSmem = kExact * 12;  // also holds the radix sort's [32][256] counters
+static_assert(kExact * 12 >= 32 * 256 * 4, "sort counters fit the exact path's shared memory");
+
+uint32_t sample_exact_max() { return kExact; }
 
 cudaError_t sample_prepare() {
   return cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, kSampleSmem);
 }
 
-cudaError_t launch_sample(const float* logits, uint32_t n, SamplerDev* s, uint32_t* token_dst, cudaStream_t st) {
-  k_sample<<<1, kST, kSampleSmem, st>>>(logits, n, s, token_dst);
+cudaError_t launch_sample(const float* logits, uint32_t n, SamplerDev* s, uint32_t* token_dst,
+                          const SampleScratch& scr, cudaStream_t st) {
+  k_sample<<<1, kST, kSampleSmem, st>>>(logits, n, s, token_dst, scr);
   return cudaGetLastError();
 }
 

@@ -1,12 +1,13 @@
 """Sampler::sample (sampling.rs:26-65) on the device against the oracle's restatement.
 
 The random source (StdRng = ChaCha12 keyed by seed_from_u64) must give the same words bit for
-bit.  Sampled ids: sets of at most 16384 ids run the reference's sequential f32 arithmetic on
-the device and can differ from the oracle only when a draw or the top-p cut falls within float
-rounding (CUDA expf vs the host's) of a boundary: greedy identical, >= 99% of draws identical.
-Larger sets (top_k 0 over a 151,936-id vocabulary) use exact fixed-point sums, checked against
-an integer model of that rule and for closeness to the oracle's pick.  Every draw consumes
-exactly one keystream word on both sides."""
+bit.  Sampled ids: every set runs the reference's sequential f32 arithmetic on the device (sets
+of at most 16384 ids sorted in shared memory, larger ones by a radix sort in device scratch), so
+ids can differ from the oracle only where the device's exp (double exp rounded to f32) and the
+host's f32 exp round a probability differently and a draw or the top-p cut falls within that
+rounding of a boundary: greedy identical, >= 99% of draws identical for small sets, every draw
+identical for the large sets tested.  Every draw consumes exactly one keystream word on both
+sides."""
 import math
 
 import numpy as np
@@ -60,12 +61,13 @@ CASES = [  # (n, temperature, top_k, top_p, logit scale, ties)
     (151936, 0.7, 16384, 0.9, 2.0, False),
     (151936, 0.0, 0, 1.0, 2.0, True),
 ]
-# sets larger than the 16384 ids the device sorts: exact fixed-point path
-FIXED = [
-    (151936, 0.7, 0, 0.9, 2.0, False),
+# sets larger than the 16384 ids the device sorts in shared memory: sorted in device scratch
+LARGE = [
+    (151936, 0.7, 0, 0.9, 2.0, False),   # BASELINE config 5's parameters over the 30B vocabulary
     (151936, 1.0, 0, 1.0, 1.0, False),
     (151936, 0.5, 100000, 0.99, 4.0, True),
     (20000, 0.8, 16385, 0.9, 3.0, False),
+    (151936, 0.7, 0, 0.9, 0.3, False),   # flat logits: the top-p cut keeps most of the vocabulary
 ]
 
 
@@ -96,52 +98,22 @@ def test_sampling_matches_oracle(cuda_engine, oracle, dev, n, temp, top_k, top_p
     assert d.words(1)[0] == o.next_u32()  # one word per draw on both sides
 
 
-def _total_key(x):
-    i = x.view(np.int32).astype(np.int64)
-    return np.where(i < 0, i ^ 0x7FFFFFFF, i)
-
-
-def _fixed_point_model(x, temp, top_k, top_p, word):
-    """The device's large-set rule in exact integer arithmetic: weights round(p * 2^40), the
-    top-p boundary is the first id whose cumulative weight reaches ceil(top_p * total), the drawn
-    id the first whose cumulative weight exceeds floor((word >> 8) * kept / 2^24)."""
-    n = x.size
-    order = np.lexsort((np.arange(n), -_total_key(x)))
-    k = top_k if 0 < top_k < n else n
-    ids = order[:k]
-    p = np.exp(((x[ids] - x[order[0]]) / np.float32(temp)).astype(np.float32).astype(np.float64)).astype(np.float32)
-    cs = np.cumsum(np.rint(p.astype(np.float64) * 2.0**40).astype(np.uint64))
-    tot = int(cs[-1])
-    tp = min(max(math.ceil(float(np.float32(top_p)) * tot), 1), tot)
-    cut = int(np.searchsorted(cs, tp, side="left"))
-    kept = int(cs[cut])
-    dd = ((word >> 8) * kept) >> 24
-    return int(ids[int(np.searchsorted(cs, dd + 1, side="left"))]), order
-
-
-@pytest.mark.parametrize("n,temp,top_k,top_p,scale,ties", FIXED)
-def test_large_sets_fixed_point(cuda_engine, oracle, dev, n, temp, top_k, top_p, scale, ties):
-    """Sets over 16384 ids: the device equals the exact fixed-point rule (up to CUDA expf vs the
-    host exp, so >= 95%), and its pick sits within 1% of the kept ids of the oracle's pick in sort
-    order (the reference's f32 running sums over tens of thousands of terms drift by more than
-    one id, so bitwise agreement with it is not expected here)."""
+@pytest.mark.parametrize("n,temp,top_k,top_p,scale,ties", LARGE)
+def test_large_sets_match_oracle(cuda_engine, oracle, dev, n, temp, top_k, top_p, scale, ties):
+    """Sets over 16384 ids (top_k 0 over a 151,936-id vocabulary): the reference's sequential f32
+    folds over the radix-sorted set, so the device picks the oracle's id on every draw."""
     rng = np.random.default_rng(n + top_k)
     seed = 7 + n + top_k
     d = cuda_engine.Sampler(seed, temp, top_k, top_p)
     o = oracle.Sampler(seed, temp, top_k, top_p)
-    words = oracle.Sampler(seed, temp, top_k, top_p)
-    exact = total = 0
+    picks = []
     for rep in range(8):
         x = _logits(rng, n, scale, ties)
         for _ in range(3):
             g, w = _sample(cuda_engine, dev, d, x), o.sample(x)
-            m, order = _fixed_point_model(x, temp, top_k, top_p, words.next_u32())
-            exact += g == m
-            total += 1
-            rank = np.empty(n, dtype=np.int64)
-            rank[order] = np.arange(n)
-            assert abs(int(rank[g]) - int(rank[w])) <= max(3, 0.01 * n), (rep, g, w)
-    assert exact >= math.ceil(0.95 * total), (exact, total)
+            assert g == w, (rep, g, w)
+            picks.append(g)
+    assert len(set(picks)) > 1  # the draws really sample
     assert d.words(1)[0] == o.next_u32()
 
 
