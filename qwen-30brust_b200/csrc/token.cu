@@ -121,9 +121,9 @@ QC_DEV bool fresh(unsigned long long v, uint32_t seq) { return (uint32_t)(v >> 3
 QC_DEV float val(unsigned long long v) { return __uint_as_float((uint32_t)v); }
 
 // Phase timestamps of thread 0 of each block (diagnostic builds only): slots 0-15
-// and 20-31 for one layer, 16-19 for the vocab projection.
+// and 20-47 for one layer, 16-19 for the vocab projection.
 #ifdef QC_TRACE
-__device__ unsigned long long g_ttrace[1024][32];
+__device__ unsigned long long g_ttrace[1024][48];
 QC_DEV void trace_at(bool on, int k) {
   if (on && threadIdx.x == 0 && blockIdx.x < 1024) g_ttrace[blockIdx.x][k] = gtimer();
 }
@@ -429,6 +429,20 @@ QC_DEV void rows_finish(const Seg* sg, uint32_t nseg, uint32_t units, const floa
   }
 }
 
+// Router rows of block c in whole 8-row groups (the first blocks hold them).  Measured: one row per
+// block (128 blocks for a 128-expert F16 router) finishes the rows sooner but makes every block's
+// gather of the 128 logits from 128 writers slower, a net loss.  rows: [b, e); bytes and src: the
+// span to copy and its offset in the matrix.
+struct RouterSlice {
+  Span rows;
+  uint32_t bytes;
+  uint64_t src;
+};
+__host__ __device__ inline RouterSlice router_slice(const MatDesc& m, uint32_t nb, uint32_t c) {
+  const Span g = span_of(groups_of(m.rows), nb, c);
+  return {Span{g.b * 8, min(m.rows, g.e * 8)}, g.n() * m.group_bytes, (uint64_t)g.b * m.group_bytes};
+}
+
 // Position splits S and query-head groups GS of the attention for `time` positions: every
 // (KV head, split, group) is one block.  The cost model is the per-block work: the score loop
 // takes the same time for up to 4 query heads (a warp per position holds 4 in registers), the
@@ -531,7 +545,8 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
 
   // ---- slices of this block (per layer; byte counts depend on the layer's formats) ----
   struct Slices {
-    Span pq, pk, pv, so, sr, sg, sd;
+    Span pq, pk, pv, so, sg, sd;
+    RouterSlice rt;
     uint32_t bq, bk, bv, bA, bO, bR, bOR, bGU, bD;
   };
   auto slices = [&](const LayerDev& L) {
@@ -546,7 +561,7 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
     s.pk = part(gq, gk);
     s.pv = part(gq + gk, gv);
     s.so = span_of(groups_of(L.o.rows), nbl, c);
-    s.sr = span_of(groups_of(L.router.rows), nbl, c);
+    s.rt = router_slice(L.router, nbl, c);
     s.sg = span_of(top * groups_of(L.gate.rows), nbl, c);
     s.sd = span_of(groups_of(L.down.rows), nbl, c);
     s.bq = s.pq.n() * L.q.group_bytes;
@@ -554,7 +569,7 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
     s.bv = s.pv.n() * L.v.group_bytes;
     s.bA = s.bq + s.bk + s.bv;
     s.bO = s.so.n() * L.o.group_bytes;
-    s.bR = s.sr.n() * L.router.group_bytes;
+    s.bR = s.rt.bytes;
     s.bOR = s.bO + s.bR;
     s.bGU = s.sg.n() * (L.gate.group_bytes + L.up.group_bytes);
     s.bD = s.sd.n() * top * L.down.group_bytes;
@@ -574,7 +589,7 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
     if (!s.bOR) return;
     mb_expect(&mbar[1], s.bOR);
     if (s.bO) bulk_copy(rQ, L.o.w + (uint64_t)s.so.b * L.o.group_bytes, s.bO, &mbar[1]);
-    if (s.bR) bulk_copy(rQ + s.bO, L.router.w + (uint64_t)s.sr.b * L.router.group_bytes, s.bR, &mbar[1]);
+    if (s.bR) bulk_copy(rQ + s.bO, L.router.w + s.rt.src, s.bR, &mbar[1]);
   };
   // vocab projection stages: stage k of this block's groups into slot k % nslots
   const Span sv = span_of(groups_of(T.out.rows), nbl, c);
@@ -653,6 +668,7 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
     }
     QC_TT(2);
     run_rows(segs, 3, L.q.units, xa, part);
+    QC_TT(32);
     __syncthreads();
     rows_finish(segs, 3, L.q.units, part, seq);
     __syncthreads();  // staging area reused below
@@ -912,6 +928,7 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
       parQ ^= 1;
     }
     run_rows(segs, 1, L.o.units, xview_at(stg, L.o.units, flO), part);
+    QC_TT(33);
     __syncthreads();
     rows_finish(segs, 1, L.o.units, part, seq);
     __syncthreads();
@@ -920,13 +937,14 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
     // ---- P4: router logits of rms(x', ffn_norm) (the same vector feeds gate/up) ----------------
     const bool flR = uses_float_x(L.router.kind) || uses_float_x(L.gate.kind) || uses_float_x(L.up.kind);
     if (tid == 0) {
-      const uint32_t r0 = s.sr.b * 8;
-      segs[0] = make_seg(L.router, rQ + s.bO, r0, min(L.router.rows, s.sr.e * 8), r0, nullptr, nullptr, LL + T.ll_rl + r0);
+      const uint32_t r0 = s.rt.rows.b;
+      segs[0] = make_seg(L.router, rQ + s.bO, r0, s.rt.rows.e, r0, nullptr, nullptr, LL + T.ll_rl + r0);
     }
     stage_ll<true>(stg, 1, T.hidden, L.router.units, flR, LL + T.ll_xmid, L.ffn_norm, T.eps, red, seq, st, l == 1, 22);
     const XView xf = xview_at(stg, L.router.units, flR);
     QC_TT(7);
     run_rows(segs, 1, L.router.units, xf, part);
+    QC_TT(39);
     __syncthreads();
     rows_finish(segs, 1, L.router.units, part, seq);
     QC_TT(8);
@@ -962,99 +980,76 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
     }
     __syncthreads();
     QC_TT(28);
+    // The selected experts this rank holds (all of them on one rank), in selection order: bit k of
+    // `mine` for slot k (top <= 32).  Each warp derives them itself, so the copies of their rows are
+    // issued by several warps at once right after the ranking.
+    const uint32_t mine = __ballot_sync(0xffffffffu, lane < top && sel[lane] - T.e_lo < T.e_n);
+    const uint32_t nl = __popc(mine);
+    const uint32_t gi = groups_of(L.gate.rows), gub = L.gate.group_bytes + L.up.group_bytes;
+    const Span sgd = span_of(nl * gi, nbl, c);  // this block's (local expert, gate/up row group) items
+    const uint32_t nitem = sgd.n(), bGUd = nitem * gub, bDd = nl * s.sd.n() * L.down.group_bytes;
+    // runs of items: one per local expert the span touches; run r covers items [i0, i1)
+    const uint32_t nruns = nitem ? (sgd.e - 1) / gi - sgd.b / gi + 1 : 0;
+    auto run_of = [&](uint32_t r, uint32_t* i0, uint32_t* i1) {
+      *i0 = r ? (sgd.b / gi + r) * gi : sgd.b;
+      *i1 = min((*i0 / gi + 1) * gi, sgd.e);
+    };
+    float* const gout = xres;  // [2][nitem * 8] gate then up results
     if (warp == 0) {
       // ops.rs:29-44 in selection order: max, exp, sequential sum, divide
-      float mx = -INFINITY;
-      for (uint32_t k = lane; k < top; k += 32) mx = fmaxf(mx, lg[sel[k]]);
-      mx = warp_max(mx);
-      for (uint32_t k = lane; k < top; k += 32) selw[k] = expf(lg[sel[k]] - mx);
-      __syncwarp();
-      if (lane == 0) {
-        float sum = 0.f;
-        for (uint32_t k = 0; k < top; k++) sum = __fadd_rn(sum, selw[k]);
-        red[1] = sum;
-      }
-      __syncwarp();
+      const float v = lane < top ? lg[sel[lane]] : -INFINITY;
+      const float mx = warp_max(v);
+      const float ex = lane < top ? expf(v - mx) : 0.f;
+      float sum = 0.f;
+      for (uint32_t k = 0; k < top; k++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, ex, k));
+      if (lane < top) selw[lane] = ex / sum;
+      if ((mine >> lane) & 1u) lsl[__popc(mine & ((1u << lane) - 1u))] = lane;
       QC_TT(29);
-      const float sum = red[1];
-      // the selected experts this rank holds (all of them on one rank), in selection order: lsl
-      if (lane == 0) {
-        uint32_t n = 0;
-        for (uint32_t k = 0; k < top; k++)
-          if (sel[k] - T.e_lo < T.e_n) lsl[n++] = k;
-        red[3] = __uint_as_float(n);
-      }
-      __syncwarp();
-      const uint32_t nl = __float_as_uint(red[3]);
-      const Span sgd = span_of(nl * groups_of(L.gate.rows), nbl, c);
-      const uint32_t bGU = sgd.n() * (L.gate.group_bytes + L.up.group_bytes), bD = nl * s.sd.n() * L.down.group_bytes;
-      // their gate/up rows into P (Q/K/V and K/V rows consumed), down rows into Q
-      const uint32_t gi = groups_of(L.gate.rows);
-      uint32_t nruns = 0;
-      for (uint32_t i = sgd.b; i < sgd.e; nruns++) i += min(gi - i % gi, sgd.e - i);
-      if (lane == 0) {
+    } else if (warp == 1) {  // their gate/up rows into P (Q/K/V and K/V rows consumed): run r, gate or up;
+      if (lane < 2 * nruns) {
+        uint32_t i0, i1;
+        run_of(lane >> 1, &i0, &i1);
+        const uint32_t e = sel[__fns(mine, 0, (int)(i0 / gi) + 1)] - T.e_lo;
+        const MatDesc& m = lane & 1u ? L.up : L.gate;
         proxy_fence();
-        if (bGU) mb_expect(&mbar[0], bGU);
-        if (bD) mb_expect(&mbar[1], bD);
+        bulk_copy(rP + (i0 - sgd.b) * gub + (lane & 1u) * (i1 - i0) * L.gate.group_bytes,
+                  m.w + (uint64_t)e * m.expert_stride + (uint64_t)(i0 % gi) * m.group_bytes, (i1 - i0) * m.group_bytes,
+                  &mbar[0]);
       }
+      if (lane == 0 && bGUd) mb_expect(&mbar[0], bGUd);
       __syncwarp();
-      for (uint32_t q = lane; q < 2 * nruns + (bD ? nl : 0); q += 32) {
-        if (q < 2 * nruns) {  // run q/2, gate (q even) or up
-          uint32_t i = sgd.b, off = 0;
-          for (uint32_t r = 0; r < q / 2; r++) {
-            const uint32_t ng = min(gi - i % gi, sgd.e - i);
-            off += ng * (L.gate.group_bytes + L.up.group_bytes);
-            i += ng;
-          }
-          const uint32_t g0 = i % gi, ng = min(gi - g0, sgd.e - i), e = sel[lsl[i / gi]] - T.e_lo;
-          const MatDesc& m = q & 1 ? L.up : L.gate;
-          bulk_copy(rP + off + (q & 1) * ng * L.gate.group_bytes,
-                    m.w + (uint64_t)e * m.expert_stride + (uint64_t)g0 * m.group_bytes, ng * m.group_bytes, &mbar[0]);
-        } else {
-          const uint32_t k = q - 2 * nruns, per = s.sd.n() * L.down.group_bytes;
-          bulk_copy(rQ + k * per,
-                    L.down.w + (uint64_t)(sel[lsl[k]] - T.e_lo) * L.down.expert_stride +
-                        (uint64_t)s.sd.b * L.down.group_bytes,
-                    per, &mbar[1]);
-        }
+      // then the down rows of every local selected expert into Q (needed one exchange later)
+      if (lane < nl && bDd) {
+        const uint32_t per = s.sd.n() * L.down.group_bytes;
+        proxy_fence();
+        bulk_copy(rQ + lane * per,
+                  L.down.w + (uint64_t)(sel[__fns(mine, 0, (int)lane + 1)] - T.e_lo) * L.down.expert_stride +
+                      (uint64_t)s.sd.b * L.down.group_bytes,
+                  per, &mbar[1]);
       }
-      QC_TT(30);
-      __syncwarp();
-      for (uint32_t k = lane; k < top; k += 32) selw[k] = selw[k] / sum;
+      if (lane == 0 && bDd) mb_expect(&mbar[1], bDd);
+    } else if (warp == 3 && lane < nruns) {  // row runs: all gate runs, then all up runs (one format per call)
+      uint32_t i0, i1;
+      run_of(lane, &i0, &i1);
+      const uint32_t r0 = (i0 % gi) * 8, r1 = min(L.gate.rows, (i0 % gi + i1 - i0) * 8), it0 = i0 - sgd.b;
+      uint8_t* const base = rP + it0 * gub;
+      segs[lane] = make_seg(L.gate, base, r0, r1, r0, nullptr, gout + it0 * 8, nullptr);
+      segs[nruns + lane] =
+          make_seg(L.up, base + (i1 - i0) * L.gate.group_bytes, r0, r1, r0, nullptr, gout + (nitem + it0) * 8, nullptr);
     }
     __syncthreads();
     QC_TT(9);
-    const uint32_t nl = __float_as_uint(red[3]);  // selected experts held here (top on one rank)
-    const Span sgd = span_of(nl * groups_of(L.gate.rows), nbl, c);
-    const uint32_t bGUd = sgd.n() * (L.gate.group_bytes + L.up.group_bytes), bDd = nl * s.sd.n() * L.down.group_bytes;
-    const uint32_t gi = groups_of(L.gate.rows), nitem = sgd.n();
-    float* const gout = xres;  // [2][nitem * 8] gate then up results
     if (bGUd) {
       mb_wait(&mbar[0], parP, st);
       parP ^= 1;
     }
     QC_TT(10);
-    uint32_t nruns = 0;
-    if (tid == 0) {  // all gate runs, then all up runs (runs of one format go to one call)
-      uint32_t off = 0;
-      for (uint32_t i = sgd.b; i < sgd.e; nruns++) {
-        const uint32_t g0 = i % gi, ng = min(gi - g0, sgd.e - i), it0 = i - sgd.b;
-        const uint32_t r0 = g0 * 8, r1 = min(L.gate.rows, (g0 + ng) * 8);
-        segs[nruns] = make_seg(L.gate, rP + off, r0, r1, r0, nullptr, gout + it0 * 8, nullptr);
-        off += ng * L.gate.group_bytes;
-        segs[T.nsegs / 2 + nruns] = make_seg(L.up, rP + off, r0, r1, r0, nullptr, gout + (nitem + it0) * 8, nullptr);
-        off += ng * L.up.group_bytes;
-        i += ng;
-      }
-      for (uint32_t k = 0; k < nruns; k++) segs[nruns + k] = segs[T.nsegs / 2 + k];
-      red[2] = __uint_as_float(nruns);
-    }
-    __syncthreads();
-    nruns = __float_as_uint(red[2]);
     run_rows(segs, 2 * nruns, L.gate.units, xf, part);
+    QC_TT(34);
     __syncthreads();
     rows_finish(segs, 2 * nruns, L.gate.units, part, seq);
     __syncthreads();
+    QC_TT(35);
     for (uint32_t idx = tid; idx < nitem * 8; idx += TNT) {
       const uint32_t i = sgd.b + idx / 8, slot = i / gi, r = (i % gi) * 8 + idx % 8;  // slot: index into lsl
       if (r < T.inter) {
@@ -1062,6 +1057,7 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
         ll_put(LL + T.ll_h + (uint64_t)slot * T.inter + r, __fmul_rn(gv / (1.f + expf(-gv)), uv), seq);
       }
     }
+    QC_TT(36);
     cp_wait_all();  // the next layer's descriptors
     __syncthreads();
     if (tid == 0) {  // region P is free: next layer's Q/K/V slice, or the first vocab stages
@@ -1099,6 +1095,7 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
         run_rows(segs + k, 1, L.down.units, xview_at(stg + k * xb, L.down.units, flD), part + k * dpart, warp % per,
                  per);
     }
+    QC_TT(37);
     __syncthreads();
     {  // every (expert, row) pair at once: unit groups summed in order into dout
       const uint32_t R = dr1 > dr0 ? dr1 - dr0 : 0, UG = unit_groups(L.down.units);
@@ -1111,6 +1108,7 @@ __global__ void __launch_bounds__(TNT, 1) k_token(const __grid_constant__ TokenP
       }
     }
     __syncthreads();
+    QC_TT(38);
     for (uint32_t r = dr0 + tid; r < dr1; r += TNT) {
       float acc = 0.f;
       for (uint32_t k = 0; k < nl; k++) acc = __fadd_rn(acc, __fmul_rn(selw[lsl[k]], dout[k * nd + r - dr0]));
@@ -1221,6 +1219,7 @@ const char* plan_token(const StepArgs& a, int max_smem, TokenPlan* p) {
   if (nb < d.kvheads || nb == 0) return "fewer SMs than KV heads";
   if (G * (D / 4) > (uint32_t)TNT) return "query heads per KV head x head_dim / 4 exceeds the block size";
   if (d.hidden % 2 || (d.heads * D) % 2 || d.inter % 2) return "hidden, heads*head_dim and the expert width must be even";
+  if (d.top > 32) return "more than 32 experts per token";
   TokenPlan t{};
   t.nb = nb;
   t.smax = std::max(1u, std::min(nb / d.kvheads, (d.ctx + kTokMinChunk - 1) / kTokMinChunk));
@@ -1248,9 +1247,10 @@ const char* plan_token(const StepArgs& a, int max_smem, TokenPlan* p) {
         const uint32_t lo = std::max(sa.b, seg0[k]), hi = std::min(sa.e, seg0[k] + segn[k]);
         if (hi > lo) bA += (hi - lo) * gb[k];
       }
-      const Span so = span_of(groups_of(L.o.rows), nb, c), sr = span_of(groups_of(L.router.rows), nb, c);
+      const Span so = span_of(groups_of(L.o.rows), nb, c);
+      const RouterSlice rt = router_slice(L.router, nb, c);
       const Span sg = span_of(d.top * groups_of(L.gate.rows), nb, c), sd = span_of(groups_of(L.down.rows), nb, c);
-      const uint32_t bOR = so.n() * L.o.group_bytes + sr.n() * L.router.group_bytes;
+      const uint32_t bOR = so.n() * L.o.group_bytes + rt.bytes;
       const uint32_t bGU = sg.n() * (L.gate.group_bytes + L.up.group_bytes);
       const uint32_t bD = sd.n() * d.top * L.down.group_bytes;
       P = std::max(P, std::max(bA, bGU));
@@ -1265,7 +1265,7 @@ const char* plan_token(const StepArgs& a, int max_smem, TokenPlan* p) {
         }
         partf = std::max(partf, ug(L.q.units) * ra);
         partf = std::max(partf, ug(L.o.units) * so.n() * 8);
-        partf = std::max(partf, ug(L.router.units) * sr.n() * 8);
+        partf = std::max(partf, ug(L.router.units) * rt.rows.n());
         partf = std::max(partf, ug(L.gate.units) * 2 * sg.n() * 8);
         partf = std::max(partf, d.top * ug(L.down.units) * sd.n() * 8);
       }
