@@ -47,6 +47,7 @@ enum {
 typedef struct qc_engine qc_engine;
 typedef struct qc_matrix qc_matrix;
 typedef struct qc_sampler qc_sampler;
+typedef struct qc_batch qc_batch;
 
 /* Model hyper-parameters; same fields and meaning as model.rs:5-19 Config. */
 typedef struct qc_config {
@@ -171,6 +172,41 @@ int qc_engine_sample(qc_engine* e, qc_sampler* s, uint32_t* token);
  * be NULL.  Argument errors leave the engine as it was; a failed step resets it. */
 int qc_decode_sample(qc_engine* e, qc_sampler* s, uint32_t n, uint32_t* tokens_out, float* logits);
 int qc_sync(qc_engine* e);
+
+/* ---- several sequences per step (no counterpart in the reference) --------------------------------
+ * The reference decodes one sequence, one token per Model::forward (model.rs:210-216).  A batch keeps
+ * n_seqs independent sequences (KV cache and position each, `context` positions at most, <= the
+ * engine's context) beside an engine's weights, and runs any mix of their tokens as one step: a
+ * decode step (one token of each of many sequences) and a prompt chunk (consecutive tokens of one
+ * sequence, each attending to the ones before it) are the same call.  The dense matrices read each
+ * weight once per step for all its tokens; the MoE half groups the step's tokens per expert and runs
+ * gate/up and down as tcgen05 tensor-core GEMMs (Q4_K gate/up and Q6_K down; other formats run the
+ * per-token kernels).  Logits agree with Model::forward on each sequence within the decode path's
+ * tolerance.  Error messages: qc_engine_error(engine).  Argument errors (unknown sequence, token
+ * outside the vocabulary, a sequence past its context) change nothing; a call that fails on the
+ * device (non-finite output) resets the sequences it carried.  The engine's own decode state is not
+ * touched, and the engine must outlive the batch. */
+int qc_batch_create(qc_engine* e, uint32_t n_seqs, uint32_t context, qc_batch** out);
+void qc_batch_destroy(qc_batch* b);
+/* Token i goes to sequence seq_ids[i] at that sequence's next position (a sequence may appear several
+ * times: its tokens take consecutive positions in call order).  logits (host, may be NULL) receives
+ * one row of vocab floats per sequence of the call, for the last of its tokens, in call order; the
+ * latest row of every sequence also stays on the device (qc_batch_logits_device) for sampling. */
+int qc_batch_forward(qc_batch* b, const uint32_t* seq_ids, const uint32_t* tokens, uint32_t n, float* logits);
+/* Model::reset for one sequence, or for all with seq = 0xffffffff. */
+int qc_batch_reset(qc_batch* b, uint32_t seq);
+int qc_batch_position(const qc_batch* b, uint32_t seq, uint32_t* pos);
+int qc_batch_logits_device(const qc_batch* b, uint32_t seq, const float** out);
+/* Sampler::sample (sampling.rs:26-65) of samplers[i] on the latest logits of sequence seq_ids[i],
+ * all n draws in one launch; ids to tokens_out (host).  The samplers live on the engine's device. */
+int qc_batch_sample(qc_batch* b, qc_sampler* const* samplers, const uint32_t* seq_ids, uint32_t n, uint32_t* tokens_out);
+/* The chat loop (main.rs:261-282) for n distinct sequences at once, on the device: `steps` times,
+ * sample every sequence's latest logits with its sampler and run the n ids as one step.
+ * tokens_out (host, may be NULL): steps x n ids, step-major. */
+int qc_batch_decode_sample(qc_batch* b, qc_sampler* const* samplers, const uint32_t* seq_ids, uint32_t n, uint32_t steps,
+                           uint32_t* tokens_out);
+/* Tokens run, device time of the steps (matvec_ms), KV and weight bytes. */
+int qc_batch_stats(const qc_batch* b, qc_stats* out);
 
 /* model.rs:202-208: clear the KV cache and set the position to 0. */
 int qc_reset(qc_engine* e);

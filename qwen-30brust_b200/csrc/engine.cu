@@ -64,6 +64,7 @@ void prepare_device(int device) {
   QC_CK(qc::token_prepare(0));
   QC_CK(qc::moe_prepare());
   QC_CK(qc::sample_prepare());
+  QC_CK(qc::batch_prepare(kMaxSmem));
   done[device] = true;
 }
 
@@ -801,20 +802,50 @@ struct qc_engine {
 
   // x, out: [T][hidden] host arrays.  path 1: the per-token decode kernels (router, gate/up, down)
   // once per token; path 2: the batched tensor-core kernels.  *ms: device time of the layer.
+  // The MoE scratch (moe_args) for at least T tokens.
+  void grow_moe(uint32_t T) {
+    if (T <= moe_cap) return;
+    QC_CK(cudaStreamSynchronize(stream));
+    cudaFree(d_moe);
+    d_moe = nullptr;
+    moe_cap = 0;
+    QC_CK(cudaMalloc(&d_moe, moe_bytes(T)));
+    moe_cap = T;
+  }
+  // Power-of-two weight scales of the tensor-core split for a layer (from bounds of |w| over its
+  // block scales, computed once per layer), into a.sw_gu / a.sw_down.
+  void moe_scales(uint32_t layer, qc::MoeArgs& a) {
+    if (moe_sw.empty()) moe_sw.assign(2 * cfg.layers, 0.f);
+    if (moe_sw[2 * layer] == 0.f) {
+      uint32_t* b = a.err;
+      uint32_t hb[2] = {0, 0};
+      QC_CK(cudaMemsetAsync(b, 0, 4, stream));
+      qc::launch_moe_wbound(a.gate, cfg.experts, b, stream);
+      qc::launch_moe_wbound(a.up, cfg.experts, b, stream);
+      QC_CK(cudaMemcpyAsync(&hb[0], b, 4, cudaMemcpyDeviceToHost, stream));
+      QC_CK(cudaMemsetAsync(b, 0, 4, stream));
+      qc::launch_moe_wbound(a.down, cfg.experts, b, stream);
+      QC_CK(cudaMemcpyAsync(&hb[1], b, 4, cudaMemcpyDeviceToHost, stream));
+      QC_CK(cudaStreamSynchronize(stream));
+      for (int i = 0; i < 2; i++) {
+        float bound;
+        std::memcpy(&bound, &hb[i], 4);
+        int ex = 0;
+        std::frexp(bound > 0.f ? bound : 1.f, &ex);
+        moe_sw[2 * layer + i] = std::ldexp(1.f, 14 - ex);
+      }
+    }
+    a.sw_gu = moe_sw[2 * layer];
+    a.sw_down = moe_sw[2 * layer + 1];
+  }
+
   void moe_layer(uint32_t layer, const float* x, uint32_t T, float* out, int path, float* ms) {
     ensure(layer < cfg.layers, "layer index out of range");
     ensure(T > 0 && x && out, "empty batch");
     ensure(path == 1 || path == 2, "MoE path must be 1 (per-token kernels) or 2 (tensor cores)");
     ensure(ep_world == 1, "an expert-parallel engine holds only its own experts");
     QC_CK(cudaSetDevice(device));
-    if (T > moe_cap) {
-      QC_CK(cudaStreamSynchronize(stream));
-      cudaFree(d_moe);
-      d_moe = nullptr;
-      moe_cap = 0;
-      QC_CK(cudaMalloc(&d_moe, moe_bytes(T)));
-      moe_cap = T;
-    }
+    grow_moe(T);
     qc::MoeArgs a = moe_args(layer, T);
     const uint64_t xbytes = (uint64_t)T * cfg.hidden * 4;
     float* d_x = reinterpret_cast<float*>(d_moe + moe_bytes(moe_cap) - 2 * align256((uint64_t)moe_cap * cfg.hidden * 4));
@@ -822,28 +853,7 @@ struct qc_engine {
     QC_CK(cudaMemcpyAsync(d_x, x, xbytes, cudaMemcpyHostToDevice, stream));
     if (path == 2) {
       if (const char* why = qc::moe_tc_supported(a)) throw ApiError(QC_ERR_INVALID, why);
-      if (moe_sw.empty()) moe_sw.assign(2 * cfg.layers, 0.f);
-      if (moe_sw[2 * layer] == 0.f) {  // bounds of |w| from the block scales, once per layer
-        uint32_t* b = a.err;
-        uint32_t hb[2] = {0, 0};
-        QC_CK(cudaMemsetAsync(b, 0, 4, stream));
-        qc::launch_moe_wbound(a.gate, cfg.experts, b, stream);
-        qc::launch_moe_wbound(a.up, cfg.experts, b, stream);
-        QC_CK(cudaMemcpyAsync(&hb[0], b, 4, cudaMemcpyDeviceToHost, stream));
-        QC_CK(cudaMemsetAsync(b, 0, 4, stream));
-        qc::launch_moe_wbound(a.down, cfg.experts, b, stream);
-        QC_CK(cudaMemcpyAsync(&hb[1], b, 4, cudaMemcpyDeviceToHost, stream));
-        QC_CK(cudaStreamSynchronize(stream));
-        for (int i = 0; i < 2; i++) {
-          float bound;
-          std::memcpy(&bound, &hb[i], 4);
-          int ex = 0;
-          std::frexp(bound > 0.f ? bound : 1.f, &ex);
-          moe_sw[2 * layer + i] = std::ldexp(1.f, 14 - ex);
-        }
-      }
-      a.sw_gu = moe_sw[2 * layer];
-      a.sw_down = moe_sw[2 * layer + 1];
+      moe_scales(layer, a);
       QC_CK(cudaMemsetAsync(a.err, 0, 4, stream));
       QC_CK(cudaEventRecord(ev0, stream));
       qc::launch_moe_tc(a, d_x, d_out, stream);
@@ -912,6 +922,341 @@ struct qc_matrix {
   ~qc_matrix() {
     cudaSetDevice(device);
     cudaFree(d);
+  }
+};
+
+// Several sequences decoded together (no counterpart in the reference, which runs
+// one sequence): per-sequence KV caches beside an engine's weights, and one device pass per step for
+// any mix of decode tokens and prompt chunks (batch.cu), with the MoE half on the tensor cores.
+struct qc_batch {
+  qc_engine* e = nullptr;
+  uint32_t n_seqs = 0, context = 0, cap = 0;  // cap: tokens per device pass
+  std::vector<uint32_t> pos;                  // next position of each sequence
+  float* d_kv = nullptr;
+  uint64_t kv_floats = 0;  // one K (or V) block of one layer of one sequence
+  uint8_t* d_buf = nullptr;
+  // pass scratch (cap tokens)
+  qc::BatchTok* d_tok = nullptr;
+  uint32_t* d_ids = nullptr;   // token ids of the pass
+  uint32_t* d_osrc = nullptr;  // token index of each logits row of the pass
+  float *d_x = nullptr, *d_x2 = nullptr, *d_q = nullptr, *d_k = nullptr, *d_v = nullptr, *d_a = nullptr;
+  uint8_t* d_xv = nullptr;
+  uint32_t xb_max = 0;
+  float* d_lg = nullptr;     // [cap][vocab] logits rows of the pass
+  float* d_last = nullptr;   // [n_seqs][vocab] the latest logits of each sequence
+  uint32_t* d_flag = nullptr;  // [0] non-finite logits
+  // sampling
+  const float** d_rows = nullptr;       // [n_seqs] logits rows of the draws
+  qc::SamplerDev** d_sv = nullptr;      // [n_seqs] samplers of the draws
+  uint32_t* d_out = nullptr;            // [n_seqs * out_cap] sampled ids of a decode loop
+  uint32_t out_cap = 0;
+  void* d_sscr = nullptr;               // [n_seqs] sample scratch (sets beyond shared memory)
+  qc_stats stats{};
+  std::string err;
+
+  ~qc_batch() {
+    cudaSetDevice(e->device);
+    if (e->stream) cudaStreamSynchronize(e->stream);
+    cudaFree(d_kv);
+    cudaFree(d_buf);
+    cudaFree(d_out);
+    cudaFree(d_sscr);
+  }
+
+  qc::BatchArgs args() const {
+    qc::BatchArgs a{};
+    a.tok = d_tok;
+    a.kv = d_kv;
+    a.kv_floats = kv_floats;
+    a.n_layers = e->cfg.layers;
+    a.heads = e->cfg.heads;
+    a.kvheads = e->cfg.kvheads;
+    a.D = e->cfg.head_dim;
+    a.ctx = context;
+    a.eps = e->cfg.eps;
+    a.rope = e->sc.rope;
+    return a;
+  }
+
+  void create(qc_engine* eng, uint32_t n, uint32_t ctx) {
+    e = eng;
+    ensure(e->ep_world == 1, "an expert-parallel engine holds only its own experts");
+    ensure(n > 0 && n <= 4096, "sequence count must be in 1..=4096");
+    ensure(ctx > 0 && ctx <= e->context, "batch context must be in 1..=" + std::to_string(e->context));
+    n_seqs = n;
+    context = ctx;
+    pos.assign(n, 0);
+    cap = 128;  // tokens per device pass (the MoE tensor-core path is measured up to 128)
+    const qc_config& c = e->cfg;
+    const uint64_t D = c.head_dim, QD = (uint64_t)c.heads * D, KD = (uint64_t)c.kvheads * D, H = c.hidden, V = c.vocab;
+    ensure(D % 32 == 0 && D <= 128 && c.heads / c.kvheads <= 32, "batched attention needs head_dim <= 128 (a multiple of 32) "
+           "and at most 32 query heads per KV head");
+    QC_CK(cudaSetDevice(e->device));
+    kv_floats = (uint64_t)c.kvheads * ctx * D;
+    const uint64_t kv_bytes = (uint64_t)n * c.layers * 2 * kv_floats * 4;
+    QC_CK(cudaMalloc(&d_kv, kv_bytes));
+    QC_CK(cudaMemsetAsync(d_kv, 0, kv_bytes, e->stream));
+    for (const qc::LayerDev& L : e->layers) {
+      xb_max = std::max(xb_max, qc::xview_bytes(L.q.units, qc::uses_float_x(L.q.kind) || qc::uses_float_x(L.k.kind) ||
+                                                               qc::uses_float_x(L.v.kind)));
+      xb_max = std::max(xb_max, qc::xview_bytes(L.o.units, qc::uses_float_x(L.o.kind)));
+      ensure(qc::batch_matvec_smem(L.q) <= (size_t)kMaxSmem && qc::batch_matvec_smem(L.o) <= (size_t)kMaxSmem,
+             "rows too wide for the batched matvec");
+    }
+    xb_max = std::max(xb_max, qc::xview_bytes(e->out.units, qc::uses_float_x(e->out.kind)));
+    ensure(qc::batch_matvec_smem(e->out) <= (size_t)kMaxSmem, "rows too wide for the batched matvec");
+    uint64_t o = 0;
+    auto take = [&](uint64_t bytes) {
+      const uint64_t at = o;
+      o = align256(o + bytes);
+      return at;
+    };
+    const uint64_t o_tok = take(cap * sizeof(qc::BatchTok)), o_ids = take(cap * 4), o_osrc = take(cap * 4);
+    const uint64_t o_x = take(cap * H * 4), o_x2 = take(cap * H * 4), o_q = take(cap * QD * 4), o_k = take(cap * KD * 4),
+                   o_v = take(cap * KD * 4), o_a = take(cap * QD * 4), o_xv = take((uint64_t)cap * xb_max),
+                   o_lg = take(cap * V * 4), o_last = take((uint64_t)n * V * 4), o_flag = take(16),
+                   o_rows = take((uint64_t)n * 8), o_sv = take((uint64_t)n * 8);
+    QC_CK(cudaMalloc(&d_buf, o));
+    QC_CK(cudaMemsetAsync(d_buf, 0, o, e->stream));
+    e->grow_moe(cap);
+    for (uint32_t l = 0; l < c.layers; l++) {  // the tensor-core weight scales of every layer, once
+      qc::MoeArgs ma = e->moe_args(l, cap);
+      if (!qc::moe_tc_supported(ma)) e->moe_scales(l, ma);
+    }
+    QC_CK(cudaMemsetAsync(e->moe_args(0, 1).err, 0, 4, e->stream));
+    d_tok = reinterpret_cast<qc::BatchTok*>(d_buf + o_tok);
+    d_ids = reinterpret_cast<uint32_t*>(d_buf + o_ids);
+    d_osrc = reinterpret_cast<uint32_t*>(d_buf + o_osrc);
+    d_x = reinterpret_cast<float*>(d_buf + o_x);
+    d_x2 = reinterpret_cast<float*>(d_buf + o_x2);
+    d_q = reinterpret_cast<float*>(d_buf + o_q);
+    d_k = reinterpret_cast<float*>(d_buf + o_k);
+    d_v = reinterpret_cast<float*>(d_buf + o_v);
+    d_a = reinterpret_cast<float*>(d_buf + o_a);
+    d_xv = d_buf + o_xv;
+    d_lg = reinterpret_cast<float*>(d_buf + o_lg);
+    d_last = reinterpret_cast<float*>(d_buf + o_last);
+    d_flag = reinterpret_cast<uint32_t*>(d_buf + o_flag);
+    d_rows = reinterpret_cast<const float**>(d_buf + o_rows);
+    d_sv = reinterpret_cast<qc::SamplerDev**>(d_buf + o_sv);
+    QC_CK(cudaStreamSynchronize(e->stream));
+  }
+
+  // One device pass: T tokens (ids in d_ids, sequence and position in d_tok), logits rows for the
+  // n_out tokens listed in d_osrc.
+  void pass(uint32_t T, uint32_t n_out) {
+    const qc_config& c = e->cfg;
+    cudaStream_t s = e->stream;
+    const uint32_t H = c.hidden, QD = c.heads * c.head_dim, KD = c.kvheads * c.head_dim;
+    const qc::BatchArgs ba = args();
+    qc::launch_batch_embed(e->embd, d_tok, d_ids, T, H, d_x, s);
+    for (uint32_t l = 0; l < c.layers; l++) {
+      const qc::LayerDev& L = e->layers[l];
+      const bool flA = qc::uses_float_x(L.q.kind) || qc::uses_float_x(L.k.kind) || qc::uses_float_x(L.v.kind);
+      const uint32_t xbA = qc::xview_bytes(L.q.units, flA), xbO = qc::xview_bytes(L.o.units, qc::uses_float_x(L.o.kind));
+      qc::launch_batch_stage(d_x, nullptr, T, H, L.q.units, flA, L.attn_norm, c.eps, d_xv, xbA, s);
+      qc::launch_batch_matvec(L.q, d_xv, xbA, T, d_q, QD, nullptr, e->sms, s);
+      qc::launch_batch_matvec(L.k, d_xv, xbA, T, d_k, KD, nullptr, e->sms, s);
+      qc::launch_batch_matvec(L.v, d_xv, xbA, T, d_v, KD, nullptr, e->sms, s);
+      qc::launch_batch_qkprep(ba, l, L.q_norm, L.k_norm, d_q, d_k, d_v, T, s);
+      qc::launch_batch_attention(ba, l, d_q, d_a, T, s);
+      qc::launch_batch_stage(d_a, nullptr, T, QD, L.o.units, qc::uses_float_x(L.o.kind), nullptr, 0.f, d_xv, xbO, s);
+      qc::launch_batch_matvec(L.o, d_xv, xbO, T, d_x, H, d_x, e->sms, s);  // x += W_o attn (model.rs:245-248)
+      // the MoE half (model.rs:249-287): tensor-core path when the formats allow, else per token
+      qc::MoeArgs ma = e->moe_args(l, T);
+      if (!qc::moe_tc_supported(ma)) {
+        e->moe_scales(l, ma);  // (measured at creation: only reads the cached scales)
+        qc::launch_moe_tc(ma, d_x, d_x2, s);
+        std::swap(d_x, d_x2);
+      } else {
+        for (uint32_t t = 0; t < T; t++) {
+          QC_CK(cudaMemcpyAsync(e->sc.x, d_x + (uint64_t)t * H, H * 4, cudaMemcpyDeviceToDevice, s));
+          qc::launch_moe_token(e->dims, e->plan, L, e->sc, e->d_state, s);
+          QC_CK(cudaMemcpyAsync(d_x + (uint64_t)t * H, e->sc.x, H * 4, cudaMemcpyDeviceToDevice, s));
+        }
+      }
+      QC_CK(cudaGetLastError());
+    }
+    if (n_out) {  // model.rs:289-301: output norm, vocabulary rows, finiteness
+      const bool flV = qc::uses_float_x(e->out.kind);
+      const uint32_t xbV = qc::xview_bytes(e->out.units, flV);
+      qc::launch_batch_stage(d_x, d_osrc, n_out, H, e->out.units, flV, e->out_norm, c.eps, d_xv, xbV, s);
+      qc::launch_batch_matvec(e->out, d_xv, xbV, n_out, d_lg, c.vocab, nullptr, e->sms, s);
+      qc::launch_batch_finite(d_lg, (uint64_t)n_out * c.vocab, d_flag, s);
+    }
+    QC_CK(cudaGetLastError());
+  }
+
+  // Raises the sticky errors of the passes since the last check.
+  void check() {
+    uint32_t h[2] = {0, 0};
+    QC_CK(cudaMemcpyAsync(&h[0], d_flag, 4, cudaMemcpyDeviceToHost, e->stream));
+    QC_CK(cudaMemcpyAsync(&h[1], e->moe_args(0, 1).err, 4, cudaMemcpyDeviceToHost, e->stream));
+    QC_CK(cudaStreamSynchronize(e->stream));
+    QC_CK(cudaMemsetAsync(d_flag, 0, 4, e->stream));
+    QC_CK(cudaMemsetAsync(e->moe_args(0, 1).err, 0, 4, e->stream));
+    e->check_flags();  // per-token MoE fallback: non-finite router logits
+    if (h[1] & 2) throw ApiError(QC_ERR_CUDA, "MoE tensor-core kernel: a wait timed out");
+    if (h[1] & 1) throw ApiError(QC_ERR_NONFINITE, "invalid MoE router");
+    if (h[0]) throw ApiError(QC_ERR_NONFINITE, "nonfinite model output");
+  }
+
+  // Validates a call's sequences and tokens; per token: its position, and whether it is the last
+  // token of its sequence in the call (those get logits rows, in call order).
+  void plan(const uint32_t* seqs, const uint32_t* toks, uint32_t n, std::vector<qc::BatchTok>& tk,
+            std::vector<uint8_t>& last) {
+    ensure(n > 0 && seqs, "empty batch");
+    std::vector<uint32_t> count(n_seqs, 0);
+    for (uint32_t i = 0; i < n; i++) {
+      ensure(seqs[i] < n_seqs, "sequence index out of range");
+      if (toks) ensure(toks[i] < e->cfg.vocab, "token outside vocabulary", QC_ERR_TOKEN);
+      count[seqs[i]]++;
+    }
+    for (uint32_t q = 0; q < n_seqs; q++)
+      ensure((uint64_t)pos[q] + count[q] <= context, "context limit " + std::to_string(context) + " reached",
+             QC_ERR_CONTEXT);
+    tk.resize(n);
+    last.assign(n, 0);
+    std::vector<uint32_t> p(pos);
+    for (uint32_t i = 0; i < n; i++) tk[i] = qc::BatchTok{seqs[i], p[seqs[i]]++};
+    std::vector<uint8_t> seen(n_seqs, 0);
+    for (uint32_t i = n; i-- > 0;)
+      if (!seen[seqs[i]]) last[i] = seen[seqs[i]] = 1;
+  }
+
+  bool started = false;  // a call has changed device state (its sequences are reset if it fails)
+
+  // Forwards of n tokens (ids on the host); logits rows of the last token of each sequence in the
+  // call to `logits` (host), in call order.
+  void forward(const uint32_t* seqs, const uint32_t* toks, uint32_t n, float* logits) {
+    std::vector<qc::BatchTok> tk;
+    std::vector<uint8_t> last;
+    ensure(toks, "null argument");
+    plan(seqs, toks, n, tk, last);
+    started = true;
+    QC_CK(cudaSetDevice(e->device));
+    e->grow_moe(cap);
+    const uint64_t V = e->cfg.vocab;
+    uint32_t rows_done = 0;
+    cudaEvent_t t0 = e->ev0, t1 = e->ev1;
+    QC_CK(cudaEventRecord(t0, e->stream));
+    for (uint32_t b = 0; b < n; b += cap) {
+      const uint32_t T = std::min(cap, n - b);
+      std::vector<uint32_t> osrc;
+      for (uint32_t i = 0; i < T; i++)
+        if (last[b + i]) osrc.push_back(i);
+      QC_CK(cudaMemcpyAsync(d_tok, tk.data() + b, T * sizeof(qc::BatchTok), cudaMemcpyHostToDevice, e->stream));
+      if (toks) QC_CK(cudaMemcpyAsync(d_ids, toks + b, T * 4, cudaMemcpyHostToDevice, e->stream));
+      if (!osrc.empty())
+        QC_CK(cudaMemcpyAsync(d_osrc, osrc.data(), osrc.size() * 4, cudaMemcpyHostToDevice, e->stream));
+      pass(T, (uint32_t)osrc.size());
+      for (uint32_t j = 0; j < osrc.size(); j++) {
+        const uint32_t sq = tk[b + osrc[j]].seq;
+        QC_CK(cudaMemcpyAsync(d_last + sq * V, d_lg + j * V, V * 4, cudaMemcpyDeviceToDevice, e->stream));
+        if (logits) QC_CK(cudaMemcpyAsync(logits + (uint64_t)(rows_done + j) * V, d_lg + j * V, V * 4,
+                                          cudaMemcpyDeviceToHost, e->stream));
+      }
+      rows_done += (uint32_t)osrc.size();
+      // the ids of the pass were read: synchronize before the next pass overwrites pageable copies
+      QC_CK(cudaStreamSynchronize(e->stream));
+    }
+    QC_CK(cudaEventRecord(t1, e->stream));
+    for (uint32_t i = 0; i < n; i++) pos[seqs[i]]++;
+    stats.tokens += n;
+    check();
+    float ms = 0.f;
+    QC_CK(cudaEventElapsedTime(&ms, t0, t1));
+    stats.matvec_ms += ms;
+  }
+
+  // Device arrays for draws of `n` sequences: their latest logits rows and their samplers.
+  void stage_draws(qc_sampler* const* smp, const uint32_t* seqs, uint32_t n) {
+    std::vector<const float*> rows(n);
+    std::vector<qc::SamplerDev*> sv(n);
+    bool large = false;
+    for (uint32_t i = 0; i < n; i++) {
+      ensure(smp[i] && smp[i]->device == e->device, "a sampler lives on another device");
+      ensure(seqs[i] < n_seqs, "sequence index out of range");
+      ensure(pos[seqs[i]] > 0, "sampling needs the logits of a previous forward");
+      rows[i] = d_last + (uint64_t)seqs[i] * e->cfg.vocab;
+      sv[i] = smp[i]->d;
+      const uint32_t k = smp[i]->top_k;
+      large |= (k > 0 && k < e->cfg.vocab ? k : e->cfg.vocab) > qc::sample_exact_max();
+    }
+    QC_CK(cudaMemcpyAsync(d_rows, rows.data(), n * 8, cudaMemcpyHostToDevice, e->stream));
+    QC_CK(cudaMemcpyAsync(d_sv, sv.data(), n * 8, cudaMemcpyHostToDevice, e->stream));
+    if (large && !d_sscr) QC_CK(cudaMalloc(&d_sscr, (uint64_t)n_seqs * qc::sample_scratch_bytes(e->cfg.vocab)));
+    QC_CK(cudaStreamSynchronize(e->stream));  // the pageable sources above
+  }
+
+  void sample(qc_sampler* const* smp, const uint32_t* seqs, uint32_t n, uint32_t* out) {
+    ensure(n > 0 && n <= n_seqs && smp && seqs && out, "invalid draws");
+    QC_CK(cudaSetDevice(e->device));
+    stage_draws(smp, seqs, n);
+    QC_CK(qc::launch_sample_batch(d_rows, e->cfg.vocab, n, d_sv, d_ids, d_sscr, e->stream));
+    QC_CK(cudaMemcpyAsync(out, d_ids, n * 4, cudaMemcpyDeviceToHost, e->stream));
+    QC_CK(cudaStreamSynchronize(e->stream));
+    check_samplers(smp, n);
+  }
+
+  void check_samplers(qc_sampler* const* smp, uint32_t n) {
+    for (uint32_t i = 0; i < n; i++) {
+      uint32_t err = 0;
+      QC_CK(cudaMemcpy(&err, &smp[i]->d->err, 4, cudaMemcpyDeviceToHost));
+      if (err) {
+        QC_CK(cudaMemset(&smp[i]->d->err, 0, 4));
+        throw ApiError(QC_ERR_INVALID, "invalid logits");
+      }
+    }
+  }
+
+  // The chat loop for n distinct sequences at once: `steps` times, sample every sequence's latest
+  // logits with its sampler and run the n sampled ids as one step.  out: steps x n ids (host).
+  void decode_sample(qc_sampler* const* smp, const uint32_t* seqs, uint32_t n, uint32_t steps, uint32_t* out) {
+    ensure(n > 0 && n <= cap && n <= n_seqs && smp && seqs, "invalid draws");
+    std::vector<uint8_t> seen(n_seqs, 0);
+    for (uint32_t i = 0; i < n; i++) {
+      ensure(seqs[i] < n_seqs && !seen[seqs[i]], "sequences of a decode loop must be distinct");
+      seen[seqs[i]] = 1;
+      ensure((uint64_t)pos[seqs[i]] + steps <= context, "prompt + max-tokens exceed --ctx", QC_ERR_CONTEXT);
+    }
+    QC_CK(cudaSetDevice(e->device));
+    stage_draws(smp, seqs, n);
+    started = true;
+    if (steps > out_cap) {
+      cudaFree(d_out);
+      d_out = nullptr;
+      out_cap = 0;
+      QC_CK(cudaMalloc(&d_out, (uint64_t)steps * n_seqs * 4));
+      out_cap = steps;
+    }
+    const uint64_t V = e->cfg.vocab;
+    std::vector<qc::BatchTok> tk(n);
+    std::vector<uint32_t> osrc(n);
+    for (uint32_t i = 0; i < n; i++) osrc[i] = i;
+    QC_CK(cudaMemcpyAsync(d_osrc, osrc.data(), n * 4, cudaMemcpyHostToDevice, e->stream));
+    QC_CK(cudaEventRecord(e->ev0, e->stream));
+    for (uint32_t st = 0; st < steps; st++) {
+      // the ids land in d_ids: the next pass's tokens (d_rows still point at the latest rows)
+      QC_CK(qc::launch_sample_batch(d_rows, (uint32_t)V, n, d_sv, d_ids, d_sscr, e->stream));
+      QC_CK(cudaMemcpyAsync(d_out + (uint64_t)st * n, d_ids, n * 4, cudaMemcpyDeviceToDevice, e->stream));
+      for (uint32_t i = 0; i < n; i++) tk[i] = qc::BatchTok{seqs[i], pos[seqs[i]] + st};
+      QC_CK(cudaMemcpyAsync(d_tok, tk.data(), n * sizeof(qc::BatchTok), cudaMemcpyHostToDevice, e->stream));
+      pass(n, n);
+      for (uint32_t i = 0; i < n; i++)
+        QC_CK(cudaMemcpyAsync(d_last + seqs[i] * V, d_lg + i * V, V * 4, cudaMemcpyDeviceToDevice, e->stream));
+      QC_CK(cudaStreamSynchronize(e->stream));  // tk is rewritten next step (pageable copy source)
+    }
+    QC_CK(cudaEventRecord(e->ev1, e->stream));
+    for (uint32_t i = 0; i < n; i++) pos[seqs[i]] += steps;
+    stats.tokens += (uint64_t)n * steps;
+    if (out) QC_CK(cudaMemcpyAsync(out, d_out, (uint64_t)steps * n * 4, cudaMemcpyDeviceToHost, e->stream));
+    QC_CK(cudaStreamSynchronize(e->stream));
+    check_samplers(smp, n);
+    check();
+    float ms = 0.f;
+    QC_CK(cudaEventElapsedTime(&ms, e->ev0, e->ev1));
+    stats.matvec_ms += ms;
   }
 };
 
@@ -1022,6 +1367,18 @@ namespace qc {
 // Sets the thread-local message returned by qc_last_error() (used by noalloc.cu).
 void set_last_error(const std::string& msg) { g_last_error = msg; }
 }  // namespace qc
+
+// A failed call that had started on the device resets the sequences it carried.
+template <class F>
+static int batch_call(qc_batch* b, const uint32_t* seqs, uint32_t n, F&& f) {
+  if (!b) return g_last_error = "null batch", QC_ERR_INVALID;
+  b->started = false;
+  const int rc = api(b->e, f);
+  if (rc != QC_OK && b->started && seqs)
+    for (uint32_t i = 0; i < n; i++)
+      if (seqs[i] < b->n_seqs) b->pos[seqs[i]] = 0;
+  return rc;
+}
 
 extern "C" {
 
@@ -1361,6 +1718,71 @@ int qc_matrix_bytes(const qc_matrix* m, uint64_t* device_bytes, uint64_t* packed
 }
 
 void qc_matrix_destroy(qc_matrix* m) { delete m; }
+
+
+// ---- several sequences per step -------------------------------------------------------------
+int qc_batch_create(qc_engine* e, uint32_t n_seqs, uint32_t context, qc_batch** out) {
+  if (!e) return g_last_error = "null engine", QC_ERR_INVALID;
+  return api(e, [&] {
+    ensure(out, "null argument");
+    *out = nullptr;
+    std::unique_ptr<qc_batch> b(new qc_batch);
+    b->create(e, n_seqs, context);
+    *out = b.release();
+  });
+}
+
+void qc_batch_destroy(qc_batch* b) { delete b; }
+
+int qc_batch_forward(qc_batch* b, const uint32_t* seq_ids, const uint32_t* tokens, uint32_t n, float* logits) {
+  return batch_call(b, seq_ids, n, [&] { b->forward(seq_ids, tokens, n, logits); });
+}
+
+int qc_batch_reset(qc_batch* b, uint32_t seq) {
+  if (!b) return g_last_error = "null batch", QC_ERR_INVALID;
+  return api(b->e, [&] {
+    ensure(seq < b->n_seqs || seq == 0xffffffffu, "sequence index out of range");
+    for (uint32_t q = 0; q < b->n_seqs; q++)
+      if (seq == 0xffffffffu || q == seq) b->pos[q] = 0;
+  });
+}
+
+int qc_batch_position(const qc_batch* b, uint32_t seq, uint32_t* pos) {
+  if (!b) return g_last_error = "null batch", QC_ERR_INVALID;
+  return api(b->e, [&] {
+    ensure(pos && seq < b->n_seqs, "invalid argument");
+    *pos = b->pos[seq];
+  });
+}
+
+int qc_batch_logits_device(const qc_batch* b, uint32_t seq, const float** out) {
+  if (!b) return g_last_error = "null batch", QC_ERR_INVALID;
+  return api(b->e, [&] {
+    ensure(out && seq < b->n_seqs, "invalid argument");
+    *out = b->d_last + (uint64_t)seq * b->e->cfg.vocab;
+  });
+}
+
+int qc_batch_sample(qc_batch* b, qc_sampler* const* samplers, const uint32_t* seq_ids, uint32_t n, uint32_t* tokens_out) {
+  if (!b) return g_last_error = "null batch", QC_ERR_INVALID;
+  return api(b->e, [&] { b->sample(samplers, seq_ids, n, tokens_out); });
+}
+
+int qc_batch_decode_sample(qc_batch* b, qc_sampler* const* samplers, const uint32_t* seq_ids, uint32_t n, uint32_t steps,
+                           uint32_t* tokens_out) {
+  return batch_call(b, seq_ids, n, [&] { b->decode_sample(samplers, seq_ids, n, steps, tokens_out); });
+}
+
+int qc_batch_stats(const qc_batch* b, qc_stats* out) {
+  if (!b) return g_last_error = "null batch", QC_ERR_INVALID;
+  return api(b->e, [&] {
+    ensure(out, "null argument");
+    *out = b->stats;
+    out->kv_bytes = (uint64_t)b->n_seqs * b->e->cfg.layers * 2 * b->kv_floats * 4;
+    out->weight_bytes = b->e->weight_bytes;
+    out->matvecs = ((5ull + 3ull * b->e->cfg.top) * b->e->cfg.layers + 1) * b->stats.tokens;
+  });
+}
 
 #ifdef QC_TRACE
 int qc_trace_read(void* host, size_t bytes) { return qc::trace_read(host, bytes) == cudaSuccess ? 0 : 2; }

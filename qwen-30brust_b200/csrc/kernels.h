@@ -197,6 +197,40 @@ uint32_t sample_exact_max();
 cudaError_t sample_prepare();
 cudaError_t launch_sample(const float* logits, uint32_t n, SamplerDev* s, uint32_t* token_dst,
                           const SampleScratch& scr, cudaStream_t st);
+// `draws` samples at once, one block each: logits row rows[b] (n floats) with sampler sv[b] (both
+// device arrays of device pointers), id to tokens[b] (device).  scratch: draws x
+// sample_scratch_bytes(n) bytes (needed when a sampler's top-k set exceeds sample_exact_max()), or null.
+cudaError_t launch_sample_batch(const float* const* rows, uint32_t n, uint32_t draws, SamplerDev* const* sv,
+                                uint32_t* tokens, void* scratch, cudaStream_t st);
+
+// ---- several sequences per step (batch.cu) --------------------------------------------------
+struct BatchTok {
+  uint32_t seq, pos;  // the token's sequence and its position there
+};
+struct BatchArgs {
+  const BatchTok* tok;  // [T] device
+  float* kv;            // [seq][layer][K, V][kvheads][ctx][head_dim]
+  uint64_t kv_floats;   // floats of one K (or V) block of one layer: kvheads * ctx * head_dim
+  uint32_t n_layers, heads, kvheads, D, ctx;
+  float eps;
+  const float2* rope;   // [ctx][D/2] (cos, sin)
+};
+cudaError_t batch_prepare(int max_smem);
+size_t batch_matvec_smem(const MatDesc& m);
+size_t batch_attention_smem(uint32_t heads, uint32_t kvheads, uint32_t D);
+// x[t] = embedding row ids[t]
+void launch_batch_embed(const MatDesc& embd, const BatchTok* tok, const uint32_t* ids, uint32_t T, uint32_t H, float* x,
+                        cudaStream_t s);
+// XView t (at xv + t * xb) of rms(x[src ? src[t] : t], w), or of the vector itself when w is null
+void launch_batch_stage(const float* x, const uint32_t* src, uint32_t T, uint32_t n, uint32_t units, bool with_float,
+                        const float* w, float eps, uint8_t* xv, uint32_t xb, cudaStream_t s);
+// y[v * ystride + r] = (add ? add[v * ystride + r] : 0) + (W x_v)[r] for the T XViews
+void launch_batch_matvec(const MatDesc& m, const uint8_t* xv, uint32_t xb, uint32_t T, float* y, uint64_t ystride,
+                         const float* add, int sms, cudaStream_t s);
+void launch_batch_qkprep(const BatchArgs& a, uint32_t layer, const float* q_norm, const float* k_norm, float* q,
+                         const float* k, const float* v, uint32_t T, cudaStream_t s);
+void launch_batch_attention(const BatchArgs& a, uint32_t layer, const float* q, float* out, uint32_t T, cudaStream_t s);
+void launch_batch_finite(const float* v, uint64_t n, uint32_t* flag, cudaStream_t s);
 // n keystream words of the sampler (advancing it), for reproducibility checks.
 void launch_sampler_words(SamplerDev* s, uint32_t n, uint32_t* out, cudaStream_t st);
 

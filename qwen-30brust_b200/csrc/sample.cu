@@ -304,8 +304,30 @@ __device__ float warp_fold(const float* __restrict__ v, uint32_t n, float* run) 
   return acc;
 }
 
-__global__ void __launch_bounds__(kST) k_sample(const float* __restrict__ lg, uint32_t n, SamplerDev* s,
-                                                uint32_t* token_dst, SampleScratch scr) {
+// One block per draw: block b samples logits row b (lg_base + b * lg_stride) with sampler sv[b]
+// (or s0 for a single draw), writing the id to dsts[b] (or dst0) and using scratch region b.
+struct SampleBatch {
+  const float* lg_base;
+  const float* const* lgv;  // per-block logits rows (device array), or null: lg_base + b * lg_stride
+  uint64_t lg_stride;
+  SamplerDev* s0;
+  SamplerDev* const* sv;
+  uint32_t* dst0;
+  uint32_t* dsts;
+  SampleScratch scr;
+  uint64_t scr_stride;  // words between the scratch regions of consecutive blocks
+};
+
+__global__ void __launch_bounds__(kST) k_sample(SampleBatch sb, uint32_t n) {
+  const uint32_t b = blockIdx.x;
+  const float* __restrict__ lg = sb.lgv ? sb.lgv[b] : sb.lg_base + b * sb.lg_stride;
+  SamplerDev* const s = sb.sv ? sb.sv[b] : sb.s0;
+  uint32_t* const token_dst = sb.dsts ? sb.dsts + b : sb.dst0;
+  SampleScratch scr = sb.scr;
+  if (scr.key0) {
+    const uint64_t o = b * sb.scr_stride;
+    scr = SampleScratch{scr.key0 + o, scr.key1 + o, scr.idx0 + o, scr.idx1 + o, scr.p + o, scr.q + o, scr.run + o};
+  }
   __shared__ Shared sh;
   extern __shared__ __align__(16) unsigned char dyn[];
   const uint32_t tid = threadIdx.x;
@@ -481,7 +503,15 @@ cudaError_t sample_prepare() {
 
 cudaError_t launch_sample(const float* logits, uint32_t n, SamplerDev* s, uint32_t* token_dst,
                           const SampleScratch& scr, cudaStream_t st) {
-  k_sample<<<1, kST, kSampleSmem, st>>>(logits, n, s, token_dst, scr);
+  k_sample<<<1, kST, kSampleSmem, st>>>(SampleBatch{logits, nullptr, 0, s, nullptr, token_dst, nullptr, scr, 0}, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_sample_batch(const float* const* rows, uint32_t n, uint32_t draws, SamplerDev* const* sv,
+                                uint32_t* tokens, void* scratch, cudaStream_t st) {
+  const SampleScratch scr = scratch ? sample_scratch_at(scratch, n) : SampleScratch{};
+  k_sample<<<draws, kST, kSampleSmem, st>>>(
+      SampleBatch{nullptr, rows, 0, nullptr, sv, nullptr, tokens, scr, scratch ? sample_scratch_bytes(n) / 4 : 0}, n);
   return cudaGetLastError();
 }
 

@@ -30,7 +30,9 @@ EXPORTS = (
     "qc_matrix_bytes", "qc_matrix_destroy", "qc_packed_matvec", "qc_profile_step", "qc_packed_matvec_noalloc",
     "qc_engine_set_decode_mode", "qc_engine_decode_path", "qc_engine_create_gguf_ep", "qc_engine_ep_handle",
     "qc_engine_ep_connect", "qc_sampler_create", "qc_sampler_destroy", "qc_sampler_sample", "qc_sampler_words",
-    "qc_engine_sample", "qc_decode_sample", "qc_moe_layer",
+    "qc_engine_sample", "qc_decode_sample", "qc_moe_layer", "qc_batch_create", "qc_batch_destroy",
+    "qc_batch_forward", "qc_batch_reset", "qc_batch_position", "qc_batch_logits_device", "qc_batch_sample",
+    "qc_batch_decode_sample", "qc_batch_stats",
 )
 
 
@@ -135,6 +137,16 @@ def lib() -> C.CDLL:
         L.qc_engine_sample.argtypes = [vp, vp, C.POINTER(u32)]
         L.qc_decode_sample.argtypes = [vp, vp, u32, vp, vp]
         L.qc_moe_layer.argtypes = [vp, u32, vp, u32, vp, i, C.POINTER(C.c_float)]
+        L.qc_batch_create.argtypes = [vp, u32, u32, pp]
+        L.qc_batch_destroy.argtypes = [vp]
+        L.qc_batch_destroy.restype = None
+        L.qc_batch_forward.argtypes = [vp, vp, vp, u32, vp]
+        L.qc_batch_reset.argtypes = [vp, u32]
+        L.qc_batch_position.argtypes = [vp, u32, C.POINTER(u32)]
+        L.qc_batch_logits_device.argtypes = [vp, u32, pp]
+        L.qc_batch_sample.argtypes = [vp, vp, vp, u32, vp]
+        L.qc_batch_decode_sample.argtypes = [vp, vp, vp, u32, u32, vp]
+        L.qc_batch_stats.argtypes = [vp, C.POINTER(Stats)]
         _lib = L
     return _lib
 
@@ -381,6 +393,78 @@ class Engine:
 
     def __exit__(self, *a):
         self.close()
+
+
+class Batch:
+    """Several sequences on one engine (qc_batch_*): per-sequence KV caches and positions, any mix of
+    their tokens per step (decode tokens of many sequences, prompt chunks of one)."""
+
+    def __init__(self, engine: Engine, n_seqs: int, context: int):
+        h = C.c_void_p()
+        engine._check(lib().qc_batch_create(engine._h, n_seqs, context, C.byref(h)))
+        self._h, self.engine, self.n_seqs, self.context = h, engine, n_seqs, context
+        self.vocab = engine.vocab
+
+    def _check(self, rc: int) -> None:
+        self.engine._check(rc)
+
+    def forward(self, seq_ids, tokens, want_logits: bool = True) -> np.ndarray | None:
+        """qc_batch_forward: returns [rows][vocab], one row per sequence of the call (its last token),
+        in call order, or None."""
+        sq = np.ascontiguousarray(seq_ids, dtype=np.uint32)
+        tk = np.ascontiguousarray(tokens, dtype=np.uint32)
+        assert sq.size == tk.size
+        rows = len(dict.fromkeys(reversed(sq.tolist())))
+        out = np.empty((rows, self.vocab), dtype=np.float32) if want_logits else None
+        self._check(lib().qc_batch_forward(self._h, sq.ctypes.data, tk.ctypes.data, sq.size,
+                                           out.ctypes.data if out is not None else None))
+        if out is not None:  # rows are in order of each sequence's last token
+            return out
+        return None
+
+    def reset(self, seq: int = 0xFFFFFFFF) -> None:
+        self._check(lib().qc_batch_reset(self._h, seq))
+
+    def position(self, seq: int) -> int:
+        p = C.c_uint32()
+        self._check(lib().qc_batch_position(self._h, seq, C.byref(p)))
+        return p.value
+
+    def logits_device_ptr(self, seq: int) -> int:
+        p = C.c_void_p()
+        self._check(lib().qc_batch_logits_device(self._h, seq, C.byref(p)))
+        return p.value
+
+    def sample(self, samplers: list, seq_ids) -> np.ndarray:
+        sq = np.ascontiguousarray(seq_ids, dtype=np.uint32)
+        sp = (C.c_void_p * len(samplers))(*[s._h.value for s in samplers])
+        out = np.empty(max(sq.size, 1), dtype=np.uint32)
+        self._check(lib().qc_batch_sample(self._h, sp, sq.ctypes.data, sq.size, out.ctypes.data))
+        return out[:sq.size]
+
+    def decode_sample(self, samplers: list, seq_ids, steps: int) -> np.ndarray:
+        """qc_batch_decode_sample: [steps][n] sampled ids."""
+        sq = np.ascontiguousarray(seq_ids, dtype=np.uint32)
+        sp = (C.c_void_p * len(samplers))(*[s._h.value for s in samplers])
+        out = np.empty((max(steps, 1), sq.size), dtype=np.uint32)
+        self._check(lib().qc_batch_decode_sample(self._h, sp, sq.ctypes.data, sq.size, steps, out.ctypes.data))
+        return out[:steps]
+
+    def stats(self) -> dict:
+        s = Stats()
+        self._check(lib().qc_batch_stats(self._h, C.byref(s)))
+        return s.as_dict()
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().qc_batch_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class Matrix:

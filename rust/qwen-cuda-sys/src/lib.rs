@@ -38,6 +38,10 @@ pub mod ffi {
     pub struct qc_sampler {
         _opaque: [u8; 0],
     }
+    #[repr(C)]
+    pub struct qc_batch {
+        _opaque: [u8; 0],
+    }
 
     /// model.rs:5-19 `Config`, with fixed-width fields.
     #[repr(C)]
@@ -173,6 +177,35 @@ pub mod ffi {
             logits: *mut c_float,
         ) -> c_int;
         pub fn qc_sync(e: *mut qc_engine) -> c_int;
+
+        pub fn qc_batch_create(e: *mut qc_engine, n_seqs: u32, context: u32, out: *mut *mut qc_batch) -> c_int;
+        pub fn qc_batch_destroy(b: *mut qc_batch);
+        pub fn qc_batch_forward(
+            b: *mut qc_batch,
+            seq_ids: *const u32,
+            tokens: *const u32,
+            n: u32,
+            logits: *mut c_float,
+        ) -> c_int;
+        pub fn qc_batch_reset(b: *mut qc_batch, seq: u32) -> c_int;
+        pub fn qc_batch_position(b: *const qc_batch, seq: u32, pos: *mut u32) -> c_int;
+        pub fn qc_batch_logits_device(b: *const qc_batch, seq: u32, out: *mut *const c_float) -> c_int;
+        pub fn qc_batch_sample(
+            b: *mut qc_batch,
+            samplers: *const *mut qc_sampler,
+            seq_ids: *const u32,
+            n: u32,
+            tokens_out: *mut u32,
+        ) -> c_int;
+        pub fn qc_batch_decode_sample(
+            b: *mut qc_batch,
+            samplers: *const *mut qc_sampler,
+            seq_ids: *const u32,
+            n: u32,
+            steps: u32,
+            tokens_out: *mut u32,
+        ) -> c_int;
+        pub fn qc_batch_stats(b: *const qc_batch, out: *mut qc_stats) -> c_int;
 
         pub fn qc_reset(e: *mut qc_engine) -> c_int;
         pub fn qc_position(e: *const qc_engine, pos: *mut u32) -> c_int;
@@ -423,6 +456,52 @@ pub mod safe {
     impl Drop for Sampler {
         fn drop(&mut self) {
             unsafe { ffi::qc_sampler_destroy(self.h) }
+        }
+    }
+
+    /// Several sequences on one engine (`qc_batch_*`): per-sequence KV caches and positions, any mix
+    /// of their tokens per step.  Borrows the engine, which must outlive it.
+    pub struct Batch<'e> {
+        h: *mut ffi::qc_batch,
+        engine: &'e mut Engine,
+    }
+    impl<'e> Batch<'e> {
+        pub fn new(engine: &'e mut Engine, n_seqs: u32, context: u32) -> Result<Self> {
+            let mut h = ptr::null_mut();
+            engine.check(unsafe { ffi::qc_batch_create(engine.h, n_seqs, context, &mut h) })?;
+            Ok(Batch { h, engine })
+        }
+        /// One step: token i to sequence seq_ids[i]; one logits row per sequence of the call (its
+        /// last token), in call order.
+        pub fn forward(&mut self, seq_ids: &[u32], tokens: &[u32]) -> Result<Vec<Vec<f32>>> {
+            if seq_ids.len() != tokens.len() {
+                return Err(Error { code: ffi::QC_ERR_INVALID, message: "seq_ids and tokens differ in length".into() });
+            }
+            let mut seen = std::collections::HashSet::new();
+            let rows = seq_ids.iter().rev().filter(|s| seen.insert(**s)).count();
+            let v = self.engine.config.vocab as usize;
+            let mut flat = vec![0f32; rows * v];
+            self.engine.check(unsafe {
+                ffi::qc_batch_forward(self.h, seq_ids.as_ptr(), tokens.as_ptr(), seq_ids.len() as u32, flat.as_mut_ptr())
+            })?;
+            Ok(flat.chunks(v).map(|c| c.to_vec()).collect())
+        }
+        /// The chat loop for distinct sequences: `steps` x n sampled ids, step-major.
+        pub fn decode_sample(&mut self, samplers: &mut [&mut Sampler], seq_ids: &[u32], steps: u32) -> Result<Vec<u32>> {
+            let sp: Vec<*mut ffi::qc_sampler> = samplers.iter_mut().map(|s| s.h).collect();
+            let mut out = vec![0u32; steps as usize * seq_ids.len()];
+            self.engine.check(unsafe {
+                ffi::qc_batch_decode_sample(self.h, sp.as_ptr(), seq_ids.as_ptr(), seq_ids.len() as u32, steps, out.as_mut_ptr())
+            })?;
+            Ok(out)
+        }
+        pub fn reset(&mut self, seq: u32) -> Result<()> {
+            self.engine.check(unsafe { ffi::qc_batch_reset(self.h, seq) })
+        }
+    }
+    impl Drop for Batch<'_> {
+        fn drop(&mut self) {
+            unsafe { ffi::qc_batch_destroy(self.h) }
         }
     }
 

@@ -31,7 +31,8 @@ SCALARS = {  # canonical name: (C spellings, Rust spellings, ctypes type)
     "char": (("char",), ("c_char",), C.c_char),
     "void": (("void",), ("c_void",), None),
 }
-OPAQUE = ("qc_engine", "qc_matrix", "qc_sampler", "qc_config", "qc_tensor_desc", "qc_stats", "qc_phase_times")
+OPAQUE = ("qc_engine", "qc_matrix", "qc_sampler", "qc_batch", "qc_config", "qc_tensor_desc", "qc_stats",
+          "qc_phase_times")
 
 
 def _canon_scalar(tok: str, lang: int) -> str:
@@ -44,14 +45,25 @@ def _canon_scalar(tok: str, lang: int) -> str:
 
 
 def c_type(decl: str):
-    """'const qc_engine* e' / 'qc_engine** out' / 'uint32_t n' -> canonical nested tuple."""
-    decl = decl.strip()
-    m = re.match(r"^(const\s+)?(\w+)\s*((?:\*\s*)*)(\w+)?$", decl)
-    assert m, decl
-    const, base, stars = bool(m.group(1)), m.group(2), m.group(3).replace(" ", "")
-    t = _canon_scalar(base, 0)
-    for i in range(len(stars)):
-        t = ("ptr", "const" if (const and i == 0) else "mut", t)
+    """'const qc_engine* e' / 'qc_engine** out' / 'qc_sampler* const* s' / 'uint32_t n' -> canonical
+    nested tuple.  A const before the base type, or after the k-th '*', makes the next pointer level
+    point to const data (Rust *const)."""
+    toks = re.findall(r"\*|\w+", decl)
+    const_next = False
+    if toks[0] == "const":
+        const_next = True
+        toks = toks[1:]
+    t = _canon_scalar(toks[0], 0)
+    rest = toks[1:]
+    if rest and rest[-1] not in ("*", "const"):
+        rest = rest[:-1]  # the parameter name
+    for tok in rest:
+        if tok == "*":
+            t = ("ptr", "const" if const_next else "mut", t)
+            const_next = False
+        else:
+            assert tok == "const", decl
+            const_next = True
     return t
 
 
@@ -145,7 +157,7 @@ def test_repr_c_structs_match_the_header():
 
 def test_every_header_function_is_bound_with_the_same_signature():
     h, r = header_functions(), rust_functions()
-    assert len(h) >= 38
+    assert len(h) >= 47
     missing = sorted(set(h) - set(r))
     assert not missing, f"not declared in lib.rs: {missing}"
     ret_map = {"int": "c_int", "void": "", "constchar*": "*const c_char"}
