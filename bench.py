@@ -404,8 +404,16 @@ def run_ours(args) -> None:
         import torch.distributed as dist
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
     ms, ms_e2e = times.tolist()
-    eng.close()
     studies = {}
+    if world == 1 and not args.layers and not args.no_studies:  # BASELINE config 5, reduced, on the same engine
+        try:
+            studies["batch"] = dict(batch_study(T, E, eng, spec, 64, 128, 16),
+                                    workload="BASELINE config 5 shape, reduced: 64 sequences x 128-token prompts, "
+                                             "16 sampled steps (bench.py --config 5 runs 2048 x 512)")
+        except Exception as exc:
+            log(f"batch study failed: {exc!r}")
+            studies["batch"] = {"error": repr(exc)}
+    eng.close()
     if world == 1 and not args.layers and not args.no_studies:  # BASELINE configs 2 and 3 beside the decode line
         for key, fn in (("matvec", lambda: matvec_study(T, E, torch, steps=5, warmup=3)),
                         ("moe_layer", lambda: moe_study(T, E, steps=7, warmup=3))):
@@ -546,6 +554,66 @@ def run_reference(args) -> None:
     }), flush=True)
 
 
+def batch_study(T, E, eng, spec, seqs: int, prompt: int, gen: int, log_every: int = 0) -> dict:
+    """BASELINE config 5 on one GPU: `seqs` sequences, each a `prompt`-token random prompt (seed 3)
+    prefilled in chunks of 128 tokens (one sequence per call), then `gen` decode steps of all
+    sequences at once on the device (qc_batch_decode_sample: sample every sequence, run the step),
+    temperature 0.7, top-p 0.9, top-k off, one seeded sampler per sequence."""
+    import torch
+    b = E.Batch(eng, seqs, CTX)
+    rng = np.random.default_rng(3)
+    prompts = rng.integers(0, spec.vocab, (seqs, prompt)).astype(np.uint32)
+    torch.cuda.synchronize()
+    s0 = b.stats()
+    w0 = time.perf_counter()
+    for q in range(seqs):
+        for c0 in range(0, prompt, 128):
+            c1 = min(prompt, c0 + 128)
+            b.forward(np.full(c1 - c0, q, dtype=np.uint32), prompts[q, c0:c1], want_logits=c1 == prompt)
+        if log_every and (q + 1) % log_every == 0:
+            log(f"batch: prefilled {q + 1}/{seqs} sequences")
+    prefill_s = time.perf_counter() - w0
+    s1 = b.stats()
+    samplers = [E.Sampler(1000 + q, 0.7, 0, 0.9) for q in range(seqs)]
+    w1 = time.perf_counter()
+    ids = b.decode_sample(samplers, np.arange(seqs, dtype=np.uint32), gen)
+    decode_s = time.perf_counter() - w1
+    s2 = b.stats()
+    kv = s2["kv_bytes"]
+    b.close()
+    pre_tok, dec_tok = seqs * prompt, seqs * gen
+    pre_ms, dec_ms = s1["matvec_ms"] - s0["matvec_ms"], s2["matvec_ms"] - s1["matvec_ms"]
+    return {"sequences": seqs, "prompt": prompt, "generated": gen, "ctx": CTX, "kv_bytes": kv,
+            "prefill": {"tok_s": pre_tok / prefill_s, "device_tok_s": pre_tok / (pre_ms / 1e3), "seconds": prefill_s,
+                        "calls": seqs * ((prompt + 127) // 128)},
+            "decode": {"tok_s": dec_tok / decode_s, "device_tok_s": dec_tok / (dec_ms / 1e3), "seconds": decode_s,
+                       "ms_per_step": dec_ms / gen, "distinct_ids_seq0": int(len(set(ids[:, 0].tolist())))},
+            "sampling": "T 0.7, top-p 0.9, top-k off, sampler seed 1000 + sequence (device, exact f32 folds)"}
+
+
+def run_batch(args) -> None:
+    """BASELINE config 5 (`--config 5`) on one GPU: the batched line."""
+    import torch
+    from qwen30brust_b200 import engine as E, tools as T
+    torch.cuda.set_device(0)
+    spec = T.QWEN3_30B_A3B
+    img = T.synth_gguf(spec)
+    eng = E.Engine(img, CTX)
+    sampler = ClockSampler(0)
+    with sampler:
+        res = batch_study(T, E, eng, spec, args.seqs, args.prompt, args.gen, log_every=8)
+    eng.close()
+    print(json.dumps({"metric": "batched decode tok/s (BASELINE config 5, one GPU)", "value": res["decode"]["tok_s"],
+                      "unit": "tok/s", "higher_is_better": True, "n_gpus": 1, "dtype": "f32 activations; Q4_K/Q6_K "
+                      "weights; MoE on tcgen05 (fp16 hi/lo split, fp32 accumulate)",
+                      "data": "synthetic: random-init N(0,0.02) weights quantized from seed 0; random prompts (seed 3)",
+                      "config": {"workload": "BASELINE config 5 on one GPU: 64 sequences x 2048-token prompts, 512 "
+                                 "sampled steps" if (args.seqs, args.prompt, args.gen) == (64, 2048, 512)
+                                 else f"BASELINE config 5 shape, reduced: {args.seqs} sequences x {args.prompt}-token "
+                                      f"prompts, {args.gen} sampled steps", "parallelism": "single GPU"},
+                      **res, "clocks": sampler.summary()}), flush=True)
+
+
 def run_matvec(args) -> None:
     """BASELINE config 2 alone (`--config 2`, optionally one `--shape`): the matvec study's JSON line."""
     import torch
@@ -589,8 +657,11 @@ def main():
     ap.add_argument("--decode-mode", type=int, default=0, choices=[0, 1],
                     help="0: whole-token kernel when the model fits it (default); 1: per-phase kernels")
     ap.add_argument("--ref-max-steps", type=int, default=32)
-    ap.add_argument("--config", type=int, default=4, choices=[2, 3, 4],
-                    help="2: matvec study; 3: MoE-layer study; 4: the decode bench (default)")
+    ap.add_argument("--config", type=int, default=4, choices=[2, 3, 4, 5],
+                    help="2: matvec study; 3: MoE-layer study; 4: the decode bench (default); 5: batched sequences")
+    ap.add_argument("--seqs", type=int, default=64, help="--config 5: sequences")
+    ap.add_argument("--prompt", type=int, default=2048, help="--config 5: prompt tokens per sequence")
+    ap.add_argument("--gen", type=int, default=512, help="--config 5: sampled steps")
     ap.add_argument("--shape", default=None, help="--config 2: one shape only (e.g. q_proj, vocab)")
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: N independent decode streams instead of one expert-parallel stream")
@@ -599,6 +670,8 @@ def main():
         ap.error("--warmup must be >= 3")
     if args.config == 2:
         run_matvec(args)
+    elif args.config == 5:
+        run_batch(args)
     elif args.config == 3:
         run_moe_layer(args)
     elif args.impl == "reference":

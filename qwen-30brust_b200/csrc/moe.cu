@@ -104,6 +104,7 @@ __device__ __forceinline__ void split8(const float (&v)[8], float s, uint4* hi, 
 __global__ void __launch_bounds__(256) k_moe_route(MoeArgs a, const float* __restrict__ x) {
   __shared__ float red[32];
   __shared__ float lg[1024];
+  extern __shared__ __align__(16) float hsm[];  // [H] the normalized input, for the router rows
   const uint32_t t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float* xr = x + (uint64_t)t * a.H;
   float ss = 0.f;
@@ -116,6 +117,7 @@ __global__ void __launch_bounds__(256) k_moe_route(MoeArgs a, const float* __res
   for (uint32_t i = tid; i < a.H; i += 256) {
     const float v = __fmul_rn(xr[i], __fmul_rn(s, a.ffn_norm[i]));
     hr[i] = v;
+    hsm[i] = v;
     mx = fmaxf(mx, fabsf(v));
   }
   mx = warp_max(mx);
@@ -127,12 +129,27 @@ __global__ void __launch_bounds__(256) k_moe_route(MoeArgs a, const float* __res
     for (int w = 0; w < 8; w++) m = fmaxf(m, red[w]);
     a.hscale[t] = pow2_scale(m);
   }
-  // router logits: one warp per expert row (F16)
+  // router logits: one warp per expert row (F16), 16-byte loads of 8 weights per lane
   for (uint32_t e = warp; e < a.E; e += 8) {
-    const __half* wr = reinterpret_cast<const __half*>(row_ptr(a.router, a.router.w, e));
-    float acc = 0.f;
-    for (uint32_t i = lane; i < a.H; i += 32) acc = __fadd_rn(acc, __fmul_rn(__half2float(wr[i]), hr[i]));
-    acc = warp_sum(acc);
+    const uint4* wr = reinterpret_cast<const uint4*>(row_ptr(a.router, a.router.w, e));
+    float acc = 0.f, acc2 = 0.f;
+    for (uint32_t c = lane; c < a.H / 8; c += 32) {
+      const uint4 v = ldg16(wr + c);
+      const float4 h0 = *reinterpret_cast<const float4*>(hsm + 8 * c), h1 = *reinterpret_cast<const float4*>(hsm + 8 * c + 4);
+      const float2 w0 = __half22float2(*reinterpret_cast<const __half2*>(&v.x)),
+                   w1 = __half22float2(*reinterpret_cast<const __half2*>(&v.y)),
+                   w2 = __half22float2(*reinterpret_cast<const __half2*>(&v.z)),
+                   w3 = __half22float2(*reinterpret_cast<const __half2*>(&v.w));
+      acc = fmaf(w0.x, h0.x, acc);
+      acc2 = fmaf(w0.y, h0.y, acc2);
+      acc = fmaf(w1.x, h0.z, acc);
+      acc2 = fmaf(w1.y, h0.w, acc2);
+      acc = fmaf(w2.x, h1.x, acc);
+      acc2 = fmaf(w2.y, h1.y, acc2);
+      acc = fmaf(w3.x, h1.z, acc);
+      acc2 = fmaf(w3.y, h1.w, acc2);
+    }
+    acc = warp_sum(acc + acc2);
     if (lane == 0) {
       lg[e] = acc;
       if (!isfinite(acc)) atomicOr(a.err, 1u);
@@ -565,7 +582,7 @@ void launch_moe_wbound(const MatDesc& m, uint32_t experts, uint32_t* out, cudaSt
 }
 
 void launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStream_t s) {
-  k_moe_route<<<a.T, 256, 0, s>>>(a, x);
+  k_moe_route<<<a.T, 256, a.H * sizeof(float), s>>>(a, x);
   k_moe_plan<<<1, 1024, 0, s>>>(a);
   k_moe_gemm<0><<<dim3((a.I + 63) / 64, a.E), kMT, moe_gemm_smem(), s>>>(a);
   k_moe_gemm<1><<<dim3((a.H + 127) / 128, a.E), kMT, moe_gemm_smem(), s>>>(a);

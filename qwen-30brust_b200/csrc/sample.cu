@@ -288,20 +288,52 @@ __device__ void sort_desc(const float* __restrict__ lg, uint32_t n, uint32_t* co
   }
 }
 
-// The reference's running f32 sum over v[0..n) (sampling.rs:44, 53): every lane of the calling warp
-// holds the same value; the running sums go to run[j] when run is not null.
-__device__ float warp_fold(const float* __restrict__ v, uint32_t n, float* run) {
-  const uint32_t lane = threadIdx.x & 31;
-  float acc = 0.f;
-  for (uint32_t b = 0; b < n; b += 32) {
-    const float x = b + lane < n ? v[b + lane] : 0.f;
-    const uint32_t m = min(32u, n - b);
-    for (uint32_t k = 0; k < m; k++) {
-      acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, x, k));
-      if (run && lane == k) run[b + k] = acc;
+// Thread 0 visits v[0..n) in order, calling step(j, v[j]) until it returns false; the whole block
+// stages the values in shared memory (buf: kChunk floats) a chunk at a time, so the serial chain
+// reads shared memory instead of waiting on global loads.  Returns the index where the visit
+// stopped, or n.  All threads of the block call it.
+constexpr uint32_t kChunk = 16384;
+template <class F>
+__device__ uint32_t block_serial(const float* __restrict__ v, uint32_t n, float* buf, Shared& sh, F step) {
+  if (threadIdx.x == 0) sh.count = n;
+  for (uint32_t c0 = 0; c0 < n; c0 += kChunk) {
+    __syncthreads();
+    if (sh.count != n) break;
+    const uint32_t m = min(kChunk, n - c0);
+    for (uint32_t i = threadIdx.x; i < m; i += kST) buf[i] = v[c0 + i];
+    __syncthreads();
+    if (threadIdx.x == 0) {  // 8 values per pass, the next 8 loaded while these are visited
+      const float4* b4 = reinterpret_cast<const float4*>(buf);
+      const uint32_t m8 = m & ~7u;
+      bool go = true;
+      float4 x0 = m8 ? b4[0] : make_float4(0.f, 0.f, 0.f, 0.f), x1 = m8 ? b4[1] : x0;
+      for (uint32_t j = 0; j < m8 && go; j += 8) {
+        float4 y0 = x0, y1 = x1;
+        if (j + 8 < m8) {
+          y0 = b4[(j + 8) / 4];
+          y1 = b4[(j + 8) / 4 + 1];
+        }
+        const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+          if (go && !step(c0 + j + k, x[k])) {
+            sh.count = c0 + j + k;
+            go = false;
+          }
+        x0 = y0;
+        x1 = y1;
+      }
+      for (uint32_t j = m8; j < m && go; j++)
+        if (!step(c0 + j, buf[j])) {
+          sh.count = c0 + j;
+          go = false;
+        }
     }
   }
-  return acc;
+  __syncthreads();
+  const uint32_t stop = sh.count;
+  __syncthreads();
+  return stop;
 }
 
 // One block per draw: block b samples logits row b (lg_base + b * lg_stride) with sampler sv[b]
@@ -428,53 +460,37 @@ __global__ void __launch_bounds__(kST) k_sample(SampleBatch sb, uint32_t n) {
       const uint32_t K = Kset, *const ids = scr.idx1;
       for (uint32_t j = tid; j < K; j += kST) scr.p[j] = exp_f32(__fdiv_rn(__fsub_rn(lg[ids[j]], mx), temp));
       __syncthreads();
-      if (warp_of() == 0) {  // the total, keeping its running sums
-        const float t = warp_fold(scr.p, K, scr.run);
-        if ((tid & 31) == 0) sh.red[0] = __float_as_uint(t);
-      }
+      float* const buf = reinterpret_cast<float*>(dyn);  // (the sort's counters are consumed)
+      float total = 0.f;  // thread 0: the total with its running sums (sampling.rs:44)
+      block_serial(scr.p, K, buf, sh, [&](uint32_t j, float x) {
+        total = __fadd_rn(total, x);
+        scr.run[j] = total;
+        return true;
+      });
+      if (tid == 0) sh.red[0] = __float_as_uint(total);
       __syncthreads();
-      const float total = __uint_as_float((uint32_t)sh.red[0]);
-      for (uint32_t j = tid; j < K; j += kST) scr.q[j] = __fdiv_rn(scr.p[j], total);
+      const float tot = __uint_as_float((uint32_t)sh.red[0]);
+      for (uint32_t j = tid; j < K; j += kST) scr.q[j] = __fdiv_rn(scr.p[j], tot);
       __syncthreads();
-      if (warp_of() == 0) {
-        const uint32_t lane = tid & 31;
-        // top-p: the first j whose cumulative sum of p / total reaches top_p (sampling.rs:45-52)
-        float cum = 0.f;
-        uint32_t keep = K;
-        for (uint32_t b = 0; b < K && keep == K; b += 32) {
-          const float x = b + lane < K ? scr.q[b + lane] : 0.f;
-          const uint32_t m = min(32u, K - b);
-          for (uint32_t k = 0; k < m; k++) {
-            cum = __fadd_rn(cum, __shfl_sync(0xffffffffu, x, k));
-            if (cum >= top_p) {
-              keep = b + k + 1;
-              break;
-            }
-          }
-        }
-        // the kept mass is the total's running sum at keep - 1 (the same fold, truncated)
+      // top-p: the first j whose cumulative sum of p / total reaches top_p (sampling.rs:45-52)
+      float cum = 0.f;
+      const uint32_t cut = block_serial(scr.q, K, buf, sh, [&](uint32_t, float x) {
+        cum = __fadd_rn(cum, x);
+        return !(cum >= top_p);
+      });
+      const uint32_t keep = cut < K ? cut + 1 : K;
+      // the draw over the kept probabilities; their mass is the total's running sum at keep - 1
+      float draw = 0.f;
+      if (tid == 0) {
         const float mass = scr.run[keep - 1];
-        uint32_t word = 0;
-        if (lane == 0) word = next_word(s);
-        word = __shfl_sync(0xffffffffu, word, 0);
-        float draw = __fmul_rn((float)(word >> 8) * (1.0f / 16777216.0f), mass);
-        uint32_t pick = ids[keep - 1];
-        bool done = false;
-        for (uint32_t b = 0; b < keep && !done; b += 32) {  // sampling.rs:56-63
-          const float x = b + lane < keep ? scr.p[b + lane] : 0.f;
-          const uint32_t m = min(32u, keep - b);
-          for (uint32_t k = 0; k < m; k++) {
-            const float pk = __shfl_sync(0xffffffffu, x, k);
-            if (draw < pk) {
-              pick = ids[b + k];
-              done = true;
-              break;
-            }
-            draw = __fsub_rn(draw, pk);
-          }
-        }
-        if (lane == 0) sh.token = pick;
+        draw = __fmul_rn((float)(next_word(s) >> 8) * (1.0f / 16777216.0f), mass);
       }
+      const uint32_t hit = block_serial(scr.p, keep, buf, sh, [&](uint32_t, float x) {  // sampling.rs:56-63
+        if (draw < x) return false;
+        draw = __fsub_rn(draw, x);
+        return true;
+      });
+      if (tid == 0) sh.token = ids[hit < keep ? hit : keep - 1];
       __syncthreads();
       token = sh.token;
     }
