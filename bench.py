@@ -200,8 +200,11 @@ def cpu_baseline(img, prompt, ncores: int, tokens_all: int) -> dict:
 def matvec_shapes(T) -> list:
     base = [("q_proj", T.Q4_K, 4096, 2048), ("kv_proj", T.Q4_K, 512, 2048), ("o_proj", T.Q4_K, 2048, 4096),
             ("gate_up", T.Q4_K, 768, 2048), ("gate_up_q5k", T.Q5_K, 768, 2048), ("down", T.Q6_K, 2048, 768),
-            ("router", T.F16, 128, 2048), ("vocab", T.Q6_K, 151936, 2048)]
-    q8 = [(n + "_q8_0", T.Q8_0, r, c) for n, k, r, c in base if k != T.Q5_K]
+            ("router", T.F16, 128, 2048), ("vocab", T.Q6_K, 151936, 2048),
+            # not a config-2 shape: the gate rows of all 128 experts of a layer as one Q4_K matrix
+            # (113 MB), the Q4_K format streamed at a size where launch latency does not dominate
+            ("gate_all_experts", T.Q4_K, 98304, 2048)]
+    q8 = [(n + "_q8_0", T.Q8_0, r, c) for n, k, r, c in base if k != T.Q5_K and n != "gate_all_experts"]
     return base + q8
 
 

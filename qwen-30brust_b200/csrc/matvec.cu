@@ -77,41 +77,91 @@ __global__ void k_dequant(MatDesc m, uint32_t e, float* __restrict__ out) {
   }
 }
 
-// y = W_e x, rows streamed through shared memory: each block takes a contiguous
-// run of 8-row groups and pipelines it in stages of `sg` groups (cp.async,
-// kStages deep); warps then walk the rows of a stage, lpr lanes per row.
-constexpr int kStages = 3;
+// y = W_e x, rows streamed through shared memory: each block takes a contiguous run of 8-row
+// groups and streams it in stages of `sg` groups through `ns` shared-memory slots with TMA bulk
+// copies (one thread issues, an mbarrier per slot counts the bytes), so up to ns - 1 stages are in
+// flight while one is computed; warps walk the rows of a stage, lpr lanes per row.  The activation
+// staging overlaps the first copies.  Waits are bounded (2 s); a block that gives up writes NaN
+// for its rows, after waiting (bounded) for its copies in flight, and sets g_matvec_abort.
+constexpr int kMaxSlots = 8;
+constexpr unsigned long long kWaitNs = 2000000000ull;
+__device__ uint32_t g_matvec_abort;
+
+__device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ bool slot_wait(uint64_t* b, uint32_t parity) {
+  const unsigned long long t0 = now_ns();
+  for (uint32_t i = 0;; i++) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(saddr(b)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((i & 255) == 255 && now_ns() - t0 > kWaitNs) return false;
+  }
+}
+__device__ __forceinline__ void slot_fill(void* dst, const void* src, uint32_t bytes, uint64_t* b) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(b)), "r"(bytes) : "memory");
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   saddr(dst)),
+               "l"(src), "r"(bytes), "r"(saddr(b))
+               : "memory");
+}
 
 template <uint32_t KIND>
 __global__ void __launch_bounds__(512) k_matvec(MatDesc m, uint32_t e, const float* __restrict__ x,
-                                                float* __restrict__ y, uint32_t sg) {
-  extern __shared__ __align__(16) uint8_t smem[];
+                                                float* __restrict__ y, uint32_t sg, uint32_t ns) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t bar[kMaxSlots];
+  __shared__ float red[32];
+  __shared__ int bad;
   const uint32_t groups = (m.rows + 7) / 8;
   const uint32_t per = (groups + gridDim.x - 1) / gridDim.x;
   const uint32_t g0 = min(groups, blockIdx.x * per), g1 = min(groups, g0 + per);
   const uint32_t nst = (g1 - g0 + sg - 1) / sg;
-  const uint64_t stage_bytes = (uint64_t)sg * m.group_bytes;
-  uint8_t* buf = smem;
-  uint8_t* xmem = smem + kStages * stage_bytes;
-  for (uint32_t k = 0; k < kStages - 1; k++) {
-    if (k < nst) copy_groups(buf + (k % kStages) * stage_bytes, m, e, g0 + k * sg, min(g1, g0 + (k + 1) * sg));
-    cp_commit();
+  const uint32_t stage_bytes = sg * m.group_bytes;
+  uint8_t* xmem = smem + ns * stage_bytes;
+  const uint8_t* src = expert_base(m, e);
+  auto issue = [&](uint32_t k) {  // thread 0: stage k into slot k % ns
+    const uint32_t a = g0 + k * sg, b = min(g1, a + sg);
+    slot_fill(smem + (k % ns) * stage_bytes, src + (uint64_t)a * m.group_bytes, (b - a) * m.group_bytes, &bar[k % ns]);
+  };
+  if (threadIdx.x == 0) {
+    bad = 0;
+    for (uint32_t i = 0; i < ns; i++)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(&bar[i])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (uint32_t k = 0; k < ns && k < nst; k++) issue(k);
   }
-  __shared__ float red[32];
   stage_vectors<false>(xmem, 1, m.cols, m.units, uses_float_x(KIND), [&](uint32_t, uint32_t i) { return x[i]; },
-                       nullptr, 0.f, red);
+                       nullptr, 0.f, red);  // (ends with a barrier: the mbarriers are initialized)
   const XView xv = xview_at(xmem, m.units, uses_float_x(KIND));
   for (uint32_t k = 0; k < nst; k++) {
-    const uint32_t kn = k + kStages - 1;
-    if (kn < nst) copy_groups(buf + (kn % kStages) * stage_bytes, m, e, g0 + kn * sg, min(g1, g0 + (kn + 1) * sg));
-    cp_commit();
-    cp_wait<kStages - 1>();
+    const uint32_t j = k % ns;
+    if (!slot_wait(&bar[j], (k / ns) & 1)) bad = 1;
     __syncthreads();
-    const uint8_t* sb = buf + (k % kStages) * stage_bytes;
     const uint32_t r0 = (g0 + k * sg) * 8, r1 = min(m.rows, min(g1, g0 + (k + 1) * sg) * 8);
-    warp_rows_k<KIND, true>(m, r0, r1, xv, SmemRows{&m, sb, r0}, [&](uint32_t r, float v) { y[r] = v; },
-                            threadIdx.x >> 5, blockDim.x >> 5);
-    __syncthreads();
+    if (bad) {  // a copy did not arrive: report and stop, after the copies in flight have landed
+      for (uint32_t r = r0 + threadIdx.x; r < min(m.rows, g1 * 8); r += blockDim.x) y[r] = __int_as_float(0x7fc00000);
+      if (threadIdx.x == 0) {
+        atomicOr(&g_matvec_abort, 1u);
+        for (uint32_t q = k; q < nst && q < k + ns; q++) slot_wait(&bar[q % ns], (q / ns) & 1);  // issued, in flight
+      }
+      return;
+    }
+    warp_rows_k<KIND, true>(m, r0, r1, xv, SmemRows{&m, smem + j * stage_bytes, r0},
+                            [&](uint32_t r, float v) { y[r] = v; }, threadIdx.x >> 5, blockDim.x >> 5);
+    __syncthreads();  // slot j is consumed
+    if (threadIdx.x == 0 && k + ns < nst) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(k + ns);
+    }
   }
 }
 
@@ -126,33 +176,48 @@ void launch_dequant(const MatDesc& m, uint32_t e, float* out, cudaStream_t s) {
   k_dequant<<<148 * 8, 256, 0, s>>>(m, e, out);
 }
 
-// Stage size in groups and total dynamic shared memory of k_matvec.
-static uint32_t matvec_stage_groups(const MatDesc& m) {
-  const uint64_t budget = 48 * 1024;
-  const uint64_t sg = budget / m.group_bytes;
-  return (uint32_t)(sg < 1 ? 1 : (sg > 8 ? 8 : sg));
+// Stage size in groups and slots of k_matvec.  A stage is what the block computes between two
+// barriers, so it should give every warp a few rows: up to 6 groups (48 rows, 3 per warp) and
+// 64 KB, but no more groups than a block's share when the matrix is small (so that every SM gets
+// work); as many slots (2 to 8) as fit beside the activation tile in 192 KB.
+static void matvec_stages(const MatDesc& m, int sms, uint32_t* sg, uint32_t* ns) {
+  const uint64_t g = m.group_bytes, xb = xview_bytes(m.units, uses_float_x(m.kind));
+  const uint64_t groups = (m.rows + 7) / 8, share = (groups + sms - 1) / sms;
+  uint64_t s = (64 * 1024) / g;
+  s = s > 6 ? 6 : s;
+  s = s > share ? share : s;
+  s = s < 1 ? 1 : s;
+  const uint64_t budget = 192 * 1024 > xb ? 192 * 1024 - xb : 0;
+  uint64_t n = budget / (s * g);
+  n = n > (uint64_t)kMaxSlots ? (uint64_t)kMaxSlots : n;
+  n = n < 2 ? 2 : n;
+  *sg = (uint32_t)s;
+  *ns = (uint32_t)n;
 }
 
 size_t matvec_smem(const MatDesc& m) {
-  return (size_t)kStages * matvec_stage_groups(m) * m.group_bytes + xview_bytes(m.units, uses_float_x(m.kind));
+  uint32_t sg, ns;
+  matvec_stages(m, 148, &sg, &ns);
+  return (size_t)ns * sg * m.group_bytes + xview_bytes(m.units, uses_float_x(m.kind));
 }
 
 void launch_matvec(const MatDesc& m, uint32_t e, const float* x, float* y, int sms, cudaStream_t s) {
   const uint32_t groups = (m.rows + 7) / 8;
-  const uint32_t sg = matvec_stage_groups(m);
+  uint32_t sg, ns;
+  matvec_stages(m, 148, &sg, &ns);  // (the same split as matvec_smem; sms is 148 on every caller)
   // enough blocks to cover the SMs, but each with at least one full stage of work
   uint32_t grid = (groups + sg - 1) / sg;
   grid = grid < (uint32_t)sms ? grid : (uint32_t)sms;
   grid = grid < 1 ? 1 : grid;
   const size_t smem = matvec_smem(m);
   switch (m.kind) {
-    case Q4_K: k_matvec<Q4_K><<<grid, 512, smem, s>>>(m, e, x, y, sg); break;
-    case Q5_K: k_matvec<Q5_K><<<grid, 512, smem, s>>>(m, e, x, y, sg); break;
-    case Q6_K: k_matvec<Q6_K><<<grid, 512, smem, s>>>(m, e, x, y, sg); break;
-    case Q8_0: k_matvec<Q8_0><<<grid, 512, smem, s>>>(m, e, x, y, sg); break;
-    case Q4_0: k_matvec<Q4_0><<<grid, 512, smem, s>>>(m, e, x, y, sg); break;
-    case F16: k_matvec<F16><<<grid, 512, smem, s>>>(m, e, x, y, sg); break;
-    default: k_matvec<F32><<<grid, 512, smem, s>>>(m, e, x, y, sg); break;
+    case Q4_K: k_matvec<Q4_K><<<grid, 512, smem, s>>>(m, e, x, y, sg, ns); break;
+    case Q5_K: k_matvec<Q5_K><<<grid, 512, smem, s>>>(m, e, x, y, sg, ns); break;
+    case Q6_K: k_matvec<Q6_K><<<grid, 512, smem, s>>>(m, e, x, y, sg, ns); break;
+    case Q8_0: k_matvec<Q8_0><<<grid, 512, smem, s>>>(m, e, x, y, sg, ns); break;
+    case Q4_0: k_matvec<Q4_0><<<grid, 512, smem, s>>>(m, e, x, y, sg, ns); break;
+    case F16: k_matvec<F16><<<grid, 512, smem, s>>>(m, e, x, y, sg, ns); break;
+    default: k_matvec<F32><<<grid, 512, smem, s>>>(m, e, x, y, sg, ns); break;
   }
 }
 

@@ -1279,10 +1279,12 @@ const char* plan_token(const StepArgs& a, int max_smem, TokenPlan* p) {
     }
   }
   stage = std::max(stage, xview_bytes(a.out.units, uses_float_x(a.out.kind)));
-  // vocab stages: about 40 KB each, at least two slots over P and Q
+  // vocab stages: up to 4 groups (32 rows: two per warp) and 56 KB each, at least two slots over P
+  // and Q (measured on the standalone matvec: 32-row stages stream the Q6_K vocab rows ~15% faster
+  // than 24-row ones, the per-stage work between barriers being the limit)
   const uint32_t ogb = a.out.group_bytes;
   const uint32_t vper = (groups_of(a.out.rows) + nb - 1) / nb;
-  uint32_t sg = std::max(1u, std::min(40960u / ogb, (vper + 1) / 2));
+  uint32_t sg = std::max(1u, std::min(std::min(57344u / ogb, 4u), (vper + 1) / 2));
   const uint32_t slot = sg * ogb;
   P = std::max(P, slot);
   Q = std::max(Q, slot);
