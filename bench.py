@@ -600,6 +600,8 @@ def run_batch(args) -> None:
     from qwen30brust_b200 import engine as E, tools as T
     torch.cuda.set_device(0)
     spec = T.QWEN3_30B_A3B
+    if args.layers:  # a shallower model of the same shapes: profiling runs only
+        spec = spec.with_(layers=args.layers)
     img = T.synth_gguf(spec)
     eng = E.Engine(img, CTX)
     sampler = ClockSampler(0)
@@ -613,7 +615,9 @@ def run_batch(args) -> None:
                       "config": {"workload": "BASELINE config 5 on one GPU: 64 sequences x 2048-token prompts, 512 "
                                  "sampled steps" if (args.seqs, args.prompt, args.gen) == (64, 2048, 512)
                                  else f"BASELINE config 5 shape, reduced: {args.seqs} sequences x {args.prompt}-token "
-                                      f"prompts, {args.gen} sampled steps", "parallelism": "single GPU"},
+                                      f"prompts, {args.gen} sampled steps" + (
+                                          f", {args.layers} layers (profiling run, not a bench line)" if args.layers
+                                          else ""), "parallelism": "single GPU"},
                       **res, "clocks": sampler.summary()}), flush=True)
 
 

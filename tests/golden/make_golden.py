@@ -17,7 +17,7 @@ Sources, all from the reference project (K410Sh4/QWEN-30BRust):
   dequantized weights.  Dequantization uses the oracle, which quant_blocks.npz
   pins bit-exactly.
 
-Usage: python tests/golden/make_golden.py   (needs the reference checkout)
+Usage: python tests/golden/make_golden.py --reference <path of the reference checkout>
 """
 from __future__ import annotations
 
@@ -31,7 +31,7 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent.parent
-REF = Path("/root/reference")
+REF = Path(".")  # the reference checkout, set from --reference by main()
 
 
 def f16_bytes(v: float) -> bytes:
@@ -208,4 +208,8 @@ def dequantize_all(img: np.ndarray, O) -> dict[str, np.ndarray]:
 
 
 if __name__ == "__main__":
+    import argparse
+    ap = argparse.ArgumentParser(description="regenerate tests/golden/ from the reference checkout")
+    ap.add_argument("--reference", required=True, type=Path, help="path of the K410Sh4/QWEN-30BRust checkout")
+    REF = ap.parse_args().reference.resolve()
     main()
