@@ -22,7 +22,8 @@ OBJ = HERE / "_build"
 CUDA_LIB = HERE / "libqwen_cuda.so"
 TOOLS_LIB = HERE / "libqwen_tools.so"
 
-CU_SOURCES = ["matvec.cu", "decode.cu", "token.cu", "engine.cu", "noalloc.cu", "sample.cu", "moe.cu", "batch.cu"]
+CU_SOURCES = ["matvec.cu", "decode.cu", "token.cu", "engine.cu", "noalloc.cu", "sample.cu", "moe.cu", "batch.cu",
+              "qgemm.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

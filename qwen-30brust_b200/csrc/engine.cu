@@ -62,9 +62,9 @@ void prepare_device(int device) {
   QC_CK(qc::matvec_prepare(kMaxSmem));
   QC_CK(qc::decode_prepare(kMaxSmem));
   QC_CK(qc::token_prepare(0));
-  QC_CK(qc::moe_prepare());
   QC_CK(qc::sample_prepare());
   QC_CK(qc::batch_prepare(kMaxSmem));
+  QC_CK(qc::qgemm_prepare());
   done[device] = true;
 }
 
@@ -754,7 +754,7 @@ struct qc_engine {
   // ---- the MoE half of one layer for a batch of tokens --------------------------------------
   uint8_t* d_moe = nullptr;  // scratch of moe_cap tokens
   uint32_t moe_cap = 0;
-  std::vector<float> moe_sw;  // per layer: power-of-two weight scales (gate/up, down); 0 = not yet measured
+  std::vector<float> moe_sw;  // per layer: Q4_K min-block scales (gate, up, down); 0 = not yet measured
 
   qc::MoeArgs moe_args(uint32_t layer, uint32_t T) {
     const qc::LayerDev& L = layers[layer];
@@ -770,7 +770,12 @@ struct qc_engine {
     a.top = cfg.top;
     a.T = T;
     a.eps = cfg.eps;
-    const uint64_t P = (uint64_t)moe_cap * cfg.top;
+    a.sms = sms;
+    a.NPgu = a.NPdn = 16;
+    a.BSgu = a.BSdn = 2;
+    if (!qc::qgemm_shape(a.gate.kind, a.H, a.gate.kind == qc::Q4_K, &a.NPgu, &a.BSgu))
+      qc::qgemm_shape(a.down.kind, a.I, a.down.kind == qc::Q4_K, &a.NPdn, &a.BSdn);
+    const uint64_t P = (uint64_t)moe_cap * cfg.top, R = qc::moe_image_rows(moe_cap, cfg.top, cfg.experts);
     uint64_t o = 0;
     auto take = [&](uint64_t bytes) {
       uint8_t* p = d_moe + o;
@@ -785,19 +790,25 @@ struct qc_engine {
     a.off = reinterpret_cast<uint32_t*>(take(cfg.experts * 4));
     a.ptok = reinterpret_cast<uint32_t*>(take(P * 4));
     a.ppair = reinterpret_cast<uint32_t*>(take(P * 4));
-    a.gu = reinterpret_cast<float*>(take(P * cfg.intermediate * 4));
-    a.gumax = reinterpret_cast<uint32_t*>(take(P * 4));
+    a.groups = reinterpret_cast<qc::QgGroup*>(take(2ull * cfg.experts * sizeof(qc::QgGroup)));
+    a.nitems = reinterpret_cast<uint32_t*>(take(8));
+    a.imgrows = reinterpret_cast<uint4*>(take(R * 16));
+    a.nrows = reinterpret_cast<uint32_t*>(take(4));
+    a.img_gu = take(R * qc::qg_image_row_bytes(cfg.hidden, a.gate.kind == qc::Q4_K));
+    a.img_dn = take(R * qc::qg_image_row_bytes(cfg.intermediate, a.down.kind == qc::Q4_K));
     a.y = reinterpret_cast<float*>(take(P * cfg.hidden * 4));
     a.err = reinterpret_cast<uint32_t*>(take(4));
     // inputs and outputs of the call follow the scratch
     return a;
   }
   uint64_t moe_bytes(uint32_t cap) const {
-    const uint64_t P = (uint64_t)cap * cfg.top;
+    const uint64_t P = (uint64_t)cap * cfg.top, R = qc::moe_image_rows(cap, cfg.top, cfg.experts);
     auto al = [](uint64_t b) { return align256(b); };
+    // (an upper bound: image rows are sized for Q4_K min chunks whatever the layer's formats)
     return al((uint64_t)cap * cfg.hidden * 4) + al(cap * 4) + 2 * al(P * 4) + 2 * al(cfg.experts * 4) +
-           2 * al(P * 4) + al(P * cfg.intermediate * 4) + al(P * 4) + al(P * cfg.hidden * 4) + al(4) +
-           2 * al((uint64_t)cap * cfg.hidden * 4);
+           2 * al(P * 4) + al(2ull * cfg.experts * sizeof(qc::QgGroup)) + al(8) + al(R * 16) + al(4) +
+           al(R * qc::qg_image_row_bytes(cfg.hidden, true)) + al(R * qc::qg_image_row_bytes(cfg.intermediate, true)) +
+           al(P * cfg.hidden * 4) + al(4) + 2 * al((uint64_t)cap * cfg.hidden * 4);
   }
 
   // x, out: [T][hidden] host arrays.  path 1: the per-token decode kernels (router, gate/up, down)
@@ -812,31 +823,31 @@ struct qc_engine {
     QC_CK(cudaMalloc(&d_moe, moe_bytes(T)));
     moe_cap = T;
   }
-  // Power-of-two weight scales of the tensor-core split for a layer (from bounds of |w| over its
-  // block scales, computed once per layer), into a.sw_gu / a.sw_down.
+  // Power-of-two scales of the Q4_K min blocks of the tensor-core GEMM for a layer (from the largest
+  // |dmin| of each expert stack, measured once per layer), into a.smin_g / smin_u / smin_d.
   void moe_scales(uint32_t layer, qc::MoeArgs& a) {
-    if (moe_sw.empty()) moe_sw.assign(2 * cfg.layers, 0.f);
-    if (moe_sw[2 * layer] == 0.f) {
-      uint32_t* b = a.err;
-      uint32_t hb[2] = {0, 0};
-      QC_CK(cudaMemsetAsync(b, 0, 4, stream));
-      qc::launch_moe_wbound(a.gate, cfg.experts, b, stream);
-      qc::launch_moe_wbound(a.up, cfg.experts, b, stream);
-      QC_CK(cudaMemcpyAsync(&hb[0], b, 4, cudaMemcpyDeviceToHost, stream));
-      QC_CK(cudaMemsetAsync(b, 0, 4, stream));
-      qc::launch_moe_wbound(a.down, cfg.experts, b, stream);
-      QC_CK(cudaMemcpyAsync(&hb[1], b, 4, cudaMemcpyDeviceToHost, stream));
-      QC_CK(cudaStreamSynchronize(stream));
-      for (int i = 0; i < 2; i++) {
-        float bound;
-        std::memcpy(&bound, &hb[i], 4);
-        int ex = 0;
-        std::frexp(bound > 0.f ? bound : 1.f, &ex);
-        moe_sw[2 * layer + i] = std::ldexp(1.f, 14 - ex);
-      }
+    if (moe_sw.empty()) moe_sw.assign(3 * cfg.layers, 0.f);
+    if (moe_sw[3 * layer] == 0.f) {
+      const qc::MatDesc* m[3] = {&a.gate, &a.up, &a.down};
+      for (int i = 0; i < 3; i++) moe_sw[3 * layer + i] = dmin_scale(*m[i], cfg.experts, a.err);
     }
-    a.sw_gu = moe_sw[2 * layer];
-    a.sw_down = moe_sw[2 * layer + 1];
+    a.smin_g = moe_sw[3 * layer];
+    a.smin_u = moe_sw[3 * layer + 1];
+    a.smin_d = moe_sw[3 * layer + 2];
+  }
+  // Q4_K: 2^k with (largest |dmin|) * 63 * 2^k < 2^14 (the min block's fp16 hi/lo split); others 1.
+  // `tmp` is one word of device scratch.
+  float dmin_scale(const qc::MatDesc& m, uint32_t experts, uint32_t* tmp) {
+    if (m.kind != qc::Q4_K) return 1.f;
+    uint32_t hb = 0;
+    QC_CK(cudaMemsetAsync(tmp, 0, 4, stream));
+    qc::launch_qg_dmin(m, experts, tmp, stream);
+    QC_CK(cudaMemcpyAsync(&hb, tmp, 4, cudaMemcpyDeviceToHost, stream));
+    QC_CK(cudaMemsetAsync(tmp, 0, 4, stream));
+    QC_CK(cudaStreamSynchronize(stream));
+    float dmax;
+    std::memcpy(&dmax, &hb, 4);
+    return qc::qg_pow2_scale(dmax * 63.f);
   }
 
   void moe_layer(uint32_t layer, const float* x, uint32_t T, float* out, int path, float* ms) {
@@ -864,6 +875,7 @@ struct qc_engine {
       QC_CK(cudaStreamSynchronize(stream));
       if (herr & 2) throw ApiError(QC_ERR_CUDA, "MoE tensor-core kernel: a wait timed out");
       if (herr & 1) throw ApiError(QC_ERR_NONFINITE, "non-finite router logits");
+      if (herr & 4) throw ApiError(QC_ERR_NONFINITE, "an expert activation outside the fp16 range of the tensor-core path");
     } else {
       const qc::LayerDev& L = layers[layer];
       QC_CK(cudaEventRecord(ev0, stream));
@@ -943,6 +955,14 @@ struct qc_batch {
   uint8_t* d_xv = nullptr;
   uint32_t xb_max = 0;
   float* d_lg = nullptr;     // [cap][vocab] logits rows of the pass
+  // tensor-core projections (qgemm.cu): per layer, which of q, k, v, o take it and their Q4_K min
+  // scales; the same for the vocabulary rows; the activation image and its vector scales
+  std::vector<uint8_t> tc;     // [layer][4]
+  std::vector<float> tc_smin;  // [layer][4]
+  bool tc_out = false;
+  float tc_out_smin = 1.f;
+  uint8_t* d_img = nullptr;
+  float* d_hs = nullptr;
   float* d_last = nullptr;   // [n_seqs][vocab] the latest logits of each sequence
   uint32_t* d_flag = nullptr;  // [0] non-finite logits
   // sampling
@@ -1012,10 +1032,30 @@ struct qc_batch {
       return at;
     };
     const uint64_t o_tok = take(cap * sizeof(qc::BatchTok)), o_ids = take(cap * 4), o_osrc = take(cap * 4);
+    // tensor-core projections where the formats allow
+    auto tc_ok = [&](const qc::MatDesc& m) {
+      uint32_t np, bs;
+      return !qc::qgemm_shape(m.kind, m.cols, true, &np, &bs);
+    };
+    tc.assign(4ull * c.layers, 0);
+    tc_smin.assign(4ull * c.layers, 1.f);
+    uint64_t img_row = 0;
+    for (uint32_t l = 0; l < c.layers; l++) {
+      const qc::LayerDev& L = e->layers[l];
+      const qc::MatDesc* m[4] = {&L.q, &L.k, &L.v, &L.o};
+      for (int i = 0; i < 4; i++) {
+        if (!tc_ok(*m[i])) continue;
+        tc[4 * l + i] = 1;
+        img_row = std::max(img_row, qc::qg_image_row_bytes(m[i]->cols, true));
+      }
+    }
+    tc_out = tc_ok(e->out);
+    if (tc_out) img_row = std::max(img_row, qc::qg_image_row_bytes(e->out.cols, true));
     const uint64_t o_x = take(cap * H * 4), o_x2 = take(cap * H * 4), o_q = take(cap * QD * 4), o_k = take(cap * KD * 4),
                    o_v = take(cap * KD * 4), o_a = take(cap * QD * 4), o_xv = take((uint64_t)cap * xb_max),
                    o_lg = take(cap * V * 4), o_last = take((uint64_t)n * V * 4), o_flag = take(16),
-                   o_rows = take((uint64_t)n * 8), o_sv = take((uint64_t)n * 8);
+                   o_rows = take((uint64_t)n * 8), o_sv = take((uint64_t)n * 8),
+                   o_img = take((uint64_t)((cap + 15) & ~15u) * img_row), o_hs = take(((cap + 15) & ~15u) * 4);
     QC_CK(cudaMalloc(&d_buf, o));
     QC_CK(cudaMemsetAsync(d_buf, 0, o, e->stream));
     e->grow_moe(cap);
@@ -1039,7 +1079,65 @@ struct qc_batch {
     d_flag = reinterpret_cast<uint32_t*>(d_buf + o_flag);
     d_rows = reinterpret_cast<const float**>(d_buf + o_rows);
     d_sv = reinterpret_cast<qc::SamplerDev**>(d_buf + o_sv);
+    d_img = d_buf + o_img;
+    d_hs = reinterpret_cast<float*>(d_buf + o_hs);
+    for (uint32_t l = 0; l < c.layers; l++) {  // Q4_K min-block scales, once
+      const qc::LayerDev& L = e->layers[l];
+      const qc::MatDesc* m[4] = {&L.q, &L.k, &L.v, &L.o};
+      for (int i = 0; i < 4; i++)
+        if (tc[4 * l + i]) tc_smin[4 * l + i] = e->dmin_scale(*m[i], 1, d_flag);
+    }
+    if (tc_out) tc_out_smin = e->dmin_scale(e->out, 1, d_flag);
     QC_CK(cudaStreamSynchronize(e->stream));
+  }
+
+  // The activation image of T vectors of K floats (rows src[i] of x, or x's first T rows), RMS-normalized
+  // with w when given; their scales go to d_hs.  Q4_K min chunks always (Q6_K GEMMs skip them).
+  void tc_image(const float* x, const uint32_t* src, uint32_t T, uint32_t K, const float* w) {
+    qc::QgImageArgs ia{};
+    ia.x = x;
+    ia.xstride = K;
+    ia.K = K;
+    ia.T = T;
+    ia.src = src;
+    ia.w = w;
+    ia.eps = e->cfg.eps;
+    ia.hs_out = d_hs;
+    ia.hasmin = 1;
+    ia.img = d_img;
+    qc::launch_qg_image(ia, (T + 15) & ~15u, e->stream);
+  }
+  struct TcOut {
+    const qc::MatDesc* m;
+    float smin;
+    float* y;
+    const float* add;
+    uint64_t ystride;
+  };
+  // y = W x (+ add) for up to 3 matrices of one format over the current image of T vectors.
+  void tc_project(const std::vector<TcOut>& outs, uint32_t T, uint32_t K) {
+    if (outs.empty()) return;
+    const uint32_t kind = outs[0].m->kind, nimg = (T + 15) & ~15u;
+    uint32_t NP = 16, BS = 2;
+    qc::qgemm_shape(kind, K, true, &NP, &BS);  // (checked when the batch was created)
+    qc::QgArgs q{};
+    q.K = K;
+    q.NP = NP;
+    q.BS = BS;
+    q.img_hasmin = 1;
+    q.img = d_img;
+    q.hs = d_hs;
+    q.err = e->moe_args(0, 1).err;
+    uint32_t items = 0;
+    for (size_t i = 0; i < outs.size(); i++) {
+      q.mats[i] = *outs[i].m;
+      q.smin[i] = outs[i].smin;
+      q.inl[i] = qc::QgGroup{items, T, nimg, 0, (uint32_t)i, 0, outs[i].y, outs[i].add, nullptr, nullptr, outs[i].ystride};
+      items += (outs[i].m->rows + 127) / 128 * ((nimg + NP - 1) / NP);
+    }
+    q.ngroups = (uint32_t)outs.size();
+    q.nitems = items;
+    qc::launch_qgemm(q, kind, false, std::min<uint32_t>(items, (uint32_t)e->sms), e->stream);
   }
 
   // One device pass: T tokens (ids in d_ids, sequence and position in d_tok), logits rows for the
@@ -1052,16 +1150,38 @@ struct qc_batch {
     qc::launch_batch_embed(e->embd, d_tok, d_ids, T, H, d_x, s);
     for (uint32_t l = 0; l < c.layers; l++) {
       const qc::LayerDev& L = e->layers[l];
-      const bool flA = qc::uses_float_x(L.q.kind) || qc::uses_float_x(L.k.kind) || qc::uses_float_x(L.v.kind);
-      const uint32_t xbA = qc::xview_bytes(L.q.units, flA), xbO = qc::xview_bytes(L.o.units, qc::uses_float_x(L.o.kind));
-      qc::launch_batch_stage(d_x, nullptr, T, H, L.q.units, flA, L.attn_norm, c.eps, d_xv, xbA, s);
-      qc::launch_batch_matvec(L.q, d_xv, xbA, T, d_q, QD, nullptr, e->sms, s);
-      qc::launch_batch_matvec(L.k, d_xv, xbA, T, d_k, KD, nullptr, e->sms, s);
-      qc::launch_batch_matvec(L.v, d_xv, xbA, T, d_v, KD, nullptr, e->sms, s);
+      const uint8_t* t4 = &tc[4 * l];
+      // Q, K, V of rms(x) (model.rs:226-240): tensor cores for the formats that allow, else dp4a matvecs
+      if (t4[0] || t4[1] || t4[2]) {
+        tc_image(d_x, nullptr, T, H, L.attn_norm);
+        const qc::MatDesc* m[3] = {&L.q, &L.k, &L.v};
+        float* y[3] = {d_q, d_k, d_v};
+        const uint64_t st[3] = {QD, KD, KD};
+        for (uint32_t kind : {(uint32_t)qc::Q4_K, (uint32_t)qc::Q6_K}) {
+          std::vector<TcOut> outs;
+          for (int i = 0; i < 3; i++)
+            if (t4[i] && m[i]->kind == kind) outs.push_back(TcOut{m[i], tc_smin[4 * l + i], y[i], nullptr, st[i]});
+          tc_project(outs, T, H);
+        }
+      }
+      if (!(t4[0] && t4[1] && t4[2])) {
+        const bool flA = qc::uses_float_x(L.q.kind) || qc::uses_float_x(L.k.kind) || qc::uses_float_x(L.v.kind);
+        const uint32_t xbA = qc::xview_bytes(L.q.units, flA);
+        qc::launch_batch_stage(d_x, nullptr, T, H, L.q.units, flA, L.attn_norm, c.eps, d_xv, xbA, s);
+        if (!t4[0]) qc::launch_batch_matvec(L.q, d_xv, xbA, T, d_q, QD, nullptr, e->sms, s);
+        if (!t4[1]) qc::launch_batch_matvec(L.k, d_xv, xbA, T, d_k, KD, nullptr, e->sms, s);
+        if (!t4[2]) qc::launch_batch_matvec(L.v, d_xv, xbA, T, d_v, KD, nullptr, e->sms, s);
+      }
       qc::launch_batch_qkprep(ba, l, L.q_norm, L.k_norm, d_q, d_k, d_v, T, s);
       qc::launch_batch_attention(ba, l, d_q, d_a, T, s);
-      qc::launch_batch_stage(d_a, nullptr, T, QD, L.o.units, qc::uses_float_x(L.o.kind), nullptr, 0.f, d_xv, xbO, s);
-      qc::launch_batch_matvec(L.o, d_xv, xbO, T, d_x, H, d_x, e->sms, s);  // x += W_o attn (model.rs:245-248)
+      if (t4[3]) {  // x += W_o attn (model.rs:245-248)
+        tc_image(d_a, nullptr, T, QD, nullptr);
+        tc_project({TcOut{&L.o, tc_smin[4 * l + 3], d_x, d_x, H}}, T, QD);
+      } else {
+        const uint32_t xbO = qc::xview_bytes(L.o.units, qc::uses_float_x(L.o.kind));
+        qc::launch_batch_stage(d_a, nullptr, T, QD, L.o.units, qc::uses_float_x(L.o.kind), nullptr, 0.f, d_xv, xbO, s);
+        qc::launch_batch_matvec(L.o, d_xv, xbO, T, d_x, H, d_x, e->sms, s);
+      }
       // the MoE half (model.rs:249-287): tensor-core path when the formats allow, else per token
       qc::MoeArgs ma = e->moe_args(l, T);
       if (!qc::moe_tc_supported(ma)) {
@@ -1078,10 +1198,15 @@ struct qc_batch {
       QC_CK(cudaGetLastError());
     }
     if (n_out) {  // model.rs:289-301: output norm, vocabulary rows, finiteness
-      const bool flV = qc::uses_float_x(e->out.kind);
-      const uint32_t xbV = qc::xview_bytes(e->out.units, flV);
-      qc::launch_batch_stage(d_x, d_osrc, n_out, H, e->out.units, flV, e->out_norm, c.eps, d_xv, xbV, s);
-      qc::launch_batch_matvec(e->out, d_xv, xbV, n_out, d_lg, c.vocab, nullptr, e->sms, s);
+      if (tc_out) {
+        tc_image(d_x, d_osrc, n_out, H, e->out_norm);
+        tc_project({TcOut{&e->out, tc_out_smin, d_lg, nullptr, c.vocab}}, n_out, H);
+      } else {
+        const bool flV = qc::uses_float_x(e->out.kind);
+        const uint32_t xbV = qc::xview_bytes(e->out.units, flV);
+        qc::launch_batch_stage(d_x, d_osrc, n_out, H, e->out.units, flV, e->out_norm, c.eps, d_xv, xbV, s);
+        qc::launch_batch_matvec(e->out, d_xv, xbV, n_out, d_lg, c.vocab, nullptr, e->sms, s);
+      }
       qc::launch_batch_finite(d_lg, (uint64_t)n_out * c.vocab, d_flag, s);
     }
     QC_CK(cudaGetLastError());
@@ -1096,8 +1221,9 @@ struct qc_batch {
     QC_CK(cudaMemsetAsync(d_flag, 0, 4, e->stream));
     QC_CK(cudaMemsetAsync(e->moe_args(0, 1).err, 0, 4, e->stream));
     e->check_flags();  // per-token MoE fallback: non-finite router logits
-    if (h[1] & 2) throw ApiError(QC_ERR_CUDA, "MoE tensor-core kernel: a wait timed out");
+    if (h[1] & 2) throw ApiError(QC_ERR_CUDA, "tensor-core kernel: a wait timed out");
     if (h[1] & 1) throw ApiError(QC_ERR_NONFINITE, "invalid MoE router");
+    if (h[1] & 4) throw ApiError(QC_ERR_NONFINITE, "an expert activation outside the fp16 range of the tensor-core path");
     if (h[0]) throw ApiError(QC_ERR_NONFINITE, "nonfinite model output");
   }
 

@@ -138,12 +138,15 @@ void launch_token(const StepArgs& a, const TokenPlan& p, unsigned long long* ll,
 cudaError_t token_prepare(int max_smem);
 
 // The MoE half of one layer for a batch of tokens (moe.cu).
+struct QgGroup;
 struct MoeArgs {
   MatDesc router, gate, up, down;  // one layer's router and expert stacks, device layout
   const float* ffn_norm;
   uint32_t H, I, E, top, T;
   float eps;
-  float sw_gu, sw_down;  // power-of-two weight scales of the fp16 hi/lo split
+  float smin_g, smin_u, smin_d;  // Q4_K min-block scales of the tensor-core GEMM (qgemm.cu)
+  uint32_t NPgu, NPdn, BSgu, BSdn;  // vectors per GEMM pass and B stages (qgemm_shape)
+  int sms;
   // scratch
   float* h;          // [T][H] normalized inputs
   float* hscale;     // [T] power-of-two scale of each token's h
@@ -153,15 +156,18 @@ struct MoeArgs {
   uint32_t* off;     // [E] first grouped pair of each expert
   uint32_t* ptok;    // [T*top] grouped pairs: token
   uint32_t* ppair;   // [T*top] grouped pairs: pair id t*top + slot
-  float* gu;         // [T*top][I] SwiGLU outputs by pair id
-  uint32_t* gumax;   // [T*top] bits of max |gu| by pair id
+  QgGroup* groups;   // [2E] GEMM groups: gate/up, then down
+  uint32_t* nitems;  // [2] their work items
+  uint4* imgrows;    // [moe_image_rows] rows of the gate/up activation image
+  uint32_t* nrows;   // [1] image rows in use
+  uint8_t* img_gu;   // gate/up activation image (hidden columns)
+  uint8_t* img_dn;   // down activation image (intermediate columns), written by the SwiGLU epilogue
   float* y;          // [T*top][H] down outputs by pair id
-  uint32_t* err;     // bit 0: non-finite router logit; bit 1: a tensor-core wait timed out
+  uint32_t* err;     // bit 0: non-finite router logit; bit 1: a tensor-core wait timed out; bit 2: fp16 range
 };
 const char* moe_tc_supported(const MoeArgs& a);
-size_t moe_gemm_smem();
-cudaError_t moe_prepare();
-void launch_moe_wbound(const MatDesc& m, uint32_t experts, uint32_t* out, cudaStream_t s);
+// Rows of the activation images for T tokens (pairs rounded up to 16 per expert), at most.
+uint32_t moe_image_rows(uint32_t T, uint32_t top, uint32_t E);
 // x [T][H] -> out [T][H]: route, plan, tensor-core gate/up + SwiGLU, down, combine.
 void launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStream_t s);
 // The per-token MoE kernels of the decode step (router, gate/up, down) on the vector c.x, in place.
@@ -233,5 +239,70 @@ void launch_batch_attention(const BatchArgs& a, uint32_t layer, const float* q, 
 void launch_batch_finite(const float* v, uint64_t n, uint32_t* flag, cudaStream_t s);
 // n keystream words of the sampler (advancing it), for reproducibility checks.
 void launch_sampler_words(SamplerDev* s, uint32_t n, uint32_t* out, cudaStream_t st);
+
+// ---- tensor-core GEMM over Q4_K / Q6_K rows (qgemm.cu) ---------------------------------------
+// A group: some rows of a matrix (or, in pair mode, of two matrices side by side) times `cnt`
+// vectors of the B image (rows imgoff .. imgoff + nimg of it, nimg a multiple of 16, rows past cnt
+// zero).  Its work items are (128-row tile, pass of up to NP vectors), items item0 .. of the launch.
+struct QgGroup {
+  uint32_t item0, cnt, nimg, imgoff;
+  uint32_t mat;  // rows from mats[mat] (pair mode: tile rows 0-63 from mats[mat], 64-127 from mats[mat + 1])
+  uint32_t e;    // expert index in those matrices
+  float* y;      // plain epilogue: y[row(n) * ystride + r] (+ add[same]), row(n) = ymap ? ymap[n] : n
+  const float* add;
+  const uint32_t* ymap;
+  const uint32_t* hsmap;  // the scale of image vector n is hs[hsmap ? hsmap[n] : n] (hs null: 1)
+  uint64_t ystride;
+};
+struct QgArgs {
+  MatDesc mats[4];
+  float smin[4];        // Q4_K: power-of-two scale of the min block (dmin * mn * smin < 2^14)
+  uint32_t pair;        // pair mode (SwiGLU: gate rows then up rows of each 128-row tile)
+  uint32_t K, NP, BS;   // columns (a multiple of 256); vectors per pass; B stages (qgemm_shape)
+  uint32_t img_hasmin;  // the image carries the Q4_K min chunks
+  const uint8_t* img;
+  const float* hs;
+  const QgGroup* groups;  // device array of ngroups, or null: inl
+  uint32_t ngroups;
+  const uint32_t* nitems_dev;  // device item count, or null: nitems
+  uint32_t nitems;
+  QgGroup inl[3];
+  uint8_t* img2;  // SwiGLU epilogue: the image of the next GEMM (K = K2, K step = tile)
+  uint32_t K2, img2_hasmin;
+  uint32_t* err;  // bit 1: a wait timed out; bit 2: a SwiGLU output outside the fp16 range
+};
+// B image rows: either `rows` (device, *nrows of them: {source row or ~0, imgoff, nimg, 0}) or the
+// dense form: rows 0 .. round16(T), source src[i] (or i) for i < T.
+struct QgImageArgs {
+  const float* x;
+  uint64_t xstride;
+  uint32_t K, T;
+  const uint32_t* src;
+  const uint4* rows;
+  const uint32_t* nrows;
+  const float* w;  // RMSNorm weight, or null
+  float eps;
+  const float* hs_in;  // per source row, or null: computed (pow2 of max |x|) and written to hs_out[i]
+  float* hs_out;
+  uint32_t hasmin;
+  uint8_t* img;
+};
+__host__ __device__ inline float qg_pow2_scale(float maxabs) {  // 2^k with maxabs * 2^k < 2^14
+  if (!(maxabs > 0.f) || !isfinite(maxabs)) return 1.f;
+  int ex;
+  frexpf(maxabs, &ex);
+  return ldexpf(1.f, 14 - ex);
+}
+const char* qgemm_supported(uint32_t kind, uint32_t cols);
+// Vectors per pass and B stages of a GEMM over `cols` columns of `kind` rows (after qgemm_prepare),
+// or the reason it cannot run.
+const char* qgemm_shape(uint32_t kind, uint32_t cols, bool img_hasmin, uint32_t* np, uint32_t* bs);
+uint64_t qg_image_row_bytes(uint32_t cols, bool hasmin);
+size_t qgemm_smem(uint32_t kind, uint32_t cols, uint32_t np, uint32_t bs, bool img_hasmin);
+cudaError_t qgemm_prepare();  // once per device
+size_t qgemm_smem_cap();      // dynamic shared memory available to the GEMM kernels (after qgemm_prepare)
+void launch_qgemm(const QgArgs& a, uint32_t kind, bool swiglu, uint32_t grid, cudaStream_t s);
+void launch_qg_image(const QgImageArgs& a, uint32_t grid, cudaStream_t s);
+void launch_qg_dmin(const MatDesc& m, uint32_t experts, uint32_t* out, cudaStream_t s);
 
 }  // namespace qc

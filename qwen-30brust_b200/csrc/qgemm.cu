@@ -1,0 +1,901 @@
+// Tensor-core GEMM over GGUF K-quant rows: y[n][r] = sum_k W[r][k] x_n[k] for a batch of activation
+// vectors, W in Q4_K or Q6_K (the engine's 8-row-group device layout), on the 5th-generation tensor
+// cores (tcgen05.mma kind::f16, fp32 accumulators in TMEM).  It replaces the reference's per-vector
+// Backend::matvec (backend.rs:28-52) wherever several vectors meet the same rows: the batched
+// attention projections and vocabulary rows of several sequences, and the grouped expert GEMMs of a
+// MoE layer (model.rs:249-287 for a batch of tokens).
+//
+// Exact operands.  A K-quant weight is d * sc * q (- dmin * mn for Q4_K) with small integers sc, q, mn
+// (quant.rs:50-77).  The A operand holds the integers only, exact in fp16:
+//   Q4_K  sc * q  (<= 63 * 15), one plane;
+//   Q6_K  sc * (q - 32) (|.| <= 4096) as hi = fp16(sc * (q - 32)) and lo = the remainder (0 or +-1),
+// and each 256-element super-block b accumulates into its own TMEM columns, so the per-block factor
+// d_b is applied once in the epilogue: y = sum_b d_b * acc_b.  The Q4_K min term
+// -sum_j dmin * mn_j * (sum of the 32 x of sub-block j) is one extra K = 16 step per super-block into
+// a separate accumulator: A = (dmin * mn_j * s_min) as fp16 hi | lo, B = the sub-block sums.
+// Activations come as a "B image" built once per batch (qg_image): x * hs (hs a power of two per
+// vector) as fp16 hi + lo planes in the layout the MMAs read, so a B stage is two bulk copies.
+// Products keep ~22 significant bits (A exact, B hi + lo); the only other rounding is the fp32
+// accumulation, so results stay within the matvec tolerance of the reference's f32 fold.
+//
+// Structure: a persistent CTA per SM (384 threads) walks work items (group, 128-row tile, pass of up
+// to NP vectors).  Warp 0 brings raw weight rows into a ring of shared-memory stages with bulk copies
+// (one stage = one super-block of 128 rows); warp 2 brings B stages; warps 4-11 turn raw rows into
+// A stages (one per K step of 64) and run the epilogue; warp 1 issues the MMAs (one elected thread)
+// and commits them to the stages' mbarriers.  Every wait is bounded (2 s): a timed-out role sets an
+// error bit, the others stop at their next wait, and copies and MMAs in flight are drained before the
+// accumulator is released.
+#include <cuda_fp16.h>
+
+#include "kernels.h"
+
+namespace qc {
+namespace {
+
+constexpr uint32_t kThreads = 384;
+constexpr uint32_t kProdWarp0 = 4;  // warps 4..11 produce A and run the epilogue
+constexpr uint32_t kProd = 256;     // producer threads
+constexpr unsigned long long kWaitNs = 2000000000ull;
+constexpr uint32_t kNone = 0xffffffffu;
+
+template <int AK>
+struct Cfg;
+template <>
+struct Cfg<Q4_K> {
+  static constexpr uint32_t blk = 144, RS = 3, AS = 2, planes = 1, kcsA = 10;
+};
+template <>
+struct Cfg<Q6_K> {
+  static constexpr uint32_t blk = 208, RS = 3, AS = 2, planes = 2, kcsA = 8;
+};
+constexpr uint32_t kMaxBS = 8;  // B stages (runtime count a.BS: as many as fit)
+template <int AK>
+constexpr uint32_t a_stage_bytes() {
+  return Cfg<AK>::planes * 128 * Cfg<AK>::kcsA * 16;
+}
+
+QC_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+QC_DEV unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+QC_DEV void mbar_init(uint64_t* m, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(m)), "r"(count) : "memory");
+}
+QC_DEV void mbar_arrive(uint64_t* m) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(m)) : "memory");
+}
+QC_DEV void mbar_expect(uint64_t* m, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(m)), "r"(bytes) : "memory");
+}
+QC_DEV void bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* m) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(m))
+               : "memory");
+}
+// Wait (at most 2 s, or until another role gave up) for the phase with the given parity.
+QC_DEV bool mbar_wait(uint64_t* m, uint32_t parity, volatile int* abort_flag) {
+  const uint32_t a = smem_u32(m);
+  const unsigned long long t0 = now_ns();
+  for (uint32_t i = 0;; i++) {
+    uint32_t ok;
+    asm volatile(
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((i & 255) == 255) {
+      if (*abort_flag) return false;
+      if (now_ns() - t0 > kWaitNs) {
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+// Drain: wait (bounded) for a phase, ignoring the abort flag.
+QC_DEV void mbar_drain(uint64_t* m, uint32_t parity) {
+  int never = 0;
+  mbar_wait(m, parity, &never);
+}
+// Barrier of the 8 producer warps on an mbarrier (count 8), so that a warp which gave up makes the
+// others' wait time out instead of blocking: false if it did.
+QC_DEV bool prod_sync(uint64_t* b, uint32_t* phase, volatile int* abort_flag) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(b);
+  const bool ok = mbar_wait(b, *phase & 1, abort_flag);
+  ++*phase;
+  __syncwarp();
+  return ok;
+}
+
+QC_DEV unsigned long long sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return (unsigned long long)((addr >> 4) & 0x3fff) | ((unsigned long long)((lbo >> 4) & 0x3fff) << 16) |
+         ((unsigned long long)((sbo >> 4) & 0x3fff) << 32) | (1ull << 46);
+}
+QC_DEV void mma(uint32_t d, unsigned long long a, unsigned long long b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+QC_DEV void mma_commit(uint64_t* m) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(m))
+               : "memory");
+}
+
+QC_DEV uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+QC_DEV uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+QC_DEV __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+// quant.rs get_scale_min_k4: 6-bit scale and min of sub-block j from the 12 scale bytes s[0..11]
+// (held as three little-endian words).
+QC_DEV void scale_min(const uint32_t (&s)[3], uint32_t j, uint32_t* sc, uint32_t* mn) {
+  auto byte = [&](uint32_t i) { return (s[i >> 2] >> (8 * (i & 3))) & 0xffu; };
+  if (j < 4) {
+    *sc = byte(j) & 63;
+    *mn = byte(j + 4) & 63;
+  } else {
+    *sc = (byte(j + 4) & 15) | ((byte(j - 4) >> 6) << 4);
+    *mn = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4);
+  }
+}
+
+// x as fp16 hi + lo (x = hi + lo to ~22 bits when |x| < 2^15), two values per word.
+QC_DEV void split2(float a, float b, uint32_t* hi, uint32_t* lo) {
+  const __half2 h = __floats2half2_rn(a, b);
+  const float2 back = __half22float2(h);
+  *hi = h2u(h);
+  *lo = h2u(__floats2half2_rn(a - back.x, b - back.y));
+}
+
+// Item -> (group, tile, pass).  Groups are ordered by first item; an empty group shares its first
+// item with the next one, so the group of item i is the last one starting at or before i.
+struct Item {
+  uint32_t g, tile, n0, N, nn;
+};
+constexpr uint32_t kMaxGroups = 1024;
+QC_DEV const QgGroup& group_at(const QgArgs& a, uint32_t g) { return a.groups ? a.groups[g] : a.inl[g]; }
+// (item0 of every group is staged in shared memory: g0[])
+QC_DEV Item decode_item(const QgArgs& a, const uint32_t* g0, uint32_t i) {
+  uint32_t lo = 0, hi = a.ngroups - 1;
+  while (lo < hi) {
+    const uint32_t mid = (lo + hi + 1) >> 1;
+    if (g0[mid] <= i) lo = mid;
+    else hi = mid - 1;
+  }
+  const QgGroup& g = group_at(a, lo);
+  const uint32_t passes = (g.nimg + a.NP - 1) / a.NP, local = i - g.item0;
+  Item it;
+  it.g = lo;
+  it.tile = local / passes;
+  it.n0 = (local % passes) * a.NP;
+  it.N = min(a.NP, g.nimg - it.n0);
+  it.nn = g.cnt > it.n0 ? min(it.N, g.cnt - it.n0) : 0;
+  return it;
+}
+// Row r (< 128) of an item's tile: its matrix and row there, or false past the matrix.
+QC_DEV bool tile_row(const QgArgs& a, uint32_t mat, uint32_t tile, uint32_t r, uint32_t* mi, uint32_t* row) {
+  if (a.pair) {
+    *mi = mat + (r >> 6);
+    *row = tile * 64 + (r & 63);
+  } else {
+    *mi = mat;
+    *row = tile * 128 + r;
+  }
+  return *row < a.mats[*mi].rows;
+}
+// Valid rows of an item's tile: rows 0 .. v0 - 1 and (pair mode) 64 .. 64 + v1 - 1.
+QC_DEV void tile_rows(const QgArgs& a, uint32_t mat, uint32_t tile, uint32_t* v0, uint32_t* v1) {
+  if (a.pair) {
+    const uint32_t r0 = a.mats[mat].rows, r1 = a.mats[mat + 1].rows;
+    *v0 = r0 > tile * 64 ? min(64u, r0 - tile * 64) : 0;
+    *v1 = r1 > tile * 64 ? min(64u, r1 - tile * 64) : 0;
+  } else {
+    const uint32_t r0 = a.mats[mat].rows;
+    *v0 = r0 > tile * 128 ? min(128u, r0 - tile * 128) : 0;
+    *v1 = 0;
+  }
+}
+
+// What the loaders and the MMA issuer need of an item, read one item ahead.
+struct ItemDesc {
+  uint32_t tile, n0, N, nimg, imgoff, mat, e;
+};
+QC_DEV ItemDesc load_item(const QgArgs& a, const uint32_t* g0, uint32_t i) {
+  const Item it = decode_item(a, g0, i);
+  const QgGroup& g = group_at(a, it.g);
+  return ItemDesc{it.tile, it.n0, it.N, g.nimg, g.imgoff, g.mat, g.e};
+}
+
+// Image layout.  K steps of 64 columns; with min chunks (Q4_K activations), the last K step of each
+// super-block carries two more 16-byte chunks (the sub-block sums).  Per K step: [plane hi, lo]
+// [row / 8][chunk][row % 8][16 bytes].
+QC_DEV uint32_t kcs_of(uint32_t s, uint32_t hasmin) { return 8 + ((hasmin && (s & 3) == 3) ? 2 : 0); }
+QC_DEV uint32_t kc_before(uint32_t s, uint32_t hasmin) { return 8 * s + (hasmin ? 2 * (s >> 2) : 0); }
+
+template <int AK, int EPI>
+__global__ void __launch_bounds__(kThreads, 1) k_qgemm(QgArgs a) {
+  using C = Cfg<AK>;
+  extern __shared__ __align__(1024) uint8_t sm[];
+  __shared__ __align__(8) uint64_t raw_full[C::RS], raw_empty[C::RS], a_full[C::AS], a_empty[C::AS], b_full[kMaxBS],
+      b_empty[kMaxBS], acc_full, psync;
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+  __shared__ uint32_t g0[kMaxGroups];
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t K = a.K, S = K / 64, nsb = K / 256;
+  const bool hasminA = AK == Q4_K;
+  const uint32_t nitems = a.nitems_dev ? *a.nitems_dev : a.nitems;
+  // shared-memory carve-up (the host sizes it with qgemm_smem)
+  const uint32_t kcsB = a.img_hasmin ? 10 : 8;
+  const uint32_t raw_bytes = 128 * C::blk, b_bytes = 2 * a.NP * kcsB * 16;
+  uint8_t* raw = sm;
+  uint8_t* area = raw + C::RS * raw_bytes;  // Q6_K: d values of the tile's rows, one copy per raw slot
+  const uint32_t area_bytes = AK == Q6_K ? 128 * nsb * 2 : 0;
+  uint8_t* ast = area + C::RS * area_bytes;
+  uint8_t* bst = ast + C::AS * a_stage_bytes<AK>();
+  const uint32_t BS = a.BS;
+  float* dsm = reinterpret_cast<float*>(bst + BS * b_bytes);  // [part][nsb][128] d of each row
+  float* hsm = dsm + 2 * nsb * 128;                              // [2][NP] 1 / scale of each vector
+  uint32_t* ysm = reinterpret_cast<uint32_t*>(hsm + 2 * a.NP);  // [2][NP] output row of each vector
+  const uint32_t img_row = 32 * kc_before(S, a.img_hasmin);     // image bytes per vector
+
+  for (uint32_t g = tid; g < a.ngroups; g += kThreads) g0[g] = group_at(a, g).item0;
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&tmem_base))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 0) {
+    abort_flag = 0;
+    for (uint32_t i = 0; i < C::RS; i++) {
+      mbar_init(&raw_full[i], 1);
+      mbar_init(&raw_empty[i], kProd / 32);
+    }
+    for (uint32_t i = 0; i < C::AS; i++) {
+      mbar_init(&a_full[i], kProd / 32);
+      mbar_init(&a_empty[i], 1);
+    }
+    for (uint32_t i = 0; i < BS; i++) {
+      mbar_init(&b_full[i], 1);
+      mbar_init(&b_empty[i], 1);
+    }
+    mbar_init(&acc_full, 1);
+    mbar_init(&psync, kProd / 32);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_base;
+  volatile int* ab = &abort_flag;
+
+  if (warp == 0) {
+    // ---- raw weight rows: one stage per (item, super-block) ----
+    uint32_t ctr = 0;
+    bool ok = true;
+    ItemDesc nx{};
+    if (blockIdx.x < nitems) nx = load_item(a, g0, blockIdx.x);
+    for (uint32_t i = blockIdx.x; i < nitems && ok; i += gridDim.x) {
+      const ItemDesc it = nx;
+      if (i + gridDim.x < nitems) nx = load_item(a, g0, i + gridDim.x);
+      for (uint32_t b = 0; b < nsb; b++, ctr++) {
+        const uint32_t slot = ctr % C::RS;
+        if (ctr >= C::RS && !mbar_wait(&raw_empty[slot], ((ctr / C::RS) - 1) & 1, ab)) {
+          ok = false;
+          break;
+        }
+        uint8_t* dst = raw + slot * raw_bytes;
+        uint32_t v0, v1;
+        tile_rows(a, it.mat, it.tile, &v0, &v1);
+        uint32_t bytes = (v0 + v1) * C::blk;
+        const bool with_area = AK == Q6_K;  // (the d values of all the tile's super-blocks, every stage)
+        if (with_area) bytes += ((v0 + 7) / 8 + (v1 + 7) / 8) * 16 * nsb;
+        if (lane == 0) mbar_expect(&raw_full[slot], bytes);
+        __syncwarp();
+        for (uint32_t r = lane; r < 128; r += 32) {
+          uint32_t mi, row;
+          if (tile_row(a, it.mat, it.tile, r, &mi, &row)) {
+            const MatDesc& m = a.mats[mi];
+            bulk_copy(dst + r * C::blk, row_ptr(m, expert_base(m, it.e), row) + b * C::blk, C::blk, &raw_full[slot]);
+          }
+        }
+        if (with_area && lane < 16) {  // the 8 rows' d values of 8-row group `lane`
+          uint32_t mi, row;
+          if (tile_row(a, it.mat, it.tile, lane * 8, &mi, &row)) {
+            const MatDesc& m = a.mats[mi];
+            const uint8_t* src = expert_base(m, it.e) + (uint64_t)(row >> 3) * m.group_bytes + 8 * m.main_bytes;
+            bulk_copy(area + slot * area_bytes + lane * 16 * nsb, src, 16 * nsb, &raw_full[slot]);
+          }
+        }
+      }
+    }
+    // drain: the copies of the last stages issued
+    if (lane == 0)
+      for (uint32_t k = ctr > C::RS ? ctr - C::RS : 0; k < ctr; k++) mbar_drain(&raw_full[k % C::RS], (k / C::RS) & 1);
+  } else if (warp == 2) {
+    // ---- B stages: one per (item, K step), two bulk copies (hi, lo) ----
+    if (lane == 0) {
+      uint32_t ctr = 0;
+      bool ok = true;
+      ItemDesc nx{};
+      if (blockIdx.x < nitems) nx = load_item(a, g0, blockIdx.x);
+      for (uint32_t i = blockIdx.x; i < nitems && ok; i += gridDim.x) {
+        const ItemDesc it = nx;
+        if (i + gridDim.x < nitems) nx = load_item(a, g0, i + gridDim.x);
+        const uint8_t* gimg = a.img + (uint64_t)it.imgoff * img_row;
+        for (uint32_t s = 0; s < S; s++, ctr++) {
+          const uint32_t slot = ctr % BS;
+          if (ctr >= BS && !mbar_wait(&b_empty[slot], ((ctr / BS) - 1) & 1, ab)) {
+            ok = false;
+            break;
+          }
+          const uint32_t kcs = kcs_of(s, a.img_hasmin), plane = it.N * kcs * 16;
+          const uint8_t* src = gimg + (uint64_t)it.nimg * 32 * kc_before(s, a.img_hasmin) + (it.n0 / 8) * kcs * 128;
+          uint8_t* dst = bst + slot * b_bytes;
+          mbar_expect(&b_full[slot], 2 * plane);
+          bulk_copy(dst, src, plane, &b_full[slot]);
+          bulk_copy(dst + plane, src + (uint64_t)it.nimg * kcs * 16, plane, &b_full[slot]);
+        }
+      }
+      for (uint32_t k = ctr > BS ? ctr - BS : 0; k < ctr; k++) mbar_drain(&b_full[k % BS], (k / BS) & 1);
+    }
+  } else if (warp == 1) {
+    // ---- MMA issue (one thread) ----
+    if (lane == 0) {
+      uint32_t actr = 0, bctr = 0, items = 0;
+      bool ok = true;
+      uint64_t* last = nullptr;
+      uint32_t last_par = 0;
+      const uint32_t NP = a.NP;
+      ItemDesc nx{};
+      if (blockIdx.x < nitems) nx = load_item(a, g0, blockIdx.x);
+      for (uint32_t i = blockIdx.x; i < nitems && ok; i += gridDim.x, items++) {
+        const ItemDesc it = nx;
+        if (i + gridDim.x < nitems) nx = load_item(a, g0, i + gridDim.x);
+        // f32 accumulator, f16 A and B, both K-major, N, M = 128
+        const uint32_t idesc = (1u << 4) | ((it.N >> 3) << 17) | ((128u >> 4) << 24);
+        for (uint32_t s = 0; s < S; s++, actr++, bctr++) {
+          const uint32_t as = actr % C::AS, bs = bctr % BS;
+          if (!mbar_wait(&a_full[as], (actr / C::AS) & 1, ab) || !mbar_wait(&b_full[bs], (bctr / BS) & 1, ab)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t sb = s >> 2, kcsB_s = kcs_of(s, a.img_hasmin);
+          const uint32_t aaddr = smem_u32(ast + as * a_stage_bytes<AK>()), baddr = smem_u32(bst + bs * b_bytes);
+          const uint32_t bplane = it.N * kcsB_s * 16, sboA = C::kcsA * 128, sboB = kcsB_s * 128;
+          const uint32_t dcol = tmem + sb * NP;
+#pragma unroll
+          for (uint32_t j = 0; j < 4; j++) {
+            const unsigned long long bh = sdesc(baddr + j * 256, 128, sboB), bl = sdesc(baddr + bplane + j * 256, 128, sboB);
+            const uint32_t acc = ((s & 3) == 0 && j == 0) ? 0u : 1u;
+            if (AK == Q4_K) {
+              const unsigned long long ad = sdesc(aaddr + j * 256, 128, sboA);
+              mma(dcol, ad, bh, idesc, acc);
+              mma(dcol, ad, bl, idesc, 1);
+            } else {
+              const unsigned long long ah = sdesc(aaddr + j * 256, 128, sboA),
+                                       al = sdesc(aaddr + 128 * C::kcsA * 16 + j * 256, 128, sboA);
+              mma(dcol, ah, bh, idesc, acc);
+              mma(dcol, ah, bl, idesc, 1);
+              mma(dcol, al, bh, idesc, 1);
+            }
+          }
+          if (hasminA && (s & 3) == 3) {  // the min term of super-block sb: chunks 8, 9
+            const unsigned long long ad = sdesc(aaddr + 4 * 256, 128, sboA), bh = sdesc(baddr + 4 * 256, 128, sboB),
+                                     bl = sdesc(baddr + bplane + 4 * 256, 128, sboB);
+            mma(tmem + nsb * NP, ad, bh, idesc, sb == 0 ? 0u : 1u);
+            mma(tmem + nsb * NP, ad, bl, idesc, 1);
+          }
+          mma_commit(&a_empty[as]);
+          mma_commit(&b_empty[bs]);
+          last = &b_empty[bs];
+          last_par = (bctr / BS) & 1;
+        }
+        if (!ok) break;
+        mma_commit(&acc_full);
+        last = &acc_full;
+        last_par = items & 1;
+      }
+      if (last) mbar_drain(last, last_par);  // every MMA issued has completed
+    }
+  } else if (warp >= kProdWarp0) {
+    // ---- A producers and epilogue: row r, half `part` of each K step ----
+    const uint32_t pt = tid - kProdWarp0 * 32, part = pt >> 7, r = pt & 127;
+    const uint32_t quarter = (warp - kProdWarp0) & 3;  // TMEM lanes 32 * quarter ..
+    float* dme = dsm + part * nsb * 128;
+    uint32_t rctr = 0, actr = 0, items = 0, pphase = 0;
+    bool ok = true;
+    for (uint32_t i = blockIdx.x; i < nitems && ok; i += gridDim.x, items++) {
+      const Item it = decode_item(a, g0, i);
+      const QgGroup& g = group_at(a, it.g);
+      uint32_t mi, row;
+      const bool valid = tile_row(a, g.mat, it.tile, r, &mi, &row);
+      const float smin = hasminA ? a.smin[mi] : 1.f;
+      float* hsv = hsm + (items & 1) * a.NP;
+      uint32_t* ysv = ysm + (items & 1) * a.NP;
+      // the scale and output row of vector pt of the pass: loads in flight during the item
+      float hs_pt = 1.f;
+      uint32_t y_pt = 0;
+      if (pt < it.N) {
+        const uint32_t n = it.n0 + pt;
+        if (a.hs && n < g.cnt) hs_pt = a.hs[g.hsmap ? g.hsmap[n] : n];
+        if (EPI == 0 && n < g.cnt) y_pt = g.ymap ? g.ymap[n] : n;
+      }
+      for (uint32_t b = 0; b < nsb && ok; b++, rctr++) {
+        const uint32_t rs = rctr % C::RS;
+        if (!mbar_wait(&raw_full[rs], (rctr / C::RS) & 1, ab)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* rw = raw + rs * raw_bytes + r * C::blk;
+        float d = 0.f, dmin = 0.f;
+        uint32_t scw[3] = {0, 0, 0};
+        if (valid) {
+          if (AK == Q4_K) {
+            const uint4 h = ld16<true>(rw);
+            d = h2f_bits(h.x);
+            dmin = h2f_bits(h.x >> 16);
+            scw[0] = h.y;
+            scw[1] = h.z;
+            scw[2] = h.w;
+          } else {
+            const __half* dv = reinterpret_cast<const __half*>(area + rs * area_bytes) + r * nsb;
+            d = __half2float(dv[b]);
+          }
+        }
+        dme[b * 128 + r] = d;
+        for (uint32_t c = 0; c < 4; c++, actr++) {
+          const uint32_t as = actr % C::AS;
+          if (actr >= C::AS && !mbar_wait(&a_empty[as], ((actr / C::AS) - 1) & 1, ab)) {
+            ok = false;
+            break;
+          }
+          uint8_t* A = ast + as * a_stage_bytes<AK>() + (r >> 3) * (C::kcsA * 128) + (r & 7) * 16;
+          if (AK == Q4_K) {
+            // qs bytes 32c + 16 part .. + 15: low nibbles = sub-block 2c, high nibbles = 2c + 1
+            uint32_t sc0 = 0, mn0 = 0, sc1 = 0, mn1 = 0;
+            scale_min(scw, 2 * c, &sc0, &mn0);
+            scale_min(scw, 2 * c + 1, &sc1, &mn1);
+            const uint4 q = valid ? ld16<true>(rw + 16 + 32 * c + 16 * part) : make_uint4(0, 0, 0, 0);
+            const __half2 s0 = __float2half2_rn((float)sc0), c0 = __float2half2_rn(-1024.f * (float)sc0);
+            const __half2 s1 = __float2half2_rn((float)sc1 * 0.0625f), c1 = __float2half2_rn(-64.f * (float)sc1);
+            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+            uint32_t lo[8], hi[8];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+              const uint32_t t0 = prmt(w[k], 0x64646464u, 0x4140u), t1 = prmt(w[k], 0x64646464u, 0x4342u);
+              lo[2 * k] = h2u(__hfma2(u2h(t0 & 0xff0fff0fu), s0, c0));
+              lo[2 * k + 1] = h2u(__hfma2(u2h(t1 & 0xff0fff0fu), s0, c0));
+              hi[2 * k] = h2u(__hfma2(u2h(t0 & 0xfff0fff0u), s1, c1));
+              hi[2 * k + 1] = h2u(__hfma2(u2h(t1 & 0xfff0fff0u), s1, c1));
+            }
+            if (!valid)
+#pragma unroll
+              for (int k = 0; k < 8; k++) lo[k] = hi[k] = 0;
+            *reinterpret_cast<uint4*>(A + (2 * part) * 128) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            *reinterpret_cast<uint4*>(A + (2 * part + 1) * 128) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+            *reinterpret_cast<uint4*>(A + (4 + 2 * part) * 128) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<uint4*>(A + (5 + 2 * part) * 128) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+            if (c == 3) {  // min block: dmin * mn_j * s_min for sub-blocks j = 4 part .. + 3, hi | lo
+              float v[4];
+#pragma unroll
+              for (int k = 0; k < 4; k++) {
+                uint32_t scx, mnx;
+                scale_min(scw, 4 * part + k, &scx, &mnx);
+                v[k] = valid ? dmin * (float)mnx * smin : 0.f;
+              }
+              uint32_t h0, l0, h1, l1;
+              split2(v[0], v[1], &h0, &l0);
+              split2(v[2], v[3], &h1, &l1);
+              *reinterpret_cast<uint2*>(A + 8 * 128 + 8 * part) = make_uint2(h0, h1);
+              *reinterpret_cast<uint2*>(A + 9 * 128 + 8 * part) = make_uint2(l0, l1);
+            }
+          } else {
+            // K step c of the super-block: half nh = c / 2, quarter qa = 2 (c % 2) + part (32 weights)
+            const uint32_t nh = c >> 1, qa = 2 * (c & 1) + part;
+            uint4 l0 = make_uint4(0, 0, 0, 0), l1 = l0, h0 = l0, h1 = l0;
+            uint32_t scb = 0;
+            if (valid) {
+              const uint8_t* ql = rw + 64 * nh + 32 * (qa & 1);
+              l0 = ld16<true>(ql);
+              l1 = ld16<true>(ql + 16);
+              h0 = ld16<true>(rw + 128 + 32 * nh);
+              h1 = ld16<true>(rw + 128 + 32 * nh + 16);
+              scb = *reinterpret_cast<const unsigned short*>(rw + 192 + 8 * nh + 2 * qa);
+            }
+            const uint32_t nsh = 4 * (qa >> 1), hsh = 2 * qa;
+            const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+            const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+            const __half2 m1056 = __float2half2_rn(-1056.f);
+#pragma unroll
+            for (int half16 = 0; half16 < 2; half16++) {  // weights 16 half16 .. + 15 share scale byte half16
+              const __half2 sv = __float2half2_rn((float)(int8_t)((scb >> (8 * half16)) & 0xff));
+              uint32_t ahi[8], alo[8];
+#pragma unroll
+              for (int k = 0; k < 4; k++) {
+                const uint32_t wl = lw[4 * half16 + k], wh = hw[4 * half16 + k];
+                const uint32_t hq = hsh <= 4 ? (wh << (4 - hsh)) : (wh >> (hsh - 4));
+                const uint32_t q = ((wl >> nsh) & 0x0f0f0f0fu) | (hq & 0x30303030u);
+                const __half2 u0 = __hadd2(u2h(prmt(q, 0x64646464u, 0x4140u)), m1056);
+                const __half2 u1 = __hadd2(u2h(prmt(q, 0x64646464u, 0x4342u)), m1056);
+                const __half2 p0 = __hmul2(u0, sv), p1 = __hmul2(u1, sv);
+                ahi[2 * k] = h2u(p0);
+                ahi[2 * k + 1] = h2u(p1);
+                alo[2 * k] = h2u(__hfma2(u0, sv, __hneg2(p0)));
+                alo[2 * k + 1] = h2u(__hfma2(u1, sv, __hneg2(p1)));
+              }
+              if (!valid)
+#pragma unroll
+                for (int k = 0; k < 8; k++) ahi[k] = alo[k] = 0;
+              const uint32_t ch = 4 * part + 2 * half16;  // chunks of this thread's 16 weights
+              uint8_t* Al = A + 128 * C::kcsA * 16;
+              *reinterpret_cast<uint4*>(A + ch * 128) = make_uint4(ahi[0], ahi[1], ahi[2], ahi[3]);
+              *reinterpret_cast<uint4*>(A + (ch + 1) * 128) = make_uint4(ahi[4], ahi[5], ahi[6], ahi[7]);
+              *reinterpret_cast<uint4*>(Al + ch * 128) = make_uint4(alo[0], alo[1], alo[2], alo[3]);
+              *reinterpret_cast<uint4*>(Al + (ch + 1) * 128) = make_uint4(alo[4], alo[5], alo[6], alo[7]);
+            }
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&a_full[as]);
+        }
+        if (!ok) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[rs]);
+      }
+      if (!ok) break;
+      // ---- epilogue: y[n][row] = (sum_b d_b acc_b + kmin acc_min) / hs_n ----
+      if (!mbar_wait(&acc_full, items & 1, ab)) {
+        ok = false;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      if (pt < it.N) {
+        hsv[pt] = 1.f / hs_pt;
+        ysv[pt] = y_pt;
+      }
+      if (!prod_sync(&psync, &pphase, ab)) {  // hsv, ysv of this item are written
+        ok = false;
+        break;
+      }
+      const uint32_t cols = it.N / 2, c0 = part * cols;
+      const float kmin = hasminA ? 32.f / smin : 0.f;
+      float* E = reinterpret_cast<float*>(ast);  // EPI 1: [128][NP + 1] (the A stages are consumed)
+      for (uint32_t cc = 0; cc < cols; cc += 8) {
+        float acc[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) acc[k] = 0.f;
+        const uint32_t taddr = tmem + ((quarter * 32) << 16) + c0 + cc, nacc = nsb + (hasminA ? 1 : 0);
+        for (uint32_t b0 = 0; b0 < nacc; b0 += 4) {  // up to 4 accumulators per wait
+          uint32_t v[4][8];
+#pragma unroll
+          for (uint32_t q = 0; q < 4; q++)
+            if (b0 + q < nacc)
+              asm volatile(
+                  "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                  : "=r"(v[q][0]), "=r"(v[q][1]), "=r"(v[q][2]), "=r"(v[q][3]), "=r"(v[q][4]), "=r"(v[q][5]),
+                    "=r"(v[q][6]), "=r"(v[q][7])
+                  : "r"(taddr + (b0 + q) * a.NP));
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+          for (uint32_t q = 0; q < 4; q++)
+            if (b0 + q < nacc) {
+              const float f = b0 + q < nsb ? dme[(b0 + q) * 128 + r] : kmin;
+#pragma unroll
+              for (int k = 0; k < 8; k++) acc[k] = fmaf(f, __uint_as_float(v[q][k]), acc[k]);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+          const uint32_t n = c0 + cc + k;
+          const float out = acc[k] * hsv[n];
+          if (EPI == 0) {
+            if (valid && n < it.nn) {
+              const uint64_t at = (uint64_t)ysv[n] * g.ystride + row;
+              g.y[at] = g.add ? __fadd_rn(g.add[at], out) : out;
+            }
+          } else {
+            E[r * (a.NP + 1) + n] = out;
+          }
+        }
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      if (EPI == 1) {
+        // SwiGLU of gate row j (tile rows 0-63) and up row j (64-127), into the next GEMM's image:
+        // K step `tile`, chunk j / 8, vector n (model.rs:259-274: g / (1 + exp(-g)) * u)
+        if (!prod_sync(&psync, &pphase, ab)) {
+          ok = false;
+          break;
+        }
+        const uint32_t h2 = a.img2_hasmin, row2 = 32 * kc_before(a.K2 / 64, h2), kcs2 = kcs_of(it.tile, h2);
+        uint8_t* gimg2 = a.img2 + (uint64_t)g.imgoff * row2 + (uint64_t)g.nimg * 32 * kc_before(it.tile, h2);
+        // with min chunks: this tile's two sub-block sums go to halves 2 (tile % 4) + {0, 1} of the
+        // min chunks of its super-block's last K step
+        uint8_t* gmin = a.img2 + (uint64_t)g.imgoff * row2 + (uint64_t)g.nimg * 32 * kc_before(it.tile | 3, h2);
+        for (uint32_t q = pt; q < it.N * 8; q += kProd) {
+          const uint32_t n = q >> 3, jc = q & 7;
+          float v[8];
+#pragma unroll
+          for (int k = 0; k < 8; k++) {
+            const uint32_t j = jc * 8 + k;
+            const float gg = E[j * (a.NP + 1) + n], uu = E[(64 + j) * (a.NP + 1) + n];
+            const bool ok_j = n < it.nn && it.tile * 64 + j < a.mats[g.mat].rows;  // (gate rows)
+            const float act = ok_j ? __fmul_rn(__fdiv_rn(gg, __fadd_rn(1.f, expf(-gg))), uu) : 0.f;
+            if (!(fabsf(act) < 65504.f)) atomicOr(a.err, 4u);  // outside the fp16 range of the image
+            v[k] = act;
+          }
+          uint32_t h[4], l[4];
+#pragma unroll
+          for (int k = 0; k < 4; k++) split2(v[2 * k], v[2 * k + 1], &h[k], &l[k]);
+          const uint32_t ng = it.n0 + n;
+          uint8_t* dst = gimg2 + (ng >> 3) * (kcs2 * 128) + jc * 128 + (ng & 7) * 16;
+          *reinterpret_cast<uint4*>(dst) = make_uint4(h[0], h[1], h[2], h[3]);
+          *reinterpret_cast<uint4*>(dst + (uint64_t)g.nimg * kcs2 * 16) = make_uint4(l[0], l[1], l[2], l[3]);
+          if (h2) {  // sums of 32 outputs: the 4 lanes jc = 4 sb .. 4 sb + 3 of vector n
+            float xs = 0.f;
+#pragma unroll
+            for (int k = 0; k < 8; k++) xs += v[k];
+            xs += __shfl_xor_sync(0xffffffffu, xs, 1);
+            xs += __shfl_xor_sync(0xffffffffu, xs, 2);
+            if ((jc & 3) == 0) {
+              const __half2 hh = __floats2half2_rn(-xs * 0.03125f, 0.f);
+              const float back = __low2float(hh);
+              const __half hl = __float2half_rn(-xs * 0.03125f - back);
+              const uint32_t pos = 2 * (it.tile & 3) + (jc >> 2);  // half index in the min chunks
+              uint8_t* m = gmin + (ng >> 3) * (10 * 128) + (ng & 7) * 16 + 2 * pos;
+              uint8_t* ml = m + (uint64_t)g.nimg * 10 * 16;
+              *reinterpret_cast<__half*>(m + 8 * 128) = __low2half(hh);
+              *reinterpret_cast<__half*>(m + 9 * 128) = __low2half(hh);
+              *reinterpret_cast<__half*>(ml + 8 * 128) = hl;
+              *reinterpret_cast<__half*>(ml + 9 * 128) = __float2half_rn(0.f);
+            }
+          }
+        }
+        if (!prod_sync(&psync, &pphase, ab)) {  // E (the A stages) is free again
+          ok = false;
+          break;
+        }
+      }
+    }
+  }
+  if (abort_flag && tid == 0) atomicOr(a.err, 2u);
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+}
+
+// ---- B image -----------------------------------------------------------------------------------
+// Image row i: the vector of source row src (x[src * xstride ..], K floats), optionally RMS-normalized
+// with weight w (ops.rs:3-15: x_i * (s * w_i)), times hs (a power of two: given per source row, or
+// chosen here from the row's largest |value| and written to hs_out[i]), as fp16 hi + lo.  Rows
+// without a source are zeros.  With min chunks, the last K step of each super-block carries the
+// sub-block sums: chunk 8 = chunk 9 = hi(-sum * 2^-5) in the hi plane, chunk 8 = lo(.), chunk 9 = 0
+// in the lo plane.
+__global__ void __launch_bounds__(256) k_qg_image(QgImageArgs a) {
+  __shared__ float red[32];
+  const uint32_t i = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
+  uint32_t src, imgoff, nimg;
+  if (a.rows) {
+    if (i >= *a.nrows) return;
+    const uint4 d = a.rows[i];
+    src = d.x;
+    imgoff = d.y;
+    nimg = d.z;
+  } else {
+    if (i >= ((a.T + 15) & ~15u)) return;
+    src = i < a.T ? (a.src ? a.src[i] : i) : kNone;
+    imgoff = 0;
+    nimg = (a.T + 15) & ~15u;
+  }
+  const uint32_t K = a.K, S = K / 64, n = i - imgoff, chunks = K / 8;
+  const uint32_t row_bytes = 32 * kc_before(S, a.hasmin);
+  uint8_t* base = a.img + (uint64_t)imgoff * row_bytes;
+  constexpr uint32_t kMaxPer = 4;  // chunks per thread (K <= 8192)
+  float v[kMaxPer][8];
+  const float* x = src != kNone ? a.x + (uint64_t)src * a.xstride : nullptr;
+#pragma unroll
+  for (uint32_t p = 0; p < kMaxPer; p++) {
+    const uint32_t t = tid + 256 * p;
+#pragma unroll
+    for (int k = 0; k < 8; k++) v[p][k] = (x && t < chunks) ? x[8 * t + k] : 0.f;
+  }
+  if (a.w) {  // RMSNorm
+    float ss = 0.f;
+#pragma unroll
+    for (uint32_t p = 0; p < kMaxPer; p++)
+#pragma unroll
+      for (int k = 0; k < 8; k++) ss = fmaf(v[p][k], v[p][k], ss);
+    ss = block_sum(ss, red);
+    const float s = 1.0f / sqrtf(ss / (float)K + a.eps);
+#pragma unroll
+    for (uint32_t p = 0; p < kMaxPer; p++) {
+      const uint32_t t = tid + 256 * p;
+#pragma unroll
+      for (int k = 0; k < 8; k++) v[p][k] = t < chunks ? __fmul_rn(v[p][k], __fmul_rn(s, a.w[8 * t + k])) : 0.f;
+    }
+  }
+  float hs;
+  if (a.hs_in) {
+    hs = src != kNone ? a.hs_in[src] : 1.f;
+  } else {
+    float mx = 0.f;
+#pragma unroll
+    for (uint32_t p = 0; p < kMaxPer; p++)
+#pragma unroll
+      for (int k = 0; k < 8; k++) mx = fmaxf(mx, fabsf(v[p][k]));
+    mx = warp_max(mx);
+    __syncthreads();
+    if (lane == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    mx = 0.f;
+    for (uint32_t w = 0; w < 8; w++) mx = fmaxf(mx, red[w]);
+    hs = qg_pow2_scale(mx);
+    if (tid == 0 && a.hs_out) a.hs_out[i] = hs;
+  }
+#pragma unroll
+  for (uint32_t p = 0; p < kMaxPer; p++) {
+    const uint32_t t = tid + 256 * p;
+    if (256 * p >= chunks) break;  // (block-uniform)
+    float xs = 0.f;
+    uint32_t h[4] = {0, 0, 0, 0}, l[4] = {0, 0, 0, 0};
+    if (t < chunks) {
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        v[p][k] *= hs;
+        xs += v[p][k];
+      }
+#pragma unroll
+      for (int k = 0; k < 4; k++) split2(v[p][2 * k], v[p][2 * k + 1], &h[k], &l[k]);
+      const uint32_t s = t >> 3, kc = t & 7, kcs = kcs_of(s, a.hasmin);
+      uint8_t* dst = base + (uint64_t)nimg * 32 * kc_before(s, a.hasmin) + (n >> 3) * kcs * 128 + kc * 128 + (n & 7) * 16;
+      *reinterpret_cast<uint4*>(dst) = make_uint4(h[0], h[1], h[2], h[3]);
+      *reinterpret_cast<uint4*>(dst + (uint64_t)nimg * kcs * 16) = make_uint4(l[0], l[1], l[2], l[3]);
+    }
+    if (a.hasmin) {  // sub-block sums: 4 chunks per sub-block, a warp per super-block (32 chunks)
+      xs += __shfl_xor_sync(0xffffffffu, xs, 1);
+      xs += __shfl_xor_sync(0xffffffffu, xs, 2);
+      float sj[8];
+#pragma unroll
+      for (int j = 0; j < 8; j++) sj[j] = -__shfl_sync(0xffffffffu, xs, 4 * j) * 0.03125f;
+      if (lane == 0 && t < chunks) {
+        uint32_t hh[4], ll[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) split2(sj[2 * k], sj[2 * k + 1], &hh[k], &ll[k]);
+        const uint32_t s = (t >> 3) | 3, kcs = 10;  // the super-block's last K step
+        uint8_t* dst = base + (uint64_t)nimg * 32 * kc_before(s, 1) + (n >> 3) * kcs * 128 + (n & 7) * 16;
+        uint8_t* dl = dst + (uint64_t)nimg * kcs * 16;
+        *reinterpret_cast<uint4*>(dst + 8 * 128) = make_uint4(hh[0], hh[1], hh[2], hh[3]);
+        *reinterpret_cast<uint4*>(dst + 9 * 128) = make_uint4(hh[0], hh[1], hh[2], hh[3]);
+        *reinterpret_cast<uint4*>(dl + 8 * 128) = make_uint4(ll[0], ll[1], ll[2], ll[3]);
+        *reinterpret_cast<uint4*>(dl + 9 * 128) = make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+}
+
+// Largest |dmin| over a Q4_K matrix (atomic max of the float bits).
+__global__ void k_qg_dmin(MatDesc m, uint32_t experts, uint32_t* out) {
+  const uint32_t blocks = m.cols / 256;
+  const uint64_t n = (uint64_t)experts * m.rows * blocks;
+  float mx = 0.f;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t e = (uint32_t)(i / ((uint64_t)m.rows * blocks)), rem = (uint32_t)(i % ((uint64_t)m.rows * blocks));
+    const uint8_t* b = row_ptr(m, expert_base(m, e), rem / blocks) + (rem % blocks) * 144;
+    const float dmin = fabsf(h2f_bits(b[2] | (b[3] << 8)));
+    if (isfinite(dmin)) mx = fmaxf(mx, dmin);
+  }
+  mx = warp_max(mx);
+  if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(mx));
+}
+
+}  // namespace
+
+const char* qgemm_supported(uint32_t kind, uint32_t cols) {
+  if (kind != Q4_K && kind != Q6_K) return "the tensor-core GEMM takes Q4_K and Q6_K rows";
+  if (cols % 256) return "the tensor-core GEMM needs a multiple of 256 columns";
+  const uint32_t acc = cols / 256 + (kind == Q4_K ? 1 : 0);
+  if (acc > 32 || cols > 8192) return "the tensor-core GEMM takes at most 8192 columns";
+  return nullptr;
+}
+
+uint64_t qg_image_row_bytes(uint32_t cols, bool hasmin) {
+  const uint64_t S = cols / 64;
+  return 32 * (8 * S + (hasmin ? 2 * (S / 4) : 0));
+}
+
+// Shared memory besides the B stages, and one B stage.
+static size_t qgemm_fixed(uint32_t kind, uint32_t cols, uint32_t np) {
+  const uint32_t nsb = cols / 256;
+  const size_t f = kind == Q4_K ? Cfg<Q4_K>::RS * 128 * Cfg<Q4_K>::blk + Cfg<Q4_K>::AS * a_stage_bytes<Q4_K>()
+                                : Cfg<Q6_K>::RS * 128 * Cfg<Q6_K>::blk + Cfg<Q6_K>::RS * 128 * nsb * 2 +
+                                      Cfg<Q6_K>::AS * a_stage_bytes<Q6_K>();
+  return f + 2 * nsb * 128 * 4 + 2 * np * 8;
+}
+static size_t qgemm_bstage(uint32_t np, bool img_hasmin) { return 2 * np * (img_hasmin ? 10 : 8) * 16; }
+
+size_t qgemm_smem(uint32_t kind, uint32_t cols, uint32_t np, uint32_t bs, bool img_hasmin) {
+  return qgemm_fixed(kind, cols, np) + bs * qgemm_bstage(np, img_hasmin);
+}
+
+static size_t g_qgemm_cap = 0;  // dynamic shared memory every GEMM kernel may use (set by qgemm_prepare)
+
+template <class F>
+static cudaError_t qgemm_attr(F* f, int optin, size_t* cap) {
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, f);
+  if (e != cudaSuccess) return e;
+  const int c = optin - (int)fa.sharedSizeBytes;
+  if (c <= 0) return cudaErrorInvalidValue;
+  e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, c);
+  if ((size_t)c < *cap) *cap = (size_t)c;
+  return e;
+}
+
+cudaError_t qgemm_prepare() {
+  int dev = 0, optin = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  size_t cap = ~(size_t)0;
+  if (e == cudaSuccess) e = qgemm_attr(k_qgemm<Q4_K, 0>, optin, &cap);
+  if (e == cudaSuccess) e = qgemm_attr(k_qgemm<Q4_K, 1>, optin, &cap);
+  if (e == cudaSuccess) e = qgemm_attr(k_qgemm<Q6_K, 0>, optin, &cap);
+  if (e == cudaSuccess) e = qgemm_attr(k_qgemm<Q6_K, 1>, optin, &cap);
+  if (e == cudaSuccess) g_qgemm_cap = cap;
+  return e;
+}
+
+size_t qgemm_smem_cap() { return g_qgemm_cap; }
+
+// Vectors per pass (NP) and B stages (BS): NP as large as the TMEM accumulators allow (one per
+// super-block, and the Q4_K min accumulator: at most 512 columns) up to 64, lowered while fewer than
+// 6 B stages fit beside the rest (B stages in flight hide the L2 latency of the activation image).
+const char* qgemm_shape(uint32_t kind, uint32_t cols, bool img_hasmin, uint32_t* np, uint32_t* bs) {
+  if (const char* why = qgemm_supported(kind, cols)) return why;
+  const uint32_t acc = cols / 256 + (kind == Q4_K ? 1 : 0);
+  uint32_t n = 512 / acc / 16 * 16;
+  n = n > 64 ? 64 : n;
+  const size_t cap = g_qgemm_cap;
+  for (;; n -= 16) {
+    const size_t fixed = qgemm_fixed(kind, cols, n);
+    const size_t b = fixed < cap ? (cap - fixed) / qgemm_bstage(n, img_hasmin) : 0;
+    if (b >= 6 || n == 16) {
+      if (b < 2) return "the tensor-core GEMM needs more shared memory than this device has";
+      *np = n;
+      *bs = b > kMaxBS ? kMaxBS : (uint32_t)b;
+      return nullptr;
+    }
+  }
+}
+
+
+
+void launch_qgemm(const QgArgs& a, uint32_t kind, bool swiglu, uint32_t grid, cudaStream_t s) {
+  const size_t smem = qgemm_smem(kind, a.K, a.NP, a.BS, a.img_hasmin != 0);
+  if (kind == Q4_K) {
+    if (swiglu) k_qgemm<Q4_K, 1><<<grid, kThreads, smem, s>>>(a);
+    else k_qgemm<Q4_K, 0><<<grid, kThreads, smem, s>>>(a);
+  } else {
+    if (swiglu) k_qgemm<Q6_K, 1><<<grid, kThreads, smem, s>>>(a);
+    else k_qgemm<Q6_K, 0><<<grid, kThreads, smem, s>>>(a);
+  }
+}
+
+void launch_qg_image(const QgImageArgs& a, uint32_t grid, cudaStream_t s) { k_qg_image<<<grid, 256, 0, s>>>(a); }
+
+void launch_qg_dmin(const MatDesc& m, uint32_t experts, uint32_t* out, cudaStream_t s) {
+  k_qg_dmin<<<296, 256, 0, s>>>(m, experts, out);
+}
+
+}  // namespace qc

@@ -88,7 +88,7 @@ def test_moe_layer_refusals(cuda_engine, tools):
     with pytest.raises(cuda_engine.QwenCudaError, match="path"):
         e.moe_layer(0, x, 3)
     q8 = tools.synth_gguf(tools.TINY.with_(kind_gate_up=tools.Q8_0))
-    with pytest.raises(cuda_engine.QwenCudaError, match="Q4_K gate/up"):
+    with pytest.raises(cuda_engine.QwenCudaError, match="takes Q4_K and Q6_K rows"):
         cuda_engine.Engine(q8, 16).moe_layer(0, x, 2)
     out, _ = cuda_engine.Engine(q8, 16).moe_layer(0, x, 1)  # the per-token kernels take any format
     assert out.shape == x.shape
