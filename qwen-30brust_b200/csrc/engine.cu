@@ -772,9 +772,9 @@ struct qc_engine {
     a.eps = cfg.eps;
     a.sms = sms;
     a.NPgu = a.NPdn = 16;
-    a.BSgu = a.BSdn = 2;
-    if (!qc::qgemm_shape(a.gate.kind, a.H, a.gate.kind == qc::Q4_K, &a.NPgu, &a.BSgu))
-      qc::qgemm_shape(a.down.kind, a.I, a.down.kind == qc::Q4_K, &a.NPdn, &a.BSdn);
+    a.ASgu = a.ASdn = a.BSgu = a.BSdn = 2;
+    if (!qc::qgemm_shape(a.gate.kind, a.H, a.gate.kind == qc::Q4_K, &a.NPgu, &a.ASgu, &a.BSgu))
+      qc::qgemm_shape(a.down.kind, a.I, a.down.kind == qc::Q4_K, &a.NPdn, &a.ASdn, &a.BSdn);
     const uint64_t P = (uint64_t)moe_cap * cfg.top, R = qc::moe_image_rows(moe_cap, cfg.top, cfg.experts);
     uint64_t o = 0;
     auto take = [&](uint64_t bytes) {
@@ -867,7 +867,7 @@ struct qc_engine {
       moe_scales(layer, a);
       QC_CK(cudaMemsetAsync(a.err, 0, 4, stream));
       QC_CK(cudaEventRecord(ev0, stream));
-      qc::launch_moe_tc(a, d_x, d_out, stream);
+      if (const char* why = qc::launch_moe_tc(a, d_x, d_out, stream)) throw ApiError(QC_ERR_CUDA, why);
       QC_CK(cudaGetLastError());
       QC_CK(cudaEventRecord(ev1, stream));
       uint32_t herr = 0;
@@ -1034,8 +1034,8 @@ struct qc_batch {
     const uint64_t o_tok = take(cap * sizeof(qc::BatchTok)), o_ids = take(cap * 4), o_osrc = take(cap * 4);
     // tensor-core projections where the formats allow
     auto tc_ok = [&](const qc::MatDesc& m) {
-      uint32_t np, bs;
-      return !qc::qgemm_shape(m.kind, m.cols, true, &np, &bs);
+      uint32_t np, as, bs;
+      return !qc::qgemm_shape(m.kind, m.cols, true, &np, &as, &bs);
     };
     tc.assign(4ull * c.layers, 0);
     tc_smin.assign(4ull * c.layers, 1.f);
@@ -1118,11 +1118,12 @@ struct qc_batch {
   void tc_project(const std::vector<TcOut>& outs, uint32_t T, uint32_t K) {
     if (outs.empty()) return;
     const uint32_t kind = outs[0].m->kind, nimg = (T + 15) & ~15u;
-    uint32_t NP = 16, BS = 2;
-    qc::qgemm_shape(kind, K, true, &NP, &BS);  // (checked when the batch was created)
+    uint32_t NP = 16, AS = 2, BS = 2;
+    qc::qgemm_shape(kind, K, true, &NP, &AS, &BS);  // (checked when the batch was created)
     qc::QgArgs q{};
     q.K = K;
     q.NP = NP;
+    q.AS = AS;
     q.BS = BS;
     q.img_hasmin = 1;
     q.img = d_img;
@@ -1137,6 +1138,8 @@ struct qc_batch {
     }
     q.ngroups = (uint32_t)outs.size();
     q.nitems = items;
+    for (size_t i = 0; i < outs.size(); i++)
+      if (const char* why = qc::qg_encode(q, (uint32_t)i, 1)) throw ApiError(QC_ERR_CUDA, why);
     qc::launch_qgemm(q, kind, false, std::min<uint32_t>(items, (uint32_t)e->sms), e->stream);
   }
 
@@ -1186,7 +1189,7 @@ struct qc_batch {
       qc::MoeArgs ma = e->moe_args(l, T);
       if (!qc::moe_tc_supported(ma)) {
         e->moe_scales(l, ma);  // (measured at creation: only reads the cached scales)
-        qc::launch_moe_tc(ma, d_x, d_x2, s);
+        if (const char* why = qc::launch_moe_tc(ma, d_x, d_x2, s)) throw ApiError(QC_ERR_CUDA, why);
         std::swap(d_x, d_x2);
       } else {
         for (uint32_t t = 0; t < T; t++) {

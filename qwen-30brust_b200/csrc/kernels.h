@@ -1,5 +1,6 @@
 // Kernel launch interface shared by the host engine (engine.cu) and the kernel files.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -145,7 +146,7 @@ struct MoeArgs {
   uint32_t H, I, E, top, T;
   float eps;
   float smin_g, smin_u, smin_d;  // Q4_K min-block scales of the tensor-core GEMM (qgemm.cu)
-  uint32_t NPgu, NPdn, BSgu, BSdn;  // vectors per GEMM pass and B stages (qgemm_shape)
+  uint32_t NPgu, NPdn, ASgu, ASdn, BSgu, BSdn;  // vectors per GEMM pass, A and B stages (qgemm_shape)
   int sms;
   // scratch
   float* h;          // [T][H] normalized inputs
@@ -169,7 +170,8 @@ const char* moe_tc_supported(const MoeArgs& a);
 // Rows of the activation images for T tokens (pairs rounded up to 16 per expert), at most.
 uint32_t moe_image_rows(uint32_t T, uint32_t top, uint32_t E);
 // x [T][H] -> out [T][H]: route, plan, tensor-core gate/up + SwiGLU, down, combine.
-void launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStream_t s);
+// (null, or why it could not launch)
+const char* launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStream_t s);
 // The per-token MoE kernels of the decode step (router, gate/up, down) on the vector c.x, in place.
 StepPlan plan_moe(const DecodeDims& d, const LayerDev& L, int sms);
 void launch_moe_token(const DecodeDims& d, const StepPlan& p, const LayerDev& L, const Scratch& c, DevState* st,
@@ -255,10 +257,12 @@ struct QgGroup {
   uint64_t ystride;
 };
 struct QgArgs {
+  CUtensorMap tmA[4];  // raw rows of mats[i] for the tensor-memory-access copies (qg_encode)
+  CUtensorMap tmD[4];  // Q6_K: the d values of mats[i]
   MatDesc mats[4];
   float smin[4];        // Q4_K: power-of-two scale of the min block (dmin * mn * smin < 2^14)
   uint32_t pair;        // pair mode (SwiGLU: gate rows then up rows of each 128-row tile)
-  uint32_t K, NP, BS;   // columns (a multiple of 256); vectors per pass; B stages (qgemm_shape)
+  uint32_t K, NP, AS, BS;  // columns (a multiple of 256); vectors per pass; A and B stages (qgemm_shape)
   uint32_t img_hasmin;  // the image carries the Q4_K min chunks
   const uint8_t* img;
   const float* hs;
@@ -294,11 +298,13 @@ __host__ __device__ inline float qg_pow2_scale(float maxabs) {  // 2^k with maxa
   return ldexpf(1.f, 14 - ex);
 }
 const char* qgemm_supported(uint32_t kind, uint32_t cols);
+// The tensor maps of q.mats[i] (an expert stack of `experts` matrices), for q.pair's tile shape.
+const char* qg_encode(QgArgs& q, uint32_t i, uint32_t experts);
 // Vectors per pass and B stages of a GEMM over `cols` columns of `kind` rows (after qgemm_prepare),
 // or the reason it cannot run.
-const char* qgemm_shape(uint32_t kind, uint32_t cols, bool img_hasmin, uint32_t* np, uint32_t* bs);
+const char* qgemm_shape(uint32_t kind, uint32_t cols, bool img_hasmin, uint32_t* np, uint32_t* as, uint32_t* bs);
 uint64_t qg_image_row_bytes(uint32_t cols, bool hasmin);
-size_t qgemm_smem(uint32_t kind, uint32_t cols, uint32_t np, uint32_t bs, bool img_hasmin);
+size_t qgemm_smem(uint32_t kind, uint32_t cols, uint32_t np, uint32_t as, uint32_t bs, bool img_hasmin);
 cudaError_t qgemm_prepare();  // once per device
 size_t qgemm_smem_cap();      // dynamic shared memory available to the GEMM kernels (after qgemm_prepare)
 void launch_qgemm(const QgArgs& a, uint32_t kind, bool swiglu, uint32_t grid, cudaStream_t s);

@@ -173,9 +173,9 @@ const char* moe_tc_supported(const MoeArgs& a) {
   if (a.I % 64) return "the tensor-core MoE path needs an intermediate size in multiples of 64";
   if (a.router.kind != F16) return "the batched MoE path takes an F16 router";
   if (a.E > 1024) return "the batched MoE path takes at most 1024 experts";
-  uint32_t np, bs;
-  if (const char* why = qgemm_shape(a.gate.kind, a.H, a.gate.kind == Q4_K, &np, &bs)) return why;
-  if (const char* why = qgemm_shape(a.down.kind, a.I, a.down.kind == Q4_K, &np, &bs)) return why;
+  uint32_t np, as, bs;
+  if (const char* why = qgemm_shape(a.gate.kind, a.H, a.gate.kind == Q4_K, &np, &as, &bs)) return why;
+  if (const char* why = qgemm_shape(a.down.kind, a.I, a.down.kind == Q4_K, &np, &as, &bs)) return why;
   return nullptr;
 }
 
@@ -184,7 +184,7 @@ uint32_t moe_image_rows(uint32_t T, uint32_t top, uint32_t E) {
   return P + 15 * (E < P ? E : P);
 }
 
-void launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStream_t s) {
+const char* launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStream_t s) {
   const uint32_t rmax = moe_image_rows(a.T, a.top, a.E);
   k_moe_route<<<a.T, 256, a.H * sizeof(float), s>>>(a, x);
   k_moe_plan<<<1, 1024, 0, s>>>(a);
@@ -206,6 +206,7 @@ void launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStream_t s)
   g.pair = 1;
   g.K = a.H;
   g.NP = a.NPgu;
+  g.AS = a.ASgu;
   g.BS = a.BSgu;
   g.img_hasmin = a.gate.kind == Q4_K;
   g.img = a.img_gu;
@@ -217,12 +218,15 @@ void launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStream_t s)
   g.K2 = a.I;
   g.img2_hasmin = a.down.kind == Q4_K;
   g.err = a.err;
+  for (uint32_t i = 0; i < 2; i++)
+    if (const char* why = qg_encode(g, i, a.E)) return why;
   launch_qgemm(g, a.gate.kind, true, a.sms, s);
   QgArgs d{};
   d.mats[0] = a.down;
   d.smin[0] = a.smin_d;
   d.K = a.I;
   d.NP = a.NPdn;
+  d.AS = a.ASdn;
   d.BS = a.BSdn;
   d.img_hasmin = a.down.kind == Q4_K;
   d.img = a.img_dn;
@@ -230,8 +234,10 @@ void launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStream_t s)
   d.ngroups = a.E;
   d.nitems_dev = a.nitems + 1;
   d.err = a.err;
+  if (const char* why = qg_encode(d, 0, a.E)) return why;
   launch_qgemm(d, a.down.kind, false, a.sms, s);
   k_moe_combine<<<a.T, 256, 0, s>>>(a, x, out);
+  return nullptr;
 }
 
 }  // namespace qc

@@ -26,6 +26,9 @@
 // error bit, the others stop at their next wait, and copies and MMAs in flight are drained before the
 // accumulator is released.
 #include <cuda_fp16.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
 
 #include "kernels.h"
 
@@ -42,13 +45,13 @@ template <int AK>
 struct Cfg;
 template <>
 struct Cfg<Q4_K> {
-  static constexpr uint32_t blk = 144, RS = 3, AS = 2, planes = 1, kcsA = 10;
+  static constexpr uint32_t blk = 144, RS = 3, planes = 1, kcsA = 10;
 };
 template <>
 struct Cfg<Q6_K> {
-  static constexpr uint32_t blk = 208, RS = 3, AS = 2, planes = 2, kcsA = 8;
+  static constexpr uint32_t blk = 208, RS = 3, planes = 2, kcsA = 8;
 };
-constexpr uint32_t kMaxBS = 8;  // B stages (runtime count a.BS: as many as fit)
+constexpr uint32_t kMaxAS = 6, kMaxBS = 8;  // A and B stages (runtime counts a.AS, a.BS: qgemm_shape)
 template <int AK>
 constexpr uint32_t a_stage_bytes() {
   return Cfg<AK>::planes * 128 * Cfg<AK>::kcsA * 16;
@@ -68,6 +71,21 @@ QC_DEV void mbar_arrive(uint64_t* m) {
 }
 QC_DEV void mbar_expect(uint64_t* m, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(m)), "r"(bytes) : "memory");
+}
+// Tiled tensor copies (no multicast): box at (x, y[, z]) of the map into shared memory.
+QC_DEV void tma2d(void* dst, const CUtensorMap* map, uint32_t x, uint32_t y, uint64_t* m) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(m))
+      : "memory");
+}
+QC_DEV void tma3d(void* dst, const CUtensorMap* map, uint32_t x, uint32_t y, uint32_t z, uint64_t* m) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(m))
+      : "memory");
 }
 QC_DEV void bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* m) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -116,11 +134,19 @@ QC_DEV unsigned long long sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
   return (unsigned long long)((addr >> 4) & 0x3fff) | ((unsigned long long)((lbo >> 4) & 0x3fff) << 16) |
          ((unsigned long long)((sbo >> 4) & 0x3fff) << 32) | (1ull << 46);
 }
-QC_DEV void mma(uint32_t d, unsigned long long a, unsigned long long b, uint32_t idesc, uint32_t acc) {
+// D (+)= A B: mma_first overwrites D, mma_acc adds to it.
+QC_DEV void mma_first(uint32_t d, unsigned long long a, unsigned long long b, uint32_t idesc) {
   asm volatile(
-      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "{\n.reg .pred p;\nsetp.ne.b32 p, 0, 0;\n"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      "l"(a), "l"(b), "r"(idesc)
+      : "memory");
+}
+QC_DEV void mma_acc(uint32_t d, unsigned long long a, unsigned long long b, uint32_t idesc) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.eq.b32 p, 0, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc)
       : "memory");
 }
 QC_DEV void mma_commit(uint64_t* m) {
@@ -223,10 +249,12 @@ QC_DEV uint32_t kcs_of(uint32_t s, uint32_t hasmin) { return 8 + ((hasmin && (s 
 QC_DEV uint32_t kc_before(uint32_t s, uint32_t hasmin) { return 8 * s + (hasmin ? 2 * (s >> 2) : 0); }
 
 template <int AK, int EPI>
-__global__ void __launch_bounds__(kThreads, 1) k_qgemm(QgArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) k_qgemm(const __grid_constant__ QgArgs a) {
   using C = Cfg<AK>;
-  extern __shared__ __align__(1024) uint8_t sm[];
-  __shared__ __align__(8) uint64_t raw_full[C::RS], raw_empty[C::RS], a_full[C::AS], a_empty[C::AS], b_full[kMaxBS],
+  extern __shared__ __align__(1024) uint8_t sm_raw[];
+  // (tensor copies want 128-byte aligned destinations: the carve-up starts at a 1024-byte boundary)
+  uint8_t* sm = sm_raw + ((1024 - (smem_u32(sm_raw) & 1023)) & 1023);
+  __shared__ __align__(8) uint64_t raw_full[C::RS], raw_empty[C::RS], a_full[kMaxAS], a_empty[kMaxAS], b_full[kMaxBS],
       b_empty[kMaxBS], acc_full, psync;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
@@ -242,7 +270,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(QgArgs a) {
   uint8_t* area = raw + C::RS * raw_bytes;  // Q6_K: d values of the tile's rows, one copy per raw slot
   const uint32_t area_bytes = AK == Q6_K ? 128 * nsb * 2 : 0;
   uint8_t* ast = area + C::RS * area_bytes;
-  uint8_t* bst = ast + C::AS * a_stage_bytes<AK>();
+  const uint32_t AS = a.AS;
+  uint8_t* bst = ast + AS * a_stage_bytes<AK>();
   const uint32_t BS = a.BS;
   float* dsm = reinterpret_cast<float*>(bst + BS * b_bytes);  // [part][nsb][128] d of each row
   float* hsm = dsm + 2 * nsb * 128;                              // [2][NP] 1 / scale of each vector
@@ -261,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(QgArgs a) {
       mbar_init(&raw_full[i], 1);
       mbar_init(&raw_empty[i], kProd / 32);
     }
-    for (uint32_t i = 0; i < C::AS; i++) {
+    for (uint32_t i = 0; i < AS; i++) {
       mbar_init(&a_full[i], kProd / 32);
       mbar_init(&a_empty[i], 1);
     }
@@ -295,26 +324,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(QgArgs a) {
           break;
         }
         uint8_t* dst = raw + slot * raw_bytes;
-        uint32_t v0, v1;
-        tile_rows(a, it.mat, it.tile, &v0, &v1);
-        uint32_t bytes = (v0 + v1) * C::blk;
-        const bool with_area = AK == Q6_K;  // (the d values of all the tile's super-blocks, every stage)
-        if (with_area) bytes += ((v0 + 7) / 8 + (v1 + 7) / 8) * 16 * nsb;
-        if (lane == 0) mbar_expect(&raw_full[slot], bytes);
-        __syncwarp();
-        for (uint32_t r = lane; r < 128; r += 32) {
-          uint32_t mi, row;
-          if (tile_row(a, it.mat, it.tile, r, &mi, &row)) {
-            const MatDesc& m = a.mats[mi];
-            bulk_copy(dst + r * C::blk, row_ptr(m, expert_base(m, it.e), row) + b * C::blk, C::blk, &raw_full[slot]);
-          }
-        }
-        if (with_area && lane < 16) {  // the 8 rows' d values of 8-row group `lane`
-          uint32_t mi, row;
-          if (tile_row(a, it.mat, it.tile, lane * 8, &mi, &row)) {
-            const MatDesc& m = a.mats[mi];
-            const uint8_t* src = expert_base(m, it.e) + (uint64_t)(row >> 3) * m.group_bytes + 8 * m.main_bytes;
-            bulk_copy(area + slot * area_bytes + lane * 16 * nsb, src, 16 * nsb, &raw_full[slot]);
+        if (lane == 0) {  // whole boxes: 128 rows of super-block b (rows past the tensor read as zeros)
+          const uint32_t halves = a.pair ? 2 : 1, hr = 128 / halves;
+          mbar_expect(&raw_full[slot], 128 * C::blk + (AK == Q6_K ? 128 * 2 * nsb : 0));
+          for (uint32_t h = 0; h < halves; h++) {
+            const uint32_t mi = it.mat + h, groups = (a.mats[mi].rows + 7) / 8;
+            if (AK == Q4_K) {
+              tma2d(dst + h * hr * C::blk, &a.tmA[mi], b * C::blk, (it.e * groups + it.tile * (hr / 8)) * 8,
+                    &raw_full[slot]);
+            } else {
+              const uint32_t z = it.e * groups + it.tile * (hr / 8);
+              tma3d(dst + h * hr * C::blk, &a.tmA[mi], b * C::blk, 0, z, &raw_full[slot]);
+              tma2d(area + slot * area_bytes + h * hr * 2 * nsb, &a.tmD[mi], 0, z, &raw_full[slot]);
+            }
           }
         }
       }
@@ -362,40 +384,37 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(QgArgs a) {
       for (uint32_t i = blockIdx.x; i < nitems && ok; i += gridDim.x, items++) {
         const ItemDesc it = nx;
         if (i + gridDim.x < nitems) nx = load_item(a, g0, i + gridDim.x);
-        // f32 accumulator, f16 A and B, both K-major, N, M = 128
-        const uint32_t idesc = (1u << 4) | ((it.N >> 3) << 17) | ((128u >> 4) << 24);
+        // f32 accumulator, f16 A and B, both K-major, M = 128, N = 2 x the pass's vectors: the B stage
+        // holds the hi plane then the lo plane of the vectors, so one MMA multiplies A by both (columns
+        // 0 .. N-1: hi, N .. 2N-1: lo; the epilogue adds the halves)
+        const uint32_t idesc = (1u << 4) | (((2 * it.N) >> 3) << 17) | ((128u >> 4) << 24);
         for (uint32_t s = 0; s < S; s++, actr++, bctr++) {
-          const uint32_t as = actr % C::AS, bs = bctr % BS;
-          if (!mbar_wait(&a_full[as], (actr / C::AS) & 1, ab) || !mbar_wait(&b_full[bs], (bctr / BS) & 1, ab)) {
+          const uint32_t as = actr % AS, bs = bctr % BS;
+          if (!mbar_wait(&a_full[as], (actr / AS) & 1, ab) || !mbar_wait(&b_full[bs], (bctr / BS) & 1, ab)) {
             ok = false;
             break;
           }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const uint32_t sb = s >> 2, kcsB_s = kcs_of(s, a.img_hasmin);
-          const uint32_t aaddr = smem_u32(ast + as * a_stage_bytes<AK>()), baddr = smem_u32(bst + bs * b_bytes);
-          const uint32_t bplane = it.N * kcsB_s * 16, sboA = C::kcsA * 128, sboB = kcsB_s * 128;
-          const uint32_t dcol = tmem + sb * NP;
-#pragma unroll
-          for (uint32_t j = 0; j < 4; j++) {
-            const unsigned long long bh = sdesc(baddr + j * 256, 128, sboB), bl = sdesc(baddr + bplane + j * 256, 128, sboB);
-            const uint32_t acc = ((s & 3) == 0 && j == 0) ? 0u : 1u;
-            if (AK == Q4_K) {
-              const unsigned long long ad = sdesc(aaddr + j * 256, 128, sboA);
-              mma(dcol, ad, bh, idesc, acc);
-              mma(dcol, ad, bl, idesc, 1);
-            } else {
-              const unsigned long long ah = sdesc(aaddr + j * 256, 128, sboA),
-                                       al = sdesc(aaddr + 128 * C::kcsA * 16 + j * 256, 128, sboA);
-              mma(dcol, ah, bh, idesc, acc);
-              mma(dcol, ah, bl, idesc, 1);
-              mma(dcol, al, bh, idesc, 1);
-            }
+          // descriptors of the stage; a K = 16 step is two 16-byte chunks further: +256 bytes (16 units)
+          const unsigned long long ad = sdesc(smem_u32(ast + as * a_stage_bytes<AK>()), 128, C::kcsA * 128);
+          const unsigned long long bd = sdesc(smem_u32(bst + bs * b_bytes), 128, kcsB_s * 128);
+          const uint32_t dcol = tmem + sb * 2 * NP;
+          if ((s & 3) == 0) mma_first(dcol, ad, bd, idesc);
+          else mma_acc(dcol, ad, bd, idesc);
+          mma_acc(dcol, ad + 16, bd + 16, idesc);
+          mma_acc(dcol, ad + 32, bd + 32, idesc);
+          mma_acc(dcol, ad + 48, bd + 48, idesc);
+          if (AK == Q6_K) {  // the lo plane of A, 128 x 8 chunks further
+            const unsigned long long al = ad + (128 * C::kcsA * 16 >> 4);
+            mma_acc(dcol, al, bd, idesc);
+            mma_acc(dcol, al + 16, bd + 16, idesc);
+            mma_acc(dcol, al + 32, bd + 32, idesc);
+            mma_acc(dcol, al + 48, bd + 48, idesc);
           }
           if (hasminA && (s & 3) == 3) {  // the min term of super-block sb: chunks 8, 9
-            const unsigned long long ad = sdesc(aaddr + 4 * 256, 128, sboA), bh = sdesc(baddr + 4 * 256, 128, sboB),
-                                     bl = sdesc(baddr + bplane + 4 * 256, 128, sboB);
-            mma(tmem + nsb * NP, ad, bh, idesc, sb == 0 ? 0u : 1u);
-            mma(tmem + nsb * NP, ad, bl, idesc, 1);
+            if (sb == 0) mma_first(tmem + nsb * 2 * NP, ad + 64, bd + 64, idesc);
+            else mma_acc(tmem + nsb * 2 * NP, ad + 64, bd + 64, idesc);
           }
           mma_commit(&a_empty[as]);
           mma_commit(&b_empty[bs]);
@@ -439,62 +458,69 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(QgArgs a) {
           break;
         }
         const uint8_t* rw = raw + rs * raw_bytes + r * C::blk;
+        // per super-block: the row's block header and all of this thread's bytes of the 4 K steps
         float d = 0.f, dmin = 0.f;
-        uint32_t scw[3] = {0, 0, 0};
-        if (valid) {
-          if (AK == Q4_K) {
-            const uint4 h = ld16<true>(rw);
-            d = h2f_bits(h.x);
-            dmin = h2f_bits(h.x >> 16);
-            scw[0] = h.y;
-            scw[1] = h.z;
-            scw[2] = h.w;
+        uint32_t sc03 = 0, sc47 = 0, mnp = 0;  // Q4_K: 6-bit scales of sub-blocks 0-3, 4-7; mins of 4 part..
+        uint4 qv[4];                          // Q4_K: qs bytes 32 c + 16 part.  Q6_K: ql, ql + 16, qh, qh + 16
+        if (AK == Q4_K) {
+          uint4 h = make_uint4(0, 0, 0, 0);
+          if (valid) {
+            h = ld16<true>(rw);
+#pragma unroll
+            for (int c = 0; c < 4; c++) qv[c] = ld16<true>(rw + 16 + 32 * c + 16 * part);
           } else {
+#pragma unroll
+            for (int c = 0; c < 4; c++) qv[c] = make_uint4(0, 0, 0, 0);
+          }
+          d = h2f_bits(h.x);
+          dmin = h2f_bits(h.x >> 16);
+          // quant.rs get_scale_min_k4, four sub-blocks per word: bytes s[0..11] = h.y, h.z, h.w
+          sc03 = h.y & 0x3f3f3f3fu;
+          sc47 = (h.w & 0x0f0f0f0fu) | ((h.y >> 2) & 0x30303030u);
+          mnp = part == 0 ? (h.z & 0x3f3f3f3fu) : (((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u));
+        } else {
+          if (valid) {
             const __half* dv = reinterpret_cast<const __half*>(area + rs * area_bytes) + r * nsb;
             d = __half2float(dv[b]);
           }
         }
         dme[b * 128 + r] = d;
-        for (uint32_t c = 0; c < 4; c++, actr++) {
-          const uint32_t as = actr % C::AS;
-          if (actr >= C::AS && !mbar_wait(&a_empty[as], ((actr / C::AS) - 1) & 1, ab)) {
+#pragma unroll
+        for (uint32_t c = 0; c < 4; c++) {
+          const uint32_t as = actr % AS;
+          if (actr >= AS && !mbar_wait(&a_empty[as], ((actr / AS) - 1) & 1, ab)) {
             ok = false;
             break;
           }
           uint8_t* A = ast + as * a_stage_bytes<AK>() + (r >> 3) * (C::kcsA * 128) + (r & 7) * 16;
           if (AK == Q4_K) {
-            // qs bytes 32c + 16 part .. + 15: low nibbles = sub-block 2c, high nibbles = 2c + 1
-            uint32_t sc0 = 0, mn0 = 0, sc1 = 0, mn1 = 0;
-            scale_min(scw, 2 * c, &sc0, &mn0);
-            scale_min(scw, 2 * c + 1, &sc1, &mn1);
-            const uint4 q = valid ? ld16<true>(rw + 16 + 32 * c + 16 * part) : make_uint4(0, 0, 0, 0);
-            const __half2 s0 = __float2half2_rn((float)sc0), c0 = __float2half2_rn(-1024.f * (float)sc0);
-            const __half2 s1 = __float2half2_rn((float)sc1 * 0.0625f), c1 = __float2half2_rn(-64.f * (float)sc1);
-            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+            // low nibbles = sub-block 2c (weight sc * q), high nibbles = 2c + 1: 1024 + 16 q as fp16, times
+            // sc / 16, minus 64 sc (exact: the results are integers below 2^10)
+            const uint32_t scw = c < 2 ? sc03 : sc47, sh = 16 * (c & 1);
+            const __half2 one024 = __float2half2_rn(1024.f);
+            const __half2 s0 = __hsub2(u2h(prmt(scw >> sh, 0x64646464u, 0x4040u)), one024);  // (sc, sc)
+            const __half2 s1 = __hsub2(u2h(prmt(scw >> sh, 0x64646464u, 0x4141u)), one024);
+            const __half2 c0 = __hmul2(s0, __float2half2_rn(-1024.f));
+            const __half2 s1q = __hmul2(s1, __float2half2_rn(0.0625f)), c1 = __hmul2(s1, __float2half2_rn(-64.f));
+            const uint32_t w[4] = {qv[c].x, qv[c].y, qv[c].z, qv[c].w};
             uint32_t lo[8], hi[8];
 #pragma unroll
             for (int k = 0; k < 4; k++) {
               const uint32_t t0 = prmt(w[k], 0x64646464u, 0x4140u), t1 = prmt(w[k], 0x64646464u, 0x4342u);
               lo[2 * k] = h2u(__hfma2(u2h(t0 & 0xff0fff0fu), s0, c0));
               lo[2 * k + 1] = h2u(__hfma2(u2h(t1 & 0xff0fff0fu), s0, c0));
-              hi[2 * k] = h2u(__hfma2(u2h(t0 & 0xfff0fff0u), s1, c1));
-              hi[2 * k + 1] = h2u(__hfma2(u2h(t1 & 0xfff0fff0u), s1, c1));
+              hi[2 * k] = h2u(__hfma2(u2h(t0 & 0xfff0fff0u), s1q, c1));
+              hi[2 * k + 1] = h2u(__hfma2(u2h(t1 & 0xfff0fff0u), s1q, c1));
             }
-            if (!valid)
-#pragma unroll
-              for (int k = 0; k < 8; k++) lo[k] = hi[k] = 0;
             *reinterpret_cast<uint4*>(A + (2 * part) * 128) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
             *reinterpret_cast<uint4*>(A + (2 * part + 1) * 128) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
             *reinterpret_cast<uint4*>(A + (4 + 2 * part) * 128) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
             *reinterpret_cast<uint4*>(A + (5 + 2 * part) * 128) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
             if (c == 3) {  // min block: dmin * mn_j * s_min for sub-blocks j = 4 part .. + 3, hi | lo
+              const float ds = dmin * smin;
               float v[4];
 #pragma unroll
-              for (int k = 0; k < 4; k++) {
-                uint32_t scx, mnx;
-                scale_min(scw, 4 * part + k, &scx, &mnx);
-                v[k] = valid ? dmin * (float)mnx * smin : 0.f;
-              }
+              for (int k = 0; k < 4; k++) v[k] = ds * (float)((mnp >> (8 * k)) & 0xffu);
               uint32_t h0, l0, h1, l1;
               split2(v[0], v[1], &h0, &l0);
               split2(v[2], v[3], &h1, &l1);
@@ -504,19 +530,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(QgArgs a) {
           } else {
             // K step c of the super-block: half nh = c / 2, quarter qa = 2 (c % 2) + part (32 weights)
             const uint32_t nh = c >> 1, qa = 2 * (c & 1) + part;
-            uint4 l0 = make_uint4(0, 0, 0, 0), l1 = l0, h0 = l0, h1 = l0;
-            uint32_t scb = 0;
-            if (valid) {
-              const uint8_t* ql = rw + 64 * nh + 32 * (qa & 1);
-              l0 = ld16<true>(ql);
-              l1 = ld16<true>(ql + 16);
-              h0 = ld16<true>(rw + 128 + 32 * nh);
-              h1 = ld16<true>(rw + 128 + 32 * nh + 16);
-              scb = *reinterpret_cast<const unsigned short*>(rw + 192 + 8 * nh + 2 * qa);
+            if ((c & 1) == 0) {  // ql and qh bytes shared by K steps c and c + 1
+              if (valid) {
+                const uint8_t* ql = rw + 64 * nh + 32 * part;
+                qv[0] = ld16<true>(ql);
+                qv[1] = ld16<true>(ql + 16);
+                qv[2] = ld16<true>(rw + 128 + 32 * nh);
+                qv[3] = ld16<true>(rw + 128 + 32 * nh + 16);
+              } else {
+#pragma unroll
+                for (int q = 0; q < 4; q++) qv[q] = make_uint4(0, 0, 0, 0);
+              }
             }
-            const uint32_t nsh = 4 * (qa >> 1), hsh = 2 * qa;
-            const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
-            const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+            uint32_t scb = 0;
+            if (valid) scb = *reinterpret_cast<const unsigned short*>(rw + 192 + 8 * nh + 2 * qa);
+            const uint32_t nsh = 4 * (c & 1), hsh = 2 * qa;
+            const uint32_t lw[8] = {qv[0].x, qv[0].y, qv[0].z, qv[0].w, qv[1].x, qv[1].y, qv[1].z, qv[1].w};
+            const uint32_t hw[8] = {qv[2].x, qv[2].y, qv[2].z, qv[2].w, qv[3].x, qv[3].y, qv[3].z, qv[3].w};
             const __half2 m1056 = __float2half2_rn(-1056.f);
 #pragma unroll
             for (int half16 = 0; half16 < 2; half16++) {  // weights 16 half16 .. + 15 share scale byte half16
@@ -535,9 +565,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(QgArgs a) {
                 alo[2 * k] = h2u(__hfma2(u0, sv, __hneg2(p0)));
                 alo[2 * k + 1] = h2u(__hfma2(u1, sv, __hneg2(p1)));
               }
-              if (!valid)
-#pragma unroll
-                for (int k = 0; k < 8; k++) ahi[k] = alo[k] = 0;
               const uint32_t ch = 4 * part + 2 * half16;  // chunks of this thread's 16 weights
               uint8_t* Al = A + 128 * C::kcsA * 16;
               *reinterpret_cast<uint4*>(A + ch * 128) = make_uint4(ahi[0], ahi[1], ahi[2], ahi[3]);
@@ -549,6 +576,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(QgArgs a) {
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
           if (lane == 0) mbar_arrive(&a_full[as]);
+          actr++;
         }
         if (!ok) break;
         __syncwarp();
@@ -569,35 +597,37 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(QgArgs a) {
         ok = false;
         break;
       }
-      const uint32_t cols = it.N / 2, c0 = part * cols;
+      const uint32_t cols = it.N / 2, c0 = part * cols;  // (N a multiple of 8)
       const float kmin = hasminA ? 32.f / smin : 0.f;
       float* E = reinterpret_cast<float*>(ast);  // EPI 1: [128][NP + 1] (the A stages are consumed)
-      for (uint32_t cc = 0; cc < cols; cc += 8) {
-        float acc[8];
-#pragma unroll
-        for (int k = 0; k < 8; k++) acc[k] = 0.f;
+      for (uint32_t cc = 0; cc < cols; cc += 4) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
         const uint32_t taddr = tmem + ((quarter * 32) << 16) + c0 + cc, nacc = nsb + (hasminA ? 1 : 0);
-        for (uint32_t b0 = 0; b0 < nacc; b0 += 4) {  // up to 4 accumulators per wait
+        for (uint32_t b0 = 0; b0 < nacc; b0 += 4) {  // up to 4 accumulators (hi and lo halves) per wait
           uint32_t v[4][8];
 #pragma unroll
           for (uint32_t q = 0; q < 4; q++)
-            if (b0 + q < nacc)
-              asm volatile(
-                  "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                  : "=r"(v[q][0]), "=r"(v[q][1]), "=r"(v[q][2]), "=r"(v[q][3]), "=r"(v[q][4]), "=r"(v[q][5]),
-                    "=r"(v[q][6]), "=r"(v[q][7])
-                  : "r"(taddr + (b0 + q) * a.NP));
+            if (b0 + q < nacc) {
+              const uint32_t t = taddr + (b0 + q) * 2 * a.NP;
+              asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(v[q][0]), "=r"(v[q][1]), "=r"(v[q][2]), "=r"(v[q][3])
+                           : "r"(t));
+              asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(v[q][4]), "=r"(v[q][5]), "=r"(v[q][6]), "=r"(v[q][7])
+                           : "r"(t + it.N));
+            }
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
           for (uint32_t q = 0; q < 4; q++)
             if (b0 + q < nacc) {
               const float f = b0 + q < nsb ? dme[(b0 + q) * 128 + r] : kmin;
 #pragma unroll
-              for (int k = 0; k < 8; k++) acc[k] = fmaf(f, __uint_as_float(v[q][k]), acc[k]);
+              for (int k = 0; k < 4; k++)
+                acc[k] = fmaf(f, __uint_as_float(v[q][k]) + __uint_as_float(v[q][4 + k]), acc[k]);
             }
         }
 #pragma unroll
-        for (int k = 0; k < 8; k++) {
+        for (int k = 0; k < 4; k++) {
           const uint32_t n = c0 + cc + k;
           const float out = acc[k] * hsv[n];
           if (EPI == 0) {
@@ -807,7 +837,49 @@ const char* qgemm_supported(uint32_t kind, uint32_t cols) {
   if (cols % 256) return "the tensor-core GEMM needs a multiple of 256 columns";
   const uint32_t acc = cols / 256 + (kind == Q4_K ? 1 : 0);
   if (acc > 32 || cols > 8192) return "the tensor-core GEMM takes at most 8192 columns";
+  if (kind == Q6_K && cols > 4096) return "the tensor-core GEMM takes at most 4096 columns of Q6_K rows";
   return nullptr;
+}
+
+// Raw rows as tensors of bytes: Q4_K rows are evenly spaced (an expert stack is one 2-D tensor of
+// experts * rows_padded rows); Q6_K rows come in groups of 8 followed by their d values, so the rows
+// are a 3-D tensor (bytes, row in group, group) and the d values a 2-D one (bytes, group).
+const char* qg_encode(QgArgs& q, uint32_t i, uint32_t experts) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (!encode) return "cuTensorMapEncodeTiled is not available";
+  const MatDesc& m = q.mats[i];
+  const uint64_t groups = (uint64_t)experts * ((m.rows + 7) / 8);
+  const uint32_t box_groups = q.pair ? 8 : 16;
+  CUresult r;
+  if (m.kind == Q4_K) {
+    const cuuint64_t dims[2] = {m.main_bytes, groups * 8}, strides[1] = {m.main_bytes};
+    const cuuint32_t box[2] = {144, box_groups * 8}, es[2] = {1, 1};
+    r = encode(&q.tmA[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(m.w), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    const cuuint64_t dims[3] = {m.main_bytes, 8, groups}, strides[2] = {m.main_bytes, m.group_bytes};
+    const cuuint32_t box[3] = {208, 8, box_groups}, es[3] = {1, 1, 1};
+    r = encode(&q.tmA[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(m.w), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r == CUDA_SUCCESS) {
+      const cuuint64_t ddims[2] = {8ull * m.d_bytes, groups}, dstr[1] = {m.group_bytes};
+      const cuuint32_t dbox[2] = {8 * m.d_bytes, box_groups}, des[2] = {1, 1};
+      r = encode(&q.tmD[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(m.w + 8ull * m.main_bytes), ddims,
+                 dstr, dbox, des, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                 CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
+  }
+  return r == CUDA_SUCCESS ? nullptr : "cuTensorMapEncodeTiled refused a weight matrix";
 }
 
 uint64_t qg_image_row_bytes(uint32_t cols, bool hasmin) {
@@ -815,18 +887,18 @@ uint64_t qg_image_row_bytes(uint32_t cols, bool hasmin) {
   return 32 * (8 * S + (hasmin ? 2 * (S / 4) : 0));
 }
 
-// Shared memory besides the B stages, and one B stage.
+// Shared memory besides the A and B stages, one A stage, one B stage.
 static size_t qgemm_fixed(uint32_t kind, uint32_t cols, uint32_t np) {
-  const uint32_t nsb = cols / 256;
-  const size_t f = kind == Q4_K ? Cfg<Q4_K>::RS * 128 * Cfg<Q4_K>::blk + Cfg<Q4_K>::AS * a_stage_bytes<Q4_K>()
-                                : Cfg<Q6_K>::RS * 128 * Cfg<Q6_K>::blk + Cfg<Q6_K>::RS * 128 * nsb * 2 +
-                                      Cfg<Q6_K>::AS * a_stage_bytes<Q6_K>();
-  return f + 2 * nsb * 128 * 4 + 2 * np * 8;
+  const uint32_t nsb = cols / 256;  // (+ 1 KB: the carve-up is aligned to 1 KB)
+  const size_t f = kind == Q4_K ? Cfg<Q4_K>::RS * 128 * Cfg<Q4_K>::blk
+                                : Cfg<Q6_K>::RS * 128 * Cfg<Q6_K>::blk + Cfg<Q6_K>::RS * 128 * nsb * 2;
+  return f + 2 * nsb * 128 * 4 + 2 * np * 8 + 1024;
 }
+static size_t qgemm_astage(uint32_t kind) { return kind == Q4_K ? a_stage_bytes<Q4_K>() : a_stage_bytes<Q6_K>(); }
 static size_t qgemm_bstage(uint32_t np, bool img_hasmin) { return 2 * np * (img_hasmin ? 10 : 8) * 16; }
 
-size_t qgemm_smem(uint32_t kind, uint32_t cols, uint32_t np, uint32_t bs, bool img_hasmin) {
-  return qgemm_fixed(kind, cols, np) + bs * qgemm_bstage(np, img_hasmin);
+size_t qgemm_smem(uint32_t kind, uint32_t cols, uint32_t np, uint32_t as, uint32_t bs, bool img_hasmin) {
+  return qgemm_fixed(kind, cols, np) + as * qgemm_astage(kind) + bs * qgemm_bstage(np, img_hasmin);
 }
 
 static size_t g_qgemm_cap = 0;  // dynamic shared memory every GEMM kernel may use (set by qgemm_prepare)
@@ -858,31 +930,39 @@ cudaError_t qgemm_prepare() {
 
 size_t qgemm_smem_cap() { return g_qgemm_cap; }
 
-// Vectors per pass (NP) and B stages (BS): NP as large as the TMEM accumulators allow (one per
-// super-block, and the Q4_K min accumulator: at most 512 columns) up to 64, lowered while fewer than
-// 6 B stages fit beside the rest (B stages in flight hide the L2 latency of the activation image).
-const char* qgemm_shape(uint32_t kind, uint32_t cols, bool img_hasmin, uint32_t* np, uint32_t* bs) {
+// Vectors per pass (NP), A stages (AS) and B stages (BS).  NP: as large as the TMEM accumulators
+// allow (one per super-block and the Q4_K min accumulator, 2 NP columns each: at most 512), up to 64,
+// a multiple of 8.  Then the
+// stages: in flight, they hide the latency of the MMAs (A) and of the activation image in L2 (B);
+// up to 4 A stages and 8 B stages, at least 3 and 4, NP lowered until they fit.
+const char* qgemm_shape(uint32_t kind, uint32_t cols, bool img_hasmin, uint32_t* np, uint32_t* as, uint32_t* bs) {
   if (const char* why = qgemm_supported(kind, cols)) return why;
   const uint32_t acc = cols / 256 + (kind == Q4_K ? 1 : 0);
-  uint32_t n = 512 / acc / 16 * 16;
+  uint32_t n = 512 / (2 * acc) / 8 * 8;  // (each accumulator: 2 n columns)
   n = n > 64 ? 64 : n;
-  const size_t cap = g_qgemm_cap;
-  for (;; n -= 16) {
-    const size_t fixed = qgemm_fixed(kind, cols, n);
-    const size_t b = fixed < cap ? (cap - fixed) / qgemm_bstage(n, img_hasmin) : 0;
-    if (b >= 6 || n == 16) {
-      if (b < 2) return "the tensor-core GEMM needs more shared memory than this device has";
-      *np = n;
-      *bs = b > kMaxBS ? kMaxBS : (uint32_t)b;
-      return nullptr;
+  if (n < 8) return "the tensor-core GEMM takes at most 4096 columns of Q4_K rows";
+  const size_t cap = g_qgemm_cap, sa = qgemm_astage(kind);
+  for (;; n -= 8) {
+    const size_t fixed = qgemm_fixed(kind, cols, n), sb = qgemm_bstage(n, img_hasmin);
+    for (uint32_t a = 4; a >= 2; a--) {
+      if (fixed + a * sa >= cap) continue;
+      const size_t b = (cap - fixed - a * sa) / sb;
+      if ((a >= 3 && b >= 4) || n == 8) {
+        if (b < 2) continue;
+        *np = n;
+        *as = a;
+        *bs = b > kMaxBS ? kMaxBS : (uint32_t)b;
+        return nullptr;
+      }
     }
+    if (n == 8) return "the tensor-core GEMM needs more shared memory than this device has";
   }
 }
 
 
 
 void launch_qgemm(const QgArgs& a, uint32_t kind, bool swiglu, uint32_t grid, cudaStream_t s) {
-  const size_t smem = qgemm_smem(kind, a.K, a.NP, a.BS, a.img_hasmin != 0);
+  const size_t smem = qgemm_smem(kind, a.K, a.NP, a.AS, a.BS, a.img_hasmin != 0);
   if (kind == Q4_K) {
     if (swiglu) k_qgemm<Q4_K, 1><<<grid, kThreads, smem, s>>>(a);
     else k_qgemm<Q4_K, 0><<<grid, kThreads, smem, s>>>(a);
