@@ -259,6 +259,7 @@ struct qc_engine {
     cudaFree(d_peers);
     cudaFree(d_ll);
     cudaFree(d_moe);
+    cudaFree(d_gemm);
     cudaFree(d_layers);
     if (own) cudaStreamDestroy(own);
   }
@@ -751,6 +752,44 @@ struct qc_engine {
     stats.matvec_ms += ms;
   }
 
+  // ---- the tensor-core GEMM's copy of the weights ---------------------------------------------
+  uint8_t* d_gemm = nullptr;
+  std::vector<qc::GemmMat> gemm;  // per layer: q, k, v, o, gate, up, down; then the output matrix (w null: none)
+
+  // The GEMM-layout copy of every Q4_K / Q6_K matrix the tensor-core paths read (batched projections,
+  // grouped experts, vocabulary rows), made once, on first use: each (64-row tile, super-block) block
+  // contiguous, so that a GEMM stage is two bulk copies.
+  void ensure_gemm() {
+    if (d_gemm) return;
+    QC_CK(cudaSetDevice(device));
+    const uint32_t L = cfg.layers;
+    std::vector<std::pair<const qc::MatDesc*, uint32_t>> mats;
+    for (uint32_t l = 0; l < L; l++) {
+      const qc::LayerDev& d = layers[l];
+      for (const qc::MatDesc* m : {&d.q, &d.k, &d.v, &d.o}) mats.push_back({m, 1u});
+      for (const qc::MatDesc* m : {&d.gate, &d.up, &d.down}) mats.push_back({m, e_n});
+    }
+    mats.push_back({&out, 1u});
+    std::vector<uint64_t> off(mats.size(), ~0ull);
+    uint64_t total = 0;
+    for (size_t i = 0; i < mats.size(); i++)
+      if (!qc::qgemm_supported(mats[i].first->kind, mats[i].first->cols)) {
+        off[i] = total;
+        total = align256(total + qc::gemm_bytes(*mats[i].first, mats[i].second));
+      }
+    gemm.assign(mats.size(), qc::GemmMat{});
+    if (total == 0) return;
+    QC_CK(cudaMalloc(&d_gemm, total));
+    for (size_t i = 0; i < mats.size(); i++)
+      if (off[i] != ~0ull) {
+        gemm[i] = qc::gemm_mat(*mats[i].first, d_gemm + off[i]);
+        qc::launch_qg_relayout(*mats[i].first, mats[i].second, gemm[i], stream);
+      }
+    QC_CK(cudaGetLastError());
+    QC_CK(cudaStreamSynchronize(stream));
+  }
+  const qc::GemmMat& gm(uint32_t layer, uint32_t which) const { return gemm[7 * layer + which]; }
+
   // ---- the MoE half of one layer for a batch of tokens --------------------------------------
   uint8_t* d_moe = nullptr;  // scratch of moe_cap tokens
   uint32_t moe_cap = 0;
@@ -763,6 +802,11 @@ struct qc_engine {
     a.gate = L.gate;
     a.up = L.up;
     a.down = L.down;
+    if (!gemm.empty()) {
+      a.ggate = gm(layer, 4);
+      a.gup = gm(layer, 5);
+      a.gdown = gm(layer, 6);
+    }
     a.ffn_norm = L.ffn_norm;
     a.H = cfg.hidden;
     a.I = cfg.intermediate;
@@ -784,6 +828,7 @@ struct qc_engine {
     };
     a.h = reinterpret_cast<float*>(take((uint64_t)moe_cap * cfg.hidden * 4));
     a.hscale = reinterpret_cast<float*>(take(moe_cap * 4));
+    a.rlg = reinterpret_cast<float*>(take((uint64_t)moe_cap * cfg.experts * 4));
     a.sel = reinterpret_cast<uint32_t*>(take(P * 4));
     a.selw = reinterpret_cast<float*>(take(P * 4));
     a.cnt = reinterpret_cast<uint32_t*>(take(cfg.experts * 4));
@@ -805,7 +850,7 @@ struct qc_engine {
     const uint64_t P = (uint64_t)cap * cfg.top, R = qc::moe_image_rows(cap, cfg.top, cfg.experts);
     auto al = [](uint64_t b) { return align256(b); };
     // (an upper bound: image rows are sized for Q4_K min chunks whatever the layer's formats)
-    return al((uint64_t)cap * cfg.hidden * 4) + al(cap * 4) + 2 * al(P * 4) + 2 * al(cfg.experts * 4) +
+    return al((uint64_t)cap * cfg.hidden * 4) + al(cap * 4) + al((uint64_t)cap * cfg.experts * 4) + 2 * al(P * 4) + 2 * al(cfg.experts * 4) +
            2 * al(P * 4) + al(2ull * cfg.experts * sizeof(qc::QgGroup)) + al(8) + al(R * 16) + al(4) +
            al(R * qc::qg_image_row_bytes(cfg.hidden, true)) + al(R * qc::qg_image_row_bytes(cfg.intermediate, true)) +
            al(P * cfg.hidden * 4) + al(4) + 2 * al((uint64_t)cap * cfg.hidden * 4);
@@ -856,6 +901,7 @@ struct qc_engine {
     ensure(path == 1 || path == 2, "MoE path must be 1 (per-token kernels) or 2 (tensor cores)");
     ensure(ep_world == 1, "an expert-parallel engine holds only its own experts");
     QC_CK(cudaSetDevice(device));
+    if (path == 2) ensure_gemm();
     grow_moe(T);
     qc::MoeArgs a = moe_args(layer, T);
     const uint64_t xbytes = (uint64_t)T * cfg.hidden * 4;
@@ -1058,6 +1104,7 @@ struct qc_batch {
                    o_img = take((uint64_t)((cap + 15) & ~15u) * img_row), o_hs = take(((cap + 15) & ~15u) * 4);
     QC_CK(cudaMalloc(&d_buf, o));
     QC_CK(cudaMemsetAsync(d_buf, 0, o, e->stream));
+    e->ensure_gemm();
     e->grow_moe(cap);
     for (uint32_t l = 0; l < c.layers; l++) {  // the tensor-core weight scales of every layer, once
       qc::MoeArgs ma = e->moe_args(l, cap);
@@ -1108,7 +1155,7 @@ struct qc_batch {
     qc::launch_qg_image(ia, (T + 15) & ~15u, e->stream);
   }
   struct TcOut {
-    const qc::MatDesc* m;
+    const qc::GemmMat* m;
     float smin;
     float* y;
     const float* add;
@@ -1138,8 +1185,6 @@ struct qc_batch {
     }
     q.ngroups = (uint32_t)outs.size();
     q.nitems = items;
-    for (size_t i = 0; i < outs.size(); i++)
-      if (const char* why = qc::qg_encode(q, (uint32_t)i, 1)) throw ApiError(QC_ERR_CUDA, why);
     qc::launch_qgemm(q, kind, false, std::min<uint32_t>(items, (uint32_t)e->sms), e->stream);
   }
 
@@ -1163,7 +1208,8 @@ struct qc_batch {
         for (uint32_t kind : {(uint32_t)qc::Q4_K, (uint32_t)qc::Q6_K}) {
           std::vector<TcOut> outs;
           for (int i = 0; i < 3; i++)
-            if (t4[i] && m[i]->kind == kind) outs.push_back(TcOut{m[i], tc_smin[4 * l + i], y[i], nullptr, st[i]});
+            if (t4[i] && m[i]->kind == kind)
+              outs.push_back(TcOut{&e->gm(l, i), tc_smin[4 * l + i], y[i], nullptr, st[i]});
           tc_project(outs, T, H);
         }
       }
@@ -1179,7 +1225,7 @@ struct qc_batch {
       qc::launch_batch_attention(ba, l, d_q, d_a, T, s);
       if (t4[3]) {  // x += W_o attn (model.rs:245-248)
         tc_image(d_a, nullptr, T, QD, nullptr);
-        tc_project({TcOut{&L.o, tc_smin[4 * l + 3], d_x, d_x, H}}, T, QD);
+        tc_project({TcOut{&e->gm(l, 3), tc_smin[4 * l + 3], d_x, d_x, H}}, T, QD);
       } else {
         const uint32_t xbO = qc::xview_bytes(L.o.units, qc::uses_float_x(L.o.kind));
         qc::launch_batch_stage(d_a, nullptr, T, QD, L.o.units, qc::uses_float_x(L.o.kind), nullptr, 0.f, d_xv, xbO, s);
@@ -1203,7 +1249,7 @@ struct qc_batch {
     if (n_out) {  // model.rs:289-301: output norm, vocabulary rows, finiteness
       if (tc_out) {
         tc_image(d_x, d_osrc, n_out, H, e->out_norm);
-        tc_project({TcOut{&e->out, tc_out_smin, d_lg, nullptr, c.vocab}}, n_out, H);
+        tc_project({TcOut{&e->gemm.back(), tc_out_smin, d_lg, nullptr, c.vocab}}, n_out, H);
       } else {
         const bool flV = qc::uses_float_x(e->out.kind);
         const uint32_t xbV = qc::xview_bytes(e->out.units, flV);

@@ -1,6 +1,5 @@
 // Kernel launch interface shared by the host engine (engine.cu) and the kernel files.
 #pragma once
-#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -138,10 +137,40 @@ const char* plan_token(const StepArgs& a, int max_smem, TokenPlan* p);
 void launch_token(const StepArgs& a, const TokenPlan& p, unsigned long long* ll, bool cooperative, cudaStream_t s);
 cudaError_t token_prepare(int max_smem);
 
+// A matrix (or expert stack) in the tensor-core GEMM's layout: 64-row tiles, a tile's super-blocks
+// back to back, each (tile, super-block) one contiguous block of its 64 rows, Q4_K [64][144] or Q6_K
+// [64][208] followed by the 64 rows' f16 d values, so that a GEMM stage is two contiguous copies.
+// Rows past `rows` are zeros.
+struct GemmMat {
+  const uint8_t* w;
+  uint32_t kind, rows, cols;
+  uint32_t tiles;           // ceil(rows / 64)
+  uint32_t blockb;          // bytes of one (tile, super-block) block
+  uint64_t tile_bytes;      // cols / 256 blocks
+  uint64_t expert_stride;   // tiles * tile_bytes
+};
+inline GemmMat gemm_mat(const MatDesc& m, const uint8_t* w) {
+  GemmMat g{};
+  g.w = w;
+  g.kind = m.kind;
+  g.rows = m.rows;
+  g.cols = m.cols;
+  g.tiles = (m.rows + 63) / 64;
+  g.blockb = 64 * (m.kind == Q4_K ? 144 : 210);
+  g.tile_bytes = (uint64_t)(m.cols / 256) * g.blockb;
+  g.expert_stride = g.tiles * g.tile_bytes;
+  return g;
+}
+// Device bytes of an expert stack in the GEMM layout.
+inline uint64_t gemm_bytes(const MatDesc& m, uint32_t experts) { return (uint64_t)experts * gemm_mat(m, nullptr).expert_stride; }
+// src (engine layout, `experts` matrices) -> dst (GEMM layout, dst.w sized by gemm_bytes).
+void launch_qg_relayout(const MatDesc& src, uint32_t experts, const GemmMat& dst, cudaStream_t s);
+
 // The MoE half of one layer for a batch of tokens (moe.cu).
 struct QgGroup;
 struct MoeArgs {
   MatDesc router, gate, up, down;  // one layer's router and expert stacks, device layout
+  GemmMat ggate, gup, gdown;       // the expert stacks in the GEMM layout
   const float* ffn_norm;
   uint32_t H, I, E, top, T;
   float eps;
@@ -151,6 +180,7 @@ struct MoeArgs {
   // scratch
   float* h;          // [T][H] normalized inputs
   float* hscale;     // [T] power-of-two scale of each token's h
+  float* rlg;        // [T][E] router logits
   uint32_t* sel;     // [T][top] selected experts, selection order
   float* selw;       // [T][top] their weights
   uint32_t* cnt;     // [E] pairs per expert
@@ -257,9 +287,7 @@ struct QgGroup {
   uint64_t ystride;
 };
 struct QgArgs {
-  CUtensorMap tmA[4];  // raw rows of mats[i] for the tensor-memory-access copies (qg_encode)
-  CUtensorMap tmD[4];  // Q6_K: the d values of mats[i]
-  MatDesc mats[4];
+  GemmMat mats[4];
   float smin[4];        // Q4_K: power-of-two scale of the min block (dmin * mn * smin < 2^14)
   uint32_t pair;        // pair mode (SwiGLU: gate rows then up rows of each 128-row tile)
   uint32_t K, NP, AS, BS;  // columns (a multiple of 256); vectors per pass; A and B stages (qgemm_shape)
@@ -298,8 +326,6 @@ __host__ __device__ inline float qg_pow2_scale(float maxabs) {  // 2^k with maxa
   return ldexpf(1.f, 14 - ex);
 }
 const char* qgemm_supported(uint32_t kind, uint32_t cols);
-// The tensor maps of q.mats[i] (an expert stack of `experts` matrices), for q.pair's tile shape.
-const char* qg_encode(QgArgs& q, uint32_t i, uint32_t experts);
 // Vectors per pass and B stages of a GEMM over `cols` columns of `kind` rows (after qgemm_prepare),
 // or the reason it cannot run.
 const char* qgemm_shape(uint32_t kind, uint32_t cols, bool img_hasmin, uint32_t* np, uint32_t* as, uint32_t* bs);

@@ -22,11 +22,13 @@ namespace qc {
 namespace {
 
 // ---- per-token routing ---------------------------------------------------------------------
+// Block (t, g): RMSNorm of token t (every block of the token computes it; block g = 0 keeps it, with
+// its power-of-two scale), then the router logits of experts 16 g .. 16 g + 15 into rlg[t][e].
+constexpr uint32_t kRouteRows = 16;
 __global__ void __launch_bounds__(256) k_moe_route(MoeArgs a, const float* __restrict__ x) {
   __shared__ float red[32];
-  __shared__ float lg[1024];
   extern __shared__ __align__(16) float hsm[];  // [H] the normalized input, for the router rows
-  const uint32_t t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t t = blockIdx.x, g = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float* xr = x + (uint64_t)t * a.H;
   float ss = 0.f;
   for (uint32_t i = tid; i < a.H; i += 256) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
@@ -37,7 +39,7 @@ __global__ void __launch_bounds__(256) k_moe_route(MoeArgs a, const float* __res
   float mx = 0.f;
   for (uint32_t i = tid; i < a.H; i += 256) {
     const float v = __fmul_rn(xr[i], __fmul_rn(s, a.ffn_norm[i]));
-    hr[i] = v;
+    if (g == 0) hr[i] = v;
     hsm[i] = v;
     mx = fmaxf(mx, fabsf(v));
   }
@@ -45,13 +47,14 @@ __global__ void __launch_bounds__(256) k_moe_route(MoeArgs a, const float* __res
   __syncthreads();
   if (lane == 0) red[warp] = mx;
   __syncthreads();
-  if (tid == 0) {
+  if (tid == 0 && g == 0) {
     float m = 0.f;
     for (int w = 0; w < 8; w++) m = fmaxf(m, red[w]);
     a.hscale[t] = qg_pow2_scale(m);
   }
   // router logits: one warp per expert row (F16), 16-byte loads of 8 weights per lane
-  for (uint32_t e = warp; e < a.E; e += 8) {
+  const uint32_t e1 = min(a.E, (g + 1) * kRouteRows);
+  for (uint32_t e = g * kRouteRows + warp; e < e1; e += 8) {
     const uint4* wr = reinterpret_cast<const uint4*>(row_ptr(a.router, a.router.w, e));
     float acc = 0.f, acc2 = 0.f;
     for (uint32_t c = lane; c < a.H / 8; c += 32) {
@@ -72,13 +75,20 @@ __global__ void __launch_bounds__(256) k_moe_route(MoeArgs a, const float* __res
     }
     acc = warp_sum(acc + acc2);
     if (lane == 0) {
-      lg[e] = acc;
+      a.rlg[(uint64_t)t * a.E + e] = acc;
       if (!isfinite(acc)) atomicOr(a.err, 1u);
     }
   }
+}
+
+// Token t: the rank of each logit (ties to the lower index) gives the selection in order, then
+// ops.rs:29-44 (softmax) over the kept logits in selection order.
+__global__ void __launch_bounds__(128) k_moe_select(MoeArgs a) {
+  __shared__ float lg[1024];
+  const uint32_t t = blockIdx.x, tid = threadIdx.x;
+  for (uint32_t e = tid; e < a.E; e += 128) lg[e] = a.rlg[(uint64_t)t * a.E + e];
   __syncthreads();
-  // rank of each logit (ties to the lower index); the top ranks are the selection, in order
-  for (uint32_t e = tid; e < a.E; e += 256) {
+  for (uint32_t e = tid; e < a.E; e += 128) {
     const uint32_t ke = total_key_u(lg[e]);
     uint32_t rank = 0;
     for (uint32_t j = 0; j < a.E; j++) {
@@ -88,7 +98,7 @@ __global__ void __launch_bounds__(256) k_moe_route(MoeArgs a, const float* __res
     if (rank < a.top) a.sel[(uint64_t)t * a.top + rank] = e;
   }
   __syncthreads();
-  if (tid == 0) {  // ops.rs:29-44 over the kept logits, in selection order
+  if (tid == 0) {
     const uint32_t* sl = a.sel + (uint64_t)t * a.top;
     float* w = a.selw + (uint64_t)t * a.top;
     float m = -INFINITY;
@@ -135,19 +145,21 @@ __global__ void __launch_bounds__(1024) k_moe_plan(MoeArgs a) {
     a.groups[e] = QgGroup{igu[e], cnt[e], n, img[e], 0, e, nullptr, nullptr, nullptr, a.ptok + off[e], 0};
     a.groups[a.E + e] = QgGroup{idn[e], cnt[e], n, img[e], 0, e, a.y, nullptr, a.ppair + off[e], nullptr, a.H};
   }
+  // (the order of an expert's pairs does not change any result: each is its own GEMM column; the
+  // loop above handles expert e in the same thread, so the count can be reset here)
+  for (uint32_t e = tid; e < a.E; e += 1024) cnt[e] = 0;
+  __syncthreads();
   for (uint32_t p = tid; p < P; p += 1024) {
     const uint32_t e = a.sel[p];
-    uint32_t before = 0;
-    for (uint32_t q = 0; q < p; q++) before += a.sel[q] == e;
-    const uint32_t pos = off[e] + before;
+    const uint32_t pos = off[e] + atomicAdd(&cnt[e], 1u);
     a.ptok[pos] = p / a.top;
     a.ppair[pos] = p;
   }
   __syncthreads();
   for (uint32_t e = warp; e < a.E; e += 32) {  // image rows: source token, or none past the pairs
-    const uint32_t n = (cnt[e] + 15) & ~15u;
+    const uint32_t c = off[e + 1] - off[e], n = (c + 15) & ~15u;
     for (uint32_t i = lane; i < n; i += 32)
-      a.imgrows[img[e] + i] = make_uint4(i < cnt[e] ? a.ptok[off[e] + i] : 0xffffffffu, img[e], n, 0);
+      a.imgrows[img[e] + i] = make_uint4(i < c ? a.ptok[off[e] + i] : 0xffffffffu, img[e], n, 0);
   }
 }
 
@@ -173,6 +185,7 @@ const char* moe_tc_supported(const MoeArgs& a) {
   if (a.I % 64) return "the tensor-core MoE path needs an intermediate size in multiples of 64";
   if (a.router.kind != F16) return "the batched MoE path takes an F16 router";
   if (a.E > 1024) return "the batched MoE path takes at most 1024 experts";
+  if (!a.ggate.w || !a.gup.w || !a.gdown.w) return "the GEMM-layout copy of the experts is missing";
   uint32_t np, as, bs;
   if (const char* why = qgemm_shape(a.gate.kind, a.H, a.gate.kind == Q4_K, &np, &as, &bs)) return why;
   if (const char* why = qgemm_shape(a.down.kind, a.I, a.down.kind == Q4_K, &np, &as, &bs)) return why;
@@ -186,7 +199,8 @@ uint32_t moe_image_rows(uint32_t T, uint32_t top, uint32_t E) {
 
 const char* launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStream_t s) {
   const uint32_t rmax = moe_image_rows(a.T, a.top, a.E);
-  k_moe_route<<<a.T, 256, a.H * sizeof(float), s>>>(a, x);
+  k_moe_route<<<dim3(a.T, (a.E + kRouteRows - 1) / kRouteRows), 256, a.H * sizeof(float), s>>>(a, x);
+  k_moe_select<<<a.T, 128, 0, s>>>(a);
   k_moe_plan<<<1, 1024, 0, s>>>(a);
   QgImageArgs ia{};
   ia.x = a.h;
@@ -199,8 +213,8 @@ const char* launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStre
   ia.img = a.img_gu;
   launch_qg_image(ia, rmax, s);
   QgArgs g{};
-  g.mats[0] = a.gate;
-  g.mats[1] = a.up;
+  g.mats[0] = a.ggate;
+  g.mats[1] = a.gup;
   g.smin[0] = a.smin_g;
   g.smin[1] = a.smin_u;
   g.pair = 1;
@@ -218,11 +232,9 @@ const char* launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStre
   g.K2 = a.I;
   g.img2_hasmin = a.down.kind == Q4_K;
   g.err = a.err;
-  for (uint32_t i = 0; i < 2; i++)
-    if (const char* why = qg_encode(g, i, a.E)) return why;
   launch_qgemm(g, a.gate.kind, true, a.sms, s);
   QgArgs d{};
-  d.mats[0] = a.down;
+  d.mats[0] = a.gdown;
   d.smin[0] = a.smin_d;
   d.K = a.I;
   d.NP = a.NPdn;
@@ -234,7 +246,6 @@ const char* launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStre
   d.ngroups = a.E;
   d.nitems_dev = a.nitems + 1;
   d.err = a.err;
-  if (const char* why = qg_encode(d, 0, a.E)) return why;
   launch_qgemm(d, a.down.kind, false, a.sms, s);
   k_moe_combine<<<a.T, 256, 0, s>>>(a, x, out);
   return nullptr;

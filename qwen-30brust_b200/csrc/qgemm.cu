@@ -26,9 +26,6 @@
 // error bit, the others stop at their next wait, and copies and MMAs in flight are drained before the
 // accumulator is released.
 #include <cuda_fp16.h>
-#include <cudaTypedefs.h>
-
-#include <mutex>
 
 #include "kernels.h"
 
@@ -72,21 +69,6 @@ QC_DEV void mbar_arrive(uint64_t* m) {
 QC_DEV void mbar_expect(uint64_t* m, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(m)), "r"(bytes) : "memory");
 }
-// Tiled tensor copies (no multicast): box at (x, y[, z]) of the map into shared memory.
-QC_DEV void tma2d(void* dst, const CUtensorMap* map, uint32_t x, uint32_t y, uint64_t* m) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(m))
-      : "memory");
-}
-QC_DEV void tma3d(void* dst, const CUtensorMap* map, uint32_t x, uint32_t y, uint32_t z, uint64_t* m) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(m))
-      : "memory");
-}
 QC_DEV void bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* m) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                    smem_u32(dst)),
@@ -94,8 +76,18 @@ QC_DEV void bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* m) {
                : "memory");
 }
 // Wait (at most 2 s, or until another role gave up) for the phase with the given parity.
+QC_DEV bool mbar_try(uint32_t a, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(a), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 QC_DEV bool mbar_wait(uint64_t* m, uint32_t parity, volatile int* abort_flag) {
   const uint32_t a = smem_u32(m);
+  if (mbar_try(a, parity)) return true;  // (the common case: no clock read)
   const unsigned long long t0 = now_ns();
   for (uint32_t i = 0;; i++) {
     uint32_t ok;
@@ -114,6 +106,17 @@ QC_DEV bool mbar_wait(uint64_t* m, uint32_t parity, volatile int* abort_flag) {
     }
   }
 }
+// A ring of n stages: the slot and phase parity of the current use, advanced without division.
+struct Ring {
+  uint32_t n, slot, phase;
+  QC_DEV explicit Ring(uint32_t stages) : n(stages), slot(0), phase(0) {}
+  QC_DEV void next() {
+    if (++slot == n) {
+      slot = 0;
+      phase ^= 1;
+    }
+  }
+};
 // Drain: wait (bounded) for a phase, ignoring the abort flag.
 QC_DEV void mbar_drain(uint64_t* m, uint32_t parity) {
   int never = 0;
@@ -162,19 +165,6 @@ QC_DEV uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 QC_DEV uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 QC_DEV __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 
-// quant.rs get_scale_min_k4: 6-bit scale and min of sub-block j from the 12 scale bytes s[0..11]
-// (held as three little-endian words).
-QC_DEV void scale_min(const uint32_t (&s)[3], uint32_t j, uint32_t* sc, uint32_t* mn) {
-  auto byte = [&](uint32_t i) { return (s[i >> 2] >> (8 * (i & 3))) & 0xffu; };
-  if (j < 4) {
-    *sc = byte(j) & 63;
-    *mn = byte(j + 4) & 63;
-  } else {
-    *sc = (byte(j + 4) & 15) | ((byte(j - 4) >> 6) << 4);
-    *mn = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4);
-  }
-}
-
 // x as fp16 hi + lo (x = hi + lo to ~22 bits when |x| < 2^15), two values per word.
 QC_DEV void split2(float a, float b, uint32_t* hi, uint32_t* lo) {
   const __half2 h = __floats2half2_rn(a, b);
@@ -219,19 +209,6 @@ QC_DEV bool tile_row(const QgArgs& a, uint32_t mat, uint32_t tile, uint32_t r, u
   }
   return *row < a.mats[*mi].rows;
 }
-// Valid rows of an item's tile: rows 0 .. v0 - 1 and (pair mode) 64 .. 64 + v1 - 1.
-QC_DEV void tile_rows(const QgArgs& a, uint32_t mat, uint32_t tile, uint32_t* v0, uint32_t* v1) {
-  if (a.pair) {
-    const uint32_t r0 = a.mats[mat].rows, r1 = a.mats[mat + 1].rows;
-    *v0 = r0 > tile * 64 ? min(64u, r0 - tile * 64) : 0;
-    *v1 = r1 > tile * 64 ? min(64u, r1 - tile * 64) : 0;
-  } else {
-    const uint32_t r0 = a.mats[mat].rows;
-    *v0 = r0 > tile * 128 ? min(128u, r0 - tile * 128) : 0;
-    *v1 = 0;
-  }
-}
-
 // What the loaders and the MMA issuer need of an item, read one item ahead.
 struct ItemDesc {
   uint32_t tile, n0, N, nimg, imgoff, mat, e;
@@ -265,11 +242,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(const __grid_constant__ Q
   const uint32_t nitems = a.nitems_dev ? *a.nitems_dev : a.nitems;
   // shared-memory carve-up (the host sizes it with qgemm_smem)
   const uint32_t kcsB = a.img_hasmin ? 10 : 8;
-  const uint32_t raw_bytes = 128 * C::blk, b_bytes = 2 * a.NP * kcsB * 16;
+  // a raw stage: two (64-row tile, super-block) blocks of the GEMM layout (rows 0-63, 64-127)
+  const uint32_t half_bytes = 64 * (AK == Q4_K ? 144 : 210), raw_bytes = 2 * half_bytes, b_bytes = 2 * a.NP * kcsB * 16;
   uint8_t* raw = sm;
-  uint8_t* area = raw + C::RS * raw_bytes;  // Q6_K: d values of the tile's rows, one copy per raw slot
-  const uint32_t area_bytes = AK == Q6_K ? 128 * nsb * 2 : 0;
-  uint8_t* ast = area + C::RS * area_bytes;
+  uint8_t* ast = raw + C::RS * raw_bytes;
   const uint32_t AS = a.AS;
   uint8_t* bst = ast + AS * a_stage_bytes<AK>();
   const uint32_t BS = a.BS;
@@ -309,45 +285,44 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(const __grid_constant__ Q
   volatile int* ab = &abort_flag;
 
   if (warp == 0) {
-    // ---- raw weight rows: one stage per (item, super-block) ----
+    // ---- raw weight rows: one stage per (item, super-block): two contiguous bulk copies ----
     uint32_t ctr = 0;
+    Ring ring(C::RS);
     bool ok = true;
     ItemDesc nx{};
     if (blockIdx.x < nitems) nx = load_item(a, g0, blockIdx.x);
     for (uint32_t i = blockIdx.x; i < nitems && ok; i += gridDim.x) {
       const ItemDesc it = nx;
       if (i + gridDim.x < nitems) nx = load_item(a, g0, i + gridDim.x);
-      for (uint32_t b = 0; b < nsb; b++, ctr++) {
-        const uint32_t slot = ctr % C::RS;
-        if (ctr >= C::RS && !mbar_wait(&raw_empty[slot], ((ctr / C::RS) - 1) & 1, ab)) {
+      for (uint32_t b = 0; b < nsb; b++, ctr++, ring.next()) {
+        const uint32_t slot = ring.slot;
+        if (ctr >= C::RS && !mbar_wait(&raw_empty[slot], ring.phase ^ 1, ab)) {
           ok = false;
           break;
         }
-        uint8_t* dst = raw + slot * raw_bytes;
-        if (lane == 0) {  // whole boxes: 128 rows of super-block b (rows past the tensor read as zeros)
-          const uint32_t halves = a.pair ? 2 : 1, hr = 128 / halves;
-          mbar_expect(&raw_full[slot], 128 * C::blk + (AK == Q6_K ? 128 * 2 * nsb : 0));
-          for (uint32_t h = 0; h < halves; h++) {
-            const uint32_t mi = it.mat + h, groups = (a.mats[mi].rows + 7) / 8;
-            if (AK == Q4_K) {
-              tma2d(dst + h * hr * C::blk, &a.tmA[mi], b * C::blk, (it.e * groups + it.tile * (hr / 8)) * 8,
+        if (lane == 0) {
+          // half h: pair mode, 64-row tile `tile` of mats[mat + h]; else tile 2 tile + h of mats[mat]
+          const GemmMat& m0 = a.mats[it.mat];
+          const GemmMat& m1 = a.mats[a.pair ? it.mat + 1 : it.mat];
+          const uint32_t t0 = a.pair ? it.tile : 2 * it.tile, t1 = a.pair ? it.tile : 2 * it.tile + 1;
+          const bool h1 = t1 < m1.tiles;
+          mbar_expect(&raw_full[slot], (h1 ? 2 : 1) * half_bytes);
+          uint8_t* dst = raw + slot * raw_bytes;
+          bulk_copy(dst, m0.w + it.e * m0.expert_stride + t0 * m0.tile_bytes + b * half_bytes, half_bytes,
                     &raw_full[slot]);
-            } else {
-              const uint32_t z = it.e * groups + it.tile * (hr / 8);
-              tma3d(dst + h * hr * C::blk, &a.tmA[mi], b * C::blk, 0, z, &raw_full[slot]);
-              tma2d(area + slot * area_bytes + h * hr * 2 * nsb, &a.tmD[mi], 0, z, &raw_full[slot]);
-            }
-          }
+          if (h1)
+            bulk_copy(dst + half_bytes, m1.w + it.e * m1.expert_stride + t1 * m1.tile_bytes + b * half_bytes,
+                      half_bytes, &raw_full[slot]);
         }
       }
     }
-    // drain: the copies of the last stages issued
-    if (lane == 0)
+    if (lane == 0)  // drain: the copies of the last stages issued
       for (uint32_t k = ctr > C::RS ? ctr - C::RS : 0; k < ctr; k++) mbar_drain(&raw_full[k % C::RS], (k / C::RS) & 1);
   } else if (warp == 2) {
     // ---- B stages: one per (item, K step), two bulk copies (hi, lo) ----
     if (lane == 0) {
       uint32_t ctr = 0;
+      Ring ring(BS);
       bool ok = true;
       ItemDesc nx{};
       if (blockIdx.x < nitems) nx = load_item(a, g0, blockIdx.x);
@@ -355,9 +330,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(const __grid_constant__ Q
         const ItemDesc it = nx;
         if (i + gridDim.x < nitems) nx = load_item(a, g0, i + gridDim.x);
         const uint8_t* gimg = a.img + (uint64_t)it.imgoff * img_row;
-        for (uint32_t s = 0; s < S; s++, ctr++) {
-          const uint32_t slot = ctr % BS;
-          if (ctr >= BS && !mbar_wait(&b_empty[slot], ((ctr / BS) - 1) & 1, ab)) {
+        for (uint32_t s = 0; s < S; s++, ctr++, ring.next()) {
+          const uint32_t slot = ring.slot;
+          if (ctr >= BS && !mbar_wait(&b_empty[slot], ring.phase ^ 1, ab)) {
             ok = false;
             break;
           }
@@ -374,7 +349,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(const __grid_constant__ Q
   } else if (warp == 1) {
     // ---- MMA issue (one thread) ----
     if (lane == 0) {
-      uint32_t actr = 0, bctr = 0, items = 0;
+      uint32_t items = 0;
+      Ring ar(AS), br(BS);
       bool ok = true;
       uint64_t* last = nullptr;
       uint32_t last_par = 0;
@@ -388,9 +364,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(const __grid_constant__ Q
         // holds the hi plane then the lo plane of the vectors, so one MMA multiplies A by both (columns
         // 0 .. N-1: hi, N .. 2N-1: lo; the epilogue adds the halves)
         const uint32_t idesc = (1u << 4) | (((2 * it.N) >> 3) << 17) | ((128u >> 4) << 24);
-        for (uint32_t s = 0; s < S; s++, actr++, bctr++) {
-          const uint32_t as = actr % AS, bs = bctr % BS;
-          if (!mbar_wait(&a_full[as], (actr / AS) & 1, ab) || !mbar_wait(&b_full[bs], (bctr / BS) & 1, ab)) {
+        for (uint32_t s = 0; s < S; s++, ar.next(), br.next()) {
+          const uint32_t as = ar.slot, bs = br.slot;
+          if (!mbar_wait(&a_full[as], ar.phase, ab) || !mbar_wait(&b_full[bs], br.phase, ab)) {
             ok = false;
             break;
           }
@@ -419,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(const __grid_constant__ Q
           mma_commit(&a_empty[as]);
           mma_commit(&b_empty[bs]);
           last = &b_empty[bs];
-          last_par = (bctr / BS) & 1;
+          last_par = br.phase;
         }
         if (!ok) break;
         mma_commit(&acc_full);
@@ -433,7 +409,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(const __grid_constant__ Q
     const uint32_t pt = tid - kProdWarp0 * 32, part = pt >> 7, r = pt & 127;
     const uint32_t quarter = (warp - kProdWarp0) & 3;  // TMEM lanes 32 * quarter ..
     float* dme = dsm + part * nsb * 128;
-    uint32_t rctr = 0, actr = 0, items = 0, pphase = 0;
+    uint32_t actr = 0, items = 0, pphase = 0;
+    Ring rr(C::RS), ar(AS);
     bool ok = true;
     for (uint32_t i = blockIdx.x; i < nitems && ok; i += gridDim.x, items++) {
       const Item it = decode_item(a, g0, i);
@@ -451,13 +428,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(const __grid_constant__ Q
         if (a.hs && n < g.cnt) hs_pt = a.hs[g.hsmap ? g.hsmap[n] : n];
         if (EPI == 0 && n < g.cnt) y_pt = g.ymap ? g.ymap[n] : n;
       }
-      for (uint32_t b = 0; b < nsb && ok; b++, rctr++) {
-        const uint32_t rs = rctr % C::RS;
-        if (!mbar_wait(&raw_full[rs], (rctr / C::RS) & 1, ab)) {
+      for (uint32_t b = 0; b < nsb && ok; b++, rr.next()) {
+        const uint32_t rs = rr.slot;
+        if (!mbar_wait(&raw_full[rs], rr.phase, ab)) {
           ok = false;
           break;
         }
-        const uint8_t* rw = raw + rs * raw_bytes + r * C::blk;
+        const uint8_t* rw = raw + rs * raw_bytes + (r >> 6) * half_bytes + (r & 63) * C::blk;
         // per super-block: the row's block header and all of this thread's bytes of the 4 K steps
         float d = 0.f, dmin = 0.f;
         uint32_t sc03 = 0, sc47 = 0, mnp = 0;  // Q4_K: 6-bit scales of sub-blocks 0-3, 4-7; mins of 4 part..
@@ -480,15 +457,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(const __grid_constant__ Q
           mnp = part == 0 ? (h.z & 0x3f3f3f3fu) : (((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u));
         } else {
           if (valid) {
-            const __half* dv = reinterpret_cast<const __half*>(area + rs * area_bytes) + r * nsb;
-            d = __half2float(dv[b]);
+            d = __half2float(*reinterpret_cast<const __half*>(raw + rs * raw_bytes + (r >> 6) * half_bytes + 64 * 208 +
+                                                              (r & 63) * 2));
           }
         }
         dme[b * 128 + r] = d;
 #pragma unroll
         for (uint32_t c = 0; c < 4; c++) {
-          const uint32_t as = actr % AS;
-          if (actr >= AS && !mbar_wait(&a_empty[as], ((actr / AS) - 1) & 1, ab)) {
+          const uint32_t as = ar.slot;
+          if (actr >= AS && !mbar_wait(&a_empty[as], ar.phase ^ 1, ab)) {
             ok = false;
             break;
           }
@@ -577,6 +554,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(const __grid_constant__ Q
           __syncwarp();
           if (lane == 0) mbar_arrive(&a_full[as]);
           actr++;
+          ar.next();
         }
         if (!ok) break;
         __syncwarp();
@@ -830,7 +808,35 @@ __global__ void k_qg_dmin(MatDesc m, uint32_t experts, uint32_t* out) {
   if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(mx));
 }
 
+// One thread per (expert, 64-row tile, super-block, row): the row's block (and d value) to the GEMM layout.
+__global__ void k_qg_relayout(MatDesc m, uint32_t experts, GemmMat g) {
+  const uint32_t nsb = m.cols / 256, blk = m.kind == Q4_K ? 144 : 208;
+  const uint64_t total = (uint64_t)experts * g.tiles * nsb * 64;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t rr = (uint32_t)(i & 63);
+    uint64_t q = i >> 6;
+    const uint32_t b = (uint32_t)(q % nsb);
+    q /= nsb;
+    const uint32_t t = (uint32_t)(q % g.tiles), e = (uint32_t)(q / g.tiles), row = t * 64 + rr;
+    uint8_t* blockp = const_cast<uint8_t*>(g.w) + e * g.expert_stride + t * g.tile_bytes + b * g.blockb;
+    uint4* dst = reinterpret_cast<uint4*>(blockp + rr * blk);
+    if (row < m.rows) {
+      const uint8_t* base = expert_base(m, e);
+      const uint4* src = reinterpret_cast<const uint4*>(row_ptr(m, base, row) + b * blk);
+      for (uint32_t k = 0; k < blk / 16; k++) dst[k] = src[k];
+      if (m.kind == Q6_K) reinterpret_cast<__half*>(blockp + 64 * 208)[rr] = drow_ptr(m, base, row)[b];
+    } else {
+      for (uint32_t k = 0; k < blk / 16; k++) dst[k] = make_uint4(0, 0, 0, 0);
+      if (m.kind == Q6_K) reinterpret_cast<__half*>(blockp + 64 * 208)[rr] = __float2half_rn(0.f);
+    }
+  }
+}
+
 }  // namespace
+
+void launch_qg_relayout(const MatDesc& src, uint32_t experts, const GemmMat& dst, cudaStream_t s) {
+  k_qg_relayout<<<148 * 8, 256, 0, s>>>(src, experts, dst);
+}
 
 const char* qgemm_supported(uint32_t kind, uint32_t cols) {
   if (kind != Q4_K && kind != Q6_K) return "the tensor-core GEMM takes Q4_K and Q6_K rows";
@@ -841,47 +847,6 @@ const char* qgemm_supported(uint32_t kind, uint32_t cols) {
   return nullptr;
 }
 
-// Raw rows as tensors of bytes: Q4_K rows are evenly spaced (an expert stack is one 2-D tensor of
-// experts * rows_padded rows); Q6_K rows come in groups of 8 followed by their d values, so the rows
-// are a 3-D tensor (bytes, row in group, group) and the d values a 2-D one (bytes, group).
-const char* qg_encode(QgArgs& q, uint32_t i, uint32_t experts) {
-  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* fn = nullptr;
-    cudaDriverEntryPointQueryResult qr;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qr) == cudaSuccess &&
-        qr == cudaDriverEntryPointSuccess)
-      encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-  });
-  if (!encode) return "cuTensorMapEncodeTiled is not available";
-  const MatDesc& m = q.mats[i];
-  const uint64_t groups = (uint64_t)experts * ((m.rows + 7) / 8);
-  const uint32_t box_groups = q.pair ? 8 : 16;
-  CUresult r;
-  if (m.kind == Q4_K) {
-    const cuuint64_t dims[2] = {m.main_bytes, groups * 8}, strides[1] = {m.main_bytes};
-    const cuuint32_t box[2] = {144, box_groups * 8}, es[2] = {1, 1};
-    r = encode(&q.tmA[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(m.w), dims, strides, box, es,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  } else {
-    const cuuint64_t dims[3] = {m.main_bytes, 8, groups}, strides[2] = {m.main_bytes, m.group_bytes};
-    const cuuint32_t box[3] = {208, 8, box_groups}, es[3] = {1, 1, 1};
-    r = encode(&q.tmA[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(m.w), dims, strides, box, es,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r == CUDA_SUCCESS) {
-      const cuuint64_t ddims[2] = {8ull * m.d_bytes, groups}, dstr[1] = {m.group_bytes};
-      const cuuint32_t dbox[2] = {8 * m.d_bytes, box_groups}, des[2] = {1, 1};
-      r = encode(&q.tmD[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(m.w + 8ull * m.main_bytes), ddims,
-                 dstr, dbox, des, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                 CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    }
-  }
-  return r == CUDA_SUCCESS ? nullptr : "cuTensorMapEncodeTiled refused a weight matrix";
-}
-
 uint64_t qg_image_row_bytes(uint32_t cols, bool hasmin) {
   const uint64_t S = cols / 64;
   return 32 * (8 * S + (hasmin ? 2 * (S / 4) : 0));
@@ -890,8 +855,7 @@ uint64_t qg_image_row_bytes(uint32_t cols, bool hasmin) {
 // Shared memory besides the A and B stages, one A stage, one B stage.
 static size_t qgemm_fixed(uint32_t kind, uint32_t cols, uint32_t np) {
   const uint32_t nsb = cols / 256;  // (+ 1 KB: the carve-up is aligned to 1 KB)
-  const size_t f = kind == Q4_K ? Cfg<Q4_K>::RS * 128 * Cfg<Q4_K>::blk
-                                : Cfg<Q6_K>::RS * 128 * Cfg<Q6_K>::blk + Cfg<Q6_K>::RS * 128 * nsb * 2;
+  const size_t f = kind == Q4_K ? Cfg<Q4_K>::RS * 128 * 144 : Cfg<Q6_K>::RS * 128 * 210;
   return f + 2 * nsb * 128 * 4 + 2 * np * 8 + 1024;
 }
 static size_t qgemm_astage(uint32_t kind) { return kind == Q4_K ? a_stage_bytes<Q4_K>() : a_stage_bytes<Q6_K>(); }
