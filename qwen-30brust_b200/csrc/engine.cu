@@ -815,10 +815,10 @@ struct qc_engine {
     a.T = T;
     a.eps = cfg.eps;
     a.sms = sms;
-    a.NPgu = a.NPdn = 16;
-    a.ASgu = a.ASdn = a.BSgu = a.BSdn = 2;
-    if (!qc::qgemm_shape(a.gate.kind, a.H, a.gate.kind == qc::Q4_K, &a.NPgu, &a.ASgu, &a.BSgu))
-      qc::qgemm_shape(a.down.kind, a.I, a.down.kind == qc::Q4_K, &a.NPdn, &a.ASdn, &a.BSdn);
+    a.NPgu = a.NPdn = 8;
+    a.SSgu = a.SSdn = 2;
+    if (!qc::qgemm_shape(a.gate.kind, a.H, a.gate.kind == qc::Q4_K, &a.NPgu, &a.SSgu))
+      qc::qgemm_shape(a.down.kind, a.I, a.down.kind == qc::Q4_K, &a.NPdn, &a.SSdn);
     const uint64_t P = (uint64_t)moe_cap * cfg.top, R = qc::moe_image_rows(moe_cap, cfg.top, cfg.experts);
     uint64_t o = 0;
     auto take = [&](uint64_t bytes) {
@@ -1080,8 +1080,8 @@ struct qc_batch {
     const uint64_t o_tok = take(cap * sizeof(qc::BatchTok)), o_ids = take(cap * 4), o_osrc = take(cap * 4);
     // tensor-core projections where the formats allow
     auto tc_ok = [&](const qc::MatDesc& m) {
-      uint32_t np, as, bs;
-      return !qc::qgemm_shape(m.kind, m.cols, true, &np, &as, &bs);
+      uint32_t np, ss;
+      return !qc::qgemm_shape(m.kind, m.cols, true, &np, &ss);
     };
     tc.assign(4ull * c.layers, 0);
     tc_smin.assign(4ull * c.layers, 1.f);
@@ -1165,13 +1165,12 @@ struct qc_batch {
   void tc_project(const std::vector<TcOut>& outs, uint32_t T, uint32_t K) {
     if (outs.empty()) return;
     const uint32_t kind = outs[0].m->kind, nimg = (T + 15) & ~15u;
-    uint32_t NP = 16, AS = 2, BS = 2;
-    qc::qgemm_shape(kind, K, true, &NP, &AS, &BS);  // (checked when the batch was created)
+    uint32_t NP = 8, SS = 2;
+    qc::qgemm_shape(kind, K, true, &NP, &SS);  // (checked when the batch was created)
     qc::QgArgs q{};
     q.K = K;
     q.NP = NP;
-    q.AS = AS;
-    q.BS = BS;
+    q.SS = SS;
     q.img_hasmin = 1;
     q.img = d_img;
     q.hs = d_hs;

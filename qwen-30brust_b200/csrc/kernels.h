@@ -175,7 +175,7 @@ struct MoeArgs {
   uint32_t H, I, E, top, T;
   float eps;
   float smin_g, smin_u, smin_d;  // Q4_K min-block scales of the tensor-core GEMM (qgemm.cu)
-  uint32_t NPgu, NPdn, ASgu, ASdn, BSgu, BSdn;  // vectors per GEMM pass, A and B stages (qgemm_shape)
+  uint32_t NPgu, NPdn, SSgu, SSdn;  // vectors per GEMM pass and stages (qgemm_shape)
   int sms;
   // scratch
   float* h;          // [T][H] normalized inputs
@@ -290,7 +290,7 @@ struct QgArgs {
   GemmMat mats[4];
   float smin[4];        // Q4_K: power-of-two scale of the min block (dmin * mn * smin < 2^14)
   uint32_t pair;        // pair mode (SwiGLU: gate rows then up rows of each 128-row tile)
-  uint32_t K, NP, AS, BS;  // columns (a multiple of 256); vectors per pass; A and B stages (qgemm_shape)
+  uint32_t K, NP, SS;   // columns (a multiple of 256); vectors per pass; stages (qgemm_shape)
   uint32_t img_hasmin;  // the image carries the Q4_K min chunks
   const uint8_t* img;
   const float* hs;
@@ -328,9 +328,9 @@ __host__ __device__ inline float qg_pow2_scale(float maxabs) {  // 2^k with maxa
 const char* qgemm_supported(uint32_t kind, uint32_t cols);
 // Vectors per pass and B stages of a GEMM over `cols` columns of `kind` rows (after qgemm_prepare),
 // or the reason it cannot run.
-const char* qgemm_shape(uint32_t kind, uint32_t cols, bool img_hasmin, uint32_t* np, uint32_t* as, uint32_t* bs);
+const char* qgemm_shape(uint32_t kind, uint32_t cols, bool img_hasmin, uint32_t* np, uint32_t* ss);
 uint64_t qg_image_row_bytes(uint32_t cols, bool hasmin);
-size_t qgemm_smem(uint32_t kind, uint32_t cols, uint32_t np, uint32_t as, uint32_t bs, bool img_hasmin);
+size_t qgemm_smem(uint32_t kind, uint32_t cols, uint32_t np, uint32_t ss, bool img_hasmin);
 cudaError_t qgemm_prepare();  // once per device
 size_t qgemm_smem_cap();      // dynamic shared memory available to the GEMM kernels (after qgemm_prepare)
 void launch_qgemm(const QgArgs& a, uint32_t kind, bool swiglu, uint32_t grid, cudaStream_t s);

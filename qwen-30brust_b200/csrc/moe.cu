@@ -186,9 +186,9 @@ const char* moe_tc_supported(const MoeArgs& a) {
   if (a.router.kind != F16) return "the batched MoE path takes an F16 router";
   if (a.E > 1024) return "the batched MoE path takes at most 1024 experts";
   if (!a.ggate.w || !a.gup.w || !a.gdown.w) return "the GEMM-layout copy of the experts is missing";
-  uint32_t np, as, bs;
-  if (const char* why = qgemm_shape(a.gate.kind, a.H, a.gate.kind == Q4_K, &np, &as, &bs)) return why;
-  if (const char* why = qgemm_shape(a.down.kind, a.I, a.down.kind == Q4_K, &np, &as, &bs)) return why;
+  uint32_t np, ss;
+  if (const char* why = qgemm_shape(a.gate.kind, a.H, a.gate.kind == Q4_K, &np, &ss)) return why;
+  if (const char* why = qgemm_shape(a.down.kind, a.I, a.down.kind == Q4_K, &np, &ss)) return why;
   return nullptr;
 }
 
@@ -220,8 +220,7 @@ const char* launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStre
   g.pair = 1;
   g.K = a.H;
   g.NP = a.NPgu;
-  g.AS = a.ASgu;
-  g.BS = a.BSgu;
+  g.SS = a.SSgu;
   g.img_hasmin = a.gate.kind == Q4_K;
   g.img = a.img_gu;
   g.hs = a.hscale;
@@ -238,8 +237,7 @@ const char* launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStre
   d.smin[0] = a.smin_d;
   d.K = a.I;
   d.NP = a.NPdn;
-  d.AS = a.ASdn;
-  d.BS = a.BSdn;
+  d.SS = a.SSdn;
   d.img_hasmin = a.down.kind == Q4_K;
   d.img = a.img_dn;
   d.groups = a.groups + a.E;

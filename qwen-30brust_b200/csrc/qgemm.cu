@@ -41,14 +41,14 @@ constexpr uint32_t kNone = 0xffffffffu;
 template <int AK>
 struct Cfg;
 template <>
-struct Cfg<Q4_K> {
-  static constexpr uint32_t blk = 144, RS = 3, planes = 1, kcsA = 10;
+struct Cfg<Q4_K> {  // KS: K steps of 64 per stage; kcsA: 16-byte chunks per A row in a stage (+2: min)
+  static constexpr uint32_t blk = 144, RS = 3, planes = 1, KS = 2, kcsA = 8 * KS + 2;
 };
 template <>
 struct Cfg<Q6_K> {
-  static constexpr uint32_t blk = 208, RS = 3, planes = 2, kcsA = 8;
+  static constexpr uint32_t blk = 208, RS = 3, planes = 2, KS = 1, kcsA = 8;
 };
-constexpr uint32_t kMaxAS = 6, kMaxBS = 8;  // A and B stages (runtime counts a.AS, a.BS: qgemm_shape)
+constexpr uint32_t kMaxSS = 8;  // stages (runtime count a.SS: qgemm_shape)
 template <int AK>
 constexpr uint32_t a_stage_bytes() {
   return Cfg<AK>::planes * 128 * Cfg<AK>::kcsA * 16;
@@ -231,8 +231,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(const __grid_constant__ Q
   extern __shared__ __align__(1024) uint8_t sm_raw[];
   // (tensor copies want 128-byte aligned destinations: the carve-up starts at a 1024-byte boundary)
   uint8_t* sm = sm_raw + ((1024 - (smem_u32(sm_raw) & 1023)) & 1023);
-  __shared__ __align__(8) uint64_t raw_full[C::RS], raw_empty[C::RS], a_full[kMaxAS], a_empty[kMaxAS], b_full[kMaxBS],
-      b_empty[kMaxBS], acc_full, psync;
+  __shared__ __align__(8) uint64_t raw_full[C::RS], raw_empty[C::RS], st_full[kMaxSS], st_empty[kMaxSS], acc_full,
+      psync;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   __shared__ uint32_t g0[kMaxGroups];
@@ -243,13 +243,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(const __grid_constant__ Q
   // shared-memory carve-up (the host sizes it with qgemm_smem)
   const uint32_t kcsB = a.img_hasmin ? 10 : 8;
   // a raw stage: two (64-row tile, super-block) blocks of the GEMM layout (rows 0-63, 64-127)
-  const uint32_t half_bytes = 64 * (AK == Q4_K ? 144 : 210), raw_bytes = 2 * half_bytes, b_bytes = 2 * a.NP * kcsB * 16;
+  const uint32_t half_bytes = 64 * (AK == Q4_K ? 144 : 210), raw_bytes = 2 * half_bytes;
+  // a stage: the A operand of KS K steps, then for each of them the B planes (hi, lo) of the pass
+  const uint32_t a_part = a_stage_bytes<AK>(), b_sub = 2 * a.NP * kcsB * 16, stage_bytes = a_part + C::KS * b_sub;
   uint8_t* raw = sm;
-  uint8_t* ast = raw + C::RS * raw_bytes;
-  const uint32_t AS = a.AS;
-  uint8_t* bst = ast + AS * a_stage_bytes<AK>();
-  const uint32_t BS = a.BS;
-  float* dsm = reinterpret_cast<float*>(bst + BS * b_bytes);  // [part][nsb][128] d of each row
+  uint8_t* stg = raw + C::RS * raw_bytes;
+  const uint32_t SS = a.SS;
+  float* dsm = reinterpret_cast<float*>(stg + SS * stage_bytes);  // [part][nsb][128] d of each row
   float* hsm = dsm + 2 * nsb * 128;                              // [2][NP] 1 / scale of each vector
   uint32_t* ysm = reinterpret_cast<uint32_t*>(hsm + 2 * a.NP);  // [2][NP] output row of each vector
   const uint32_t img_row = 32 * kc_before(S, a.img_hasmin);     // image bytes per vector
@@ -266,13 +266,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(const __grid_constant__ Q
       mbar_init(&raw_full[i], 1);
       mbar_init(&raw_empty[i], kProd / 32);
     }
-    for (uint32_t i = 0; i < AS; i++) {
-      mbar_init(&a_full[i], kProd / 32);
-      mbar_init(&a_empty[i], 1);
-    }
-    for (uint32_t i = 0; i < BS; i++) {
-      mbar_init(&b_full[i], 1);
-      mbar_init(&b_empty[i], 1);
+    for (uint32_t i = 0; i < SS; i++) {
+      mbar_init(&st_full[i], kProd / 32 + 1);  // the producer warps and the B copier (with the bytes)
+      mbar_init(&st_empty[i], 1);
     }
     mbar_init(&acc_full, 1);
     mbar_init(&psync, kProd / 32);
@@ -319,10 +315,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(const __grid_constant__ Q
     if (lane == 0)  // drain: the copies of the last stages issued
       for (uint32_t k = ctr > C::RS ? ctr - C::RS : 0; k < ctr; k++) mbar_drain(&raw_full[k % C::RS], (k / C::RS) & 1);
   } else if (warp == 2) {
-    // ---- B stages: one per (item, K step), two bulk copies (hi, lo) ----
+    // ---- B planes of each stage's K steps: two bulk copies (hi, lo) per K step ----
     if (lane == 0) {
       uint32_t ctr = 0;
-      Ring ring(BS);
+      Ring ring(SS);
       bool ok = true;
       ItemDesc nx{};
       if (blockIdx.x < nitems) nx = load_item(a, g0, blockIdx.x);
@@ -330,72 +326,85 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(const __grid_constant__ Q
         const ItemDesc it = nx;
         if (i + gridDim.x < nitems) nx = load_item(a, g0, i + gridDim.x);
         const uint8_t* gimg = a.img + (uint64_t)it.imgoff * img_row;
-        for (uint32_t s = 0; s < S; s++, ctr++, ring.next()) {
+        for (uint32_t s0 = 0; s0 < S; s0 += C::KS, ctr++, ring.next()) {
           const uint32_t slot = ring.slot;
-          if (ctr >= BS && !mbar_wait(&b_empty[slot], ring.phase ^ 1, ab)) {
+          if (ctr >= SS && !mbar_wait(&st_empty[slot], ring.phase ^ 1, ab)) {
             ok = false;
             break;
           }
-          const uint32_t kcs = kcs_of(s, a.img_hasmin), plane = it.N * kcs * 16;
-          const uint8_t* src = gimg + (uint64_t)it.nimg * 32 * kc_before(s, a.img_hasmin) + (it.n0 / 8) * kcs * 128;
-          uint8_t* dst = bst + slot * b_bytes;
-          mbar_expect(&b_full[slot], 2 * plane);
-          bulk_copy(dst, src, plane, &b_full[slot]);
-          bulk_copy(dst + plane, src + (uint64_t)it.nimg * kcs * 16, plane, &b_full[slot]);
+          uint32_t bytes = 0;
+#pragma unroll
+          for (uint32_t j = 0; j < C::KS; j++) bytes += 2 * it.N * kcs_of(s0 + j, a.img_hasmin) * 16;
+          mbar_expect(&st_full[slot], bytes);
+#pragma unroll
+          for (uint32_t j = 0; j < C::KS; j++) {
+            const uint32_t s = s0 + j, kcs = kcs_of(s, a.img_hasmin), plane = it.N * kcs * 16;
+            const uint8_t* src = gimg + (uint64_t)it.nimg * 32 * kc_before(s, a.img_hasmin) + (it.n0 / 8) * kcs * 128;
+            uint8_t* dst = stg + slot * stage_bytes + a_part + j * b_sub;
+            bulk_copy(dst, src, plane, &st_full[slot]);
+            bulk_copy(dst + plane, src + (uint64_t)it.nimg * kcs * 16, plane, &st_full[slot]);
+          }
         }
       }
-      for (uint32_t k = ctr > BS ? ctr - BS : 0; k < ctr; k++) mbar_drain(&b_full[k % BS], (k / BS) & 1);
+      for (uint32_t k = ctr > SS ? ctr - SS : 0; k < ctr; k++) mbar_drain(&st_full[k % SS], (k / SS) & 1);
     }
   } else if (warp == 1) {
     // ---- MMA issue (one thread) ----
     if (lane == 0) {
       uint32_t items = 0;
-      Ring ar(AS), br(BS);
+      Ring sr(SS);
       bool ok = true;
       uint64_t* last = nullptr;
       uint32_t last_par = 0;
       const uint32_t NP = a.NP;
+      // descriptors of stage 0 (A; B of each K step per chunk count): slot k is k * stage_bytes further
+      const unsigned long long ad0 = sdesc(smem_u32(stg), 128, C::kcsA * 128);
+      const unsigned long long bd8 = sdesc(smem_u32(stg + a_part), 128, 8 * 128),
+                               bd10 = sdesc(smem_u32(stg + a_part), 128, 10 * 128);
       ItemDesc nx{};
       if (blockIdx.x < nitems) nx = load_item(a, g0, blockIdx.x);
       for (uint32_t i = blockIdx.x; i < nitems && ok; i += gridDim.x, items++) {
         const ItemDesc it = nx;
         if (i + gridDim.x < nitems) nx = load_item(a, g0, i + gridDim.x);
-        // f32 accumulator, f16 A and B, both K-major, M = 128, N = 2 x the pass's vectors: the B stage
+        // f32 accumulator, f16 A and B, both K-major, M = 128, N = 2 x the pass's vectors: a B K step
         // holds the hi plane then the lo plane of the vectors, so one MMA multiplies A by both (columns
         // 0 .. N-1: hi, N .. 2N-1: lo; the epilogue adds the halves)
         const uint32_t idesc = (1u << 4) | (((2 * it.N) >> 3) << 17) | ((128u >> 4) << 24);
-        for (uint32_t s = 0; s < S; s++, ar.next(), br.next()) {
-          const uint32_t as = ar.slot, bs = br.slot;
-          if (!mbar_wait(&a_full[as], ar.phase, ab) || !mbar_wait(&b_full[bs], br.phase, ab)) {
+        for (uint32_t s0 = 0; s0 < S; s0 += C::KS, sr.next()) {
+          if (!mbar_wait(&st_full[sr.slot], sr.phase, ab)) {
             ok = false;
             break;
           }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t sb = s >> 2, kcsB_s = kcs_of(s, a.img_hasmin);
-          // descriptors of the stage; a K = 16 step is two 16-byte chunks further: +256 bytes (16 units)
-          const unsigned long long ad = sdesc(smem_u32(ast + as * a_stage_bytes<AK>()), 128, C::kcsA * 128);
-          const unsigned long long bd = sdesc(smem_u32(bst + bs * b_bytes), 128, kcsB_s * 128);
-          const uint32_t dcol = tmem + sb * 2 * NP;
-          if ((s & 3) == 0) mma_first(dcol, ad, bd, idesc);
-          else mma_acc(dcol, ad, bd, idesc);
-          mma_acc(dcol, ad + 16, bd + 16, idesc);
-          mma_acc(dcol, ad + 32, bd + 32, idesc);
-          mma_acc(dcol, ad + 48, bd + 48, idesc);
-          if (AK == Q6_K) {  // the lo plane of A, 128 x 8 chunks further
-            const unsigned long long al = ad + (128 * C::kcsA * 16 >> 4);
-            mma_acc(dcol, al, bd, idesc);
-            mma_acc(dcol, al + 16, bd + 16, idesc);
-            mma_acc(dcol, al + 32, bd + 32, idesc);
-            mma_acc(dcol, al + 48, bd + 48, idesc);
+          const unsigned long long so = (unsigned long long)(sr.slot * stage_bytes) >> 4;
+#pragma unroll
+          for (uint32_t j = 0; j < C::KS; j++) {
+            const uint32_t s = s0 + j, sb = s >> 2;
+            // K step j's A chunks start 8 j chunks into the row group; a K = 16 step is +256 bytes (16 units)
+            const unsigned long long ad = ad0 + so + j * 64;
+            const unsigned long long bd = (kcs_of(s, a.img_hasmin) == 10 ? bd10 : bd8) + so + (j * b_sub >> 4);
+            const uint32_t dcol = tmem + sb * 2 * NP;
+            if ((s & 3) == 0) mma_first(dcol, ad, bd, idesc);
+            else mma_acc(dcol, ad, bd, idesc);
+            mma_acc(dcol, ad + 16, bd + 16, idesc);
+            mma_acc(dcol, ad + 32, bd + 32, idesc);
+            mma_acc(dcol, ad + 48, bd + 48, idesc);
+            if (AK == Q6_K) {  // the lo plane of A, 128 x 8 chunks further
+              const unsigned long long al = ad + (128 * C::kcsA * 16 >> 4);
+              mma_acc(dcol, al, bd, idesc);
+              mma_acc(dcol, al + 16, bd + 16, idesc);
+              mma_acc(dcol, al + 32, bd + 32, idesc);
+              mma_acc(dcol, al + 48, bd + 48, idesc);
+            }
+            if (hasminA && (s & 3) == 3) {  // the min term of super-block sb: A chunks 8 KS, 8 KS + 1; B 8, 9
+              const unsigned long long am = ad0 + so + 8 * C::KS * 8;
+              if (sb == 0) mma_first(tmem + nsb * 2 * NP, am, bd + 64, idesc);
+              else mma_acc(tmem + nsb * 2 * NP, am, bd + 64, idesc);
+            }
           }
-          if (hasminA && (s & 3) == 3) {  // the min term of super-block sb: chunks 8, 9
-            if (sb == 0) mma_first(tmem + nsb * 2 * NP, ad + 64, bd + 64, idesc);
-            else mma_acc(tmem + nsb * 2 * NP, ad + 64, bd + 64, idesc);
-          }
-          mma_commit(&a_empty[as]);
-          mma_commit(&b_empty[bs]);
-          last = &b_empty[bs];
-          last_par = br.phase;
+          mma_commit(&st_empty[sr.slot]);
+          last = &st_empty[sr.slot];
+          last_par = sr.phase;
         }
         if (!ok) break;
         mma_commit(&acc_full);
@@ -409,8 +418,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(const __grid_constant__ Q
     const uint32_t pt = tid - kProdWarp0 * 32, part = pt >> 7, r = pt & 127;
     const uint32_t quarter = (warp - kProdWarp0) & 3;  // TMEM lanes 32 * quarter ..
     float* dme = dsm + part * nsb * 128;
-    uint32_t actr = 0, items = 0, pphase = 0;
-    Ring rr(C::RS), ar(AS);
+    uint32_t sctr = 0, items = 0, pphase = 0;
+    Ring rr(C::RS), sr(SS);
     bool ok = true;
     for (uint32_t i = blockIdx.x; i < nitems && ok; i += gridDim.x, items++) {
       const Item it = decode_item(a, g0, i);
@@ -464,12 +473,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(const __grid_constant__ Q
         dme[b * 128 + r] = d;
 #pragma unroll
         for (uint32_t c = 0; c < 4; c++) {
-          const uint32_t as = ar.slot;
-          if (actr >= AS && !mbar_wait(&a_empty[as], ar.phase ^ 1, ab)) {
+          const uint32_t j = c % C::KS;  // K step within the stage
+          if (j == 0 && sctr >= SS && !mbar_wait(&st_empty[sr.slot], sr.phase ^ 1, ab)) {
             ok = false;
             break;
           }
-          uint8_t* A = ast + as * a_stage_bytes<AK>() + (r >> 3) * (C::kcsA * 128) + (r & 7) * 16;
+          uint8_t* Arow = stg + sr.slot * stage_bytes + (r >> 3) * (C::kcsA * 128) + (r & 7) * 16;
+          uint8_t* A = Arow + j * 8 * 128;
           if (AK == Q4_K) {
             // low nibbles = sub-block 2c (weight sc * q), high nibbles = 2c + 1: 1024 + 16 q as fp16, times
             // sc / 16, minus 64 sc (exact: the results are integers below 2^10)
@@ -501,8 +511,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(const __grid_constant__ Q
               uint32_t h0, l0, h1, l1;
               split2(v[0], v[1], &h0, &l0);
               split2(v[2], v[3], &h1, &l1);
-              *reinterpret_cast<uint2*>(A + 8 * 128 + 8 * part) = make_uint2(h0, h1);
-              *reinterpret_cast<uint2*>(A + 9 * 128 + 8 * part) = make_uint2(l0, l1);
+              *reinterpret_cast<uint2*>(Arow + 8 * C::KS * 128 + 8 * part) = make_uint2(h0, h1);
+              *reinterpret_cast<uint2*>(Arow + (8 * C::KS + 1) * 128 + 8 * part) = make_uint2(l0, l1);
             }
           } else {
             // K step c of the super-block: half nh = c / 2, quarter qa = 2 (c % 2) + part (32 weights)
@@ -550,11 +560,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(const __grid_constant__ Q
               *reinterpret_cast<uint4*>(Al + (ch + 1) * 128) = make_uint4(alo[4], alo[5], alo[6], alo[7]);
             }
           }
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&a_full[as]);
-          actr++;
-          ar.next();
+          if (j == C::KS - 1) {  // the stage's A part is written
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&st_full[sr.slot]);
+            sctr++;
+            sr.next();
+          }
         }
         if (!ok) break;
         __syncwarp();
@@ -577,7 +589,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_qgemm(const __grid_constant__ Q
       }
       const uint32_t cols = it.N / 2, c0 = part * cols;  // (N a multiple of 8)
       const float kmin = hasminA ? 32.f / smin : 0.f;
-      float* E = reinterpret_cast<float*>(ast);  // EPI 1: [128][NP + 1] (the A stages are consumed)
+      float* E = reinterpret_cast<float*>(stg);  // EPI 1: [128][NP + 1] (the stages are consumed)
       for (uint32_t cc = 0; cc < cols; cc += 4) {
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         const uint32_t taddr = tmem + ((quarter * 32) << 16) + c0 + cc, nacc = nsb + (hasminA ? 1 : 0);
@@ -852,17 +864,19 @@ uint64_t qg_image_row_bytes(uint32_t cols, bool hasmin) {
   return 32 * (8 * S + (hasmin ? 2 * (S / 4) : 0));
 }
 
-// Shared memory besides the A and B stages, one A stage, one B stage.
+// Shared memory besides the stages, and one stage (the A operand of KS K steps and their B planes).
 static size_t qgemm_fixed(uint32_t kind, uint32_t cols, uint32_t np) {
   const uint32_t nsb = cols / 256;  // (+ 1 KB: the carve-up is aligned to 1 KB)
   const size_t f = kind == Q4_K ? Cfg<Q4_K>::RS * 128 * 144 : Cfg<Q6_K>::RS * 128 * 210;
   return f + 2 * nsb * 128 * 4 + 2 * np * 8 + 1024;
 }
-static size_t qgemm_astage(uint32_t kind) { return kind == Q4_K ? a_stage_bytes<Q4_K>() : a_stage_bytes<Q6_K>(); }
-static size_t qgemm_bstage(uint32_t np, bool img_hasmin) { return 2 * np * (img_hasmin ? 10 : 8) * 16; }
+static size_t qgemm_stage(uint32_t kind, uint32_t np, bool img_hasmin) {
+  const size_t b = 2 * np * (img_hasmin ? 10 : 8) * 16;
+  return kind == Q4_K ? a_stage_bytes<Q4_K>() + Cfg<Q4_K>::KS * b : a_stage_bytes<Q6_K>() + Cfg<Q6_K>::KS * b;
+}
 
-size_t qgemm_smem(uint32_t kind, uint32_t cols, uint32_t np, uint32_t as, uint32_t bs, bool img_hasmin) {
-  return qgemm_fixed(kind, cols, np) + as * qgemm_astage(kind) + bs * qgemm_bstage(np, img_hasmin);
+size_t qgemm_smem(uint32_t kind, uint32_t cols, uint32_t np, uint32_t ss, bool img_hasmin) {
+  return qgemm_fixed(kind, cols, np) + ss * qgemm_stage(kind, np, img_hasmin);
 }
 
 static size_t g_qgemm_cap = 0;  // dynamic shared memory every GEMM kernel may use (set by qgemm_prepare)
@@ -894,39 +908,32 @@ cudaError_t qgemm_prepare() {
 
 size_t qgemm_smem_cap() { return g_qgemm_cap; }
 
-// Vectors per pass (NP), A stages (AS) and B stages (BS).  NP: as large as the TMEM accumulators
-// allow (one per super-block and the Q4_K min accumulator, 2 NP columns each: at most 512), up to 64,
-// a multiple of 8.  Then the
-// stages: in flight, they hide the latency of the MMAs (A) and of the activation image in L2 (B);
-// up to 4 A stages and 8 B stages, at least 3 and 4, NP lowered until they fit.
-const char* qgemm_shape(uint32_t kind, uint32_t cols, bool img_hasmin, uint32_t* np, uint32_t* as, uint32_t* bs) {
+// Vectors per pass (NP) and stages (SS).  NP: as large as the TMEM accumulators allow (one per
+// super-block and the Q4_K min accumulator, 2 NP columns each: at most 512), up to 64, a multiple of
+// 8; lowered until 3 stages fit (up to 8).
+const char* qgemm_shape(uint32_t kind, uint32_t cols, bool img_hasmin, uint32_t* np, uint32_t* ss) {
   if (const char* why = qgemm_supported(kind, cols)) return why;
   const uint32_t acc = cols / 256 + (kind == Q4_K ? 1 : 0);
   uint32_t n = 512 / (2 * acc) / 8 * 8;  // (each accumulator: 2 n columns)
   n = n > 64 ? 64 : n;
   if (n < 8) return "the tensor-core GEMM takes at most 4096 columns of Q4_K rows";
-  const size_t cap = g_qgemm_cap, sa = qgemm_astage(kind);
+  const size_t cap = g_qgemm_cap;
   for (;; n -= 8) {
-    const size_t fixed = qgemm_fixed(kind, cols, n), sb = qgemm_bstage(n, img_hasmin);
-    for (uint32_t a = 4; a >= 2; a--) {
-      if (fixed + a * sa >= cap) continue;
-      const size_t b = (cap - fixed - a * sa) / sb;
-      if ((a >= 3 && b >= 4) || n == 8) {
-        if (b < 2) continue;
-        *np = n;
-        *as = a;
-        *bs = b > kMaxBS ? kMaxBS : (uint32_t)b;
-        return nullptr;
-      }
+    const size_t fixed = qgemm_fixed(kind, cols, n), st = qgemm_stage(kind, n, img_hasmin);
+    const size_t k = fixed < cap ? (cap - fixed) / st : 0;
+    if (k >= 3 || n == 8) {
+      if (k < 2) return "the tensor-core GEMM needs more shared memory than this device has";
+      *np = n;
+      *ss = k > kMaxSS ? kMaxSS : (uint32_t)k;
+      return nullptr;
     }
-    if (n == 8) return "the tensor-core GEMM needs more shared memory than this device has";
   }
 }
 
 
 
 void launch_qgemm(const QgArgs& a, uint32_t kind, bool swiglu, uint32_t grid, cudaStream_t s) {
-  const size_t smem = qgemm_smem(kind, a.K, a.NP, a.AS, a.BS, a.img_hasmin != 0);
+  const size_t smem = qgemm_smem(kind, a.K, a.NP, a.SS, a.img_hasmin != 0);
   if (kind == Q4_K) {
     if (swiglu) k_qgemm<Q4_K, 1><<<grid, kThreads, smem, s>>>(a);
     else k_qgemm<Q4_K, 0><<<grid, kThreads, smem, s>>>(a);
