@@ -153,3 +153,29 @@ def test_batch_sampling_matches_oracle_samplers(cuda_engine, oracle, tools):
     b.close()
     b2.close()
     eng.close()
+
+
+def test_batch_format_mix_matches_oracle(cuda_engine, oracle, tools):
+    """Q6_K attention rows and a Q4_K output matrix on the tensor cores, a Q8_0 O projection on the
+    CUDA-core batched matvec beside them, Q4_K expert down rows: per-sequence logits as the oracle's."""
+    spec = tools.TINY.with_(kind_attn=tools.Q6_K, kind_attn_out=tools.Q8_0, kind_output=tools.Q4_K,
+                            kind_down=tools.Q4_K)
+    img = tools.synth_gguf(spec)
+    eng = cuda_engine.Engine(img, 64)
+    b = cuda_engine.Batch(eng, 3, 64)
+    refs = [oracle.Model(img, 64) for _ in range(3)]
+    rng = np.random.default_rng(13)
+    prompts = [rng.integers(0, spec.vocab, n).tolist() for n in (9, 4, 30)]
+    rows = b.forward([q for q in range(3) for _ in prompts[q]], sum(prompts, []))
+    for q in range(3):
+        want = None
+        for t in prompts[q]:
+            want = refs[q].forward(t)
+        _close(rows[q], want, f"prompt of {q}")
+    for step in range(4):
+        toks = rng.integers(0, spec.vocab, 3).tolist()
+        rows = b.forward([2, 0, 1], [toks[2], toks[0], toks[1]])
+        for r, q in zip(rows, (2, 0, 1)):
+            _close(r, refs[q].forward(toks[q]), f"step {step} seq {q}")
+    b.close()
+    eng.close()

@@ -2,9 +2,10 @@
 oracle's per-token restatement of model.rs:245-287.
 
 Path 1 runs the per-token decode kernels once per token; path 2 groups the tokens per expert and
-runs gate/up and down as tcgen05 tensor-core GEMMs on exactly dequantized weights split into
-fp16 hi + lo.  Both must match the oracle's MoE output (out - x) within 5e-4 of its largest
-element (two chained matvecs at the north star's 1e-4 each, plus SwiGLU), and each other."""
+runs gate/up and down as tcgen05 tensor-core GEMMs: the K-quant integers as exact fp16 operands,
+one accumulator per 256-column super-block scaled by its d in the epilogue, activations as fp16
+hi + lo.  Both must match the oracle's MoE output (out - x) within 5e-4 of its largest element
+(two chained matvecs at the north star's 1e-4 each, plus SwiGLU), and each other."""
 import numpy as np
 import pytest
 
@@ -54,10 +55,17 @@ def _check(got, ref, x, tol=5e-4):
 SPECS = {
     "tiny": lambda tools: (tools.TINY, 0.0),
     "30b_layer": lambda tools: (tools.QWEN3_30B_A3B.with_(layers=1, vocab=512), 1.1),
+    # the other formats Q4_K_M files give expert matrices: Q4_K down (the SwiGLU epilogue then writes
+    # the down GEMM's min chunks), Q6_K gate/up (pair tiles of Q6_K rows)
+    "tiny_q4k_down": lambda tools: (tools.TINY.with_(kind_down=tools.Q4_K), 0.0),
+    "tiny_q6k_gate_up": lambda tools: (tools.TINY.with_(kind_gate_up=tools.Q6_K), 0.0),
+    "30b_q4k_down": lambda tools: (tools.QWEN3_30B_A3B.with_(layers=1, vocab=512, kind_down=tools.Q4_K), 1.1),
 }
 
 
-@pytest.mark.parametrize("which,tokens", [("tiny", [1, 5, 40]), ("30b_layer", [1, 8, 32, 130])])
+@pytest.mark.parametrize("which,tokens", [("tiny", [1, 5, 40]), ("30b_layer", [1, 8, 32, 130]),
+                                          ("tiny_q4k_down", [3, 33]), ("tiny_q6k_gate_up", [3, 33]),
+                                          ("30b_q4k_down", [40])])
 def test_moe_layer_paths_match_oracle(cuda_engine, oracle, tools, which, tokens):
     spec, skew = SPECS[which](tools)
     img = tools.synth_gguf(spec)
