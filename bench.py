@@ -610,7 +610,7 @@ def run_batch(args) -> None:
     eng.close()
     print(json.dumps({"metric": "batched decode tok/s (BASELINE config 5, one GPU)", "value": res["decode"]["tok_s"],
                       "unit": "tok/s", "higher_is_better": True, "n_gpus": 1, "dtype": "f32 activations; Q4_K/Q6_K "
-                      "weights; MoE on tcgen05 (fp16 hi/lo split, fp32 accumulate)",
+                      "weights; projections and MoE on tcgen05 (exact K-quant integers x fp16 hi/lo activations, fp32 accumulate)",
                       "data": "synthetic: random-init N(0,0.02) weights quantized from seed 0; random prompts (seed 3)",
                       "config": {"workload": "BASELINE config 5 on one GPU: 64 sequences x 2048-token prompts, 512 "
                                  "sampled steps" if (args.seqs, args.prompt, args.gen) == (64, 2048, 512)
@@ -645,7 +645,7 @@ def run_moe_layer(args) -> None:
     print(json.dumps({
         "metric": "MoE layer tokens/s (BASELINE config 3), per-token decode kernels vs tcgen05 grouped GEMMs",
         "unit": "tok/s", "higher_is_better": True, "steps": args.steps, "warmup": args.warmup,
-        "dtype": "f32 activations; Q4_K gate/up, Q6_K down, F16 router; tensor path fp16 hi/lo split, fp32 accumulate",
+        "dtype": "f32 activations; Q4_K gate/up, Q6_K down, F16 router; tensor path: exact K-quant integers x fp16 hi/lo activations, fp32 accumulate",
         "config": {"workload": "BASELINE config 3: one Qwen3-30B-A3B MoE layer", "experts": 128, "top": 8},
         **res, "clocks": sampler.summary()}), flush=True)
 

@@ -147,9 +147,11 @@ int qc_decode_enqueue(qc_engine* e, uint32_t n);
  * SwiGLU, weighted combine, residual) for n_tokens independent token vectors at once.
  * x, out: n_tokens x hidden floats in host memory.  path 1 runs the per-token decode kernels
  * once per token (matvecs); path 2 the batched kernels: tokens grouped per expert, gate/up and
- * down as tcgen05 tensor-core GEMMs (Q4_K gate/up and Q6_K down only).  device_ms (may be NULL)
- * receives the device time of the layer, copies excluded.  The KV cache and position are not
- * touched.  Not available on expert-parallel engines. */
+ * down as tcgen05 tensor-core GEMMs (gate/up and down in Q4_K or Q6_K; other formats are refused
+ * on this path).  The first path-2 call makes the engine's GEMM-layout copy of the Q4_K/Q6_K
+ * weights (about their size again in device memory).  device_ms (may be NULL) receives the device
+ * time of the layer, copies excluded.  The KV cache and position are not touched.  Not available on
+ * expert-parallel engines. */
 int qc_moe_layer(qc_engine* e, uint32_t layer, const float* x, uint32_t n_tokens, float* out, int path,
                  float* device_ms);
 
@@ -179,9 +181,11 @@ int qc_sync(qc_engine* e);
  * engine's context) beside an engine's weights, and runs any mix of their tokens as one step: a
  * decode step (one token of each of many sequences) and a prompt chunk (consecutive tokens of one
  * sequence, each attending to the ones before it) are the same call.  The dense matrices read each
- * weight once per step for all its tokens; the MoE half groups the step's tokens per expert and runs
- * gate/up and down as tcgen05 tensor-core GEMMs (Q4_K gate/up and Q6_K down; other formats run the
- * per-token kernels).  Logits agree with Model::forward on each sequence within the decode path's
+ * weight once per step for all its tokens (tcgen05 tensor-core GEMMs for Q4_K/Q6_K matrices, a
+ * CUDA-core batched matvec for other formats); the MoE half groups the step's tokens per expert and
+ * runs gate/up and down as tensor-core GEMMs (Q4_K or Q6_K experts; other formats run the per-token
+ * kernels).  Creating a batch makes the engine's GEMM-layout copy of the Q4_K/Q6_K weights (about
+ * their size again in device memory) if it does not exist yet.  Logits agree with Model::forward on each sequence within the decode path's
  * tolerance.  Error messages: qc_engine_error(engine).  Argument errors (unknown sequence, token
  * outside the vocabulary, a sequence past its context) change nothing; a call that fails on the
  * device (non-finite output) resets the sequences it carried.  The engine's own decode state is not
