@@ -24,7 +24,7 @@ namespace {
 
 constexpr int kST = 1024;
 constexpr uint32_t kExact = 16384;  // (key, index) and probability of each: 12 B in shared memory
-constexpr int kSortE = 16;           // radix sort: elements per thread per tile (tile = kST * kSortE)
+constexpr int kSortE = 8;            // radix sort: elements per thread per tile (tile = kST * kSortE)
 
 // exp(x) for the probabilities: double exp rounded once to f32.
 __device__ __forceinline__ float exp_f32(float x) { return __double2float_rn(exp((double)x)); }
@@ -76,7 +76,6 @@ struct Found {
 
 struct Shared {
   unsigned long long hist[256];
-  uint32_t offs[256];
   unsigned long long red[33];
   Found found;
   uint32_t sel_b, count, token;
@@ -212,89 +211,164 @@ __device__ __forceinline__ bool ahead_or_at(uint32_t i, uint32_t k, const Found&
   return k > f.key || (k == f.key && i <= f.idx);
 }
 
+// The lanes of the warp whose digit d (8 bits) equals this lane's, among the lanes with valid set:
+// one ballot per digit bit (match.any costs far more per element at this rate).  0 for invalid lanes.
+__device__ __forceinline__ uint32_t digit_peers(uint32_t d, bool valid) {
+  uint32_t peers = __ballot_sync(0xffffffffu, valid);
+#pragma unroll
+  for (int b = 0; b < 8; b++) {
+    const uint32_t bit = (d >> b) & 1u, bal = __ballot_sync(0xffffffffu, bit);
+    peers &= bit ? bal : ~bal;
+  }
+  return valid ? peers : 0u;
+}
+
+// Exclusive scan of v[0..256) in place, by one warp (8 per lane); returns the sum to every lane.
+__device__ uint32_t warp_scan256(uint32_t* v) {
+  const uint32_t lane = threadIdx.x & 31;
+  uint32_t x[8], s = 0;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    x[i] = v[lane * 8 + i];
+    s += x[i];
+  }
+  uint32_t incl = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= (uint32_t)o) incl += t;
+  }
+  uint32_t run = incl - s;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    v[lane * 8 + i] = run;
+    run += x[i];
+  }
+  return __shfl_sync(0xffffffffu, incl, 31);
+}
+
+constexpr uint32_t kTile = kST * kSortE;                          // ids per tile of the radix sort
+constexpr uint32_t kSortWords = 32 * 256 + 2 * kTile + 4 * 256 + 2 * 256;  // its shared memory
+
 // All n ids in (key descending, index ascending) order: a stable LSD radix sort of the inverted key
-// (4 passes of 8 bits) from index order.  Each pass counts the digits, then walks tiles of
-// kST * kSortE ids: warp w takes 32 * kSortE consecutive ids in rounds of 32, ranks each id among
-// the same digit in its warp (match_any; earlier rounds counted in cnt[w][digit]), and after a
-// scan of the warps' counts per digit every id lands at offs[digit] + (ids of that digit in
-// earlier warps) + its rank: index order is kept within each digit.  Result in key[1], idx[1].
-// cnt: [32][256] words of shared memory.
+// (4 passes of 8 bits) from index order.  One read first counts all four digits (global start of
+// each digit per pass).  Each pass then walks tiles of kTile ids: warp w takes 32 * kSortE
+// consecutive ids in rounds of 32 and ranks each among the same digit in its warp (ballots; earlier
+// rounds counted in cnt[w][digit]); a scan over the warps per digit and over the tile's digits gives
+// every id its place in the tile sorted by digit (shared memory), and the sorted tile goes out in
+// order, so each digit's run of the tile is one contiguous write at that digit's global position.
+// Index order is kept within each digit.  Result in key[1], idx[1].  sm: kSortWords words of shared
+// memory.
 __device__ void sort_desc(const float* __restrict__ lg, uint32_t n, uint32_t* const key[2], uint32_t* const idx[2],
-                          uint32_t* cnt, Shared& sh) {
+                          uint32_t* sm) {
   const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t lt = (1u << lane) - 1u;
+  uint32_t* const cnt = sm;                // [32][256] per-warp digit counts, then their prefixes
+  uint32_t* const tk = cnt + 32 * 256;     // [kTile] the tile's keys in digit order
+  uint32_t* const ti = tk + kTile;         // [kTile] and their indices
+  uint32_t* const gof = ti + kTile;        // [4][256] global start of each digit, per pass
+  uint32_t* const lst = gof + 4 * 256;     // [256] the tile's digit starts
+  uint32_t* const tot = lst + 256;         // [256] the tile's digit counts
+  for (uint32_t b = tid; b < 4 * 256; b += kST) gof[b] = 0;
+  for (uint32_t b = tid; b < 32 * 256; b += kST) cnt[b] = 0;
+  __syncthreads();
+  for (uint32_t base = 0; base < n; base += kTile) {  // the four digit histograms
+    uint32_t kv[kSortE];
+#pragma unroll
+    for (int e = 0; e < kSortE; e++) {
+      const uint32_t j = base + e * kST + tid;
+      kv[e] = j < n ? ~order_key(lg[j]) : 0u;
+    }
+#pragma unroll
+    for (int e = 0; e < kSortE; e++) {
+      const bool valid = base + e * kST + tid < n;
+      if (valid) {  // the mantissa digits are spread out: plain atomics
+        atomicAdd(&gof[kv[e] & 255u], 1u);
+        atomicAdd(&gof[256 + ((kv[e] >> 8) & 255u)], 1u);
+        atomicAdd(&gof[512 + ((kv[e] >> 16) & 255u)], 1u);
+      }
+      // the sign and exponent digit bunches up: one atomic per distinct digit of a warp
+      const uint32_t d = kv[e] >> 24, peers = digit_peers(d, valid);
+      if (valid && (peers & lt) == 0) atomicAdd(&gof[768 + d], (uint32_t)__popc(peers));
+    }
+  }
+  __syncthreads();
+  if (warp < 4) warp_scan256(gof + warp * 256);
+  __syncthreads();
   for (int pass = 0; pass < 4; pass++) {
     const int shf = 8 * pass;
     const uint32_t* ks = pass ? key[(pass - 1) & 1] : nullptr;  // pass 0 reads the logits
     const uint32_t* is = pass ? idx[(pass - 1) & 1] : nullptr;
     uint32_t* kd = key[pass & 1];
     uint32_t* id = idx[pass & 1];
-    auto kget = [&](uint32_t j) { return ks ? ks[j] : ~order_key(lg[j]); };
-    auto iget = [&](uint32_t j) { return is ? is[j] : j; };
-    for (uint32_t b = tid; b < 256; b += kST) sh.offs[b] = 0;
-    for (uint32_t b = tid; b < 32 * 256; b += kST) cnt[b] = 0;
-    __syncthreads();
-    for (uint32_t j = tid; j < n; j += kST) atomicAdd(&sh.offs[(kget(j) >> shf) & 255u], 1u);
-    __syncthreads();
-    if (tid == 0) {  // exclusive scan of the digit counts
-      uint32_t run = 0;
-      for (int b = 0; b < 256; b++) {
-        const uint32_t c = sh.offs[b];
-        sh.offs[b] = run;
-        run += c;
-      }
-    }
-    __syncthreads();
-    for (uint32_t base = 0; base < n; base += kST * kSortE) {
+    uint32_t* const go = gof + pass * 256;
+    for (uint32_t base = 0; base < n; base += kTile) {
       const uint32_t w0 = base + warp * 32 * kSortE;
-      uint32_t rank[kSortE];
+      uint32_t rank[kSortE], kv[kSortE], iv[kSortE];
+#pragma unroll
+      for (int e = 0; e < kSortE; e++) {  // the tile's keys and indices, loads all in flight together
+        const uint32_t j = w0 + e * 32 + lane;
+        kv[e] = j < n ? (ks ? ks[j] : ~order_key(lg[j])) : 0u;
+        iv[e] = j < n ? (is ? is[j] : j) : 0u;
+      }
 #pragma unroll
       for (int e = 0; e < kSortE; e++) {
-        const uint32_t j = w0 + e * 32 + lane;
-        const uint32_t d = j < n ? (kget(j) >> shf) & 255u : 256u + lane;  // past n: a class of its own
-        const uint32_t m = __match_any_sync(0xffffffffu, d);
+        const bool valid = w0 + e * 32 + lane < n;
+        const uint32_t d = (kv[e] >> shf) & 255u, peers = digit_peers(d, valid);
+        const int lead = valid ? __ffs(peers) - 1 : (int)lane;
         uint32_t r = 0;
-        if (d < 256) r = cnt[warp * 256 + d];
+        if (valid && lead == (int)lane) {
+          r = cnt[warp * 256 + d];
+          cnt[warp * 256 + d] = r + __popc(peers);
+        }
+        rank[e] = __shfl_sync(0xffffffffu, r, lead) + __popc(peers & lt);
         __syncwarp();
-        if (d < 256 && (m & lt) == 0) cnt[warp * 256 + d] = r + __popc(m);  // the group's first lane
-        __syncwarp();
-        rank[e] = r + __popc(m & lt);
       }
       __syncthreads();
-      if (tid < 256) {  // per digit: the warps' counts become their starting positions
-        uint32_t run = sh.offs[tid];
+      if (tid < 256) {  // per digit: the warps' counts become their starting positions in the digit
+        uint32_t run = 0;
+#pragma unroll 8
         for (int w = 0; w < 32; w++) {
           const uint32_t c = cnt[w * 256 + tid];
           cnt[w * 256 + tid] = run;
           run += c;
         }
-        sh.offs[tid] = run;
+        tot[tid] = run;
+        lst[tid] = run;
       }
       __syncthreads();
+      if (warp == 0) warp_scan256(lst);
+      __syncthreads();
 #pragma unroll
-      for (int e = 0; e < kSortE; e++) {
-        const uint32_t j = w0 + e * 32 + lane;
-        if (j < n) {
-          const uint32_t k = kget(j);
-          const uint32_t pos = cnt[warp * 256 + ((k >> shf) & 255u)] + rank[e];
-          kd[pos] = k;
-          id[pos] = iget(j);
+      for (int e = 0; e < kSortE; e++) {  // the tile in digit order, in shared memory
+        if (w0 + e * 32 + lane < n) {
+          const uint32_t d = (kv[e] >> shf) & 255u, lp = lst[d] + cnt[warp * 256 + d] + rank[e];
+          tk[lp] = kv[e];
+          ti[lp] = iv[e];
         }
       }
       __syncthreads();
+      const uint32_t m = min(kTile, n - base);
+      for (uint32_t i = tid; i < m; i += kST) {  // out in order: runs of one digit are contiguous
+        const uint32_t k = tk[i], d = (k >> shf) & 255u, g = go[d] + i - lst[d];
+        kd[g] = k;
+        id[g] = ti[i];
+      }
+      __syncthreads();
+      if (tid < 256) go[tid] += tot[tid];
       for (uint32_t b = tid; b < 32 * 256; b += kST) cnt[b] = 0;
       __syncthreads();
     }
   }
 }
 
-// Thread 0 visits v[0..n) in order, calling step(j, v[j]) until it returns false; the whole block
-// stages the values in shared memory (buf: kChunk floats) a chunk at a time, so the serial chain
-// reads shared memory instead of waiting on global loads.  Returns the index where the visit
-// stopped, or n.  All threads of the block call it.
+// Thread 0 visits v[0..n) in order, a chunk at a time: visit(c0, buf, m) sees v[c0 .. c0 + m) in
+// shared memory and returns how many of them it consumed before stopping (m: go on).  The whole block
+// stages each chunk (buf: kChunk floats), so the serial chain reads shared memory instead of waiting on
+// global loads.  Returns the index where the visit stopped, or n.  All threads of the block call it.
 constexpr uint32_t kChunk = 16384;
 template <class F>
-__device__ uint32_t block_serial(const float* __restrict__ v, uint32_t n, float* buf, Shared& sh, F step) {
+__device__ uint32_t block_chunks(const float* __restrict__ v, uint32_t n, float* buf, Shared& sh, F visit) {
   if (threadIdx.x == 0) sh.count = n;
   for (uint32_t c0 = 0; c0 < n; c0 += kChunk) {
     __syncthreads();
@@ -302,38 +376,106 @@ __device__ uint32_t block_serial(const float* __restrict__ v, uint32_t n, float*
     const uint32_t m = min(kChunk, n - c0);
     for (uint32_t i = threadIdx.x; i < m; i += kST) buf[i] = v[c0 + i];
     __syncthreads();
-    if (threadIdx.x == 0) {  // 8 values per pass, the next 8 loaded while these are visited
-      const float4* b4 = reinterpret_cast<const float4*>(buf);
-      const uint32_t m8 = m & ~7u;
-      bool go = true;
-      float4 x0 = m8 ? b4[0] : make_float4(0.f, 0.f, 0.f, 0.f), x1 = m8 ? b4[1] : x0;
-      for (uint32_t j = 0; j < m8 && go; j += 8) {
-        float4 y0 = x0, y1 = x1;
-        if (j + 8 < m8) {
-          y0 = b4[(j + 8) / 4];
-          y1 = b4[(j + 8) / 4 + 1];
-        }
-        const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-        for (int k = 0; k < 8; k++)
-          if (go && !step(c0 + j + k, x[k])) {
-            sh.count = c0 + j + k;
-            go = false;
-          }
-        x0 = y0;
-        x1 = y1;
-      }
-      for (uint32_t j = m8; j < m && go; j++)
-        if (!step(c0 + j, buf[j])) {
-          sh.count = c0 + j;
-          go = false;
-        }
+    if (threadIdx.x == 0) {
+      const uint32_t used = visit(c0, buf, m);
+      if (used < m) sh.count = c0 + used;
     }
   }
   __syncthreads();
   const uint32_t stop = sh.count;
   __syncthreads();
   return stop;
+}
+
+// The three sequential f32 chains of the large-set path (sampling.rs:41-63), eight terms per step
+// (each still one rounded operation after the other, exactly as the reference folds them):
+// total = fold of p with every eighth running sum; the top-p cut (the cumulative sum of q never decreases,
+// so if the eighth partial sum stays below top_p all eight do); the pick (draw < p_j exactly when
+// draw - p_j rounds below zero, and once negative the remainder stays negative).
+struct TotalChain {
+  float total;
+  float* run;
+  __device__ uint32_t operator()(uint32_t c0, const float* b, uint32_t m) {
+    uint32_t j = 0;
+    for (; j + 8 <= m; j += 8) {
+      const float4 x0 = *reinterpret_cast<const float4*>(b + j), x1 = *reinterpret_cast<const float4*>(b + j + 4);
+      float t = total;
+      t = __fadd_rn(t, x0.x); t = __fadd_rn(t, x0.y); t = __fadd_rn(t, x0.z); t = __fadd_rn(t, x0.w);
+      t = __fadd_rn(t, x1.x); t = __fadd_rn(t, x1.y); t = __fadd_rn(t, x1.z); t = __fadd_rn(t, x1.w);
+      run[c0 + j + 7] = t;  // one running sum per 8 terms (positions 7 mod 8; run_at recomputes the rest)
+      total = t;
+    }
+    for (; j < m; j++) {
+      total = __fadd_rn(total, b[j]);
+      run[c0 + j] = total;
+    }
+    return m;
+  }
+};
+struct CutChain {
+  float cum, top_p;
+  __device__ uint32_t operator()(uint32_t, const float* b, uint32_t m) {
+    uint32_t j = 0;
+    for (; j + 8 <= m; j += 8) {
+      const float4 x0 = *reinterpret_cast<const float4*>(b + j), x1 = *reinterpret_cast<const float4*>(b + j + 4);
+      float c[8];
+      c[0] = __fadd_rn(cum, x0.x); c[1] = __fadd_rn(c[0], x0.y); c[2] = __fadd_rn(c[1], x0.z);
+      c[3] = __fadd_rn(c[2], x0.w); c[4] = __fadd_rn(c[3], x1.x); c[5] = __fadd_rn(c[4], x1.y);
+      c[6] = __fadd_rn(c[5], x1.z); c[7] = __fadd_rn(c[6], x1.w);
+      if (c[7] >= top_p) {
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+          if (c[k] >= top_p) return j + k;
+      }
+      cum = c[7];
+    }
+    for (; j < m; j++) {
+      cum = __fadd_rn(cum, b[j]);
+      if (cum >= top_p) return j;
+    }
+    return m;
+  }
+};
+struct PickChain {
+  float draw;
+  __device__ uint32_t operator()(uint32_t, const float* b, uint32_t m) {
+    uint32_t j = 0;
+    for (; j + 8 <= m; j += 8) {
+      const float4 x0 = *reinterpret_cast<const float4*>(b + j), x1 = *reinterpret_cast<const float4*>(b + j + 4);
+      float e[8];
+      e[0] = __fsub_rn(draw, x0.x); e[1] = __fsub_rn(e[0], x0.y); e[2] = __fsub_rn(e[1], x0.z);
+      e[3] = __fsub_rn(e[2], x0.w); e[4] = __fsub_rn(e[3], x1.x); e[5] = __fsub_rn(e[4], x1.y);
+      e[6] = __fsub_rn(e[5], x1.z); e[7] = __fsub_rn(e[6], x1.w);
+      if (e[7] < 0.f) {
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+          if (e[k] < 0.f) return j + k;
+      }
+      draw = e[7];
+    }
+    for (; j < m; j++) {
+      if (draw < b[j]) return j;
+      draw = __fsub_rn(draw, b[j]);
+    }
+    return m;
+  }
+};
+
+// The running sum of the fold of p after term q, from the stored sums (positions 7 mod 8, and every
+// position of a chunk's tail): the same additions as the fold, in the same order.
+__device__ float run_at(const float* p, const float* run, uint32_t q, uint32_t n) {
+  const uint32_t c0 = q / kChunk * kChunk, m = min(kChunk, n - c0), tail = c0 + (m & ~7u);
+  if ((q & 7) == 7 || q >= tail) return run[q];
+  const uint32_t j0 = q & ~7u;
+  float t = j0 ? run[j0 - 1] : 0.f;
+  for (uint32_t j = j0; j <= q; j++) t = __fadd_rn(t, p[j]);
+  return t;
+}
+
+// The logit of a sorted key (the sort keeps ~order_key(logit)): order_key inverted.
+__device__ __forceinline__ float key_value(uint32_t nk) {
+  const uint32_t k = ~nk;
+  return __uint_as_float((k >> 31) ? (k ^ 0x80000000u) : ~k);
 }
 
 // One block per draw: block b samples logits row b (lg_base + b * lg_stride) with sampler sv[b]
@@ -456,40 +598,32 @@ __global__ void __launch_bounds__(kST) k_sample(SampleBatch sb, uint32_t n) {
       // all n ids sorted in scratch; the top-k set is the first Kset of them (sampling.rs:32-39)
       uint32_t* const key[2] = {scr.key0, scr.key1};
       uint32_t* const idx[2] = {scr.idx0, scr.idx1};
-      sort_desc(lg, n, key, idx, reinterpret_cast<uint32_t*>(dyn), sh);
+      sort_desc(lg, n, key, idx, reinterpret_cast<uint32_t*>(dyn));
       const uint32_t K = Kset, *const ids = scr.idx1;
-      for (uint32_t j = tid; j < K; j += kST) scr.p[j] = exp_f32(__fdiv_rn(__fsub_rn(lg[ids[j]], mx), temp));
+      // probabilities in sorted order, from the sorted keys (no gather of the logits)
+      for (uint32_t j = tid; j < K; j += kST) scr.p[j] = exp_f32(__fdiv_rn(__fsub_rn(key_value(scr.key1[j]), mx), temp));
       __syncthreads();
       float* const buf = reinterpret_cast<float*>(dyn);  // (the sort's counters are consumed)
-      float total = 0.f;  // thread 0: the total with its running sums (sampling.rs:44)
-      block_serial(scr.p, K, buf, sh, [&](uint32_t j, float x) {
-        total = __fadd_rn(total, x);
-        scr.run[j] = total;
-        return true;
-      });
+      TotalChain tc{0.f, scr.run};  // thread 0: the total with its running sums (sampling.rs:44)
+      block_chunks(scr.p, K, buf, sh, [&](uint32_t c0, const float* b, uint32_t m) { return tc(c0, b, m); });
+      const float total = tc.total;
       if (tid == 0) sh.red[0] = __float_as_uint(total);
       __syncthreads();
       const float tot = __uint_as_float((uint32_t)sh.red[0]);
       for (uint32_t j = tid; j < K; j += kST) scr.q[j] = __fdiv_rn(scr.p[j], tot);
       __syncthreads();
       // top-p: the first j whose cumulative sum of p / total reaches top_p (sampling.rs:45-52)
-      float cum = 0.f;
-      const uint32_t cut = block_serial(scr.q, K, buf, sh, [&](uint32_t, float x) {
-        cum = __fadd_rn(cum, x);
-        return !(cum >= top_p);
-      });
+      CutChain cc{0.f, top_p};
+      const uint32_t cut = block_chunks(scr.q, K, buf, sh, [&](uint32_t c0, const float* b, uint32_t m) { return cc(c0, b, m); });
       const uint32_t keep = cut < K ? cut + 1 : K;
       // the draw over the kept probabilities; their mass is the total's running sum at keep - 1
       float draw = 0.f;
       if (tid == 0) {
-        const float mass = scr.run[keep - 1];
+        const float mass = run_at(scr.p, scr.run, keep - 1, K);
         draw = __fmul_rn((float)(next_word(s) >> 8) * (1.0f / 16777216.0f), mass);
       }
-      const uint32_t hit = block_serial(scr.p, keep, buf, sh, [&](uint32_t, float x) {  // sampling.rs:56-63
-        if (draw < x) return false;
-        draw = __fsub_rn(draw, x);
-        return true;
-      });
+      PickChain pc{draw};  // sampling.rs:56-63
+      const uint32_t hit = block_chunks(scr.p, keep, buf, sh, [&](uint32_t c0, const float* b, uint32_t m) { return pc(c0, b, m); });
       if (tid == 0) sh.token = ids[hit < keep ? hit : keep - 1];
       __syncthreads();
       token = sh.token;
@@ -508,8 +642,9 @@ __global__ void k_sampler_words(SamplerDev* s, uint32_t n, uint32_t* out) {
 
 }  // namespace
 
-constexpr int kSampleSmem = kExact * 12;  // also holds the radix sort's [32][256] counters
-static_assert(kExact * 12 >= 32 * 256 * 4, "sort counters fit the exact path's shared memory");
+constexpr int kSampleSmem = kExact * 12;  // also holds the radix sort's tiles and counters
+static_assert(kExact * 12 >= kSortWords * 4, "the radix sort fits the exact path's shared memory");
+static_assert(kExact * 12 >= kChunk * 4, "a chain chunk fits the exact path's shared memory");
 
 uint32_t sample_exact_max() { return kExact; }
 
