@@ -557,16 +557,27 @@ def run_reference(args) -> None:
     }), flush=True)
 
 
-def batch_study(T, E, eng, spec, seqs: int, prompt: int, gen: int, log_every: int = 0) -> dict:
-    """BASELINE config 5 on one GPU: `seqs` sequences, each a `prompt`-token random prompt (seed 3)
-    prefilled in chunks of 128 tokens (one sequence per call), then `gen` decode steps of all
-    sequences at once on the device (qc_batch_decode_sample: sample every sequence, run the step),
-    temperature 0.7, top-p 0.9, top-k off, one seeded sampler per sequence."""
+def batch_study(T, E, eng, spec, seqs: int, prompt: int, gen: int, log_every: int = 0, rank: int = 0,
+                world: int = 1) -> dict:
+    """`seqs` sequences, each a `prompt`-token random prompt (seed 3) prefilled in
+    chunks of 128 tokens (one sequence per call), then `gen` decode steps of all sequences at once on
+    the device (qc_batch_decode_sample: sample every sequence, run the step), temperature 0.7, top-p
+    0.9, top-k off, one seeded sampler per sequence.  With world > 1 (an expert-parallel engine) this
+    rank runs sequences [rank * seqs / world, (rank + 1) * seqs / world) and the counts returned are
+    this rank's."""
     import torch
-    b = E.Batch(eng, seqs, CTX)
+    n = seqs // world
+    first = rank * n
+    b = E.Batch(eng, n, CTX)
+    if world > 1:
+        E.connect_group(b)
     rng = np.random.default_rng(3)
-    prompts = rng.integers(0, spec.vocab, (seqs, prompt)).astype(np.uint32)
+    prompts = rng.integers(0, spec.vocab, (seqs, prompt)).astype(np.uint32)[first:first + n]
+    seqs = n
     torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
     s0 = b.stats()
     w0 = time.perf_counter()
     for q in range(seqs):
@@ -577,7 +588,9 @@ def batch_study(T, E, eng, spec, seqs: int, prompt: int, gen: int, log_every: in
             log(f"batch: prefilled {q + 1}/{seqs} sequences")
     prefill_s = time.perf_counter() - w0
     s1 = b.stats()
-    samplers = [E.Sampler(1000 + q, 0.7, 0, 0.9) for q in range(seqs)]
+    samplers = [E.Sampler(1000 + first + q, 0.7, 0, 0.9, device=torch.cuda.current_device()) for q in range(seqs)]
+    if world > 1:
+        dist.barrier()
     w1 = time.perf_counter()
     ids = b.decode_sample(samplers, np.arange(seqs, dtype=np.uint32), gen)
     decode_s = time.perf_counter() - w1
@@ -595,29 +608,67 @@ def batch_study(T, E, eng, spec, seqs: int, prompt: int, gen: int, log_every: in
 
 
 def run_batch(args) -> None:
-    """BASELINE config 5 (`--config 5`) on one GPU: the batched line."""
+    """BASELINE config 5 (`--config 5`): the batched line; under torchrun with N > 1 ranks the
+    BASELINE split: sequences data-parallel, experts sharded, dispatch / combine per layer between
+    the ranks (qc_batch_ep_*).  Times: the slowest rank's (device and wall)."""
     import torch
     from qwen30brust_b200 import engine as E, tools as T
-    torch.cuda.set_device(0)
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+        if args.seqs % world:
+            raise SystemExit("--seqs must be a multiple of the rank count")
     spec = T.QWEN3_30B_A3B
     if args.layers:  # a shallower model of the same shapes: profiling runs only
         spec = spec.with_(layers=args.layers)
-    img = T.synth_gguf(spec)
-    eng = E.Engine(img, CTX)
-    sampler = ClockSampler(0)
+    img, path = synth_image(T, spec, rank, world)
+    if world > 1:
+        src = np.memmap(path, dtype=np.uint8, mode="r")
+        eng = E.Engine.expert_parallel(src, CTX, local, rank, world)
+        del src
+    else:
+        eng = E.Engine(img, CTX)
+    sampler = ClockSampler(local)
     with sampler:
-        res = batch_study(T, E, eng, spec, args.seqs, args.prompt, args.gen, log_every=8)
+        res = batch_study(T, E, eng, spec, args.seqs, args.prompt, args.gen, log_every=8 if rank == 0 else 0,
+                          rank=rank, world=world)
     eng.close()
-    print(json.dumps({"metric": "batched decode tok/s (BASELINE config 5, one GPU)", "value": res["decode"]["tok_s"],
-                      "unit": "tok/s", "higher_is_better": True, "n_gpus": 1, "dtype": "f32 activations; Q4_K/Q6_K "
+    if world > 1:  # whole-job rates: all ranks' tokens over the slowest rank's times
+        pre_dev = res["sequences"] * res["prompt"] / res["prefill"]["device_tok_s"]  # this rank's device seconds
+        t = torch.tensor([res["prefill"]["seconds"], res["decode"]["seconds"], pre_dev, res["decode"]["ms_per_step"]],
+                         dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        pre_s, dec_s, pre_dev_s, dec_ms = t.tolist()
+        pre_tok, dec_tok = args.seqs * args.prompt, args.seqs * args.gen
+        res["sequences"] = args.seqs
+        res["prefill"].update(tok_s=pre_tok / pre_s, device_tok_s=pre_tok / pre_dev_s, seconds=pre_s)
+        res["decode"].update(tok_s=dec_tok / dec_s, device_tok_s=dec_tok / (dec_ms * args.gen / 1e3), seconds=dec_s,
+                             ms_per_step=dec_ms)
+        res["expert_parallel"] = {"ranks": world, "experts_per_rank": spec.experts // world,
+                                  "sequences_per_rank": args.seqs // world,
+                                  "exchange": "per layer: every rank's normalized inputs and selections gathered "
+                                              "(hidden x 4 B per token), expert outputs pulled by each token's rank "
+                                              "(top x hidden x 4 B per token), two flag barriers"}
+        dist.destroy_process_group()
+        if rank != 0:
+            return
+    print(json.dumps({"metric": "batched decode tok/s (BASELINE config 5)", "value": res["decode"]["tok_s"],
+                      "unit": "tok/s", "higher_is_better": True, "n_gpus": world, "dtype": "f32 activations; Q4_K/Q6_K "
                       "weights; projections and MoE on tcgen05 (exact K-quant integers x fp16 hi/lo activations, fp32 accumulate)",
                       "data": "synthetic: random-init N(0,0.02) weights quantized from seed 0; random prompts (seed 3)",
-                      "config": {"workload": "BASELINE config 5 on one GPU: 64 sequences x 2048-token prompts, 512 "
+                      "config": {"workload": "BASELINE config 5: 64 sequences x 2048-token prompts, 512 "
                                  "sampled steps" if (args.seqs, args.prompt, args.gen) == (64, 2048, 512)
                                  else f"BASELINE config 5 shape, reduced: {args.seqs} sequences x {args.prompt}-token "
                                       f"prompts, {args.gen} sampled steps" + (
                                           f", {args.layers} layers (profiling run, not a bench line)" if args.layers
-                                          else ""), "parallelism": "single GPU"},
+                                          else ""),
+                                 "parallelism": f"expert parallel x{world} (sequences data-parallel)" if world > 1
+                                 else "single GPU"},
                       **res, "clocks": sampler.summary()}), flush=True)
 
 

@@ -211,6 +211,21 @@ int qc_batch_decode_sample(qc_batch* b, qc_sampler* const* samplers, const uint3
                            uint32_t* tokens_out);
 /* Tokens run, device time of the steps (matvec_ms), KV and weight bytes. */
 int qc_batch_stats(const qc_batch* b, qc_stats* out);
+/* Expert parallelism of a batch (BASELINE config 5 over 2-8 GPUs: dispatch and combine of the MoE
+ * half; no counterpart in the reference, which runs one sequence on one device): a batch of an expert-parallel engine (qc_engine_create_gguf_ep)
+ * holds this rank's own sequences (attention, dense rows and vocabulary run data-parallel) and, per
+ * layer, exchanges the MoE half with the other ranks through their exchange regions over NVLink:
+ * every rank publishes its tokens' normalized inputs and router selections, each rank runs its
+ * experts' GEMMs over the pairs of all ranks' tokens routed to them, and each token's home rank sums
+ * its experts' outputs in selection order (the same arithmetic as one GPU).  Two barriers per layer
+ * (system-scope flags, waits bounded at 2 s).  The batch needs the tensor-core MoE path (Q4_K/Q6_K
+ * experts).  Before the first forward each rank exports qc_batch_ep_handle, the host gathers the
+ * handles in rank order and passes them to qc_batch_ep_connect on every rank.  All ranks must then
+ * make the same forward / decode calls with the same token counts, in the same order; a rank that
+ * stops or a count mismatch ends the others' call with an error, after which every rank's batch
+ * must be destroyed and created again. */
+int qc_batch_ep_handle(qc_batch* b, void* handle, int* device_id);
+int qc_batch_ep_connect(qc_batch* b, const void* handles, const int* device_ids);
 
 /* model.rs:202-208: clear the KV cache and set the position to 0. */
 int qc_reset(qc_engine* e);

@@ -874,7 +874,7 @@ struct qc_engine {
     if (moe_sw.empty()) moe_sw.assign(3 * cfg.layers, 0.f);
     if (moe_sw[3 * layer] == 0.f) {
       const qc::MatDesc* m[3] = {&a.gate, &a.up, &a.down};
-      for (int i = 0; i < 3; i++) moe_sw[3 * layer + i] = dmin_scale(*m[i], cfg.experts, a.err);
+      for (int i = 0; i < 3; i++) moe_sw[3 * layer + i] = dmin_scale(*m[i], e_n, a.err);
     }
     a.smin_g = moe_sw[3 * layer];
     a.smin_u = moe_sw[3 * layer + 1];
@@ -1019,14 +1019,67 @@ struct qc_batch {
   void* d_sscr = nullptr;               // [n_seqs] sample scratch (sets beyond shared memory)
   qc_stats stats{};
   std::string err;
+  // expert parallelism (an engine holding experts/world of every layer): this rank's exchange region
+  // (moe.cu MoeEp layout, two buffer sets), the peers' regions mapped by CUDA IPC, the barrier count
+  // and the running layer count that picks the buffer set
+  uint8_t* d_ep = nullptr;
+  uint8_t* ep_peer[8] = {};
+  uint8_t** d_ep_peers = nullptr;
+  qc::MoeEp ep_set[2] = {};
+  bool ep_connected = false, ep_failed = false;
+  unsigned long long ep_seq = 0, ep_layers = 0;
 
   ~qc_batch() {
     cudaSetDevice(e->device);
     if (e->stream) cudaStreamSynchronize(e->stream);
+    for (uint32_t q = 0; q < e->ep_world && q < 8; q++)
+      if (q != e->ep_rank && ep_peer[q]) cudaIpcCloseMemHandle(ep_peer[q]);
+    cudaFree(d_ep);
+    cudaFree(d_ep_peers);
     cudaFree(d_kv);
     cudaFree(d_buf);
     cudaFree(d_out);
     cudaFree(d_sscr);
+  }
+
+  // ---- expert parallelism: exchange-region handles (as qc_engine's) ---------------------------
+  void ep_handle(void* out_handle, int* pci) {
+    ensure(e->ep_world > 1, "not an expert-parallel engine");
+    QC_CK(cudaSetDevice(e->device));
+    cudaIpcMemHandle_t h;
+    QC_CK(cudaIpcGetMemHandle(&h, d_ep));
+    std::memcpy(out_handle, &h, sizeof h);
+    cudaDeviceProp prop;
+    QC_CK(cudaGetDeviceProperties(&prop, e->device));
+    *pci = prop.pciDomainID * 65536 + prop.pciBusID * 256 + prop.pciDeviceID;
+  }
+  void ep_connect(const uint8_t* handles, const int* pci) {
+    const uint32_t W = e->ep_world, R = e->ep_rank;
+    ensure(W > 1, "not an expert-parallel engine");
+    ensure(!ep_connected, "expert-parallel batch already connected");
+    for (uint32_t a = 0; a < W; a++)
+      for (uint32_t b = a + 1; b < W; b++)
+        ensure(pci[a] != pci[b], "expert-parallel ranks must be on different GPUs");  // kernels wait on each other
+    QC_CK(cudaSetDevice(e->device));
+    for (uint32_t q = 0; q < W; q++) {
+      if (q == R) {
+        ep_peer[q] = d_ep;
+        continue;
+      }
+      cudaIpcMemHandle_t h;
+      std::memcpy(&h, handles + 64 * q, sizeof h);
+      void* ptr = nullptr;
+      QC_CK(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+      ep_peer[q] = static_cast<uint8_t*>(ptr);
+    }
+    QC_CK(cudaMemcpy(d_ep_peers, ep_peer, 8 * sizeof(uint8_t*), cudaMemcpyHostToDevice));
+    ep_connected = true;
+  }
+  // Entry check of every call that runs passes.
+  void ep_ready() const {
+    if (e->ep_world == 1) return;
+    ensure(ep_connected, "expert-parallel batch is not connected to its peers");
+    ensure(!ep_failed, "an expert-parallel exchange of this batch failed; create a new batch on every rank");
   }
 
   qc::BatchArgs args() const {
@@ -1046,7 +1099,6 @@ struct qc_batch {
 
   void create(qc_engine* eng, uint32_t n, uint32_t ctx) {
     e = eng;
-    ensure(e->ep_world == 1, "an expert-parallel engine holds only its own experts");
     ensure(n > 0 && n <= 4096, "sequence count must be in 1..=4096");
     ensure(ctx > 0 && ctx <= e->context, "batch context must be in 1..=" + std::to_string(e->context));
     n_seqs = n;
@@ -1105,10 +1157,26 @@ struct qc_batch {
     QC_CK(cudaMalloc(&d_buf, o));
     QC_CK(cudaMemsetAsync(d_buf, 0, o, e->stream));
     e->ensure_gemm();
-    e->grow_moe(cap);
+    const uint32_t W = e->ep_world;
+    e->grow_moe(W * cap);  // (expert parallelism: every rank's tokens of a pass)
     for (uint32_t l = 0; l < c.layers; l++) {  // the tensor-core weight scales of every layer, once
       qc::MoeArgs ma = e->moe_args(l, cap);
-      if (!qc::moe_tc_supported(ma)) e->moe_scales(l, ma);
+      const char* why = qc::moe_tc_supported(ma);
+      if (W > 1 && why) throw ApiError(QC_ERR_INVALID, std::string("expert-parallel batches need the tensor-core MoE path: ") + why);
+      if (!why) e->moe_scales(l, ma);
+    }
+    if (W > 1) {
+      const uint64_t eb = qc::moe_ep_layout(cap, c.hidden, c.top, W, &ep_set[0], &ep_set[1]);
+      QC_CK(cudaMalloc(&d_ep, eb));
+      QC_CK(cudaMemsetAsync(d_ep, 0, eb, e->stream));
+      QC_CK(cudaMalloc(&d_ep_peers, 8 * sizeof(uint8_t*)));
+      for (qc::MoeEp& m : ep_set) {
+        m.rank = e->ep_rank;
+        m.world = W;
+        m.e_n = e->e_n;
+        m.peers = d_ep_peers;
+        m.own = d_ep;
+      }
     }
     QC_CK(cudaMemsetAsync(e->moe_args(0, 1).err, 0, 4, e->stream));
     d_tok = reinterpret_cast<qc::BatchTok*>(d_buf + o_tok);
@@ -1232,7 +1300,14 @@ struct qc_batch {
       }
       // the MoE half (model.rs:249-287): tensor-core path when the formats allow, else per token
       qc::MoeArgs ma = e->moe_args(l, T);
-      if (!qc::moe_tc_supported(ma)) {
+      if (e->ep_world > 1) {  // tokens of every rank to the experts of this rank, and back
+        e->moe_scales(l, ma);
+        qc::MoeEp ep = ep_set[ep_layers++ & 1];
+        ep.T = T;
+        if (const char* why = qc::launch_moe_tc_ep(ma, ep, ep_seq + 1, d_x, d_x2, s)) throw ApiError(QC_ERR_CUDA, why);
+        ep_seq += 2;
+        std::swap(d_x, d_x2);
+      } else if (!qc::moe_tc_supported(ma)) {
         e->moe_scales(l, ma);  // (measured at creation: only reads the cached scales)
         if (const char* why = qc::launch_moe_tc(ma, d_x, d_x2, s)) throw ApiError(QC_ERR_CUDA, why);
         std::swap(d_x, d_x2);
@@ -1269,6 +1344,14 @@ struct qc_batch {
     QC_CK(cudaMemsetAsync(d_flag, 0, 4, e->stream));
     QC_CK(cudaMemsetAsync(e->moe_args(0, 1).err, 0, 4, e->stream));
     e->check_flags();  // per-token MoE fallback: non-finite router logits
+    if (h[1] & 8) {
+      ep_failed = true;
+      throw ApiError(QC_ERR_CUDA, "expert-parallel exchange: a peer did not reach the barrier within 2 s");
+    }
+    if (h[1] & 16) {
+      ep_failed = true;
+      throw ApiError(QC_ERR_INVALID, "expert-parallel ranks ran passes of different token counts");
+    }
     if (h[1] & 2) throw ApiError(QC_ERR_CUDA, "tensor-core kernel: a wait timed out");
     if (h[1] & 1) throw ApiError(QC_ERR_NONFINITE, "invalid MoE router");
     if (h[1] & 4) throw ApiError(QC_ERR_NONFINITE, "an expert activation outside the fp16 range of the tensor-core path");
@@ -1306,6 +1389,7 @@ struct qc_batch {
     std::vector<qc::BatchTok> tk;
     std::vector<uint8_t> last;
     ensure(toks, "null argument");
+    ep_ready();
     plan(seqs, toks, n, tk, last);
     started = true;
     QC_CK(cudaSetDevice(e->device));
@@ -1388,6 +1472,7 @@ struct qc_batch {
   // logits with its sampler and run the n sampled ids as one step.  out: steps x n ids (host).
   void decode_sample(qc_sampler* const* smp, const uint32_t* seqs, uint32_t n, uint32_t steps, uint32_t* out) {
     ensure(n > 0 && n <= cap && n <= n_seqs && smp && seqs, "invalid draws");
+    ep_ready();
     std::vector<uint8_t> seen(n_seqs, 0);
     for (uint32_t i = 0; i < n; i++) {
       ensure(seqs[i] < n_seqs && !seen[seqs[i]], "sequences of a decode loop must be distinct");
@@ -1945,6 +2030,22 @@ int qc_batch_sample(qc_batch* b, qc_sampler* const* samplers, const uint32_t* se
 int qc_batch_decode_sample(qc_batch* b, qc_sampler* const* samplers, const uint32_t* seq_ids, uint32_t n, uint32_t steps,
                            uint32_t* tokens_out) {
   return batch_call(b, seq_ids, n, [&] { b->decode_sample(samplers, seq_ids, n, steps, tokens_out); });
+}
+
+int qc_batch_ep_handle(qc_batch* b, void* handle, int* device_id) {
+  if (!b) return g_last_error = "null batch", QC_ERR_INVALID;
+  return api(b->e, [&] {
+    ensure(handle && device_id, "null argument");
+    b->ep_handle(handle, device_id);
+  });
+}
+
+int qc_batch_ep_connect(qc_batch* b, const void* handles, const int* device_ids) {
+  if (!b) return g_last_error = "null batch", QC_ERR_INVALID;
+  return api(b->e, [&] {
+    ensure(handles && device_ids, "null argument");
+    b->ep_connect(static_cast<const uint8_t*>(handles), device_ids);
+  });
 }
 
 int qc_batch_stats(const qc_batch* b, qc_stats* out) {

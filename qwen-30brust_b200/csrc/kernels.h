@@ -177,6 +177,7 @@ struct MoeArgs {
   float smin_g, smin_u, smin_d;  // Q4_K min-block scales of the tensor-core GEMM (qgemm.cu)
   uint32_t NPgu, NPdn, SSgu, SSdn;  // vectors per GEMM pass and stages (qgemm_shape)
   int sms;
+  uint32_t e_lo, e_n;  // experts the GEMM weights hold: [e_lo, e_lo + e_n) (e_n 0: all E)
   // scratch
   float* h;          // [T][H] normalized inputs
   float* hscale;     // [T] power-of-two scale of each token's h
@@ -194,7 +195,8 @@ struct MoeArgs {
   uint8_t* img_gu;   // gate/up activation image (hidden columns)
   uint8_t* img_dn;   // down activation image (intermediate columns), written by the SwiGLU epilogue
   float* y;          // [T*top][H] down outputs by pair id
-  uint32_t* err;     // bit 0: non-finite router logit; bit 1: a tensor-core wait timed out; bit 2: fp16 range
+  uint32_t* err;     // bit 0: non-finite router logit; bit 1: a tensor-core wait timed out; bit 2: fp16 range;
+                     // bit 3: an expert-parallel barrier timed out; bit 4: ranks with different token counts
 };
 const char* moe_tc_supported(const MoeArgs& a);
 // Rows of the activation images for T tokens (pairs rounded up to 16 per expert), at most.
@@ -202,6 +204,32 @@ uint32_t moe_image_rows(uint32_t T, uint32_t top, uint32_t E);
 // x [T][H] -> out [T][H]: route, plan, tensor-core gate/up + SwiGLU, down, combine.
 // (null, or why it could not launch)
 const char* launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStream_t s);
+
+// Expert parallelism of the batched MoE layer: `world` ranks, one GPU each, every rank with T tokens
+// of its own sequences and experts [rank * e_n, (rank + 1) * e_n).  Each rank's exchange region
+// (device memory of that rank, mapped into every other rank) holds, at the byte offsets below:
+//   flags [8] u64   flags[q]: the latest barrier number rank q has passed (written by rank q)
+//   hdr   u32       this layer's T
+//   h     [T][H]    the tokens' normalized inputs; hs [T] their scales; sel [T][top] their experts
+//   y     [world * T * top][H]  down outputs of the pairs routed here, by global pair id
+//                   (global token g = rank * T + t, pair g * top + slot)
+// hdr .. y are double-buffered by the caller (one set per parity of a running layer count).
+struct MoeEp {
+  uint32_t rank, world, e_n, T;
+  uint8_t* const* peers;  // [world] every rank's exchange region (device array; own included)
+  uint8_t* own;           // this rank's region
+  uint64_t o_flags, o_hdr, o_h, o_hs, o_sel, o_y;
+};
+// Bytes of one rank's exchange region and the offsets of the two buffer sets (b = 0, 1).
+uint64_t moe_ep_layout(uint32_t cap, uint32_t H, uint32_t top, uint32_t world, MoeEp* set0, MoeEp* set1);
+// As launch_moe_tc, over all ranks' tokens for this rank's experts: route and select into the
+// exchange, barrier `seq`, gather every rank's inputs and selections, plan / image / GEMMs over the
+// pairs of the local experts (down outputs into the exchange), barrier `seq + 1`, then the combine
+// of this rank's tokens from the ranks that hold their experts, in selection order.  a.T = ep.T
+// (this rank's tokens); a's scratch holds world * T tokens.  Barrier waits give up after 2 s
+// (err bit 3); ranks with different T set err bit 4.
+const char* launch_moe_tc_ep(const MoeArgs& a, const MoeEp& ep, unsigned long long seq, const float* x, float* out,
+                             cudaStream_t s);
 // The per-token MoE kernels of the decode step (router, gate/up, down) on the vector c.x, in place.
 StepPlan plan_moe(const DecodeDims& d, const LayerDev& L, int sms);
 void launch_moe_token(const DecodeDims& d, const StepPlan& p, const LayerDev& L, const Scratch& c, DevState* st,

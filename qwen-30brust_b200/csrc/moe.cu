@@ -116,12 +116,19 @@ __global__ void __launch_bounds__(128) k_moe_select(MoeArgs a) {
 // Expert e's pairs are rows imgoff_e .. imgoff_e + nimg_e of the activation images (nimg_e = its pair
 // count rounded up to 16); its gate/up group has ceil(I / 64) tiles and its down group ceil(H / 128),
 // each times ceil(nimg_e / NP) passes.
+// Only pairs of the experts the weights hold ([e_lo, e_lo + e_n)) are planned; group expert ids are
+// relative to e_lo.
 __global__ void __launch_bounds__(1024) k_moe_plan(MoeArgs a) {
   __shared__ uint32_t cnt[1024], off[1025], igu[1025], idn[1025], img[1025];
   const uint32_t tid = threadIdx.x, P = a.T * a.top, lane = tid & 31, warp = tid >> 5;
+  const uint32_t elo = a.e_n ? a.e_lo : 0, en = a.e_n ? a.e_n : a.E;
+  auto held = [&](uint32_t e) { return e - elo < en; };
   for (uint32_t e = tid; e < a.E; e += 1024) cnt[e] = 0;
   __syncthreads();
-  for (uint32_t p = tid; p < P; p += 1024) atomicAdd(&cnt[a.sel[p]], 1u);
+  for (uint32_t p = tid; p < P; p += 1024) {
+    const uint32_t e = a.sel[p];
+    if (held(e)) atomicAdd(&cnt[e], 1u);
+  }
   __syncthreads();
   if (tid == 0) {
     const uint32_t tgu = (a.I + 63) / 64, tdn = (a.H + 127) / 128;
@@ -142,8 +149,9 @@ __global__ void __launch_bounds__(1024) k_moe_plan(MoeArgs a) {
     a.cnt[e] = cnt[e];
     a.off[e] = off[e];
     const uint32_t n = (cnt[e] + 15) & ~15u;
-    a.groups[e] = QgGroup{igu[e], cnt[e], n, img[e], 0, e, nullptr, nullptr, nullptr, a.ptok + off[e], 0};
-    a.groups[a.E + e] = QgGroup{idn[e], cnt[e], n, img[e], 0, e, a.y, nullptr, a.ppair + off[e], nullptr, a.H};
+    const uint32_t le = held(e) ? e - elo : 0;
+    a.groups[e] = QgGroup{igu[e], cnt[e], n, img[e], 0, le, nullptr, nullptr, nullptr, a.ptok + off[e], 0};
+    a.groups[a.E + e] = QgGroup{idn[e], cnt[e], n, img[e], 0, le, a.y, nullptr, a.ppair + off[e], nullptr, a.H};
   }
   // (the order of an expert's pairs does not change any result: each is its own GEMM column; the
   // loop above handles expert e in the same thread, so the count can be reset here)
@@ -151,6 +159,7 @@ __global__ void __launch_bounds__(1024) k_moe_plan(MoeArgs a) {
   __syncthreads();
   for (uint32_t p = tid; p < P; p += 1024) {
     const uint32_t e = a.sel[p];
+    if (!held(e)) continue;
     const uint32_t pos = off[e] + atomicAdd(&cnt[e], 1u);
     a.ptok[pos] = p / a.top;
     a.ppair[pos] = p;
@@ -176,31 +185,90 @@ __global__ void __launch_bounds__(256) k_moe_combine(MoeArgs a, const float* __r
   }
 }
 
-}  // namespace
-
-const char* moe_tc_supported(const MoeArgs& a) {
-  if (a.gate.kind != a.up.kind) return "the tensor-core MoE path needs gate and up rows of one format";
-  if (const char* why = qgemm_supported(a.gate.kind, a.H)) return why;
-  if (const char* why = qgemm_supported(a.down.kind, a.I)) return why;
-  if (a.I % 64) return "the tensor-core MoE path needs an intermediate size in multiples of 64";
-  if (a.router.kind != F16) return "the batched MoE path takes an F16 router";
-  if (a.E > 1024) return "the batched MoE path takes at most 1024 experts";
-  if (!a.ggate.w || !a.gup.w || !a.gdown.w) return "the GEMM-layout copy of the experts is missing";
-  uint32_t np, ss;
-  if (const char* why = qgemm_shape(a.gate.kind, a.H, a.gate.kind == Q4_K, &np, &ss)) return why;
-  if (const char* why = qgemm_shape(a.down.kind, a.I, a.down.kind == Q4_K, &np, &ss)) return why;
-  return nullptr;
+// ---- expert parallelism: barriers, gather, combine across the ranks' exchange regions ---------------
+// Peer data is read with ld.global.cv (fetched again, never a stale cached line); the barrier flags
+// with system-scope release / acquire.
+__device__ __forceinline__ unsigned long long ep_now() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
 }
 
-uint32_t moe_image_rows(uint32_t T, uint32_t top, uint32_t E) {
-  const uint32_t P = T * top;
-  return P + 15 * (E < P ? E : P);
+// Rank `rank` passes barrier `seq`: this layer's T into its header, then flags[rank] = seq in every
+// rank's region, after a system-scope fence (the earlier kernels' writes of h, hs, sel or y first).
+__global__ void k_ep_signal(MoeEp ep, unsigned long long seq) {
+  if (threadIdx.x != 0) return;
+  *reinterpret_cast<volatile uint32_t*>(ep.peers[ep.rank] + ep.o_hdr) = ep.T;
+  __threadfence_system();
+  for (uint32_t q = 0; q < ep.world; q++) {
+    unsigned long long* f = reinterpret_cast<unsigned long long*>(ep.peers[q] + ep.o_flags) + ep.rank;
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(f), "l"(seq) : "memory");
+  }
 }
 
-const char* launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStream_t s) {
+// Waits until every rank has passed barrier `seq` (lane q polls flags[q] of this rank's region), at
+// most 2 s; then err bit 3 and no further waiting (a barrier that timed out stays failed until the
+// host has read the error).
+__global__ void k_ep_wait(MoeEp ep, unsigned long long seq, uint32_t* err) {
+  const uint32_t q = threadIdx.x;
+  if (q >= ep.world) return;
+  const unsigned long long* f = reinterpret_cast<const unsigned long long*>(ep.peers[ep.rank] + ep.o_flags) + q;
+  const unsigned long long t0 = ep_now();
+  for (;;) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(f) : "memory");
+    if (v >= seq) return;
+    if (*reinterpret_cast<volatile uint32_t*>(err) & 8u) return;
+    if (ep_now() - t0 > 2000000000ull) {
+      atomicOr(err, 8u);
+      return;
+    }
+    __nanosleep(200);
+  }
+}
+
+// Block g = (rank q, token t): token t of rank q becomes global token g of this rank's scratch (its
+// normalized input, scale and selected experts).  Block 0 checks every rank's T.
+__global__ void __launch_bounds__(256) k_ep_gather(MoeArgs a, MoeEp ep) {
+  const uint32_t g = blockIdx.x, q = g / ep.T, t = g % ep.T, tid = threadIdx.x;
+  const uint8_t* src = ep.peers[q];
+  if (g == 0 && tid < ep.world && __ldcv(reinterpret_cast<const unsigned int*>(ep.peers[tid] + ep.o_hdr)) != ep.T)
+    atomicOr(a.err, 16u);
+  const float4* hs = reinterpret_cast<const float4*>(src + ep.o_h) + (uint64_t)t * (a.H / 4);
+  float4* hd = reinterpret_cast<float4*>(a.h) + (uint64_t)g * (a.H / 4);
+  for (uint32_t i = tid; i < a.H / 4; i += 256) hd[i] = __ldcv(hs + i);
+  if (tid == 0) a.hscale[g] = __ldcv(reinterpret_cast<const float*>(src + ep.o_hs) + t);
+  if (tid < a.top)
+    a.sel[(uint64_t)g * a.top + tid] = __ldcv(reinterpret_cast<const unsigned int*>(src + ep.o_sel) + (uint64_t)t * a.top + tid);
+}
+
+// x + (w_0 y_0 + w_1 y_1 + ...) in selection order for this rank's token t, each y read from the rank
+// that holds the expert (model.rs:275-287).
+__global__ void __launch_bounds__(256) k_moe_combine_ep(MoeArgs a, MoeEp ep, const float* __restrict__ x,
+                                                        float* __restrict__ out) {
+  const uint32_t t = blockIdx.x, g = ep.rank * ep.T + t;
+  const uint32_t* sl = reinterpret_cast<const uint32_t*>(ep.peers[ep.rank] + ep.o_sel) + (uint64_t)t * a.top;
+  for (uint32_t r = threadIdx.x; r < a.H / 4; r += 256) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (uint32_t k = 0; k < a.top; k++) {
+      const uint32_t e = sl[k];
+      const float w = a.selw[(uint64_t)t * a.top + k];
+      const float4 y = __ldcv(reinterpret_cast<const float4*>(ep.peers[e / ep.e_n] + ep.o_y) +
+                              ((uint64_t)g * a.top + k) * (a.H / 4) + r);
+      acc.x = __fadd_rn(acc.x, __fmul_rn(w, y.x));
+      acc.y = __fadd_rn(acc.y, __fmul_rn(w, y.y));
+      acc.z = __fadd_rn(acc.z, __fmul_rn(w, y.z));
+      acc.w = __fadd_rn(acc.w, __fmul_rn(w, y.w));
+    }
+    const float4 xv = reinterpret_cast<const float4*>(x)[(uint64_t)t * (a.H / 4) + r];
+    reinterpret_cast<float4*>(out)[(uint64_t)t * (a.H / 4) + r] =
+        make_float4(__fadd_rn(xv.x, acc.x), __fadd_rn(xv.y, acc.y), __fadd_rn(xv.z, acc.z), __fadd_rn(xv.w, acc.w));
+  }
+}
+
+// Plan, activation image and the two GEMMs over the pairs of a.sel (down outputs into a.y).
+void launch_moe_groups(const MoeArgs& a, cudaStream_t s) {
   const uint32_t rmax = moe_image_rows(a.T, a.top, a.E);
-  k_moe_route<<<dim3(a.T, (a.E + kRouteRows - 1) / kRouteRows), 256, a.H * sizeof(float), s>>>(a, x);
-  k_moe_select<<<a.T, 128, 0, s>>>(a);
   k_moe_plan<<<1, 1024, 0, s>>>(a);
   QgImageArgs ia{};
   ia.x = a.h;
@@ -245,7 +313,78 @@ const char* launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStre
   d.nitems_dev = a.nitems + 1;
   d.err = a.err;
   launch_qgemm(d, a.down.kind, false, a.sms, s);
+}
+
+}  // namespace
+
+const char* moe_tc_supported(const MoeArgs& a) {
+  if (a.gate.kind != a.up.kind) return "the tensor-core MoE path needs gate and up rows of one format";
+  if (const char* why = qgemm_supported(a.gate.kind, a.H)) return why;
+  if (const char* why = qgemm_supported(a.down.kind, a.I)) return why;
+  if (a.I % 64) return "the tensor-core MoE path needs an intermediate size in multiples of 64";
+  if (a.router.kind != F16) return "the batched MoE path takes an F16 router";
+  if (a.E > 1024) return "the batched MoE path takes at most 1024 experts";
+  if (!a.ggate.w || !a.gup.w || !a.gdown.w) return "the GEMM-layout copy of the experts is missing";
+  uint32_t np, ss;
+  if (const char* why = qgemm_shape(a.gate.kind, a.H, a.gate.kind == Q4_K, &np, &ss)) return why;
+  if (const char* why = qgemm_shape(a.down.kind, a.I, a.down.kind == Q4_K, &np, &ss)) return why;
+  return nullptr;
+}
+
+uint32_t moe_image_rows(uint32_t T, uint32_t top, uint32_t E) {
+  const uint32_t P = T * top;
+  return P + 15 * (E < P ? E : P);
+}
+
+const char* launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStream_t s) {
+  k_moe_route<<<dim3(a.T, (a.E + kRouteRows - 1) / kRouteRows), 256, a.H * sizeof(float), s>>>(a, x);
+  k_moe_select<<<a.T, 128, 0, s>>>(a);
+  launch_moe_groups(a, s);
   k_moe_combine<<<a.T, 256, 0, s>>>(a, x, out);
+  return nullptr;
+}
+
+uint64_t moe_ep_layout(uint32_t cap, uint32_t H, uint32_t top, uint32_t world, MoeEp* set0, MoeEp* set1) {
+  uint64_t o = 256;  // flags
+  auto take = [&](uint64_t bytes) {
+    const uint64_t at = o;
+    o = (o + bytes + 255) & ~255ull;
+    return at;
+  };
+  for (MoeEp* m : {set0, set1}) {
+    m->o_flags = 0;
+    m->o_hdr = take(16);
+    m->o_h = take((uint64_t)cap * H * 4);
+    m->o_hs = take((uint64_t)cap * 4);
+    m->o_sel = take((uint64_t)cap * top * 4);
+    m->o_y = take((uint64_t)world * cap * top * H * 4);
+  }
+  return o;
+}
+
+const char* launch_moe_tc_ep(const MoeArgs& a, const MoeEp& ep, unsigned long long seq, const float* x, float* out,
+                             cudaStream_t s) {
+  if (ep.T == 0 || a.T != ep.T || ep.world < 2 || ep.world > 8 || ep.e_n * ep.world != a.E || a.H % 4)
+    return "invalid expert-parallel layer arguments";
+  uint8_t* const own = ep.own;
+  MoeArgs l = a;  // this rank's tokens: normalized inputs, scales and selections into the exchange
+  l.h = reinterpret_cast<float*>(own + ep.o_h);
+  l.hscale = reinterpret_cast<float*>(own + ep.o_hs);
+  l.sel = reinterpret_cast<uint32_t*>(own + ep.o_sel);
+  k_moe_route<<<dim3(l.T, (l.E + kRouteRows - 1) / kRouteRows), 256, l.H * sizeof(float), s>>>(l, x);
+  k_moe_select<<<l.T, 128, 0, s>>>(l);
+  k_ep_signal<<<1, 32, 0, s>>>(ep, seq);
+  k_ep_wait<<<1, 32, 0, s>>>(ep, seq, a.err);
+  MoeArgs g = a;  // every rank's tokens, this rank's experts
+  g.T = ep.world * ep.T;
+  g.e_lo = ep.rank * ep.e_n;
+  g.e_n = ep.e_n;
+  g.y = reinterpret_cast<float*>(own + ep.o_y);
+  k_ep_gather<<<g.T, 256, 0, s>>>(g, ep);
+  launch_moe_groups(g, s);
+  k_ep_signal<<<1, 32, 0, s>>>(ep, seq + 1);
+  k_ep_wait<<<1, 32, 0, s>>>(ep, seq + 1, a.err);
+  k_moe_combine_ep<<<l.T, 256, 0, s>>>(l, ep, x, out);
   return nullptr;
 }
 

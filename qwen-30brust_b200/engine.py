@@ -32,14 +32,14 @@ EXPORTS = (
     "qc_engine_ep_connect", "qc_sampler_create", "qc_sampler_destroy", "qc_sampler_sample", "qc_sampler_words",
     "qc_engine_sample", "qc_decode_sample", "qc_moe_layer", "qc_batch_create", "qc_batch_destroy",
     "qc_batch_forward", "qc_batch_reset", "qc_batch_position", "qc_batch_logits_device", "qc_batch_sample",
-    "qc_batch_decode_sample", "qc_batch_stats",
+    "qc_batch_decode_sample", "qc_batch_stats", "qc_batch_ep_handle", "qc_batch_ep_connect",
 )
 
 
 def connect_group(eng, group=None) -> None:
-    """Connect an expert-parallel engine to its peers: all-gather every rank's
-    ep_handle() over torch.distributed (any backend; rank order of `group`),
-    then Engine.connect.  Each rank of the group must call it."""
+    """Connect an expert-parallel engine (or a Batch of one) to its peers:
+    all-gather every rank's ep_handle() over torch.distributed (any backend;
+    rank order of `group`), then .connect.  Each rank of the group must call it."""
     import torch.distributed as dist
     allh = [None] * dist.get_world_size(group)
     dist.all_gather_object(allh, eng.ep_handle(), group=group)
@@ -147,6 +147,8 @@ def lib() -> C.CDLL:
         L.qc_batch_sample.argtypes = [vp, vp, vp, u32, vp]
         L.qc_batch_decode_sample.argtypes = [vp, vp, vp, u32, u32, vp]
         L.qc_batch_stats.argtypes = [vp, C.POINTER(Stats)]
+        L.qc_batch_ep_handle.argtypes = [vp, vp, C.POINTER(C.c_int)]
+        L.qc_batch_ep_connect.argtypes = [vp, vp, vp]
         _lib = L
     return _lib
 
@@ -454,6 +456,20 @@ class Batch:
         s = Stats()
         self._check(lib().qc_batch_stats(self._h, C.byref(s)))
         return s.as_dict()
+
+    def ep_handle(self) -> tuple[bytes, int]:
+        """(64-byte IPC handle of this rank's exchange region, id of its GPU): batches of an
+        expert-parallel engine."""
+        buf = (C.c_uint8 * 64)()
+        dev = C.c_int()
+        self._check(lib().qc_batch_ep_handle(self._h, buf, C.byref(dev)))
+        return bytes(buf), dev.value
+
+    def connect(self, handles: list[tuple[bytes, int]]) -> None:
+        """qc_batch_ep_connect with every rank's ep_handle() in rank order."""
+        hb = np.frombuffer(b"".join(h for h, _ in handles), dtype=np.uint8).copy()
+        ids = np.array([d for _, d in handles], dtype=np.int32)
+        self._check(lib().qc_batch_ep_connect(self._h, hb.ctypes.data, ids.ctypes.data))
 
     def close(self) -> None:
         if getattr(self, "_h", None):

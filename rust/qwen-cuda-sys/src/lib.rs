@@ -206,6 +206,8 @@ pub mod ffi {
             tokens_out: *mut u32,
         ) -> c_int;
         pub fn qc_batch_stats(b: *const qc_batch, out: *mut qc_stats) -> c_int;
+        pub fn qc_batch_ep_handle(b: *mut qc_batch, handle: *mut c_void, device_id: *mut c_int) -> c_int;
+        pub fn qc_batch_ep_connect(b: *mut qc_batch, handles: *const c_void, device_ids: *const c_int) -> c_int;
 
         pub fn qc_reset(e: *mut qc_engine) -> c_int;
         pub fn qc_position(e: *const qc_engine, pos: *mut u32) -> c_int;
