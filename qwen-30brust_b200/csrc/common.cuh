@@ -325,6 +325,15 @@ QC_DEV void stage_vectors(uint8_t* mem, uint32_t nv, uint32_t n, uint32_t units,
 
 QC_DEV int dp4a(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
 QC_DEV float combine(int a0, int a1, int a2) { return (float)a0 + 256.f * (float)a1 + 65536.f * (float)a2; }
+// The plane sums as one integer, sum q * xi = a0 + 256 a1 + 65536 a2, computed mod 2^32: exact when
+// the true sum fits an int32, i.e. |sum q xi| <= n * max|q| * 2^21 < 2^31 (32 codes of up to 5 bits,
+// or 16 codes of up to 6 bits; not 8-bit codes).  One int-to-float conversion instead of three.
+QC_DEV int icombine(int a0, int a1, int a2) {
+  return (int)((uint32_t)a0 + ((uint32_t)a1 << 8) + ((uint32_t)a2 << 16));
+}
+// The float of a small integer (|x| < 2^22) without the conversion unit: the bits of 1.5 * 2^23
+// plus x hold 1.5 * 2^23 + x exactly, and the subtraction is exact.
+QC_DEV float small_i2f(int x) { return __int_as_float(0x4B400000 + x) - 12582912.f; }
 
 // The activation data of one unit held in registers: d[4p + q] = digit plane p,
 // elements 16q..16q+15; s = sums of xi over the four 16-element groups; sb = scale.
@@ -353,7 +362,18 @@ QC_DEV uint32_t wsel(const uint4& t, int j) {
 // Digit word j (elements 4j..4j+3, j < 16) of plane p.
 QC_DEV uint32_t dword(const UnitX& ux, int p, int j) { return wsel(ux.d[4 * p + (j >> 2)], j); }
 
-// sum of 32 codes (codes[j]: elements h*32 + 4j .. +3) times xi, exact in three dp4a chains.
+// sum of 32 codes (codes[j]: elements h*32 + 4j .. +3) times xi, exact in three dp4a chains: as an
+// integer (codes of up to 5 bits), or as a float (any int8 codes).
+QC_DEV int idot32i(const uint32_t (&codes)[8], const UnitX& ux, int h) {
+  int a0 = 0, a1 = 0, a2 = 0;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    a0 = dp4a(codes[j], dword(ux, 0, 8 * h + j), a0);
+    a1 = dp4a(codes[j], dword(ux, 1, 8 * h + j), a1);
+    a2 = dp4a(codes[j], dword(ux, 2, 8 * h + j), a2);
+  }
+  return icombine(a0, a1, a2);
+}
 QC_DEV float idot32(const uint32_t (&codes)[8], const UnitX& ux, int h) {
   int a0 = 0, a1 = 0, a2 = 0;
 #pragma unroll
@@ -364,8 +384,8 @@ QC_DEV float idot32(const uint32_t (&codes)[8], const UnitX& ux, int h) {
   }
   return combine(a0, a1, a2);
 }
-// As idot32 but split into the two 16-element halves (Q6_K scale groups).
-QC_DEV void idot16x2(const uint32_t (&codes)[8], const UnitX& ux, int h, float* lo, float* hi) {
+// As idot32i but split into the two 16-element halves (Q6_K scale groups; codes of up to 6 bits).
+QC_DEV void idot16x2i(const uint32_t (&codes)[8], const UnitX& ux, int h, int* lo, int* hi) {
   int a0 = 0, a1 = 0, a2 = 0, b0 = 0, b1 = 0, b2 = 0;
 #pragma unroll
   for (int j = 0; j < 4; j++) {
@@ -376,8 +396,8 @@ QC_DEV void idot16x2(const uint32_t (&codes)[8], const UnitX& ux, int h, float* 
     b1 = dp4a(codes[j + 4], dword(ux, 1, 8 * h + j + 4), b1);
     b2 = dp4a(codes[j + 4], dword(ux, 2, 8 * h + j + 4), b2);
   }
-  *lo = combine(a0, a1, a2);
-  *hi = combine(b0, b1, b2);
+  *lo = icombine(a0, a1, a2);
+  *hi = icombine(b0, b1, b2);
 }
 
 // 6-bit scale and min of sub-blocks j and j+1 (j even) from the 12 packed bytes
@@ -393,10 +413,10 @@ QC_DEV void kq_scale_pair(uint32_t s0, uint32_t s1, uint32_t s2, uint32_t j, flo
   const uint32_t sl = a & 0x3f3fu, ml = b & 0x3f3fu;
   const uint32_t sh = (c & 0x0f0fu) | (((a >> 6) & 0x0303u) << 4), mh = ((c >> 4) & 0x0f0fu) | (((b >> 6) & 0x0303u) << 4);
   const uint32_t sv = hi ? sh : sl, mv = hi ? mh : ml;
-  *sc0 = (float)(sv & 0xff);
-  *sc1 = (float)(sv >> 8);
-  *m0 = (float)(mv & 0xff);
-  *m1 = (float)(mv >> 8);
+  *sc0 = small_i2f((int)(sv & 0xff));
+  *sc1 = small_i2f((int)(sv >> 8));
+  *m0 = small_i2f((int)(mv & 0xff));
+  *m1 = small_i2f((int)(mv >> 8));
 }
 
 // ---- unit dot products: the contribution of unit u (64 elements) of one row ----
@@ -415,7 +435,7 @@ QC_DEV float unit_q4k(const uint8_t* row, uint32_t u, const UnitX& ux) {
     lo[j] = w[j] & 0x0f0f0f0fu;
     hi[j] = (w[j] >> 4) & 0x0f0f0f0fu;
   }
-  const float qlo = idot32(lo, ux, 0), qhi = idot32(hi, ux, 1);
+  const float qlo = (float)idot32i(lo, ux, 0), qhi = (float)idot32i(hi, ux, 1);
   float sc0, m0, sc1, m1;
   kq_scale_pair(hd.y, hd.z, hd.w, 2 * p, &sc0, &m0, &sc1, &m1);
   const float d = h2f_bits(hd.x), dmin = h2f_bits(hd.x >> 16);
@@ -441,7 +461,7 @@ QC_DEV float unit_q5k(const uint8_t* row, uint32_t u, const UnitX& ux) {
     lo[j] = (w[j] & 0x0f0f0f0fu) | (((h[j] >> g0) & 0x01010101u) << 4);
     hi[j] = ((w[j] >> 4) & 0x0f0f0f0fu) | (((h[j] >> g1) & 0x01010101u) << 4);
   }
-  const float qlo = idot32(lo, ux, 0), qhi = idot32(hi, ux, 1);
+  const float qlo = (float)idot32i(lo, ux, 0), qhi = (float)idot32i(hi, ux, 1);
   float sc0, m0, sc1, m1;
   kq_scale_pair(hd.y, hd.z, hd.w, g0, &sc0, &m0, &sc1, &m1);
   const float d = h2f_bits(hd.x), dmin = h2f_bits(hd.x >> 16);
@@ -470,13 +490,14 @@ QC_DEV float unit_q6k(const uint8_t* row, const __half* drow, uint32_t u, const 
     ca[j] = ((la[j] >> ns) & 0x0f0f0f0fu) | (((qh[j] >> s0) & 0x03030303u) << 4);
     cb[j] = ((lb[j] >> ns) & 0x0f0f0f0fu) | (((qh[j] >> s1) & 0x03030303u) << 4);
   }
-  float qa0, qa1, qb0, qb1;
-  idot16x2(ca, ux, 0, &qa0, &qa1);
-  idot16x2(cb, ux, 1, &qb0, &qb1);
+  int ia0, ia1, ib0, ib1;
+  idot16x2i(ca, ux, 0, &ia0, &ia1);
+  idot16x2i(cb, ux, 1, &ib0, &ib1);
+  const float qa0 = (float)ia0, qa1 = (float)ia1, qb0 = (float)ib0, qb1 = (float)ib1;
   // the four scales sit in bytes c*8 + 4h .. +3, i.e. in word 2c + h of the 16 scale bytes
   const uint32_t sw = (c ? (hh ? sc.w : sc.z) : (hh ? sc.y : sc.x));
-  const float sa0 = (float)(int8_t)byte_of(sw, 0), sa1 = (float)(int8_t)byte_of(sw, 1);
-  const float sb0 = (float)(int8_t)byte_of(sw, 2), sb1 = (float)(int8_t)byte_of(sw, 3);
+  const float sa0 = small_i2f((int8_t)byte_of(sw, 0)), sa1 = small_i2f((int8_t)byte_of(sw, 1));
+  const float sb0 = small_i2f((int8_t)byte_of(sw, 2)), sb1 = small_i2f((int8_t)byte_of(sw, 3));
   // sum (q - 32) x = sum q x - 32 sum x over each 16-element group
   const float r = sa0 * (qa0 - 32.f * (float)ux.s.x) + sa1 * (qa1 - 32.f * (float)ux.s.y) +
                   sb0 * (qb0 - 32.f * (float)ux.s.z) + sb1 * (qb1 - 32.f * (float)ux.s.w);
@@ -508,7 +529,7 @@ QC_DEV float unit_q40(const uint8_t* row, const __half* drow, uint32_t u, const 
     c1[j] = wb[j] & 0x0f0f0f0fu;
     c1[j + 4] = (wb[j] >> 4) & 0x0f0f0f0fu;
   }
-  const float q0 = idot32(c0, ux, 0), q1 = idot32(c1, ux, 1);
+  const float q0 = (float)idot32i(c0, ux, 0), q1 = (float)idot32i(c1, ux, 1);
   const __half2 dd = *reinterpret_cast<const __half2*>(drow + 2 * u);
   const float r0 = q0 - 8.f * (float)(ux.s.x + ux.s.y), r1 = q1 - 8.f * (float)(ux.s.z + ux.s.w);
   return (__low2float(dd) * r0 + __high2float(dd) * r1) * ux.sb;
@@ -606,7 +627,39 @@ QC_DEV void warp_rows_k(const MatDesc& m, uint32_t r0, uint32_t r1, const XView&
                         uint32_t warp, uint32_t nw) {
   const uint32_t lpr = m.lpr, G = 32 / lpr, lane = threadIdx.x & 31;
   const uint32_t lr = lane % lpr, slot = lane / lpr, stride = nw * G;
-  if (m.upl == 1) {
+  if (m.upl == 1 && lpr >= 4) {
+    // four row groups per pass (b + i * stride, i < 4): four independent dot chains per lane, and
+    // one reduction for all four: a shuffle over lr ^ h (h = lpr / 2) trades the pairs (0, 1) / (2, 3),
+    // one over lr ^ h/2 trades within each pair, then the remaining lpr / 4 lanes are summed (row i
+    // ends on lane lr = i * lpr / 4)
+    const auto ux = load_x<KIND>(xv, lr);
+    const uint32_t h = lpr >> 1, q = lpr >> 2;
+    const bool up = lr & h, mid = lr & q;
+#pragma unroll 1
+    for (uint32_t b = r0 + warp * G; b < r1; b += 4 * stride) {
+      float v[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const uint32_t r = b + i * stride + slot;
+        v[i] = 0.f;
+        if (r < r1) {
+          const uint8_t* row;
+          const __half* drow;
+          addr(r, &row, &drow);
+          v[i] = unit_dot<KIND, S>(row, drow, lr, ux);
+        }
+      }
+      const float k0 = up ? v[2] : v[0], k1 = up ? v[3] : v[1];
+      const float w0 = k0 + __shfl_xor_sync(0xffffffffu, up ? v[0] : v[2], h);
+      const float w1 = k1 + __shfl_xor_sync(0xffffffffu, up ? v[1] : v[3], h);
+      float w = (mid ? w1 : w0) + __shfl_xor_sync(0xffffffffu, mid ? w0 : w1, q);
+      for (uint32_t o = q >> 1; o > 0; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
+      if ((lr & (q - 1)) == 0) {
+        const uint32_t i = (up ? 2 : 0) + (mid ? 1 : 0), r = b + i * stride + slot;
+        if (r < r1) emit(r, w);
+      }
+    }
+  } else if (m.upl == 1) {
     const auto ux = load_x<KIND>(xv, lr);
 #pragma unroll 2
     for (uint32_t b = r0 + warp * G; b < r1; b += stride) {
