@@ -627,7 +627,35 @@ QC_DEV void warp_rows_k(const MatDesc& m, uint32_t r0, uint32_t r1, const XView&
                         uint32_t warp, uint32_t nw) {
   const uint32_t lpr = m.lpr, G = 32 / lpr, lane = threadIdx.x & 31;
   const uint32_t lr = lane % lpr, slot = lane / lpr, stride = nw * G;
-  if (m.upl == 1 && lpr >= 4) {
+  // (formats of 6- and 8-bit codes hold more registers per row: two row groups per pass there)
+  constexpr bool kFour = !(KIND == Q6_K || KIND == Q8_0);
+  if (m.upl == 1 && lpr >= 2 && !kFour) {
+    // two row groups per pass (b and b + stride): one shuffle trades half of each lane's pair of sums
+    // with its partner lr ^ h, then one reduction over h lanes finishes both (row b on lane lr 0, row
+    // b + stride on lane h)
+    const auto ux = load_x<KIND>(xv, lr);
+    const uint32_t h = lpr >> 1;
+    const bool up = lr >= h;
+#pragma unroll 1
+    for (uint32_t b = r0 + warp * G; b < r1; b += 2 * stride) {
+      const uint32_t ra = b + slot, rb = b + stride + slot;
+      float va = 0.f, vb = 0.f;
+      const uint8_t* row;
+      const __half* drow;
+      if (ra < r1) {
+        addr(ra, &row, &drow);
+        va = unit_dot<KIND, S>(row, drow, lr, ux);
+      }
+      if (rb < r1) {
+        addr(rb, &row, &drow);
+        vb = unit_dot<KIND, S>(row, drow, lr, ux);
+      }
+      float v = (up ? vb : va) + __shfl_xor_sync(0xffffffffu, up ? va : vb, h);
+      for (uint32_t o = h >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lr == 0 && ra < r1) emit(ra, v);
+      if (lr == h && rb < r1) emit(rb, v);
+    }
+  } else if (m.upl == 1 && lpr >= 4) {
     // four row groups per pass (b + i * stride, i < 4): four independent dot chains per lane, and
     // one reduction for all four: a shuffle over lr ^ h (h = lpr / 2) trades the pairs (0, 1) / (2, 3),
     // one over lr ^ h/2 trades within each pair, then the remaining lpr / 4 lanes are summed (row i
