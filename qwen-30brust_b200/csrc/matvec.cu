@@ -79,10 +79,12 @@ __global__ void k_dequant(MatDesc m, uint32_t e, float* __restrict__ out) {
 
 // y = W_e x, rows streamed through shared memory: each block takes a contiguous run of 8-row
 // groups and streams it in stages of `sg` groups through `ns` shared-memory slots with TMA bulk
-// copies (one thread issues, an mbarrier per slot counts the bytes), so up to ns - 1 stages are in
-// flight while one is computed; warps walk the rows of a stage, lpr lanes per row.  The activation
-// staging overlaps the first copies.  Waits are bounded (2 s); a block that gives up writes NaN
-// for its rows, after waiting (bounded) for its copies in flight, and sets g_matvec_abort.
+// copies (an mbarrier per slot counts the bytes), so up to ns - 1 stages are in flight while one is
+// computed; warps walk the rows of a stage, lpr lanes per row.  Warps do not wait for each other:
+// each releases a slot when done with its rows (a per-slot count of releases), and the warp whose
+// release completes a stage's count refills the slot with stage k + ns.  The activation staging
+// overlaps the first copies.  Waits are bounded (2 s); a block that gives up writes NaN for its
+// rows, after waiting (bounded) for its copies in flight, and sets g_matvec_abort.
 constexpr int kMaxSlots = 8;
 constexpr unsigned long long kWaitNs = 2000000000ull;
 __device__ uint32_t g_matvec_abort;
@@ -93,7 +95,8 @@ __device__ __forceinline__ unsigned long long now_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-__device__ __forceinline__ bool slot_wait(uint64_t* b, uint32_t parity) {
+// Waits for the phase of `parity` of b: false after 2 s, or as soon as *bad is set.
+__device__ __forceinline__ bool slot_wait(uint64_t* b, uint32_t parity, const volatile int* bad = nullptr) {
   const unsigned long long t0 = now_ns();
   for (uint32_t i = 0;; i++) {
     uint32_t ok;
@@ -103,7 +106,7 @@ __device__ __forceinline__ bool slot_wait(uint64_t* b, uint32_t parity) {
         : "r"(saddr(b)), "r"(parity)
         : "memory");
     if (ok) return true;
-    if ((i & 255) == 255 && now_ns() - t0 > kWaitNs) return false;
+    if ((i & 255) == 255 && ((bad && *bad) || now_ns() - t0 > kWaitNs)) return false;
   }
 }
 __device__ __forceinline__ void slot_fill(void* dst, const void* src, uint32_t bytes, uint64_t* b) {
@@ -119,6 +122,8 @@ __global__ void __launch_bounds__(512) k_matvec(MatDesc m, uint32_t e, const flo
                                                 float* __restrict__ y, uint32_t sg, uint32_t ns) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bar[kMaxSlots];
+  __shared__ uint32_t released[kMaxSlots];  // releases of each slot by warps, over all its stages
+  __shared__ int last[kMaxSlots];           // the latest stage issued into each slot
   __shared__ float red[32];
   __shared__ int bad;
   const uint32_t groups = (m.rows + 7) / 8;
@@ -128,39 +133,51 @@ __global__ void __launch_bounds__(512) k_matvec(MatDesc m, uint32_t e, const flo
   const uint32_t stage_bytes = sg * m.group_bytes;
   uint8_t* xmem = smem + ns * stage_bytes;
   const uint8_t* src = expert_base(m, e);
-  auto issue = [&](uint32_t k) {  // thread 0: stage k into slot k % ns
+  auto issue = [&](uint32_t k) {  // one thread: stage k into slot k % ns
     const uint32_t a = g0 + k * sg, b = min(g1, a + sg);
+    last[k % ns] = (int)k;
     slot_fill(smem + (k % ns) * stage_bytes, src + (uint64_t)a * m.group_bytes, (b - a) * m.group_bytes, &bar[k % ns]);
   };
   if (threadIdx.x == 0) {
     bad = 0;
-    for (uint32_t i = 0; i < ns; i++)
+    for (uint32_t i = 0; i < ns; i++) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(saddr(&bar[i])) : "memory");
+      released[i] = 0;
+      last[i] = -1;
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     for (uint32_t k = 0; k < ns && k < nst; k++) issue(k);
   }
   stage_vectors<false>(xmem, 1, m.cols, m.units, uses_float_x(KIND), [&](uint32_t, uint32_t i) { return x[i]; },
                        nullptr, 0.f, red);  // (ends with a barrier: the mbarriers are initialized)
   const XView xv = xview_at(xmem, m.units, uses_float_x(KIND));
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   for (uint32_t k = 0; k < nst; k++) {
     const uint32_t j = k % ns;
-    if (!slot_wait(&bar[j], (k / ns) & 1)) bad = 1;
-    __syncthreads();
-    const uint32_t r0 = (g0 + k * sg) * 8, r1 = min(m.rows, min(g1, g0 + (k + 1) * sg) * 8);
-    if (bad) {  // a copy did not arrive: report and stop, after the copies in flight have landed
-      for (uint32_t r = r0 + threadIdx.x; r < min(m.rows, g1 * 8); r += blockDim.x) y[r] = __int_as_float(0x7fc00000);
-      if (threadIdx.x == 0) {
-        atomicOr(&g_matvec_abort, 1u);
-        for (uint32_t q = k; q < nst && q < k + ns; q++) slot_wait(&bar[q % ns], (q / ns) & 1);  // issued, in flight
-      }
-      return;
+    if (!slot_wait(&bar[j], (k / ns) & 1, &bad)) {
+      bad = 1;
+      break;
     }
+    const uint32_t r0 = (g0 + k * sg) * 8, r1 = min(m.rows, min(g1, g0 + (k + 1) * sg) * 8);
     warp_rows_k<KIND, true>(m, r0, r1, xv, SmemRows{&m, smem + j * stage_bytes, r0},
-                            [&](uint32_t r, float v) { y[r] = v; }, threadIdx.x >> 5, blockDim.x >> 5);
-    __syncthreads();  // slot j is consumed
-    if (threadIdx.x == 0 && k + ns < nst) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(k + ns);
+                            [&](uint32_t r, float v) { y[r] = v; }, warp, nw);
+    __syncwarp();
+    if (lane == 0) {  // this warp is done with slot j; the last of the stage refills it
+      __threadfence_block();
+      if (atomicAdd(&released[j], 1u) == (k / ns + 1) * nw - 1 && k + ns < nst) {
+        __threadfence_block();
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        issue(k + ns);
+      }
+    }
+  }
+  __syncthreads();
+  if (bad) {  // a copy did not arrive: report, after the copies in flight have landed
+    for (uint32_t r = g0 * 8 + threadIdx.x; r < min(m.rows, g1 * 8); r += blockDim.x) y[r] = __int_as_float(0x7fc00000);
+    if (threadIdx.x == 0) {
+      atomicOr(&g_matvec_abort, 1u);
+      for (uint32_t q = 0; q < ns; q++)
+        if (last[q] >= 0) slot_wait(&bar[q], ((uint32_t)last[q] / ns) & 1);
     }
   }
 }
