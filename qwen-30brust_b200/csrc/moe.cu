@@ -85,14 +85,18 @@ __global__ void __launch_bounds__(256) k_moe_route(MoeArgs a, const float* __res
 // ops.rs:29-44 (softmax) over the kept logits in selection order.
 __global__ void __launch_bounds__(128) k_moe_select(MoeArgs a) {
   __shared__ float lg[1024];
+  __shared__ uint32_t key[1024];  // total-order keys of the logits, computed once
   const uint32_t t = blockIdx.x, tid = threadIdx.x;
-  for (uint32_t e = tid; e < a.E; e += 128) lg[e] = a.rlg[(uint64_t)t * a.E + e];
+  for (uint32_t e = tid; e < a.E; e += 128) {
+    lg[e] = a.rlg[(uint64_t)t * a.E + e];
+    key[e] = total_key_u(lg[e]);
+  }
   __syncthreads();
   for (uint32_t e = tid; e < a.E; e += 128) {
-    const uint32_t ke = total_key_u(lg[e]);
+    const uint32_t ke = key[e];
     uint32_t rank = 0;
     for (uint32_t j = 0; j < a.E; j++) {
-      const uint32_t kj = total_key_u(lg[j]);
+      const uint32_t kj = key[j];
       rank += kj > ke || (kj == ke && j < e);
     }
     if (rank < a.top) a.sel[(uint64_t)t * a.top + rank] = e;
@@ -130,19 +134,45 @@ __global__ void __launch_bounds__(1024) k_moe_plan(MoeArgs a) {
     if (held(e)) atomicAdd(&cnt[e], 1u);
   }
   __syncthreads();
-  if (tid == 0) {
+  {  // per expert (thread e; E <= 1024): pairs, image rows, gate/up and down items, scanned together
+    __shared__ uint4 wsum[32];
     const uint32_t tgu = (a.I + 63) / 64, tdn = (a.H + 127) / 128;
-    off[0] = igu[0] = idn[0] = img[0] = 0;
-    for (uint32_t e = 0; e < a.E; e++) {
-      const uint32_t c = cnt[e], n = (c + 15) & ~15u;
-      off[e + 1] = off[e] + c;
-      img[e + 1] = img[e] + n;
-      igu[e + 1] = igu[e] + tgu * ((n + a.NPgu - 1) / a.NPgu);
-      idn[e + 1] = idn[e] + tdn * ((n + a.NPdn - 1) / a.NPdn);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (tid < a.E) {
+      const uint32_t c = cnt[tid], n = (c + 15) & ~15u;
+      v = make_uint4(c, n, tgu * ((n + a.NPgu - 1) / a.NPgu), tdn * ((n + a.NPdn - 1) / a.NPdn));
     }
-    a.nitems[0] = igu[a.E];
-    a.nitems[1] = idn[a.E];
-    *a.nrows = img[a.E];
+    auto scan = [&](uint4 x) {  // inclusive over the warp's lanes
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint4 y = make_uint4(__shfl_up_sync(0xffffffffu, x.x, o), __shfl_up_sync(0xffffffffu, x.y, o),
+                                   __shfl_up_sync(0xffffffffu, x.z, o), __shfl_up_sync(0xffffffffu, x.w, o));
+        if (lane >= (uint32_t)o) x = make_uint4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w);
+      }
+      return x;
+    };
+    uint4 inc = scan(v);
+    if (lane == 31) wsum[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {  // the warps' totals, exclusive
+      const uint4 w = wsum[lane], wi = scan(w);
+      wsum[lane] = make_uint4(wi.x - w.x, wi.y - w.y, wi.z - w.z, wi.w - w.w);
+    }
+    __syncthreads();
+    const uint4 base = wsum[warp];
+    inc = make_uint4(inc.x + base.x, inc.y + base.y, inc.z + base.z, inc.w + base.w);
+    if (tid < a.E) {
+      off[tid + 1] = inc.x;
+      img[tid + 1] = inc.y;
+      igu[tid + 1] = inc.z;
+      idn[tid + 1] = inc.w;
+    }
+    if (tid == 0) off[0] = img[0] = igu[0] = idn[0] = 0;
+    if (tid == a.E - 1) {
+      a.nitems[0] = inc.z;
+      a.nitems[1] = inc.w;
+      *a.nrows = inc.y;
+    }
   }
   __syncthreads();
   for (uint32_t e = tid; e < a.E; e += 1024) {
@@ -173,16 +203,23 @@ __global__ void __launch_bounds__(1024) k_moe_plan(MoeArgs a) {
 }
 
 // ---- combine in selection order + residual ---------------------------------------------------
+// Block (t, c): elements 1024 c .. 1024 c + 1023 of token t, four per thread (H is a multiple of 4).
 __global__ void __launch_bounds__(256) k_moe_combine(MoeArgs a, const float* __restrict__ x, float* __restrict__ out) {
-  const uint32_t t = blockIdx.x;
-  for (uint32_t r = threadIdx.x; r < a.H; r += 256) {
-    float acc = 0.f;
-    for (uint32_t k = 0; k < a.top; k++) {
-      const uint32_t p = t * a.top + k;
-      acc = __fadd_rn(acc, __fmul_rn(a.selw[p], a.y[(uint64_t)p * a.H + r]));
-    }
-    out[(uint64_t)t * a.H + r] = __fadd_rn(x[(uint64_t)t * a.H + r], acc);
+  const uint32_t t = blockIdx.x, r = blockIdx.y * 256 + threadIdx.x;
+  if (r >= a.H / 4) return;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (uint32_t k = 0; k < a.top; k++) {
+    const uint32_t p = t * a.top + k;
+    const float w = a.selw[p];
+    const float4 y = reinterpret_cast<const float4*>(a.y)[(uint64_t)p * (a.H / 4) + r];
+    acc.x = __fadd_rn(acc.x, __fmul_rn(w, y.x));
+    acc.y = __fadd_rn(acc.y, __fmul_rn(w, y.y));
+    acc.z = __fadd_rn(acc.z, __fmul_rn(w, y.z));
+    acc.w = __fadd_rn(acc.w, __fmul_rn(w, y.w));
   }
+  const float4 xv = reinterpret_cast<const float4*>(x)[(uint64_t)t * (a.H / 4) + r];
+  reinterpret_cast<float4*>(out)[(uint64_t)t * (a.H / 4) + r] =
+      make_float4(__fadd_rn(xv.x, acc.x), __fadd_rn(xv.y, acc.y), __fadd_rn(xv.z, acc.z), __fadd_rn(xv.w, acc.w));
 }
 
 // ---- expert parallelism: barriers, gather, combine across the ranks' exchange regions ---------------
@@ -243,12 +280,12 @@ __global__ void __launch_bounds__(256) k_ep_gather(MoeArgs a, MoeEp ep) {
 }
 
 // x + (w_0 y_0 + w_1 y_1 + ...) in selection order for this rank's token t, each y read from the rank
-// that holds the expert (model.rs:275-287).
+// that holds the expert (model.rs:275-287).  Block (t, c): elements 1024 c .. 1024 c + 1023.
 __global__ void __launch_bounds__(256) k_moe_combine_ep(MoeArgs a, MoeEp ep, const float* __restrict__ x,
                                                         float* __restrict__ out) {
   const uint32_t t = blockIdx.x, g = ep.rank * ep.T + t;
   const uint32_t* sl = reinterpret_cast<const uint32_t*>(ep.peers[ep.rank] + ep.o_sel) + (uint64_t)t * a.top;
-  for (uint32_t r = threadIdx.x; r < a.H / 4; r += 256) {
+  for (uint32_t r = blockIdx.y * 256 + threadIdx.x; r < min(a.H / 4, (blockIdx.y + 1) * 256); r += 256) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (uint32_t k = 0; k < a.top; k++) {
       const uint32_t e = sl[k];
@@ -340,7 +377,7 @@ const char* launch_moe_tc(const MoeArgs& a, const float* x, float* out, cudaStre
   k_moe_route<<<dim3(a.T, (a.E + kRouteRows - 1) / kRouteRows), 256, a.H * sizeof(float), s>>>(a, x);
   k_moe_select<<<a.T, 128, 0, s>>>(a);
   launch_moe_groups(a, s);
-  k_moe_combine<<<a.T, 256, 0, s>>>(a, x, out);
+  k_moe_combine<<<dim3(a.T, (a.H / 4 + 255) / 256), 256, 0, s>>>(a, x, out);
   return nullptr;
 }
 
@@ -384,7 +421,7 @@ const char* launch_moe_tc_ep(const MoeArgs& a, const MoeEp& ep, unsigned long lo
   launch_moe_groups(g, s);
   k_ep_signal<<<1, 32, 0, s>>>(ep, seq + 1);
   k_ep_wait<<<1, 32, 0, s>>>(ep, seq + 1, a.err);
-  k_moe_combine_ep<<<l.T, 256, 0, s>>>(l, ep, x, out);
+  k_moe_combine_ep<<<dim3(l.T, (l.H / 4 + 255) / 256), 256, 0, s>>>(l, ep, x, out);
   return nullptr;
 }
 
