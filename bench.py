@@ -607,6 +607,22 @@ def batch_study(T, E, eng, spec, seqs: int, prompt: int, gen: int, log_every: in
             "sampling": "T 0.7, top-p 0.9, top-k off, sampler seed 1000 + sequence (device, exact f32 folds)"}
 
 
+def batch_job_rates(res: dict, seqs: int, prompt: int, gen: int, slowest) -> dict:
+    """A batched run over several ranks as one job: `res` is this rank's batch_study result (its own
+    sequences), `slowest(values)` the element-wise maximum of `values` over the ranks (a collective:
+    every rank calls it).  Rates are all `seqs` sequences' tokens over the slowest rank's wall and
+    device times; the result describes the whole job."""
+    pre_dev = res["sequences"] * res["prompt"] / res["prefill"]["device_tok_s"]  # this rank's device seconds
+    pre_s, dec_s, pre_dev_s, dec_ms = slowest(
+        [res["prefill"]["seconds"], res["decode"]["seconds"], pre_dev, res["decode"]["ms_per_step"]])
+    pre_tok, dec_tok = seqs * prompt, seqs * gen
+    out = dict(res, sequences=seqs, prefill=dict(res["prefill"]), decode=dict(res["decode"]))
+    out["prefill"].update(tok_s=pre_tok / pre_s, device_tok_s=pre_tok / pre_dev_s, seconds=pre_s)
+    out["decode"].update(tok_s=dec_tok / dec_s, device_tok_s=dec_tok / (dec_ms * gen / 1e3), seconds=dec_s,
+                         ms_per_step=dec_ms)
+    return out
+
+
 def run_batch(args) -> None:
     """BASELINE config 5 (`--config 5`): the batched line; under torchrun with N > 1 ranks the
     BASELINE split: sequences data-parallel, experts sharded, dispatch / combine per layer between
@@ -639,16 +655,11 @@ def run_batch(args) -> None:
                           rank=rank, world=world)
     eng.close()
     if world > 1:  # whole-job rates: all ranks' tokens over the slowest rank's times
-        pre_dev = res["sequences"] * res["prompt"] / res["prefill"]["device_tok_s"]  # this rank's device seconds
-        t = torch.tensor([res["prefill"]["seconds"], res["decode"]["seconds"], pre_dev, res["decode"]["ms_per_step"]],
-                         dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        pre_s, dec_s, pre_dev_s, dec_ms = t.tolist()
-        pre_tok, dec_tok = args.seqs * args.prompt, args.seqs * args.gen
-        res["sequences"] = args.seqs
-        res["prefill"].update(tok_s=pre_tok / pre_s, device_tok_s=pre_tok / pre_dev_s, seconds=pre_s)
-        res["decode"].update(tok_s=dec_tok / dec_s, device_tok_s=dec_tok / (dec_ms * args.gen / 1e3), seconds=dec_s,
-                             ms_per_step=dec_ms)
+        def slowest(v: list[float]) -> list[float]:
+            t = torch.tensor(v, dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return t.tolist()
+        res = batch_job_rates(res, args.seqs, args.prompt, args.gen, slowest)
         res["expert_parallel"] = {"ranks": world, "experts_per_rank": spec.experts // world,
                                   "sequences_per_rank": args.seqs // world,
                                   "exchange": "per layer: every rank's normalized inputs and selections gathered "
