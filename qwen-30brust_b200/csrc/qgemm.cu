@@ -725,11 +725,18 @@ __global__ void __launch_bounds__(256) k_qg_image(QgImageArgs a) {
   constexpr uint32_t kMaxPer = 4;  // chunks per thread (K <= 8192)
   float v[kMaxPer][8];
   const float* x = src != kNone ? a.x + (uint64_t)src * a.xstride : nullptr;
+  const bool x16 = x && (reinterpret_cast<uintptr_t>(x) & 15) == 0;  // 8 floats as two 16-byte loads
 #pragma unroll
   for (uint32_t p = 0; p < kMaxPer; p++) {
     const uint32_t t = tid + 256 * p;
+    if (x16 && t < chunks) {
+      const float4 u0 = reinterpret_cast<const float4*>(x)[2 * t], u1 = reinterpret_cast<const float4*>(x)[2 * t + 1];
+      v[p][0] = u0.x, v[p][1] = u0.y, v[p][2] = u0.z, v[p][3] = u0.w;
+      v[p][4] = u1.x, v[p][5] = u1.y, v[p][6] = u1.z, v[p][7] = u1.w;
+    } else {
 #pragma unroll
-    for (int k = 0; k < 8; k++) v[p][k] = (x && t < chunks) ? x[8 * t + k] : 0.f;
+      for (int k = 0; k < 8; k++) v[p][k] = (x && t < chunks) ? x[8 * t + k] : 0.f;
+    }
   }
   if (a.w) {  // RMSNorm
     float ss = 0.f;
@@ -739,11 +746,20 @@ __global__ void __launch_bounds__(256) k_qg_image(QgImageArgs a) {
       for (int k = 0; k < 8; k++) ss = fmaf(v[p][k], v[p][k], ss);
     ss = block_sum(ss, red);
     const float s = 1.0f / sqrtf(ss / (float)K + a.eps);
+    const bool w16 = (reinterpret_cast<uintptr_t>(a.w) & 15) == 0;
 #pragma unroll
     for (uint32_t p = 0; p < kMaxPer; p++) {
       const uint32_t t = tid + 256 * p;
+      float w[8];
+      if (w16 && t < chunks) {
+        const float4 u0 = reinterpret_cast<const float4*>(a.w)[2 * t], u1 = reinterpret_cast<const float4*>(a.w)[2 * t + 1];
+        w[0] = u0.x, w[1] = u0.y, w[2] = u0.z, w[3] = u0.w, w[4] = u1.x, w[5] = u1.y, w[6] = u1.z, w[7] = u1.w;
+      } else {
 #pragma unroll
-      for (int k = 0; k < 8; k++) v[p][k] = t < chunks ? __fmul_rn(v[p][k], __fmul_rn(s, a.w[8 * t + k])) : 0.f;
+        for (int k = 0; k < 8; k++) w[k] = t < chunks ? a.w[8 * t + k] : 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; k++) v[p][k] = t < chunks ? __fmul_rn(v[p][k], __fmul_rn(s, w[k])) : 0.f;
     }
   }
   float hs;
