@@ -436,6 +436,34 @@ pub mod safe {
         pub fn raw(&self) -> *mut ffi::qc_engine {
             self.h
         }
+
+        /// Expert parallelism: this rank's share (experts [rank E / world, (rank + 1) E / world)) of
+        /// the model in `image`, one process and GPU per rank.  Usable after `ep_connect`.
+        pub fn expert_parallel(image: &[u8], context: u32, device: i32, rank: u32, world: u32) -> Result<Self> {
+            let mut h = ptr::null_mut();
+            global(unsafe {
+                ffi::qc_engine_create_gguf_ep(image.as_ptr(), image.len(), context, device, rank, world, &mut h)
+            })?;
+            Engine::wrap(h)
+        }
+        /// This rank's exchange-buffer handle and GPU id, to be given to every rank.
+        pub fn ep_handle(&self) -> Result<([u8; 64], i32)> {
+            let mut h = [0u8; 64];
+            let mut dev: c_int = 0;
+            self.check(unsafe { ffi::qc_engine_ep_handle(self.h, h.as_mut_ptr().cast(), &mut dev) })?;
+            Ok((h, dev))
+        }
+        /// Every rank's `ep_handle()`, in rank order.
+        pub fn ep_connect(&mut self, handles: &[([u8; 64], i32)]) -> Result<()> {
+            let (flat, ids) = flatten_handles(handles);
+            self.check(unsafe { ffi::qc_engine_ep_connect(self.h, flat.as_ptr().cast(), ids.as_ptr()) })
+        }
+    }
+    /// (handles: n x 64 bytes, device ids: n) of a list of (handle, id) pairs.
+    fn flatten_handles(handles: &[([u8; 64], i32)]) -> (Vec<u8>, Vec<c_int>) {
+        let flat = handles.iter().flat_map(|(h, _)| h.iter().copied()).collect();
+        let ids = handles.iter().map(|(_, d)| *d as c_int).collect();
+        (flat, ids)
     }
     impl Drop for Engine {
         fn drop(&mut self) {
@@ -499,6 +527,19 @@ pub mod safe {
         }
         pub fn reset(&mut self, seq: u32) -> Result<()> {
             self.engine.check(unsafe { ffi::qc_batch_reset(self.h, seq) })
+        }
+        /// Batches of an expert-parallel engine: this rank's exchange-region handle and GPU id.
+        pub fn ep_handle(&self) -> Result<([u8; 64], i32)> {
+            let mut h = [0u8; 64];
+            let mut dev: c_int = 0;
+            self.engine.check(unsafe { ffi::qc_batch_ep_handle(self.h, h.as_mut_ptr().cast(), &mut dev) })?;
+            Ok((h, dev))
+        }
+        /// Every rank's batch `ep_handle()`, in rank order; then every rank makes the same calls
+        /// with the same token counts.
+        pub fn ep_connect(&mut self, handles: &[([u8; 64], i32)]) -> Result<()> {
+            let (flat, ids) = flatten_handles(handles);
+            self.engine.check(unsafe { ffi::qc_batch_ep_connect(self.h, flat.as_ptr().cast(), ids.as_ptr()) })
         }
     }
     impl Drop for Batch<'_> {
