@@ -64,7 +64,7 @@ def peaks() -> dict:
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one k_token launch, from an ncu capture of
 # `bench.py --layers 4` (4 layers of the same shapes): fixed part (vocab projection, logits) + per layer;
 # a 48-layer token is scaled by the layer count (traffic grows in proportion to the layers).
-TOKEN_TRAFFIC_FIXED, TOKEN_TRAFFIC_PER_LAYER = 255.9e6, 40.46e6
+TOKEN_TRAFFIC_FIXED, TOKEN_TRAFFIC_PER_LAYER = 255.9e6, 39.65e6
 
 
 def model_bytes(spec, tools, pos_first: int, steps: int) -> dict:
