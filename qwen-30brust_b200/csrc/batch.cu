@@ -102,7 +102,8 @@ __global__ void __launch_bounds__(256) k_b_qkprep(BatchArgs a, uint32_t layer, c
   float* buf = hv + warp * D;
   float* kc = seq_kv(a, tk.seq, layer, 0);
   float* vc = seq_kv(a, tk.seq, layer, 1);
-  for (uint32_t h = warp; h < QH + KH; h += nw) {
+  // block (t, y): heads nw y .. nw y + nw - 1 of token t (query heads, then KV heads), one per warp
+  for (uint32_t h = blockIdx.y * nw + warp; h < min(QH + KH, (blockIdx.y + 1) * nw); h += nw) {
     const bool isq = h < QH;
     const float* src = isq ? q + ((uint64_t)t * QH + h) * D : k + ((uint64_t)t * KH + (h - QH)) * D;
     for (uint32_t i = lane; i < D; i += 32) buf[i] = src[i];
@@ -262,7 +263,8 @@ void launch_batch_matvec(const MatDesc& m, const uint8_t* xv, uint32_t xb, uint3
 
 void launch_batch_qkprep(const BatchArgs& a, uint32_t layer, const float* q_norm, const float* k_norm, float* q,
                          const float* k, const float* v, uint32_t T, cudaStream_t s) {
-  k_b_qkprep<<<T, 256, 8 * a.D * sizeof(float), s>>>(a, layer, q_norm, k_norm, q, k, v);
+  k_b_qkprep<<<dim3(T, (a.heads + a.kvheads + 7) / 8), 256, 8 * a.D * sizeof(float), s>>>(a, layer, q_norm, k_norm, q,
+                                                                                          k, v);
 }
 
 size_t batch_attention_smem(uint32_t heads, uint32_t kvheads, uint32_t D) {
